@@ -1,0 +1,16 @@
+"""pytest setup: the `gpu` marker and import paths.
+
+`-m "not gpu"` runs the oracle checks, host-side logic and the C-ABI
+export check on CPU; `-m gpu` runs the CUDA parity tests on a B200.
+"""
+import os
+import sys
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+for p in (ROOT, os.path.join(ROOT, "cat-nn-compiler_b200")):
+    if p not in sys.path:
+        sys.path.insert(0, p)
+
+
+def pytest_configure(config):
+    config.addinivalue_line("markers", "gpu: needs a CUDA B200 (sm_100a) device")
