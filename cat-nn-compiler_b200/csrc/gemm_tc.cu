@@ -1,0 +1,480 @@
+// bf16 GEMM on the 5th-generation tensor cores (tcgen05) with TMEM
+// accumulators, fed by TMA. Persistent, warp-specialized:
+//   warp 0      TMA producer (one elected thread) over a STAGES-deep ring
+//   warp 1      TMEM owner + MMA issuer (one thread), 128 x BN x 16 MMAs
+//   warps 2..5  epilogue: TMEM -> registers -> bias/activation -> HBM
+// Two TMEM accumulators (2*BN columns) let the epilogue of tile i overlap
+// the MMAs of tile i+1. Every mbarrier wait is bounded (see tc::mbar_wait).
+//
+// One kernel covers the three shapes the hot path needs:
+//   mode 0  plain C = op(A)·op(B)       (linear fwd, dgrad, wgrad, LM head)
+//   mode 1  M-grouped: rows [off[g], off[g+1]) of A and C use B_g
+//           (MoE expert GEMMs over the expert-sorted token rows)
+//   mode 2  K-grouped: C_g = A_gᵀ·B_g over the rows of group g
+//           (MoE expert weight gradients)
+// Operands are K-major or MN-major (instruction-descriptor transpose bits),
+// so no transposed copies of weights or activations are ever made.
+#include <cudaTypedefs.h>
+
+#include "ops.cuh"
+#include "tc_prims.cuh"
+
+namespace catnn {
+
+struct TcArgs {
+    int mode, groups;
+    const int32_t* offsets;
+    int M, N, K;
+    int b_group_rows;
+    void* C;
+    long long ldc, c_group_stride;
+    int c_bf16, vec_ok;
+    const float* bias;
+    int act, accumulate;
+    int* status;
+};
+
+static constexpr int BM = 128, BK = 64;
+
+struct TileInfo {
+    int g, m0, n0, kstart, klen, mlimit, arow0;
+};
+
+// Total tiles and the t-th tile of the static schedule. Groups are few
+// (experts), so a linear scan is cheaper than a device-side prefix sum.
+template <int BN>
+__device__ __forceinline__ int total_tiles(const TcArgs& a) {
+    int nt = (a.N + BN - 1) / BN;
+    if (a.mode == 0) return ((a.M + BM - 1) / BM) * nt;
+    if (a.mode == 2) return a.groups * ((a.M + BM - 1) / BM) * nt;
+    int tot = 0;
+    for (int g = 0; g < a.groups; ++g) tot += ((a.offsets[g + 1] - a.offsets[g] + BM - 1) / BM) * nt;
+    return tot;
+}
+
+template <int BN>
+__device__ __forceinline__ TileInfo tile_at(const TcArgs& a, int t) {
+    TileInfo ti;
+    int nt = (a.N + BN - 1) / BN;
+    if (a.mode == 0) {
+        ti.g = 0;
+        ti.m0 = (t / nt) * BM;
+        ti.n0 = (t % nt) * BN;
+        ti.kstart = 0;
+        ti.klen = a.K;
+        ti.mlimit = a.M;
+        ti.arow0 = 0;
+    } else if (a.mode == 2) {
+        int mt = (a.M + BM - 1) / BM;
+        int per = mt * nt;
+        ti.g = t / per;
+        int r = t % per;
+        ti.m0 = (r / nt) * BM;
+        ti.n0 = (r % nt) * BN;
+        ti.kstart = a.offsets[ti.g];
+        ti.klen = a.offsets[ti.g + 1] - ti.kstart;
+        ti.mlimit = a.M;
+        ti.arow0 = 0;
+    } else {
+        int g = 0;
+        for (; g < a.groups; ++g) {
+            int cnt = ((a.offsets[g + 1] - a.offsets[g] + BM - 1) / BM) * nt;
+            if (t < cnt) break;
+            t -= cnt;
+        }
+        ti.g = g;
+        ti.m0 = (t / nt) * BM;
+        ti.n0 = (t % nt) * BN;
+        ti.kstart = 0;
+        ti.klen = a.K;
+        ti.arow0 = a.offsets[g];
+        ti.mlimit = a.offsets[g + 1] - a.offsets[g];
+    }
+    return ti;
+}
+
+__device__ __forceinline__ float act_apply(float v, int act) {
+    if (act == CATNN_ACT_RELU) return fmaxf(v, 0.f);
+    if (act == CATNN_ACT_GELU) {
+        const float k = 0.7978845608028654f;
+        return 0.5f * v * (1.0f + tanhf(k * (v + 0.044715f * v * v * v)));
+    }
+    return v;
+}
+
+template <bool A_MN, bool B_MN, int BN, int STAGES>
+__global__ void __launch_bounds__(192, 1)
+    k_gemm_tc(const __grid_constant__ CUtensorMap mapA, const __grid_constant__ CUtensorMap mapB, TcArgs a) {
+    constexpr uint32_t A_BYTES = BM * BK * 2;
+    constexpr uint32_t B_BYTES = BN * BK * 2;
+    constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
+    constexpr uint32_t IDESC = tc::idesc_bf16(BM, BN, A_MN, B_MN);
+    constexpr uint32_t TMEM_COLS = 2 * BN;
+
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+    uint64_t* full = (uint64_t*)(smem + STAGES * STAGE_BYTES);
+    uint64_t* empty = full + STAGES;
+    uint64_t* tfull = empty + STAGES;
+    uint64_t* tempty = tfull + 2;
+    uint64_t* drain = tempty + 2;
+    uint32_t* tmem_slot = (uint32_t*)(drain + 1);
+
+    int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; ++s) {
+            tc::mbar_init(&full[s], 1);
+            tc::mbar_init(&empty[s], 1);
+        }
+        for (int i = 0; i < 2; ++i) {
+            tc::mbar_init(&tfull[i], 1);
+            tc::mbar_init(&tempty[i], 4);
+        }
+        tc::mbar_init(drain, 1);
+        tc::fence_mbar_init();
+        tc::prefetch_tmap(&mapA);
+        tc::prefetch_tmap(&mapB);
+    }
+    if (warp == 1) tc::tmem_alloc(tmem_slot, TMEM_COLS);
+    tc::tc_fence_before();
+    __syncthreads();
+    tc::tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+    const int ntiles = total_tiles<BN>(a);
+
+    if (warp == 0 && lane == 0) {
+        // ---------------- TMA producer
+        int s = 0;
+        uint32_t ph = 0;
+        int last_ph[STAGES];
+        for (int i = 0; i < STAGES; ++i) last_ph[i] = -1;
+        bool ok = true;
+        for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
+            TileInfo ti = tile_at<BN>(a, t);
+            int nkb = (ti.klen + BK - 1) / BK;
+            for (int kb = 0; kb < nkb; ++kb) {
+                if (!tc::mbar_wait(&empty[s], ph ^ 1, a.status, 1)) {
+                    ok = false;
+                    break;
+                }
+                uint8_t* sA = smem + s * STAGE_BYTES;
+                uint8_t* sB = sA + A_BYTES;
+                tc::mbar_arrive_expect_tx(&full[s], STAGE_BYTES);
+                int k = ti.kstart + kb * BK;
+                if (!A_MN) {
+                    tc::tma_load_2d(sA, &mapA, kb * BK, ti.arow0 + ti.m0, &full[s]);
+                } else {
+#pragma unroll
+                    for (int j = 0; j < BM / 64; ++j) tc::tma_load_2d(sA + j * 8192, &mapA, ti.m0 + 64 * j, k, &full[s]);
+                }
+                if (!B_MN) {
+                    int brow = (a.mode == 1 ? ti.g * a.b_group_rows : 0) + ti.n0;
+                    tc::tma_load_2d(sB, &mapB, kb * BK, brow, &full[s]);
+                } else {
+                    int brow = (a.mode == 1 ? ti.g * a.b_group_rows : 0) + k;
+#pragma unroll
+                    for (int j = 0; j < BN / 64; ++j) tc::tma_load_2d(sB + j * 8192, &mapB, ti.n0 + 64 * j, brow, &full[s]);
+                }
+                last_ph[s] = (int)ph;
+                if (++s == STAGES) {
+                    s = 0;
+                    ph ^= 1;
+                }
+            }
+        }
+        if (!ok) {
+            // Abort: let the copies already in flight land before the CTA exits.
+            for (int i = 0; i < STAGES; ++i)
+                if (last_ph[i] >= 0) tc::mbar_wait(&full[i], (uint32_t)last_ph[i], a.status, 1, 400000000ll, false);
+        }
+    } else if (warp == 1 && lane == 0) {
+        // ---------------- MMA issuer
+        int s = 0;
+        uint32_t ph = 0;
+        int it = 0;
+        bool ok = true;
+        for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x, ++it) {
+            TileInfo ti = tile_at<BN>(a, t);
+            int acc = it & 1;
+            if (!tc::mbar_wait(&tempty[acc], ((it >> 1) & 1) ^ 1, a.status, 2)) break;
+            tc::tc_fence_after();
+            uint32_t d = tmem_base + acc * BN;
+            int nkb = (ti.klen + BK - 1) / BK;
+            for (int kb = 0; kb < nkb; ++kb) {
+                if (!tc::mbar_wait(&full[s], ph, a.status, 2)) {
+                    ok = false;
+                    break;
+                }
+                tc::tc_fence_after();
+                uint32_t sA = tc::smem_u32(smem + s * STAGE_BYTES);
+                uint32_t sB = sA + A_BYTES;
+#pragma unroll
+                for (int kk = 0; kk < BK / 16; ++kk) {
+                    uint64_t ad = A_MN ? tc::sdesc(sA + kk * 2048, 8192, 1024) : tc::sdesc(sA + kk * 32, 16, 1024);
+                    uint64_t bd = B_MN ? tc::sdesc(sB + kk * 2048, 8192, 1024) : tc::sdesc(sB + kk * 32, 16, 1024);
+                    tc::mma_bf16(d, ad, bd, IDESC, (kb | kk) != 0);
+                }
+                tc::mma_commit(&empty[s]);
+                if (++s == STAGES) {
+                    s = 0;
+                    ph ^= 1;
+                }
+            }
+            if (ok) tc::mma_commit(&tfull[acc]);
+        }
+        // Drain: no MMA may still write TMEM when it is freed.
+        tc::mma_commit(drain);
+        tc::mbar_wait(drain, 0, a.status, 2, 400000000ll, false);
+    } else if (warp >= 2) {
+        // ---------------- epilogue
+        const int q = warp & 3;
+        int it = 0;
+        for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++it) {
+            TileInfo ti = tile_at<BN>(a, t);
+            int acc = it & 1;
+            if (!tc::mbar_wait(&tfull[acc], (it >> 1) & 1, a.status, 3)) break;
+            tc::tc_fence_after();
+            int row = ti.m0 + q * 32 + lane;
+            bool rv = row < ti.mlimit;
+            long long crow;
+            if (a.mode == 0) crow = (long long)row * a.ldc;
+            else if (a.mode == 1) crow = (long long)(ti.arow0 + row) * a.ldc;
+            else crow = (long long)ti.g * a.c_group_stride + (long long)row * a.ldc;
+#pragma unroll 1
+            for (int cc = 0; cc < BN / 32; ++cc) {
+                int col0 = ti.n0 + cc * 32;
+                if (col0 >= a.N) break;  // warp-uniform
+                uint32_t r[32];
+                tc::tmem_ld32(tmem_base + ((uint32_t)(q * 32) << 16) + acc * BN + cc * 32, r);
+                tc::tmem_ld_wait();
+                if (!rv) continue;
+                float v[32];
+#pragma unroll
+                for (int i = 0; i < 32; ++i) {
+                    float x = ti.klen > 0 ? __uint_as_float(r[i]) : 0.f;
+                    int col = col0 + i;
+                    if (a.bias && col < a.N) x += a.bias[col];
+                    v[i] = x;
+                }
+                bool full_chunk = a.vec_ok && (col0 + 32 <= a.N);
+                if (a.c_bf16) {
+                    bf16* p = (bf16*)a.C + crow + col0;
+                    if (full_chunk) {
+#pragma unroll
+                        for (int i4 = 0; i4 < 4; ++i4) {
+                            uint4 old;
+                            if (a.accumulate) old = *(const uint4*)(p + i4 * 8);
+                            const bf16* ob = (const bf16*)&old;
+                            uint4 pk;
+                            __nv_bfloat162* pp = (__nv_bfloat162*)&pk;
+#pragma unroll
+                            for (int j = 0; j < 4; ++j) {
+                                float x0 = v[i4 * 8 + 2 * j], x1 = v[i4 * 8 + 2 * j + 1];
+                                if (a.accumulate) {
+                                    x0 += __bfloat162float(ob[2 * j]);
+                                    x1 += __bfloat162float(ob[2 * j + 1]);
+                                }
+                                pp[j] = __floats2bfloat162_rn(act_apply(x0, a.act), act_apply(x1, a.act));
+                            }
+                            *(uint4*)(p + i4 * 8) = pk;
+                        }
+                    } else {
+                        for (int i = 0; i < 32 && col0 + i < a.N; ++i) {
+                            float x = v[i];
+                            if (a.accumulate) x += __bfloat162float(p[i]);
+                            p[i] = __float2bfloat16_rn(act_apply(x, a.act));
+                        }
+                    }
+                } else {
+                    float* p = (float*)a.C + crow + col0;
+                    if (full_chunk) {
+#pragma unroll
+                        for (int i4 = 0; i4 < 8; ++i4) {
+                            float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+                            if (a.accumulate) o = *(const float4*)(p + i4 * 4);
+                            float4 w;
+                            w.x = act_apply(v[i4 * 4 + 0] + o.x, a.act);
+                            w.y = act_apply(v[i4 * 4 + 1] + o.y, a.act);
+                            w.z = act_apply(v[i4 * 4 + 2] + o.z, a.act);
+                            w.w = act_apply(v[i4 * 4 + 3] + o.w, a.act);
+                            *(float4*)(p + i4 * 4) = w;
+                        }
+                    } else {
+                        for (int i = 0; i < 32 && col0 + i < a.N; ++i) {
+                            float x = v[i];
+                            if (a.accumulate) x += p[i];
+                            p[i] = act_apply(x, a.act);
+                        }
+                    }
+                }
+            }
+            tc::tc_fence_before();
+            __syncwarp();
+            if (lane == 0) tc::mbar_arrive(&tempty[acc]);
+        }
+    }
+    tc::tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc::tc_fence_after();
+        tc::tmem_dealloc(tmem_base, TMEM_COLS);
+    }
+}
+
+// ------------------------------------------------------------------ host
+
+static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    if (!fn) {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        CUDA_OK(cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q));
+        CATNN_CHECK(p && q == cudaDriverEntryPointSuccess, CATNN_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+        fn = (PFN_cuTensorMapEncodeTiled_v12000)p;
+    }
+    return fn;
+}
+
+// 2-D bf16 map over a row-major [rows, cols] matrix with leading dimension
+// ld (elements), box [box_cols (inner, 64 = 128 B), box_rows], 128B swizzle.
+static CUtensorMap make_map(const void* base, i64 rows, i64 cols, i64 ld, int box_cols, int box_rows) {
+    CUtensorMap m;
+    cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+    cuuint64_t strides[1] = {(cuuint64_t)(ld * 2)};
+    cuuint32_t box[2] = {(cuuint32_t)box_cols, (cuuint32_t)box_rows};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+                             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    CATNN_CHECK(r == CUDA_SUCCESS, CATNN_ERR_CUDA, "cuTensorMapEncodeTiled failed (" + std::to_string((int)r) + ")");
+    return m;
+}
+
+template <bool A_MN, bool B_MN, int BN, int STAGES>
+static void launch_tc(Context* c, const CUtensorMap& ma, const CUtensorMap& mb, const TcArgs& a, int grid) {
+    constexpr size_t smem = (size_t)STAGES * (BM * BK * 2 + BN * BK * 2) + 1024 + 256;
+    static bool attr_set[64] = {false};
+    int dev = c->device;
+    if (!attr_set[dev]) {
+        CUDA_OK(cudaFuncSetAttribute(k_gemm_tc<A_MN, B_MN, BN, STAGES>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     (int)smem));
+        attr_set[dev] = true;
+    }
+    k_gemm_tc<A_MN, B_MN, BN, STAGES><<<grid, 192, smem, c->stream>>>(ma, mb, a);
+    launched(c);
+}
+
+template <int BN, int STAGES>
+static void dispatch_tc(Context* c, bool a_mn, bool b_mn, const CUtensorMap& ma, const CUtensorMap& mb,
+                        const TcArgs& a, int grid) {
+    if (!a_mn && !b_mn) launch_tc<false, false, BN, STAGES>(c, ma, mb, a, grid);
+    else if (!a_mn && b_mn) launch_tc<false, true, BN, STAGES>(c, ma, mb, a, grid);
+    else if (a_mn && !b_mn) launch_tc<true, false, BN, STAGES>(c, ma, mb, a, grid);
+    else launch_tc<true, true, BN, STAGES>(c, ma, mb, a, grid);
+}
+
+static bool aligned16(const void* p) { return ((uintptr_t)p & 15) == 0; }
+
+// Builds both maps for op(A) [M(or rows), K] and op(B) [K, N] and launches.
+static void run_tc(Context* c, TcArgs a, bool a_mn, bool b_mn, const bf16* A, i64 a_rows, i64 a_cols, i64 lda,
+                   const bf16* B, i64 b_rows, i64 b_cols, i64 ldb, int grid_bound) {
+    const int BN = a.N <= 128 ? 128 : 256;
+    CUtensorMap ma = make_map(A, a_rows, a_cols, lda, 64, a_mn ? 64 : BM);
+    CUtensorMap mb = make_map(B, b_rows, b_cols, ldb, 64, b_mn ? 64 : BN);
+    a.status = c->status;
+    int grid = grid_bound < c->sm_count ? grid_bound : c->sm_count;
+    if (grid < 1) grid = 1;
+    if (BN == 128) dispatch_tc<128, 6>(c, a_mn, b_mn, ma, mb, a, grid);
+    else dispatch_tc<256, 4>(c, a_mn, b_mn, ma, mb, a, grid);
+}
+
+// Shapes the TMA path accepts: 16-byte aligned bases and row pitches.
+static bool tc_ok(const void* A, i64 lda, const void* B, i64 ldb) {
+    return aligned16(A) && aligned16(B) && (lda % 8) == 0 && (ldb % 8) == 0;
+}
+
+void gemm_bf16_simt(Context* c, bool ta, bool tb, i64 M, i64 N, i64 K, const bf16* A, i64 lda, const bf16* B, i64 ldb,
+                    void* C, i64 ldc, int c_dtype, const float* bias, int act, bool accumulate);
+
+void gemm_bf16_tc(Context* c, bool ta, bool tb, i64 M, i64 N, i64 K, const bf16* A, i64 lda, const bf16* B, i64 ldb,
+                  void* C, i64 ldc, int c_dtype, const float* bias, int act, bool accumulate) {
+    if (M <= 0 || N <= 0) return;
+    // Tiny or unaligned problems (e.g. the router's N = E) use the CUDA-core kernel.
+    if (N < 16 || K < 16 || !tc_ok(A, lda, B, ldb) || M * N < 128 * 64) {
+        gemm_bf16_simt(c, ta, tb, M, N, K, A, lda, B, ldb, C, ldc, c_dtype, bias, act, accumulate);
+        return;
+    }
+    CATNN_CHECK(M < (1ll << 31) && N < (1ll << 31) && K < (1ll << 31), CATNN_ERR_SHAPE, "gemm: dimension too large");
+    TcArgs a{};
+    a.mode = 0;
+    a.groups = 1;
+    a.M = (int)M;
+    a.N = (int)N;
+    a.K = (int)K;
+    a.C = C;
+    a.ldc = ldc;
+    a.c_bf16 = c_dtype == CATNN_BF16;
+    a.vec_ok = aligned16(C) && ((ldc * (a.c_bf16 ? 2 : 4)) % 16 == 0);
+    a.bias = bias;
+    a.act = act;
+    a.accumulate = accumulate ? 1 : 0;
+    const int BN = N <= 128 ? 128 : 256;
+    int tiles = cdiv(M, BM) * cdiv(N, BN);
+    // op(A): ta=0 -> A [M,K] K-major; ta=1 -> A [K,M] MN-major.
+    // op(B): tb=1 -> B [N,K] K-major; tb=0 -> B [K,N] MN-major.
+    run_tc(c, a, ta, !tb, A, ta ? K : M, ta ? M : K, lda, B, tb ? N : K, tb ? K : N, ldb, tiles);
+}
+
+void gemm_grouped_bf16_tc(Context* c, bool tb, i64 total_rows, i64 N, i64 K, int groups, const int32_t* offsets,
+                          const bf16* A, i64 lda, const bf16* B, i64 strideB, i64 ldb, void* C, i64 ldc, int c_dtype,
+                          int act, bool accumulate) {
+    if (total_rows <= 0 || N <= 0 || groups <= 0) return;
+    CATNN_CHECK(tc_ok(A, lda, B, ldb) && N >= 16 && K >= 16, CATNN_ERR_UNSUPPORTED,
+                "grouped gemm: operands must be 16-byte aligned with N, K >= 16");
+    // Expert matrices must be stacked contiguously: one 2-D map spans them.
+    CATNN_CHECK(strideB == (tb ? N : K) * ldb, CATNN_ERR_SHAPE, "grouped gemm: B groups must be contiguous");
+    TcArgs a{};
+    a.mode = 1;
+    a.groups = groups;
+    a.offsets = offsets;
+    a.M = (int)total_rows;
+    a.N = (int)N;
+    a.K = (int)K;
+    a.b_group_rows = (int)(tb ? N : K);
+    a.C = C;
+    a.ldc = ldc;
+    a.c_bf16 = c_dtype == CATNN_BF16;
+    a.vec_ok = aligned16(C) && ((ldc * (a.c_bf16 ? 2 : 4)) % 16 == 0);
+    a.act = act;
+    a.accumulate = accumulate ? 1 : 0;
+    const int BN = N <= 128 ? 128 : 256;
+    int bound = (cdiv(total_rows, BM) + groups) * cdiv(N, BN);
+    run_tc(c, a, false, !tb, A, total_rows, K, lda, B, (i64)groups * (tb ? N : K), tb ? K : N, ldb, bound);
+}
+
+void gemm_grouped_wgrad_bf16_tc(Context* c, i64 total_rows, i64 N, i64 K, int groups, const int32_t* offsets,
+                                const bf16* A, i64 lda, const bf16* D, i64 ldd, void* dB, i64 strideB, int c_dtype,
+                                bool accumulate) {
+    if (N <= 0 || K <= 0 || groups <= 0) return;
+    CATNN_CHECK(tc_ok(A, lda, D, ldd) && N >= 16 && K >= 16, CATNN_ERR_UNSUPPORTED,
+                "grouped wgrad: operands must be 16-byte aligned with N, K >= 16");
+    TcArgs a{};
+    a.mode = 2;
+    a.groups = groups;
+    a.offsets = offsets;
+    a.M = (int)K;  // output rows = A's width
+    a.N = (int)N;
+    a.K = 0;
+    a.C = dB;
+    a.ldc = N;
+    a.c_group_stride = strideB;
+    a.c_bf16 = c_dtype == CATNN_BF16;
+    a.vec_ok = aligned16(dB) && ((N * (a.c_bf16 ? 2 : 4)) % 16 == 0);
+    a.accumulate = accumulate ? 1 : 0;
+    const int BN = N <= 128 ? 128 : 256;
+    int tiles = groups * cdiv(K, BM) * cdiv(N, BN);
+    // A_g: rows of X [rows, K] read MN-major (M = K); D_g: rows of [rows, N] read MN-major.
+    run_tc(c, a, true, true, A, total_rows, K, lda, D, total_rows, N, ldd, tiles);
+}
+
+}  // namespace catnn

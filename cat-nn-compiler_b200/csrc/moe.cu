@@ -1,0 +1,342 @@
+// MoE routing and data movement: top-k router (bit-exact indices), the
+// stable counting-sort permutation, permute / weighted unpermute and their
+// adjoints, the router straight-through adjoint, and the SwiGLU gate.
+//
+// The reference runs the experts token by token (moe.rs:207-221); here the
+// (token, slot) pairs are sorted by expert once so every expert becomes one
+// dense GEMM over its rows. Rows of an expert are in token order and each
+// expert's row block is padded to `align` rows (zeros) so tensor-core tiles
+// never straddle two experts.
+#include "ops.cuh"
+
+namespace catnn {
+
+// lens/moe.rs:175-187 — k selections of the largest remaining logit, ties
+// to the lower index (a stable descending sort), then softmax over the k
+// selected: w = exp(l - max) / max(Σ, 1e-30), summed in selection order.
+__global__ void k_router_topk(const float* __restrict__ logits, i64 T, int E, int k, int32_t* __restrict__ idx,
+                              float* __restrict__ w) {
+    i64 t = blockIdx.x * (i64)blockDim.x + threadIdx.x;
+    if (t >= T) return;
+    const float* row = logits + t * E;
+    unsigned long long taken = 0ull;
+    float sel[64];
+    int kk = k < E ? k : E;
+    for (int j = 0; j < kk; ++j) {
+        int best = -1;
+        float bv = 0.f;
+        for (int e = 0; e < E; ++e) {
+            if (taken >> e & 1ull) continue;
+            float v = row[e];
+            if (best < 0 || v > bv) {
+                best = e;
+                bv = v;
+            }
+        }
+        taken |= 1ull << best;
+        idx[t * k + j] = best;
+        sel[j] = bv;
+    }
+    float mx = -INFINITY;
+    for (int j = 0; j < kk; ++j) mx = fmaxf(mx, sel[j]);
+    float s = 0.f;
+    for (int j = 0; j < kk; ++j) {
+        sel[j] = expf(sel[j] - mx);
+        s = __fadd_rn(s, sel[j]);
+    }
+    float inv = 1.0f / fmaxf(s, 1e-30f);
+    for (int j = 0; j < kk; ++j) w[t * k + j] = __fmul_rn(sel[j], inv);
+}
+
+void router_topk(Context* c, const float* logits, i64 T, i64 E, i64 k, int32_t* idx, float* w) {
+    if (T <= 0) return;
+    CATNN_CHECK(E >= 1 && E <= 64 && k >= 1 && k <= E, CATNN_ERR_SHAPE, "router: need 1 <= k <= E <= 64");
+    k_router_topk<<<cdiv(T, 128), 128, 0, c->stream>>>(logits, T, (int)E, (int)k, idx, w);
+    launched(c);
+}
+
+// Single CTA, 1024 threads. Thread i owns pairs [i*chunk, (i+1)*chunk) in
+// order; per-thread expert counts go to shared memory, are scanned down the
+// threads per expert, and each thread then places its pairs stably.
+// offsets[e] is padded to `align`; src_of[r] is the pair index t*k+j of
+// sorted row r, or -1 on padding rows; row_of[pair] is the pair's row.
+__global__ void __launch_bounds__(1024) k_permute_map(const int32_t* __restrict__ idx, i64 P, int E, int align,
+                                                      int32_t* __restrict__ counts, int32_t* __restrict__ offsets,
+                                                      int32_t* __restrict__ row_of, int32_t* __restrict__ src_of,
+                                                      i64 rows_cap, int* __restrict__ err) {
+    extern __shared__ int32_t cnt[];  // [1024][E] then [E+1] offsets
+    int tid = threadIdx.x, nt = blockDim.x;
+    i64 chunk = (P + nt - 1) / nt;
+    i64 p0 = tid * chunk, p1 = p0 + chunk < P ? p0 + chunk : P;
+    for (int e = 0; e < E; ++e) cnt[tid * E + e] = 0;
+    for (i64 p = p0; p < p1; ++p) {
+        int e = idx[p];
+        if (e < 0 || e >= E) {
+            atomicExch(err, 1);
+            continue;
+        }
+        cnt[tid * E + e] += 1;
+    }
+    __syncthreads();
+    int32_t* off = cnt + nt * E;
+    if (tid < E) {
+        int run = 0;
+        for (int i = 0; i < nt; ++i) {
+            int v = cnt[i * E + tid];
+            cnt[i * E + tid] = run;
+            run += v;
+        }
+        counts[tid] = run;
+        off[tid] = run;  // temporarily the count
+    }
+    __syncthreads();
+    if (tid == 0) {
+        int o = 0;
+        for (int e = 0; e < E; ++e) {
+            int n = off[e];
+            offsets[e] = o;
+            off[e] = o;
+            o += (n + align - 1) / align * align;
+        }
+        offsets[E] = o;
+        off[E] = o;
+        if ((i64)o > rows_cap) atomicExch(err, 2);
+    }
+    __syncthreads();
+    if ((i64)off[E] > rows_cap) return;
+    for (i64 p = p0; p < p1; ++p) {
+        int e = idx[p];
+        if (e < 0 || e >= E) continue;
+        int r = off[e] + cnt[tid * E + e];
+        cnt[tid * E + e] += 1;
+        row_of[p] = r;
+        src_of[r] = (int32_t)p;
+    }
+    __syncthreads();
+    // padding rows, then every row past the last expert up to the capacity
+    for (int e = 0; e < E; ++e) {
+        int n = counts[e];
+        for (int r = off[e] + n + tid; r < off[e + 1]; r += nt) src_of[r] = -1;
+    }
+    for (i64 r = off[E] + tid; r < rows_cap; r += nt) src_of[r] = -1;
+}
+
+void permute_map(Context* c, const int32_t* idx, i64 T, i64 E, i64 k, int align, i64 rows_cap, int32_t* counts,
+                 int32_t* offsets, int32_t* row_of, int32_t* src_of) {
+    if (T <= 0) {
+        CUDA_OK(cudaMemsetAsync(counts, 0, E * 4, c->stream));
+        CUDA_OK(cudaMemsetAsync(offsets, 0, (E + 1) * 4, c->stream));
+        return;
+    }
+    CATNN_CHECK(E >= 1 && E <= 32, CATNN_ERR_SHAPE, "permute_map: 1 <= E <= 32");
+    CATNN_CHECK(align >= 1, CATNN_ERR_INVALID, "permute_map: align >= 1");
+    i64 P = T * k;
+    CATNN_CHECK(P < (1ll << 31), CATNN_ERR_SHAPE, "permute_map: too many pairs");
+    size_t smem = (size_t)(1024 * E + E + 1) * 4;
+    static bool attr[64] = {false};
+    if (!attr[c->device]) {
+        CUDA_OK(cudaFuncSetAttribute(k_permute_map, cudaFuncAttributeMaxDynamicSharedMemorySize, (1024 * 32 + 33) * 4));
+        attr[c->device] = true;
+    }
+    k_permute_map<<<1, 1024, smem, c->stream>>>(idx, P, (int)E, align, counts, offsets, row_of, src_of, rows_cap,
+                                                c->status + 8);
+    launched(c);
+}
+
+// xp[r] = x[src_of[r] / k] (zeros on padding rows). One warp per row, 16-byte vectors.
+template <typename T>
+__global__ void k_permute(const T* __restrict__ x, const int32_t* __restrict__ src_of, i64 rows, i64 hidden, int k,
+                          T* __restrict__ xp) {
+    i64 r = blockIdx.x * 4 + (threadIdx.x >> 5);
+    int lane = threadIdx.x & 31;
+    if (r >= rows) return;
+    int p = src_of[r];
+    T* dst = xp + r * hidden;
+    if ((hidden * sizeof(T)) % 16 == 0) {
+        i64 nv = hidden * sizeof(T) / 16;
+        uint4* d = (uint4*)dst;
+        if (p < 0) {
+            for (i64 i = lane; i < nv; i += 32) d[i] = make_uint4(0, 0, 0, 0);
+        } else {
+            const uint4* s = (const uint4*)(x + (i64)(p / k) * hidden);
+            for (i64 i = lane; i < nv; i += 32) d[i] = s[i];
+        }
+    } else {
+        for (i64 i = lane; i < hidden; i += 32) dst[i] = p < 0 ? T(0.f) : x[(i64)(p / k) * hidden + i];
+    }
+}
+
+void permute_rows(Context* c, const void* x, const int32_t* src_of, i64 rows, i64 hidden, i64 k, void* xp, int dtype) {
+    if (rows <= 0) return;
+    if (dtype == CATNN_BF16)
+        k_permute<<<cdiv(rows, 4), 128, 0, c->stream>>>((const bf16*)x, src_of, rows, hidden, (int)k, (bf16*)xp);
+    else k_permute<<<cdiv(rows, 4), 128, 0, c->stream>>>((const float*)x, src_of, rows, hidden, (int)k, (float*)xp);
+    launched(c);
+}
+
+// y[t] (+)= Σ_j w[t,j] · yp[row_of[t,j]], slots in order (moe.rs:212-219:
+// out starts at 0 and adds w·y per slot; with accumulate the finished sum
+// is then added to y, as x + moe(x) does).
+template <typename T>
+__global__ void k_unpermute(const T* __restrict__ yp, const int32_t* __restrict__ row_of, const float* __restrict__ w,
+                            i64 Tn, int k, i64 hidden, T* __restrict__ y, int acc) {
+    i64 t = blockIdx.y;
+    for (i64 i = blockIdx.x * (i64)blockDim.x + threadIdx.x; i < hidden; i += (i64)gridDim.x * blockDim.x) {
+        float s = 0.f;
+        for (int j = 0; j < k; ++j) {
+            int r = row_of[t * k + j];
+            s = __fadd_rn(s, __fmul_rn(w[t * k + j], ld(yp + (i64)r * hidden + i)));
+        }
+        if (acc) s = __fadd_rn(ld(y + t * hidden + i), s);
+        st(y + t * hidden + i, s);
+    }
+}
+
+void unpermute_rows(Context* c, const void* yp, const int32_t* row_of, const float* w, i64 T, i64 k, i64 hidden, void* y,
+                    int dtype, bool accumulate) {
+    if (T <= 0 || hidden <= 0) return;
+    CATNN_CHECK(T <= 2147483647ll, CATNN_ERR_SHAPE, "unpermute: too many tokens");
+    dim3 grid(cdiv(hidden, 256), (unsigned)T);
+    if (dtype == CATNN_BF16)
+        k_unpermute<<<grid, 256, 0, c->stream>>>((const bf16*)yp, row_of, w, T, (int)k, hidden, (bf16*)y, accumulate);
+    else k_unpermute<<<grid, 256, 0, c->stream>>>((const float*)yp, row_of, w, T, (int)k, hidden, (float*)y, accumulate);
+    launched(c);
+}
+
+// Per sorted row r (pair p = src_of[r], token t = p/k):
+// dw[p] = <yp[r], dy[t]> (adjoint.rs:504), dyp[r] = w[p]·dy[t]; zeros on padding rows.
+template <typename T>
+__global__ void k_unpermute_bwd(const T* __restrict__ yp, const int32_t* __restrict__ src_of, const float* __restrict__ w,
+                                const T* __restrict__ dy, i64 rows, int k, i64 hidden, float* __restrict__ dw,
+                                T* __restrict__ dyp) {
+    i64 r = blockIdx.x * 4 + (threadIdx.x >> 5);
+    int lane = threadIdx.x & 31;
+    if (r >= rows) return;
+    int p = src_of[r];
+    if (p < 0) {
+        for (i64 i = lane; i < hidden; i += 32) dyp[r * hidden + i] = T(0.f);
+        return;
+    }
+    i64 t = p / k;
+    float wt = w[p], dot = 0.f;
+    for (i64 i = lane; i < hidden; i += 32) {
+        float g = ld(dy + t * hidden + i);
+        dot += ld(yp + r * hidden + i) * g;
+        st(dyp + r * hidden + i, __fmul_rn(g, wt));
+    }
+    dot = warp_sum(dot);
+    if (lane == 0) dw[p] = dot;
+}
+
+// dx[t] (+)= Σ_j dxp[row_of[t,j]] in slot order.
+template <typename T>
+__global__ void k_permute_bwd(const T* __restrict__ dxp, const int32_t* __restrict__ row_of, i64 Tn, int k, i64 hidden,
+                              T* __restrict__ dx, int acc) {
+    i64 t = blockIdx.y;
+    for (i64 i = blockIdx.x * (i64)blockDim.x + threadIdx.x; i < hidden; i += (i64)gridDim.x * blockDim.x) {
+        float s = 0.f;
+        for (int j = 0; j < k; ++j) s = __fadd_rn(s, ld(dxp + (i64)row_of[t * k + j] * hidden + i));
+        if (acc) s = __fadd_rn(ld(dx + t * hidden + i), s);
+        st(dx + t * hidden + i, s);
+    }
+}
+
+void unpermute_bwd(Context* c, const void* yp, const int32_t* src_of, i64 rows, const float* w, const void* dy, i64 k,
+                   i64 hidden, float* dw, void* dyp, int dtype) {
+    if (rows <= 0) return;
+    if (dtype == CATNN_BF16)
+        k_unpermute_bwd<<<cdiv(rows, 4), 128, 0, c->stream>>>((const bf16*)yp, src_of, w, (const bf16*)dy, rows, (int)k,
+                                                               hidden, dw, (bf16*)dyp);
+    else
+        k_unpermute_bwd<<<cdiv(rows, 4), 128, 0, c->stream>>>((const float*)yp, src_of, w, (const float*)dy, rows, (int)k,
+                                                               hidden, dw, (float*)dyp);
+    launched(c);
+}
+
+void permute_bwd(Context* c, const void* dxp, const int32_t* row_of, i64 T, i64 k, i64 hidden, void* dx, int dtype,
+                 bool accumulate) {
+    if (T <= 0 || hidden <= 0) return;
+    dim3 grid(cdiv(hidden, 256), (unsigned)T);
+    if (dtype == CATNN_BF16)
+        k_permute_bwd<<<grid, 256, 0, c->stream>>>((const bf16*)dxp, row_of, T, (int)k, hidden, (bf16*)dx, accumulate);
+    else k_permute_bwd<<<grid, 256, 0, c->stream>>>((const float*)dxp, row_of, T, (int)k, hidden, (float*)dx, accumulate);
+    launched(c);
+}
+
+// adjoint.rs:267-279 — on the selected experts dlogits = w·(g - <w,g>).
+__global__ void k_router_ste(const int32_t* __restrict__ idx, const float* __restrict__ w, const float* __restrict__ dw,
+                             i64 T, int E, int k, float* __restrict__ dlog) {
+    i64 t = blockIdx.x * (i64)blockDim.x + threadIdx.x;
+    if (t >= T) return;
+    float dot = 0.f;
+    for (int j = 0; j < k; ++j) dot = __fadd_rn(dot, __fmul_rn(w[t * k + j], dw[t * k + j]));
+    for (int e = 0; e < E; ++e) dlog[t * E + e] = 0.f;
+    for (int j = 0; j < k; ++j) dlog[t * E + idx[t * k + j]] = __fmul_rn(w[t * k + j], __fsub_rn(dw[t * k + j], dot));
+}
+
+void router_ste(Context* c, const int32_t* idx, const float* w, const float* dw, i64 T, i64 E, i64 k, float* dlogits) {
+    if (T <= 0) return;
+    k_router_ste<<<cdiv(T, 128), 128, 0, c->stream>>>(idx, w, dw, T, (int)E, (int)k, dlogits);
+    launched(c);
+}
+
+// moe.rs:12-14 / adjoint.rs:208-215
+__device__ __forceinline__ float silu_f(float x) { return x / (1.0f + expf(-x)); }
+__device__ __forceinline__ float silu_grad_f(float x) {
+    float s = 1.0f / (1.0f + expf(-x));
+    return s + x * s * (1.0f - s);
+}
+
+// h = silu(a) ⊙ c. a, c: [rows, F] views with leading dimension lda
+// (a fused [a | c] buffer passes cc = a + F and lda = 2F).
+template <typename T>
+__global__ void k_swiglu(const T* __restrict__ a, const T* __restrict__ cc, T* __restrict__ h, i64 rows, i64 F, i64 lda,
+                         i64 ldh) {
+    i64 n = rows * F;
+    for (i64 i = blockIdx.x * (i64)blockDim.x + threadIdx.x; i < n; i += (i64)gridDim.x * blockDim.x) {
+        i64 r = i / F, f = i % F;
+        float av = ld(a + r * lda + f), cv = ld(cc + r * lda + f);
+        st(h + r * ldh + f, silu_f(av) * cv);
+    }
+}
+
+// adjoint.rs:239-242: da = dh·c·silu'(a), dc = dh·silu(a).
+template <typename T>
+__global__ void k_swiglu_bwd(const T* __restrict__ a, const T* __restrict__ cc, const T* __restrict__ dh,
+                             T* __restrict__ da, T* __restrict__ dc, i64 rows, i64 F, i64 lda, i64 ldd) {
+    i64 n = rows * F;
+    for (i64 i = blockIdx.x * (i64)blockDim.x + threadIdx.x; i < n; i += (i64)gridDim.x * blockDim.x) {
+        i64 r = i / F, f = i % F;
+        float av = ld(a + r * lda + f), cv = ld(cc + r * lda + f), g = ld(dh + r * F + f);
+        st(da + r * ldd + f, g * cv * silu_grad_f(av));
+        st(dc + r * ldd + f, g * silu_f(av));
+    }
+}
+
+void swiglu_act(Context* c, const void* a, const void* cc, void* h, i64 rows, i64 F, i64 lda, i64 ldh, int dtype) {
+    i64 n = rows * F;
+    if (n <= 0) return;
+    int grid = (int)((n + 255) / 256);
+    if (grid > c->sm_count * 8) grid = c->sm_count * 8;
+    if (dtype == CATNN_BF16)
+        k_swiglu<<<grid, 256, 0, c->stream>>>((const bf16*)a, (const bf16*)cc, (bf16*)h, rows, F, lda, ldh);
+    else k_swiglu<<<grid, 256, 0, c->stream>>>((const float*)a, (const float*)cc, (float*)h, rows, F, lda, ldh);
+    launched(c);
+}
+
+void swiglu_act_bwd(Context* c, const void* a, const void* cc, const void* dh, void* da, void* dc, i64 rows, i64 F,
+                    i64 lda, i64 ldd, int dtype) {
+    i64 n = rows * F;
+    if (n <= 0) return;
+    int grid = (int)((n + 255) / 256);
+    if (grid > c->sm_count * 8) grid = c->sm_count * 8;
+    if (dtype == CATNN_BF16)
+        k_swiglu_bwd<<<grid, 256, 0, c->stream>>>((const bf16*)a, (const bf16*)cc, (const bf16*)dh, (bf16*)da, (bf16*)dc,
+                                                   rows, F, lda, ldd);
+    else
+        k_swiglu_bwd<<<grid, 256, 0, c->stream>>>((const float*)a, (const float*)cc, (const float*)dh, (float*)da,
+                                                   (float*)dc, rows, F, lda, ldd);
+    launched(c);
+}
+
+}  // namespace catnn

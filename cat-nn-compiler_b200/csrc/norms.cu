@@ -1,0 +1,356 @@
+// Row kernels: softmax and its adjoint, fused softmax cross-entropy
+// (forward + backward in one pass pair), MSE, LayerNorm and RMSNorm with
+// their adjoints. One CTA per row; reductions are block-wide with a fixed
+// order (deterministic run to run). Weight-vector gradients (dgamma,
+// dbeta, dw) are column reductions done in row chunks, then chunk order:
+// no atomics, so every run gives the same bits.
+#include "ops.cuh"
+
+namespace catnn {
+
+static int row_threads(i64 last) {
+    if (last <= 64) return 32;
+    if (last <= 256) return 64;
+    if (last <= 1024) return 128;
+    return 256;
+}
+
+// ---------------------------------------------------------------- softmax
+// cpu.rs:31-52: y = exp(x - max) * (1 / max(sum, 1e-30)).
+template <typename T>
+__global__ void k_softmax(const T* __restrict__ x, T* __restrict__ y, i64 last) {
+    __shared__ float red[32];
+    const T* in = x + blockIdx.x * last;
+    T* out = y + blockIdx.x * last;
+    float mx = -INFINITY;
+    for (i64 i = threadIdx.x; i < last; i += blockDim.x) mx = fmaxf(mx, ld(in + i));
+    mx = block_max(mx, red);
+    float s = 0.f;
+    for (i64 i = threadIdx.x; i < last; i += blockDim.x) s += expf(ld(in + i) - mx);
+    s = block_sum(s, red);
+    float inv = 1.0f / fmaxf(s, 1e-30f);
+    for (i64 i = threadIdx.x; i < last; i += blockDim.x) st(out + i, expf(ld(in + i) - mx) * inv);
+}
+
+// adjoint.rs:92-104: dx = y * (dy - <y, dy>).
+template <typename T>
+__global__ void k_softmax_bwd(const T* __restrict__ y, const T* __restrict__ dy, T* __restrict__ dx, i64 last) {
+    __shared__ float red[32];
+    i64 o = blockIdx.x * last;
+    float d = 0.f;
+    for (i64 i = threadIdx.x; i < last; i += blockDim.x) d += ld(y + o + i) * ld(dy + o + i);
+    d = block_sum(d, red);
+    for (i64 i = threadIdx.x; i < last; i += blockDim.x) st(dx + o + i, ld(y + o + i) * (ld(dy + o + i) - d));
+}
+
+void softmax_fwd(Context* c, const void* x, void* y, i64 rows, i64 last, int dtype) {
+    if (rows <= 0 || last <= 0) return;
+    int t = row_threads(last);
+    if (dtype == CATNN_BF16) k_softmax<<<rows, t, 0, c->stream>>>((const bf16*)x, (bf16*)y, last);
+    else k_softmax<<<rows, t, 0, c->stream>>>((const float*)x, (float*)y, last);
+    launched(c);
+}
+void softmax_bwd(Context* c, const void* y, const void* dy, void* dx, i64 rows, i64 last, int dtype) {
+    if (rows <= 0 || last <= 0) return;
+    int t = row_threads(last);
+    if (dtype == CATNN_BF16) k_softmax_bwd<<<rows, t, 0, c->stream>>>((const bf16*)y, (const bf16*)dy, (bf16*)dx, last);
+    else k_softmax_bwd<<<rows, t, 0, c->stream>>>((const float*)y, (const float*)dy, (float*)dx, last);
+    launched(c);
+}
+
+// ---------------------------------------------------------- cross-entropy
+// adjoint.rs:123-145, fused. Pass 1 (online max/sum, one read of the row),
+// then dlogits = p / rows with 1/rows taken off at the target, and the row
+// loss -ln(max(p_t, 1e-30)) into a per-row buffer that a single CTA sums in
+// row order.
+template <typename T>
+__global__ void k_xent_rows(const T* __restrict__ logits, const uint32_t* __restrict__ tg, i64 vocab, i64 rows,
+                            T* __restrict__ dlog, float* __restrict__ row_loss, int* __restrict__ err) {
+    __shared__ float red[32];
+    __shared__ float sh_m, sh_s;
+    i64 r = blockIdx.x;
+    const T* in = logits + r * vocab;
+    T* out = dlog + r * vocab;
+    // online max/sum per thread, then merge
+    float m = -INFINITY, s = 0.f;
+    for (i64 i = threadIdx.x; i < vocab; i += blockDim.x) {
+        float v = ld(in + i);
+        if (v > m) {
+            s = s * expf(m - v) + 1.0f;
+            m = v;
+        } else {
+            s += expf(v - m);
+        }
+    }
+    float gm = block_max(m, red);
+    float sc = (m == -INFINITY) ? 0.f : s * expf(m - gm);
+    float gs = block_sum(sc, red);
+    if (threadIdx.x == 0) {
+        sh_m = gm;
+        sh_s = gs;
+    }
+    __syncthreads();
+    float inv = 1.0f / fmaxf(sh_s, 1e-30f);
+    float fr = (float)rows;
+    uint32_t t = tg[r];
+    bool bad = (i64)t >= vocab;
+    if (bad && threadIdx.x == 0 && err) atomicExch(err, 1);
+    for (i64 i = threadIdx.x; i < vocab; i += blockDim.x) {
+        float p = expf(ld(in + i) - sh_m) * inv;
+        float d = p / fr;
+        if (i == (i64)t) {
+            d = d - 1.0f / fr;
+            row_loss[r] = -logf(fmaxf(p, 1e-30f));
+        }
+        st(out + i, d);
+    }
+    if (bad && threadIdx.x == 0) row_loss[r] = 0.f;
+}
+
+__global__ void k_sum_rows_mean(const float* __restrict__ v, i64 n, float* __restrict__ out) {
+    __shared__ float red[32];
+    float s = 0.f;
+    // fixed assignment: thread t sums elements t, t+B, ... in order
+    for (i64 i = threadIdx.x; i < n; i += blockDim.x) s += v[i];
+    s = block_sum(s, red);
+    if (threadIdx.x == 0) *out = s / (float)n;
+}
+
+void xent_fwdbwd(Context* c, const void* logits, const uint32_t* targets, i64 rows, i64 vocab, float* loss,
+                 void* dlogits, int dtype, int* err) {
+    if (rows <= 0 || vocab <= 0) return;
+    float* rl = (float*)c->scratch_for(rows * 4);
+    int t = row_threads(vocab);
+    if (dtype == CATNN_BF16)
+        k_xent_rows<<<rows, t, 0, c->stream>>>((const bf16*)logits, targets, vocab, rows, (bf16*)dlogits, rl, err);
+    else
+        k_xent_rows<<<rows, t, 0, c->stream>>>((const float*)logits, targets, vocab, rows, (float*)dlogits, rl, err);
+    k_sum_rows_mean<<<1, 1024, 0, c->stream>>>(rl, rows, loss);
+    launched(c, 2);
+}
+
+// adjoint.rs:106-119: loss = Σ e² / n, d = 2e/n.
+__global__ void k_mse(const float* __restrict__ p, const float* __restrict__ t, i64 n, float* __restrict__ loss,
+                      float* __restrict__ d) {
+    __shared__ float red[32];
+    float s = 0.f, fn = (float)n;
+    for (i64 i = threadIdx.x; i < n; i += blockDim.x) {
+        float e = p[i] - t[i];
+        s += e * e;
+        d[i] = 2.0f * e / fn;
+    }
+    s = block_sum(s, red);
+    if (threadIdx.x == 0) *loss = s / fn;
+}
+void mse_fwdbwd(Context* c, const float* pred, const float* target, i64 n, float* loss, float* d) {
+    if (n <= 0) return;
+    k_mse<<<1, 1024, 0, c->stream>>>(pred, target, n, loss, d);
+    launched(c);
+}
+
+// ---------------------------------------------------------------- LayerNorm
+// cpu.rs:54-78: two-pass population variance; y = (x-mean)*inv*g + b.
+template <typename T>
+__global__ void k_ln_fwd(const T* __restrict__ x, const float* __restrict__ g, const float* __restrict__ b,
+                         T* __restrict__ y, i64 last, float eps) {
+    __shared__ float red[32];
+    const T* in = x + blockIdx.x * last;
+    float s = 0.f;
+    for (i64 i = threadIdx.x; i < last; i += blockDim.x) s += ld(in + i);
+    float mean = block_sum(s, red) / (float)last;
+    float v = 0.f;
+    for (i64 i = threadIdx.x; i < last; i += blockDim.x) {
+        float d = ld(in + i) - mean;
+        v += d * d;
+    }
+    float var = block_sum(v, red) / (float)last;
+    float inv = 1.0f / sqrtf(var + eps);
+    for (i64 i = threadIdx.x; i < last; i += blockDim.x)
+        st(y + blockIdx.x * last + i, (ld(in + i) - mean) * inv * g[i] + b[i]);
+}
+
+// adjoint.rs:530-577, row part: dx = (inv/n)(n·dxhat - Σdxhat - xhat·Σ(dxhat·xhat)),
+// dxhat = dy·γ. Saves mean/inv per row for the column pass.
+template <typename T>
+__global__ void k_ln_bwd_rows(const T* __restrict__ x, const float* __restrict__ g, const T* __restrict__ dy,
+                              T* __restrict__ dx, float* __restrict__ stats, i64 last, float eps) {
+    __shared__ float red[32];
+    i64 o = blockIdx.x * last;
+    float s = 0.f;
+    for (i64 i = threadIdx.x; i < last; i += blockDim.x) s += ld(x + o + i);
+    float n = (float)last;
+    float mean = block_sum(s, red) / n;
+    float v = 0.f;
+    for (i64 i = threadIdx.x; i < last; i += blockDim.x) {
+        float d = ld(x + o + i) - mean;
+        v += d * d;
+    }
+    float inv = 1.0f / sqrtf(block_sum(v, red) / n + eps);
+    float sd = 0.f, sdx = 0.f;
+    for (i64 i = threadIdx.x; i < last; i += blockDim.x) {
+        float xh = (ld(x + o + i) - mean) * inv;
+        float dxh = ld(dy + o + i) * g[i];
+        sd += dxh;
+        sdx += dxh * xh;
+    }
+    sd = block_sum(sd, red);
+    sdx = block_sum(sdx, red);
+    for (i64 i = threadIdx.x; i < last; i += blockDim.x) {
+        float xh = (ld(x + o + i) - mean) * inv;
+        float dxh = ld(dy + o + i) * g[i];
+        st(dx + o + i, (inv / n) * (n * dxh - sd - xh * sdx));
+    }
+    if (threadIdx.x == 0) {
+        stats[2 * blockIdx.x] = mean;
+        stats[2 * blockIdx.x + 1] = inv;
+    }
+}
+
+static const int NCOL_ROWS = 128;
+// Column partials for dgamma (Σ dy·xhat) and dbeta (Σ dy) over a chunk of rows.
+template <typename T>
+__global__ void k_ln_cols(const T* __restrict__ x, const T* __restrict__ dy, const float* __restrict__ stats,
+                          i64 rows, i64 last, float* __restrict__ pg, float* __restrict__ pb) {
+    i64 j = blockIdx.x * (i64)blockDim.x + threadIdx.x;
+    if (j >= last) return;
+    i64 r0 = (i64)blockIdx.y * NCOL_ROWS, r1 = min(rows, r0 + NCOL_ROWS);
+    float sg = 0.f, sb = 0.f;
+    for (i64 r = r0; r < r1; ++r) {
+        float d = ld(dy + r * last + j);
+        float xh = (ld(x + r * last + j) - stats[2 * r]) * stats[2 * r + 1];
+        sg += d * xh;
+        sb += d;
+    }
+    pg[(i64)blockIdx.y * last + j] = sg;
+    if (pb) pb[(i64)blockIdx.y * last + j] = sb;
+}
+__global__ void k_cols_final(const float* __restrict__ p, int chunks, i64 last, float* __restrict__ out, int acc) {
+    i64 j = blockIdx.x * (i64)blockDim.x + threadIdx.x;
+    if (j >= last) return;
+    float s = 0.f;
+    for (int ch = 0; ch < chunks; ++ch) s += p[(i64)ch * last + j];
+    out[j] = acc ? out[j] + s : s;
+}
+
+void layernorm_fwd(Context* c, const void* x, const float* g, const float* b, void* y, i64 rows, i64 last,
+                   float eps, int dtype) {
+    if (rows <= 0 || last <= 0) return;
+    int t = row_threads(last);
+    if (dtype == CATNN_BF16) k_ln_fwd<<<rows, t, 0, c->stream>>>((const bf16*)x, g, b, (bf16*)y, last, eps);
+    else k_ln_fwd<<<rows, t, 0, c->stream>>>((const float*)x, g, b, (float*)y, last, eps);
+    launched(c);
+}
+
+void layernorm_bwd(Context* c, const void* x, const float* g, const void* dy, void* dx, float* dg, float* db,
+                   i64 rows, i64 last, float eps, int dtype) {
+    if (last <= 0) return;
+    if (rows <= 0) {
+        if (dg) CUDA_OK(cudaMemsetAsync(dg, 0, last * 4, c->stream));
+        if (db) CUDA_OK(cudaMemsetAsync(db, 0, last * 4, c->stream));
+        return;
+    }
+    int chunks = cdiv(rows, NCOL_ROWS);
+    size_t need = (size_t)rows * 2 * 4 + (size_t)chunks * last * 4 * 2;
+    float* stats = (float*)c->scratch_for(need);
+    float* pg = stats + rows * 2;
+    float* pb = pg + (i64)chunks * last;
+    int t = row_threads(last);
+    dim3 gc(cdiv(last, 128), chunks);
+    if (dtype == CATNN_BF16) {
+        k_ln_bwd_rows<<<rows, t, 0, c->stream>>>((const bf16*)x, g, (const bf16*)dy, (bf16*)dx, stats, last, eps);
+        k_ln_cols<<<gc, 128, 0, c->stream>>>((const bf16*)x, (const bf16*)dy, stats, rows, last, pg, pb);
+    } else {
+        k_ln_bwd_rows<<<rows, t, 0, c->stream>>>((const float*)x, g, (const float*)dy, (float*)dx, stats, last, eps);
+        k_ln_cols<<<gc, 128, 0, c->stream>>>((const float*)x, (const float*)dy, stats, rows, last, pg, pb);
+    }
+    if (dg) k_cols_final<<<cdiv(last, 128), 128, 0, c->stream>>>(pg, chunks, last, dg, 0);
+    if (db) k_cols_final<<<cdiv(last, 128), 128, 0, c->stream>>>(pb, chunks, last, db, 0);
+    launched(c, 2 + (dg ? 1 : 0) + (db ? 1 : 0));
+}
+
+// ---------------------------------------------------------------- RMSNorm
+// moe.rs:17-32: y = x * (1/sqrt(mean(x²)+eps)) * w.
+template <typename T>
+__global__ void k_rms_fwd(const T* __restrict__ x, const float* __restrict__ w, T* __restrict__ y, i64 last, float eps) {
+    __shared__ float red[32];
+    const T* in = x + blockIdx.x * last;
+    float s = 0.f;
+    for (i64 i = threadIdx.x; i < last; i += blockDim.x) {
+        float v = ld(in + i);
+        s += v * v;
+    }
+    float inv = 1.0f / sqrtf(block_sum(s, red) / (float)last + eps);
+    for (i64 i = threadIdx.x; i < last; i += blockDim.x) st(y + blockIdx.x * last + i, ld(in + i) * inv * w[i]);
+}
+
+// adjoint.rs:148-193, row part: dx = dy·inv·w + dms·(2x/n) with
+// dms = Σ(dy·x·w) · (-0.5) · (ms+eps)^-1.5; optional + dres (residual).
+template <typename T>
+__global__ void k_rms_bwd_rows(const T* __restrict__ x, const float* __restrict__ w, const T* __restrict__ dy,
+                               const T* __restrict__ dres, T* __restrict__ dx, float* __restrict__ invs, i64 last,
+                               float eps) {
+    __shared__ float red[32];
+    i64 o = blockIdx.x * last;
+    float n = (float)last;
+    float s = 0.f, di = 0.f;
+    for (i64 i = threadIdx.x; i < last; i += blockDim.x) {
+        float v = ld(x + o + i);
+        s += v * v;
+        di += ld(dy + o + i) * v * w[i];
+    }
+    float ms = block_sum(s, red) / n;
+    di = block_sum(di, red);
+    float inv = 1.0f / sqrtf(ms + eps);
+    float dms = di * -0.5f * powf(ms + eps, -1.5f);
+    for (i64 i = threadIdx.x; i < last; i += blockDim.x) {
+        float v = ld(x + o + i);
+        float r = ld(dy + o + i) * inv * w[i] + dms * (2.0f * v / n);
+        if (dres) r += ld(dres + o + i);
+        st(dx + o + i, r);
+    }
+    if (threadIdx.x == 0) invs[blockIdx.x] = inv;
+}
+
+template <typename T>
+__global__ void k_rms_cols(const T* __restrict__ x, const T* __restrict__ dy, const float* __restrict__ invs, i64 rows,
+                           i64 last, float* __restrict__ pw) {
+    i64 j = blockIdx.x * (i64)blockDim.x + threadIdx.x;
+    if (j >= last) return;
+    i64 r0 = (i64)blockIdx.y * NCOL_ROWS, r1 = min(rows, r0 + NCOL_ROWS);
+    float sw = 0.f;
+    for (i64 r = r0; r < r1; ++r) sw += ld(dy + r * last + j) * ld(x + r * last + j) * invs[r];
+    pw[(i64)blockIdx.y * last + j] = sw;
+}
+
+void rmsnorm_fwd(Context* c, const void* x, const float* w, void* y, i64 rows, i64 last, float eps, int dtype) {
+    if (rows <= 0 || last <= 0) return;
+    int t = row_threads(last);
+    if (dtype == CATNN_BF16) k_rms_fwd<<<rows, t, 0, c->stream>>>((const bf16*)x, w, (bf16*)y, last, eps);
+    else k_rms_fwd<<<rows, t, 0, c->stream>>>((const float*)x, w, (float*)y, last, eps);
+    launched(c);
+}
+
+void rmsnorm_bwd(Context* c, const void* x, const float* w, const void* dy, void* dx, float* dw, i64 rows, i64 last,
+                 float eps, int dtype, bool dw_accumulate, const void* dres) {
+    if (last <= 0) return;
+    if (rows <= 0) {
+        if (dw && !dw_accumulate) CUDA_OK(cudaMemsetAsync(dw, 0, last * 4, c->stream));
+        return;
+    }
+    int chunks = cdiv(rows, NCOL_ROWS);
+    float* invs = (float*)c->scratch_for((size_t)rows * 4 + (size_t)chunks * last * 4);
+    float* pw = invs + rows;
+    int t = row_threads(last);
+    dim3 gc(cdiv(last, 128), chunks);
+    if (dtype == CATNN_BF16) {
+        k_rms_bwd_rows<<<rows, t, 0, c->stream>>>((const bf16*)x, w, (const bf16*)dy, (const bf16*)dres, (bf16*)dx, invs, last, eps);
+        if (dw) k_rms_cols<<<gc, 128, 0, c->stream>>>((const bf16*)x, (const bf16*)dy, invs, rows, last, pw);
+    } else {
+        k_rms_bwd_rows<<<rows, t, 0, c->stream>>>((const float*)x, w, (const float*)dy, (const float*)dres, (float*)dx, invs, last, eps);
+        if (dw) k_rms_cols<<<gc, 128, 0, c->stream>>>((const float*)x, (const float*)dy, invs, rows, last, pw);
+    }
+    if (dw) k_cols_final<<<cdiv(last, 128), 128, 0, c->stream>>>(pw, chunks, last, dw, dw_accumulate ? 1 : 0);
+    launched(c, dw ? 3 : 1);
+}
+
+}  // namespace catnn

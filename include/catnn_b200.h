@@ -1,0 +1,255 @@
+/*
+ * catnn_b200.h — C ABI of libcatnn_b200, the B200 (sm_100a) execution backend
+ * for catnn's data-parallel hot path.
+ *
+ * Conventions
+ * - Every entry point returns int status (CATNN_OK = 0). On failure the
+ *   text is available from catnn_last_error() (thread-local). No C++
+ *   exception crosses this boundary.
+ * - Tensors are device pointers, row-major, dense, with explicit sizes.
+ *   Shapes follow the reference's layouts: linear weights are [in, out]
+ *   (crates/catnn-core/src/category/morphism.rs:249-252), embedding and
+ *   LM-head tables are [vocab, hidden], expert weights w1/w3 [hidden, mid],
+ *   w2 [mid, hidden], Q [B,S,H,hd], K/V [B,S,Hkv,hd].
+ * - `dtype` selects the storage type of the activations/weights of a call:
+ *   CATNN_F32 runs the fp32 parity path (FFMA, rtol 1e-5 vs the reference);
+ *   CATNN_BF16 runs the tensor-core path (bf16 operands, fp32 accumulation,
+ *   rtol 2e-2 / atol 1e-3). Scalars, losses, router weights, norms' weight
+ *   vectors and optimizer state are always fp32.
+ * - All work is enqueued on the context's stream (catnn_ctx_set_stream);
+ *   calls return before the GPU finishes unless documented otherwise.
+ * - Every call first makes the context's device current: a context may be
+ *   driven from different host threads, one at a time.
+ *
+ * Each declaration names the reference interface (file:line in
+ * dkarapetyan-afk/cat-nn-compiler) whose behaviour it reproduces.
+ */
+#ifndef CATNN_B200_H
+#define CATNN_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes. The first five mirror CatError variants
+ * (crates/catnn-core/src/error.rs:9-54). */
+#define CATNN_OK 0
+#define CATNN_ERR_SHAPE 1        /* CatError::ShapeMismatch */
+#define CATNN_ERR_DTYPE 2        /* CatError::DTypeMismatch */
+#define CATNN_ERR_UNKNOWN_PORT 3 /* CatError::UnknownPort */
+#define CATNN_ERR_WIRING 4       /* CatError::Wiring */
+#define CATNN_ERR_UNLAWFUL 5     /* CatError::Unlawful */
+#define CATNN_ERR_CUDA 6         /* a CUDA runtime call failed */
+#define CATNN_ERR_INVALID 7      /* null handle / bad argument */
+#define CATNN_ERR_TIMEOUT 8      /* a bounded device wait ran out */
+#define CATNN_ERR_UNSUPPORTED 9  /* combination not built (e.g. dtype) */
+#define CATNN_ERR_COMM 10        /* collective backend failure */
+
+#define CATNN_F32 0
+#define CATNN_BF16 1
+
+#define CATNN_ACT_NONE 0
+#define CATNN_ACT_RELU 1 /* cpu.rs:14 */
+#define CATNN_ACT_GELU 2 /* cpu.rs:20, tanh approximation */
+
+typedef struct catnn_ctx catnn_ctx;
+
+/* ------------------------------------------------------------ context */
+int catnn_version(void);
+/* Text of the last failure on this host thread ("" if none). */
+const char* catnn_last_error(void);
+/* Per-device context; replaces the CPU DeviceHandler state
+ * (crates/catnn-rt/src/handler.rs:14-28). */
+int catnn_ctx_create(int device, catnn_ctx** out);
+int catnn_ctx_destroy(catnn_ctx* ctx);
+/* stream: a cudaStream_t (NULL = legacy default stream). */
+int catnn_ctx_set_stream(catnn_ctx* ctx, void* stream);
+int catnn_ctx_synchronize(catnn_ctx* ctx);
+/* Number of kernels this context has launched (for launch accounting). */
+int catnn_ctx_launch_count(catnn_ctx* ctx, uint64_t* out);
+/* Device memory owned by the caller, and host<->device copies (synchronous
+ * w.r.t. the context stream on return). */
+int catnn_malloc(catnn_ctx* ctx, size_t bytes, void** out);
+int catnn_free(catnn_ctx* ctx, void* ptr);
+int catnn_upload(catnn_ctx* ctx, void* dst_dev, const void* src_host, size_t bytes);
+int catnn_download(catnn_ctx* ctx, void* dst_host, const void* src_dev, size_t bytes);
+/* FNV-1a checksum over the f32 bit patterns of a device tensor, the value
+ * DeviceHandler::run_kernel records per kernel (handler.rs:46-53,
+ * tensor.rs:279-288). Synchronous. */
+int catnn_checksum_f32(catnn_ctx* ctx, const float* x, int64_t n, uint64_t* out);
+
+/* ------------------------------------------------------------ dense */
+/* C[M,N] = act(op(A)·op(B) + bias) (+ C if accumulate).
+ * op(A) is [M,K]: trans_a=0 reads A as [M,K] (lda >= K), trans_a=1 as [K,M].
+ * op(B) is [K,N]: trans_b=0 reads B as [K,N] (ldb >= N), trans_b=1 as [N,K].
+ * A/B in `dtype`; C in c_dtype; bias fp32 [N] or NULL.
+ * The contraction behind cpu::matmul_mk_kn (crates/catnn-compile/src/kernel/cpu.rs:186). */
+int catnn_gemm(catnn_ctx* ctx, int trans_a, int trans_b, int64_t M, int64_t N, int64_t K,
+               const void* A, int64_t lda, const void* B, int64_t ldb, void* C, int64_t ldc,
+               int dtype, int c_dtype, const float* bias, int act, int accumulate);
+/* y[M,N] = act(x[M,K]·w[K,N] + b). cpu::linear (cpu.rs:135) and
+ * apply_fused_linear_relu (cpu.rs:306). b may be NULL. */
+int catnn_linear_fwd(catnn_ctx* ctx, const void* x, const void* w, const float* b, void* y,
+                     int64_t M, int64_t K, int64_t N, int act, int dtype);
+/* dx = dy·wᵀ, dw = xᵀ·dy, db = Σ_rows dy. adjoint::linear_backward
+ * (crates/catnn-compile/src/kernel/adjoint.rs:35). dx/dw/db may each be NULL. */
+int catnn_linear_bwd(catnn_ctx* ctx, const void* x, const void* w, const void* dy, void* dx,
+                     void* dw, float* db, int64_t M, int64_t K, int64_t N, int dtype);
+/* logits = x·wᵀ, w [vocab, hidden]. moe::lm_head (moe.rs:325). */
+int catnn_lm_head_fwd(catnn_ctx* ctx, const void* x, const void* w, void* y, int64_t rows,
+                      int64_t hidden, int64_t vocab, int dtype);
+/* LmHead adjoint (adjoint.rs:903-913). */
+int catnn_lm_head_bwd(catnn_ctx* ctx, const void* x, const void* w, const void* dy, void* dx,
+                      void* dw, int64_t rows, int64_t hidden, int64_t vocab, int dtype);
+
+/* ------------------------------------------------------------ elementwise */
+int catnn_relu_fwd(catnn_ctx* ctx, const void* x, void* y, int64_t n, int dtype);      /* cpu.rs:14 */
+int catnn_gelu_fwd(catnn_ctx* ctx, const void* x, void* y, int64_t n, int dtype);      /* cpu.rs:20 */
+int catnn_relu_bwd(catnn_ctx* ctx, const void* x, const void* dy, void* dx, int64_t n, int dtype); /* adjoint.rs:63 */
+int catnn_gelu_bwd(catnn_ctx* ctx, const void* x, const void* dy, void* dx, int64_t n, int dtype); /* adjoint.rs:76 */
+/* y = a + b; b has n elements, or b_len = last-dim elements broadcast
+ * over rows (cpu.rs:80-98). */
+int catnn_add(catnn_ctx* ctx, const void* a, const void* b, void* y, int64_t n, int64_t b_len, int dtype);
+int catnn_mul(catnn_ctx* ctx, const void* a, const void* b, void* y, int64_t n, int dtype); /* cpu.rs:100 */
+
+/* ------------------------------------------------------------ softmax / losses */
+int catnn_softmax_fwd(catnn_ctx* ctx, const void* x, void* y, int64_t rows, int64_t last, int dtype); /* cpu.rs:31 */
+int catnn_softmax_bwd(catnn_ctx* ctx, const void* y, const void* dy, void* dx, int64_t rows,
+                      int64_t last, int dtype); /* adjoint.rs:92 */
+/* Mean softmax cross-entropy, fused forward + backward. loss: device fp32
+ * scalar; dlogits may alias logits. Targets >= vocab are a ShapeMismatch
+ * (detected on device, reported by the call, which synchronizes only when
+ * check != 0). adjoint::cross_entropy (adjoint.rs:123). */
+int catnn_xent_fwdbwd(catnn_ctx* ctx, const void* logits, const uint32_t* targets, int64_t rows,
+                      int64_t vocab, float* loss, void* dlogits, int dtype, int check);
+/* Mean squared error, d = 2(p - t)/n. adjoint::mse_loss (adjoint.rs:106). fp32. */
+int catnn_mse_fwdbwd(catnn_ctx* ctx, const float* pred, const float* target, int64_t n, float* loss, float* d);
+
+/* ------------------------------------------------------------ norms */
+int catnn_layernorm_fwd(catnn_ctx* ctx, const void* x, const float* gamma, const float* beta, void* y,
+                        int64_t rows, int64_t last, float eps, int dtype); /* cpu.rs:54 */
+int catnn_layernorm_bwd(catnn_ctx* ctx, const void* x, const float* gamma, const void* dy, void* dx,
+                        float* dgamma, float* dbeta, int64_t rows, int64_t last, float eps,
+                        int dtype); /* adjoint.rs:530 */
+int catnn_rmsnorm_fwd(catnn_ctx* ctx, const void* x, const float* w, void* y, int64_t rows,
+                      int64_t last, float eps, int dtype); /* moe.rs:17 */
+int catnn_rmsnorm_bwd(catnn_ctx* ctx, const void* x, const float* w, const void* dy, void* dx,
+                      float* dw, int64_t rows, int64_t last, float eps, int dtype); /* adjoint.rs:148 */
+
+/* ------------------------------------------------------------ embedding */
+/* y[t] = table[ids[t]]. Synchronizes to report an id >= vocab as a
+ * ShapeMismatch, as moe::embedding does (moe.rs:34-45). */
+int catnn_embedding_fwd(catnn_ctx* ctx, const uint32_t* ids, int64_t n, const void* table,
+                        int64_t vocab, int64_t hidden, void* y, int dtype);
+/* dw[v] = Σ_{t: ids[t]=v} dy[t], summed in t order (deterministic, no
+ * atomics); dw is fp32 [vocab, hidden]. adjoint::embedding_backward
+ * (adjoint.rs:195). Uses context scratch. */
+int catnn_embedding_bwd(catnn_ctx* ctx, const uint32_t* ids, int64_t n, const void* dy, float* dw,
+                        int64_t vocab, int64_t hidden, int dtype);
+
+/* ------------------------------------------------------------ attention */
+/* Rotate interleaved pairs of x [B,S,heads,hd] in place by pos·θ^(-2i/hd);
+ * inverse=1 applies the adjoint rotation. moe.rs:47 / adjoint.rs:454. */
+int catnn_rope(catnn_ctx* ctx, void* x, int64_t b, int64_t s, int64_t heads, int64_t hd,
+               double theta, int inverse, int dtype);
+/* Attention core on projected (and rotated) q [B,S,H,hd], k/v [B,S,Hkv,hd]:
+ * o [B,S,H*hd], lse fp32 [B,H,S] (log-sum-exp of the scaled scores, kept
+ * for the backward). causal: j <= i; window > 0 further limits to
+ * j > i - window (moe.rs:105). Scale 1/sqrt(hd). Head h reads kv head
+ * h / (H/Hkv). The inner loops of moe::gqa (moe.rs:100-133) and
+ * cpu::attention (cpu.rs:254-295). */
+int catnn_attention_fwd(catnn_ctx* ctx, const void* q, const void* k, const void* v, void* o,
+                        float* lse, int64_t b, int64_t s, int64_t n_heads, int64_t n_kv,
+                        int64_t hd, int causal, int64_t window, int dtype);
+/* Adjoint of catnn_attention_fwd given o, lse and dout. The inner loops of
+ * gqa_backward (adjoint.rs:366-407) and attention_backward (adjoint.rs:652-703). */
+int catnn_attention_bwd(catnn_ctx* ctx, const void* q, const void* k, const void* v, const void* o,
+                        const float* lse, const void* dout, void* dq, void* dk, void* dv,
+                        int64_t b, int64_t s, int64_t n_heads, int64_t n_kv, int64_t hd, int causal,
+                        int64_t window, int dtype);
+/* Full MHA op x [B,S,d] -> y (cpu::attention, cpu.rs:235; causal=0 is the
+ * reference as-is). Weights [d,d]. Uses context scratch. */
+int catnn_mha_fwd(catnn_ctx* ctx, const void* x, const void* wq, const void* wk, const void* wv,
+                  const void* wo, void* y, int64_t b, int64_t s, int64_t d, int64_t n_heads,
+                  int causal, int dtype);
+/* attention_backward (adjoint.rs:582). */
+int catnn_mha_bwd(catnn_ctx* ctx, const void* x, const void* wq, const void* wk, const void* wv,
+                  const void* wo, const void* dy, void* dx, void* dwq, void* dwk, void* dwv,
+                  void* dwo, int64_t b, int64_t s, int64_t d, int64_t n_heads, int causal, int dtype);
+/* GQA + RoPE + optional window (moe::gqa, moe.rs:64). window <= 0: none. */
+int catnn_gqa_fwd(catnn_ctx* ctx, const void* x, const void* wq, const void* wk, const void* wv,
+                  const void* wo, void* y, int64_t b, int64_t s, int64_t d, int64_t n_heads,
+                  int64_t n_kv, int64_t hd, double theta, int64_t window, int dtype);
+/* gqa_backward (adjoint.rs:287). */
+int catnn_gqa_bwd(catnn_ctx* ctx, const void* x, const void* wq, const void* wk, const void* wv,
+                  const void* wo, const void* dy, void* dx, void* dwq, void* dwk, void* dwv,
+                  void* dwo, int64_t b, int64_t s, int64_t d, int64_t n_heads, int64_t n_kv,
+                  int64_t hd, double theta, int64_t window, int dtype);
+
+/* ------------------------------------------------------------ MoE */
+/* Per row of logits [T,E]: the k largest, ties to the lower index, then a
+ * softmax over those k. idx int32 [T,k], w fp32 [T,k]. Bit-exact indices.
+ * lens::moe::topk_softmax (crates/catnn-core/src/lens/moe.rs:175). */
+int catnn_router_topk(catnn_ctx* ctx, const float* logits, int64_t T, int64_t E, int64_t k,
+                      int32_t* idx, float* w);
+/* Stable counting sort of the T·k (token, slot) pairs by expert (E <= 32).
+ * counts int32 [E]; offsets int32 [E+1], each expert's block padded to a
+ * multiple of `align` rows; row_of int32 [T·k]: sorted row of pair t·k+j;
+ * src_of int32 [T·k + E·(align-1)]: pair index of each sorted row, -1 on
+ * padding. Rows of one expert are in token order. Synchronizes to report an
+ * out-of-range expert index. The permutation moe::moe performs implicitly
+ * (moe.rs:207-221). */
+int catnn_moe_permute_map(catnn_ctx* ctx, const int32_t* idx, int64_t T, int64_t E, int64_t k,
+                          int64_t align, int32_t* counts, int32_t* offsets, int32_t* row_of,
+                          int32_t* src_of);
+/* xp[r] = x[src_of[r] / k] for r < rows (zero rows where src_of[r] < 0). */
+int catnn_moe_permute(catnn_ctx* ctx, const void* x, const int32_t* src_of, int64_t rows,
+                      int64_t hidden, int64_t k, void* xp, int dtype);
+/* y[t] = Σ_j w[t,j] · yp[row_of[t·k+j]] in j order (moe.rs:217-219). */
+int catnn_moe_unpermute(catnn_ctx* ctx, const void* yp, const int32_t* row_of, const float* w,
+                        int64_t T, int64_t k, int64_t hidden, void* y, int dtype);
+/* SwiGLU expert w2(silu(x·w1) ⊙ (x·w3)) on x [T,hidden]. moe::swiglu (moe.rs:159). */
+int catnn_swiglu_fwd(catnn_ctx* ctx, const void* x, const void* w1, const void* w3, const void* w2,
+                     void* y, int64_t T, int64_t hidden, int64_t mid, int dtype);
+/* swiglu_backward (adjoint.rs:217). */
+int catnn_swiglu_bwd(catnn_ctx* ctx, const void* x, const void* w1, const void* w3, const void* w2,
+                     const void* dy, void* dx, void* dw1, void* dw3, void* dw2, int64_t T,
+                     int64_t hidden, int64_t mid, int dtype);
+/* Full MoE block: route, permute, grouped SwiGLU experts, weighted
+ * unpermute. w1s/w3s [E,hidden,mid], w2s [E,mid,hidden]. moe::moe (moe.rs:197). */
+int catnn_moe_fwd(catnn_ctx* ctx, const void* x, const void* gate, const void* w1s, const void* w3s,
+                  const void* w2s, void* y, int64_t T, int64_t hidden, int64_t mid, int64_t E,
+                  int64_t k, int dtype);
+/* moe_backward (adjoint.rs:471) including the router STE adjoint
+ * (adjoint.rs:255). */
+int catnn_moe_bwd(catnn_ctx* ctx, const void* x, const void* gate, const void* w1s, const void* w3s,
+                  const void* w2s, const void* dy, void* dx, void* dgate, void* dw1s, void* dw3s,
+                  void* dw2s, int64_t T, int64_t hidden, int64_t mid, int64_t E, int64_t k, int dtype);
+
+/* ------------------------------------------------------------ optimizers */
+/* p -= lr·g (Sgd::put, crates/catnn-core/src/lens/optim.rs:32). fp32
+ * master; shadow_bf16 (optional) receives bf16(p). */
+int catnn_sgd(catnn_ctx* ctx, float* p, const float* g, int64_t n, float lr, void* shadow_bf16);
+/* One Adam step at step count t (t >= 1, already incremented), in place on
+ * p, m, v (Adam::put, optim.rs:95-119; bias correction 1-β^t, divisors
+ * clamped at 1e-30). g may be fp32 or bf16 (g_dtype). */
+int catnn_adam(catnn_ctx* ctx, float* p, const void* g, float* m, float* v, int64_t n, uint64_t t,
+               float lr, float beta1, float beta2, float eps, int g_dtype, void* shadow_bf16);
+
+/* ------------------------------------------------------------ training steps */
+/* One MLP step: forward, loss, backward (train::mlp_step, train.rs:71).
+ * ce=1: softmax cross-entropy on labels (u32 [batch]); ce=0: MSE on
+ * y_mse [batch,dout]. Gradients into dw1 [din,hid], db1, dw2 [hid,dout],
+ * db2 (fp32). loss: device fp32 scalar. Uses context scratch. */
+int catnn_mlp_step(catnn_ctx* ctx, const float* w1, const float* b1, const float* w2, const float* b2,
+                   const float* x, const uint32_t* labels, const float* y_mse, int ce, int64_t batch,
+                   int64_t din, int64_t hid, int64_t dout, float* loss, float* dw1, float* db1,
+                   float* dw2, float* db2);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* CATNN_B200_H */

@@ -1,0 +1,53 @@
+"""Shared helpers for the GPU parity tests: seeded inputs, host<->device
+moves and the tolerance checks written into every comparison.
+
+Tolerances (from the parity contract):
+- fp32 path: |gpu - ref| <= 1e-5·|ref| + 1e-5·max|ref|  (RTOL_F32 with a
+  scale-aware floor: summation order differs from the reference's)
+- bf16 path: |gpu - ref| <= 2e-2·|ref| + 1e-3·max(1, max|ref|)
+- integer / index / permutation outputs and the bit-exact ops: equality.
+"""
+import numpy as np
+import torch
+
+RTOL_F32 = 1e-5
+RTOL_BF16, ATOL_BF16 = 2e-2, 1e-3
+
+
+def dev(a, dtype=torch.float32):
+    return torch.as_tensor(np.ascontiguousarray(a)).to(device="cuda", dtype=dtype).contiguous()
+
+
+def host(t):
+    return t.detach().float().cpu().numpy()
+
+
+def close_f32(got, ref, rtol=RTOL_F32, floor=RTOL_F32, what=""):
+    got = host(got) if torch.is_tensor(got) else np.asarray(got, np.float32)
+    ref = np.asarray(ref, np.float32)
+    assert got.shape == ref.shape or got.size == ref.size, (what, got.shape, ref.shape)
+    got = got.reshape(ref.shape)
+    scale = float(np.max(np.abs(ref))) if ref.size else 0.0
+    err = np.abs(got.astype(np.float64) - ref.astype(np.float64))
+    bound = rtol * np.abs(ref) + floor * max(scale, 1e-30)
+    bad = err > bound
+    assert not bad.any(), f"{what}: {int(bad.sum())}/{ref.size} out of tolerance; max err {err.max():.3e}, scale {scale:.3e}"
+
+
+def close_bf16(got, ref, what=""):
+    got = host(got) if torch.is_tensor(got) else np.asarray(got, np.float32)
+    ref = np.asarray(ref, np.float32).reshape(got.shape)
+    scale = max(1.0, float(np.max(np.abs(ref)))) if ref.size else 1.0
+    err = np.abs(got.astype(np.float64) - ref)
+    bound = RTOL_BF16 * np.abs(ref) + ATOL_BF16 * scale
+    bad = err > bound
+    assert not bad.any(), f"{what}: {int(bad.sum())}/{ref.size} out of tolerance; max err {err.max():.3e}"
+
+
+def bf16_round(a):
+    """Round an fp32 array to bf16 and back (the inputs the bf16 path sees)."""
+    return torch.as_tensor(np.ascontiguousarray(a, np.float32)).to(torch.bfloat16).float().numpy()
+
+
+def rng(seed):
+    return np.random.default_rng(seed)

@@ -1,0 +1,343 @@
+"""Per-operator parity of the CUDA kernels (through the C ABI) against the
+oracle on identical seeded inputs. fp32 path at rtol 1e-5; the ops the
+reference computes with one rounding per step (add, mul, SGD, Adam,
+embedding gather/scatter, router indices, permutations, checksums) are
+compared bit for bit."""
+import numpy as np
+import pytest
+import torch
+
+from gpu_util import bf16_round, close_bf16, close_f32, dev, host, rng
+from oracle import oracle as O
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _lib():
+    import catnn_b200
+    catnn_b200.load()
+
+
+from catnn_b200 import ops  # noqa: E402
+from catnn_b200.errors import ShapeMismatch  # noqa: E402
+
+
+@pytest.mark.parametrize("m,k,n", [(64, 784, 256), (64, 256, 10), (7, 13, 5), (1, 1, 1), (130, 257, 129)])
+def test_linear_fwd_bwd_f32(m, k, n):
+    r = rng(m * 1000 + n)
+    x = r.standard_normal((m, k)).astype(np.float32)
+    w = (r.standard_normal((k, n)) / np.sqrt(k)).astype(np.float32)
+    b = r.standard_normal(n).astype(np.float32)
+    dy = r.standard_normal((m, n)).astype(np.float32)
+    close_f32(ops.linear(dev(x), dev(w), dev(b)), O.linear(x, w, b), what="linear")
+    close_f32(ops.linear(dev(x), dev(w), dev(b), act="relu"), O.relu(O.linear(x, w, b)), what="linear+relu")
+    gx, gw, gb = ops.linear_backward(dev(x), dev(w), dev(dy))
+    rx, rw, rb = O.linear_backward(x, w, dy)
+    close_f32(gx, rx, what="dx")
+    close_f32(gw, rw, what="dw")
+    close_f32(gb, rb, what="db")
+
+
+def test_linear_kat_identity():
+    y = ops.linear(dev([[1.0, 2.0]]), dev([[1.0, 0.0], [0.0, 1.0]]))
+    assert host(y).tolist() == [[1.0, 2.0]]
+
+
+def test_elementwise():
+    r = rng(1)
+    x = r.standard_normal(10007).astype(np.float32) * 3
+    dy = r.standard_normal(10007).astype(np.float32)
+    assert np.array_equal(host(ops.relu(dev(x))), O.relu(x))
+    assert np.array_equal(host(ops.relu_backward(dev(x), dev(dy))), O.relu_backward(x, dy))
+    close_f32(ops.gelu(dev(x)), O.gelu(x), what="gelu")
+    close_f32(ops.gelu_backward(dev(x), dev(dy)), O.gelu_backward(x, dy), what="gelu'")
+    assert np.array_equal(host(ops.add(dev(x), dev(dy))), O.add(x, dy))
+    assert np.array_equal(host(ops.mul(dev(x), dev(dy))), O.mul(x, dy))
+    a = x.reshape(-1, 1).repeat(4, 1)[:1000].reshape(250, 16)
+    bias = dy[:16]
+    assert np.array_equal(host(ops.add(dev(a), dev(bias))), O.add(a, bias))
+    with pytest.raises(ShapeMismatch):
+        ops.add(dev(a), dev(dy[:7]))
+    # reference KATs
+    assert host(ops.relu(dev([-1.0, 0.0, 2.0, -0.5]))).tolist() == [0.0, 0.0, 2.0, 0.0]
+    assert host(ops.relu_backward(dev([-1.0, 2.0, 0.0]), dev([1.0, 1.0, 1.0]))).tolist() == [0.0, 1.0, 0.0]
+
+
+@pytest.mark.parametrize("rows,last", [(64, 10), (33, 1024), (4, 32000), (3, 1)])
+def test_softmax_and_ce(rows, last):
+    r = rng(rows + last)
+    z = (r.standard_normal((rows, last)) * 4).astype(np.float32)
+    close_f32(ops.softmax_last(dev(z)), O.softmax_last(z), what="softmax")
+    y = O.softmax_last(z)
+    dy = r.standard_normal((rows, last)).astype(np.float32)
+    close_f32(ops.softmax_backward(dev(y), dev(dy)), O.softmax_backward(y, dy), what="softmax'")
+    tg = r.integers(0, last, rows)
+    loss, d = ops.cross_entropy(dev(z), dev(tg, torch.int32))
+    rl, rd = O.cross_entropy(z, tg)
+    close_f32(loss, np.float32(rl), what="ce loss")
+    close_f32(d, rd, what="dlogits")
+
+
+def test_ce_rejects_bad_target():
+    with pytest.raises(ShapeMismatch):
+        ops.cross_entropy(dev(np.zeros((2, 3))), dev([0, 3], torch.int32))
+
+
+def test_softmax_grad_row_sum_kat():
+    y = ops.softmax_last(dev([[1.0, 2.0, 3.0]]))
+    dx = ops.softmax_backward(y, dev([[1.0, 1.0, 1.0]]))
+    assert abs(float(host(dx).sum())) < 1e-5
+
+
+def test_mse():
+    r = rng(3)
+    p, t = r.standard_normal(37).astype(np.float32), r.standard_normal(37).astype(np.float32)
+    loss, d = ops.mse_loss(dev(p), dev(t))
+    rl, rd = O.mse_loss(p, t)
+    close_f32(loss, np.float32(rl), what="mse")
+    close_f32(d, rd, what="mse d")
+
+
+@pytest.mark.parametrize("rows,last", [(16, 512), (5, 33), (300, 256), (2, 4096)])
+def test_norms(rows, last):
+    r = rng(rows * 7 + last)
+    x = (r.standard_normal((rows, last)) * 2 + 0.5).astype(np.float32)
+    g = r.standard_normal(last).astype(np.float32)
+    b = r.standard_normal(last).astype(np.float32)
+    dy = r.standard_normal((rows, last)).astype(np.float32)
+    close_f32(ops.layer_norm(dev(x), dev(g), dev(b)), O.layer_norm(x, g, b), what="ln")
+    gx, gg, gb = ops.layer_norm_backward(dev(x), dev(g), dev(dy))
+    rx, rg, rb = O.layer_norm_backward(x, g, dy)
+    close_f32(gx, rx, rtol=1e-4, floor=1e-5, what="ln dx")
+    close_f32(gg, rg, what="ln dgamma")
+    close_f32(gb, rb, what="ln dbeta")
+    close_f32(ops.rmsnorm(dev(x), dev(g)), O.rmsnorm(x, g), what="rms")
+    gx, gw = ops.rmsnorm_backward(dev(x), dev(g), dev(dy))
+    rx, rw = O.rmsnorm_backward(x, g, dy)
+    close_f32(gx, rx, rtol=1e-4, floor=1e-5, what="rms dx")
+    close_f32(gw, rw, what="rms dw")
+
+
+def test_embedding_exact():
+    r = rng(5)
+    table = r.standard_normal((1024, 256)).astype(np.float32)
+    ids = r.integers(0, 1024, 1000).astype(np.uint32)
+    ids[:50] = 7  # heavy repeats
+    y = ops.embedding(dev(ids, torch.int32), dev(table))
+    assert np.array_equal(host(y), O.embedding(ids, table))
+    dy = r.standard_normal((1000, 256)).astype(np.float32)
+    dw = ops.embedding_backward(dev(ids, torch.int32), dev(dy), 1024)
+    assert np.array_equal(host(dw), O.embedding_backward(ids, dy, 1024)), "scatter-add must be bit-exact (t order)"
+    with pytest.raises(ShapeMismatch):
+        ops.embedding(dev([0, 1024], torch.int32), dev(table))
+
+
+def test_rope_matches_reference_angles():
+    r = rng(6)
+    q = r.standard_normal((2, 37, 3, 64)).astype(np.float32)
+    for theta in (1e4, 1e6):
+        g = ops.rope(dev(q).clone(), theta)
+        close_f32(g, O.rope(q, theta), rtol=1e-6, floor=1e-6, what="rope")
+        back = ops.rope(g, theta, inverse=True)
+        close_f32(back, O.rope(O.rope(q, theta), -theta), rtol=1e-6, floor=1e-6, what="rope^-1")
+
+
+@pytest.mark.parametrize("b,s,h,kv,hd,window", [(1, 6, 2, 1, 4, 4), (2, 33, 4, 2, 8, 8), (2, 130, 4, 4, 64, None),
+                                                 (1, 70, 2, 2, 128, None)])
+def test_gqa_fwd_bwd(b, s, h, kv, hd, window):
+    r = rng(s * 10 + hd)
+    d = h * hd
+    x = r.standard_normal((b, s, d)).astype(np.float32)
+    wq = (r.standard_normal((d, h * hd)) / np.sqrt(d)).astype(np.float32)
+    wk = (r.standard_normal((d, kv * hd)) / np.sqrt(d)).astype(np.float32)
+    wv = (r.standard_normal((d, kv * hd)) / np.sqrt(d)).astype(np.float32)
+    wo = (r.standard_normal((h * hd, d)) / np.sqrt(d)).astype(np.float32)
+    dy = r.standard_normal((b, s, d)).astype(np.float32)
+    y = ops.gqa(*(dev(a) for a in (x, wq, wk, wv, wo)), h, kv, 1e4, window)
+    close_f32(y, O.gqa(x, wq, wk, wv, wo, h, kv, 1e4, window), rtol=1e-4, floor=1e-5, what="gqa")
+    got = ops.gqa_backward(*(dev(a) for a in (x, wq, wk, wv, wo, dy)), h, kv, 1e4, window)
+    ref = O.gqa_backward(x, wq, wk, wv, wo, dy, h, kv, 1e4, window)
+    for name, g, rr in zip(("dx", "dwq", "dwk", "dwv", "dwo"), got, ref):
+        close_f32(g, rr, rtol=1e-4, floor=1e-5, what=f"gqa {name}")
+
+
+@pytest.mark.parametrize("causal", [False, True])
+def test_mha_fwd_bwd(causal):
+    r = rng(11 + causal)
+    b, s, d, h = 2, 40, 64, 4
+    x = r.standard_normal((b, s, d)).astype(np.float32)
+    ws = [(r.standard_normal((d, d)) * 0.1).astype(np.float32) for _ in range(4)]
+    dy = r.standard_normal((b, s, d)).astype(np.float32)
+    close_f32(ops.attention(dev(x), *(dev(w) for w in ws), h, causal), O.attention(x, *ws, h, causal), rtol=1e-4,
+              floor=1e-5, what="mha")
+    got = ops.attention_backward(dev(x), *(dev(w) for w in ws), dev(dy), h, causal)
+    ref = O.attention_backward(x, *ws, dy, h, causal)
+    for name, g, rr in zip(("dx", "dwq", "dwk", "dwv", "dwo"), got, ref):
+        close_f32(g, rr, rtol=1e-4, floor=1e-5, what=f"mha {name}")
+
+
+def test_router_topk_bit_exact():
+    r = rng(12)
+    logits = r.standard_normal((4096, 8)).astype(np.float32)
+    logits[:64] = np.round(logits[:64])  # many ties
+    logits[64:70] = 0.5
+    idx, w = ops.router_topk(dev(logits), 2)
+    ri = np.stack([O.topk_softmax(row, 2)[0] for row in logits])
+    rw = np.stack([O.topk_softmax(row, 2)[1] for row in logits])
+    assert np.array_equal(host(idx).astype(np.int64), ri)
+    close_f32(w, rw, rtol=1e-6, floor=1e-7, what="router w")
+    idx, w = ops.router_topk(dev([[1.0, 3.0, 0.0, 2.0]]), 2)
+    assert host(idx).astype(int).tolist() == [[1, 3]]
+    assert abs(float(host(w).sum()) - 1.0) < 1e-6
+
+
+@pytest.mark.parametrize("align", [1, 128])
+def test_permute_map_stable(align):
+    r = rng(13)
+    T, E, k = 1000, 8, 2
+    logits = r.standard_normal((T, E)).astype(np.float32)
+    idx, _ = ops.router_topk(dev(logits), k)
+    counts, offsets, row_of, src_of = ops.moe_permute_map(idx, E, align)
+    idx_h = host(idx).astype(np.int64).reshape(-1)
+    order = np.argsort(idx_h, kind="stable")
+    cnt = np.bincount(idx_h, minlength=E)
+    assert host(counts).astype(int).tolist() == cnt.tolist()
+    off = np.zeros(E + 1, np.int64)
+    for e in range(E):
+        off[e + 1] = off[e] + -(-cnt[e] // align) * align
+    assert host(offsets).astype(int).tolist() == off.tolist()
+    src = src_of.cpu().numpy()
+    rows = []
+    for e in range(E):
+        blk = src[off[e]:off[e + 1]]
+        rows.extend(blk[:cnt[e]].tolist())
+        assert (blk[cnt[e]:] == -1).all()
+    assert rows == order.tolist(), "rows of an expert must be its pairs in token order"
+    ro = row_of.cpu().numpy()
+    assert (src[ro] == np.arange(T * k)).all()
+
+
+def test_swiglu_fwd_bwd():
+    r = rng(14)
+    x = r.standard_normal((9, 32)).astype(np.float32)
+    w1, w3 = (r.standard_normal((32, 64)) * 0.2).astype(np.float32), (r.standard_normal((32, 64)) * 0.2).astype(np.float32)
+    w2 = (r.standard_normal((64, 32)) * 0.2).astype(np.float32)
+    dy = r.standard_normal((9, 32)).astype(np.float32)
+    close_f32(ops.swiglu(*(dev(a) for a in (x, w1, w3, w2))), O.swiglu(x, w1, w3, w2), rtol=1e-4, floor=1e-5, what="swiglu")
+    got = ops.swiglu_backward(*(dev(a) for a in (x, w1, w3, w2, dy)))
+    for name, g, rr in zip(("dx", "dw1", "dw3", "dw2"), got, O.swiglu_backward(x, w1, w3, w2, dy)):
+        close_f32(g, rr, rtol=1e-4, floor=1e-5, what=f"swiglu {name}")
+
+
+@pytest.mark.parametrize("T,H,F,E,k", [(64, 32, 64, 4, 2), (300, 64, 96, 8, 2)])
+def test_moe_fwd_bwd_f32(T, H, F, E, k):
+    r = rng(T + H)
+    x = r.standard_normal((T, H)).astype(np.float32)
+    gate = r.standard_normal((H, E)).astype(np.float32)
+    w1s = (r.standard_normal((E, H, F)) * 0.1).astype(np.float32)
+    w3s = (r.standard_normal((E, H, F)) * 0.1).astype(np.float32)
+    w2s = (r.standard_normal((E, F, H)) * 0.1).astype(np.float32)
+    dy = r.standard_normal((T, H)).astype(np.float32)
+    close_f32(ops.moe(*(dev(a) for a in (x, gate, w1s, w3s, w2s)), k), O.moe(x, gate, w1s, w3s, w2s, k), rtol=1e-4,
+              floor=1e-5, what="moe")
+    got = ops.moe_backward(*(dev(a) for a in (x, gate, w1s, w3s, w2s, dy)), k)
+    ref = O.moe_backward(x, gate, w1s, w3s, w2s, dy, k)
+    for name, g, rr in zip(("dx", "dgate", "dw1", "dw3", "dw2"), got, ref):
+        close_f32(g, rr, rtol=1e-4, floor=1e-5, what=f"moe {name}")
+
+
+def test_optimizers_bit_exact():
+    r = rng(15)
+    p = r.standard_normal(100003).astype(np.float32)
+    g = r.standard_normal(100003).astype(np.float32)
+    pd = dev(p)
+    ops.sgd_(pd, dev(g), 0.05)
+    assert np.array_equal(host(pd), O.sgd_put(p, g, 0.05))
+    assert host(ops.sgd_(dev([1.0, 2.0]), dev([1.0, -1.0]), 0.5)).tolist() == [0.5, 2.5]
+    m, v = np.zeros_like(p), np.zeros_like(p)
+    pd, md, vd = dev(p), dev(m), dev(v)
+    rp = p
+    for t in range(1, 4):
+        gt = (g * t).astype(np.float32)
+        ops.adam_(pd, dev(gt), md, vd, t, 1e-3)
+        rp, m, v, tt = O.adam_put(rp, gt, m, v, t - 1, 1e-3)
+        assert tt == t
+    assert np.array_equal(host(pd), rp), "Adam must match optim.rs bit for bit"
+    assert np.array_equal(host(md), m) and np.array_equal(host(vd), v)
+
+
+def test_lm_head():
+    r = rng(16)
+    x = r.standard_normal((50, 64)).astype(np.float32)
+    w = (r.standard_normal((300, 64)) * 0.1).astype(np.float32)
+    dy = r.standard_normal((50, 300)).astype(np.float32)
+    close_f32(ops.lm_head(dev(x), dev(w)), O.lm_head(x, w), what="lm_head")
+    gx, gw = ops.lm_head_backward(dev(x), dev(w), dev(dy))
+    rx, rw = O.lm_head_backward(x, w, dy)
+    close_f32(gx, rx, what="lm dx")
+    close_f32(gw, rw, what="lm dw")
+
+
+def test_checksum_matches_reference():
+    x = O.lcg(4097, 3)
+    assert ops.checksum(dev(x)) == O.checksum(x)
+
+
+def test_mlp_step_matches_oracle():
+    r = rng(0)
+    w1 = r.uniform(-np.sqrt(6 / 1040), np.sqrt(6 / 1040), (784, 256)).astype(np.float32)
+    w2 = r.uniform(-np.sqrt(6 / 266), np.sqrt(6 / 266), (256, 10)).astype(np.float32)
+    b1, b2 = np.zeros(256, np.float32), np.zeros(10, np.float32)
+    x = r.standard_normal((64, 784)).astype(np.float32)
+    lab = r.integers(0, 10, 64)
+    loss, *grads = ops.mlp_step(dev(w1), dev(b1), dev(w2), dev(b2), dev(x), labels=dev(lab, torch.int32))
+    rl, *rg = O.mlp_step(w1, b1, w2, b2, x, labels=lab)
+    close_f32(loss, np.float32(rl), what="mlp loss")
+    for name, g, rr in zip(("dw1", "db1", "dw2", "db2"), grads, rg):
+        close_f32(g, rr, what=f"mlp {name}")
+
+
+# ------------------------------------------------------------------ bf16 / tcgen05
+@pytest.mark.parametrize("ta,tb", [(False, False), (False, True), (True, False), (True, True)])
+@pytest.mark.parametrize("M,N,K", [(256, 512, 256), (200, 300, 136), (1024, 1024, 1024), (128, 64, 64)])
+def test_gemm_bf16_tensor_core(ta, tb, M, N, K):
+    r = rng(M + N + K + 2 * ta + tb)
+    a = bf16_round((r.standard_normal((K, M) if ta else (M, K)) / np.sqrt(K)).astype(np.float32))
+    b = bf16_round(r.standard_normal((N, K) if tb else (K, N)).astype(np.float32))
+    ref = (a.T if ta else a).astype(np.float64) @ (b.T if tb else b).astype(np.float64)
+    for out_dtype in (torch.float32, torch.bfloat16):
+        c = ops.gemm(dev(a, torch.bfloat16), dev(b, torch.bfloat16), ta, tb, out_dtype=out_dtype)
+        close_bf16(c, ref.astype(np.float32), what=f"gemm ta={ta} tb={tb} {out_dtype}")
+
+
+def test_gemm_bf16_bias_act_accumulate():
+    r = rng(21)
+    M, N, K = 384, 256, 192
+    a = bf16_round(r.standard_normal((M, K)).astype(np.float32) / 8)
+    b = bf16_round(r.standard_normal((K, N)).astype(np.float32))
+    bias = r.standard_normal(N).astype(np.float32)
+    ref = a.astype(np.float64) @ b + bias
+    c = ops.gemm(dev(a, torch.bfloat16), dev(b, torch.bfloat16), out_dtype=torch.float32, bias=dev(bias), act="relu")
+    close_bf16(c, np.maximum(ref, 0).astype(np.float32), what="bias+relu")
+    c0 = dev(r.standard_normal((M, N)).astype(np.float32))
+    ref2 = host(c0) + a.astype(np.float64) @ b
+    ops.gemm(dev(a, torch.bfloat16), dev(b, torch.bfloat16), out=c0, accumulate=True)
+    close_bf16(c0, ref2.astype(np.float32), what="accumulate")
+
+
+def test_moe_bf16_grouped_tensor_core():
+    r = rng(22)
+    T, H, F, E, k = 512, 128, 256, 4, 2
+    x = bf16_round(r.standard_normal((T, H)).astype(np.float32))
+    gate = bf16_round(r.standard_normal((H, E)).astype(np.float32) * 0.3)
+    w1s = bf16_round((r.standard_normal((E, H, F)) / np.sqrt(H)).astype(np.float32))
+    w3s = bf16_round((r.standard_normal((E, H, F)) / np.sqrt(H)).astype(np.float32))
+    w2s = bf16_round((r.standard_normal((E, F, H)) / np.sqrt(F)).astype(np.float32))
+    dy = bf16_round(r.standard_normal((T, H)).astype(np.float32))
+    args = [dev(a, torch.bfloat16) for a in (x, gate, w1s, w3s, w2s)]
+    close_bf16(ops.moe(*args, k), O.moe(x, gate, w1s, w3s, w2s, k), what="moe bf16")
+    got = ops.moe_backward(*args, dev(dy, torch.bfloat16), k)
+    ref = O.moe_backward(x, gate, w1s, w3s, w2s, dy, k)
+    for name, g, rr in zip(("dx", "dgate", "dw1", "dw3", "dw2"), got, ref):
+        close_bf16(g, rr, what=f"moe bf16 {name}")
