@@ -23,11 +23,12 @@ int moe_align(int dtype) { return dtype == CATNN_BF16 ? 128 : 1; }
 
 // Expert GEMM over the expert-sorted rows: C[rows_g] = A[rows_g] · op(B_g).
 void grouped(Context* c, int dtype, bool tb, i64 rows, i64 N, i64 K, int E, const int32_t* off, const void* A, const void* B,
-             void* C, bool accumulate) {
+             void* C, bool accumulate, int c_dtype = -1) {
     i64 strideB = N * K;
+    if (c_dtype < 0) c_dtype = dtype;
     if (dtype == CATNN_BF16)
         gemm_grouped_bf16_tc(c, tb, rows, N, K, E, off, (const bf16*)A, K, (const bf16*)B, strideB, tb ? K : N, C, N,
-                             CATNN_BF16, CATNN_ACT_NONE, accumulate);
+                             c_dtype, CATNN_ACT_NONE, accumulate);
     else
         gemm_grouped_f32(c, false, tb, rows, N, K, E, off, (const float*)A, K, (const float*)B, strideB, tb ? K : N,
                          (float*)C, N, 0, accumulate);
@@ -50,14 +51,18 @@ struct MoeTemps {
     i64 rows_cap;
 };
 
+// Pre-activations (a, c), expert outputs (yp) and dh stay fp32 on every
+// path: the bf16 path rounds only the tensors that feed a tensor-core GEMM
+// (xp, h, dyp, da, dc) and the block output.
 MoeTemps moe_temps(Context* c, i64 T, i64 H, i64 F, i64 E, i64 k, int dtype, bool bwd) {
     size_t e = dsize(dtype);
+    const size_t f4 = 4;
     i64 P = T * k;
     i64 cap = P + E * (moe_align(dtype) - 1);
     std::initializer_list<size_t> sizes = {
         (size_t)T * E * 4, (size_t)P * 4, (size_t)P * 4, (size_t)T * E * 4, (size_t)P * 4, (size_t)E * 4,
-        (size_t)(E + 1) * 4, (size_t)P * 4, (size_t)cap * 4, cap * H * e, cap * F * e, cap * F * e, cap * F * e,
-        cap * H * e, cap * H * e, cap * F * e, cap * F * e, cap * F * e, cap * H * e, (size_t)T * E * e};
+        (size_t)(E + 1) * 4, (size_t)P * 4, (size_t)cap * 4, cap * H * e, cap * F * f4, cap * F * f4, cap * F * e,
+        cap * H * f4, cap * H * e, cap * F * f4, cap * F * e, cap * F * e, cap * H * e, (size_t)T * E * e};
     Carver cv(c->work_for(Carver::need(sizes)));
     MoeTemps t{};
     t.rows_cap = cap;
@@ -71,13 +76,13 @@ MoeTemps moe_temps(Context* c, i64 T, i64 H, i64 F, i64 E, i64 k, int dtype, boo
     t.row_of = cv.take<int32_t>(P);
     t.src_of = cv.take<int32_t>(cap);
     t.xp = cv.take<char>(cap * H * e);
-    t.a = cv.take<char>(cap * F * e);
-    t.cc = cv.take<char>(cap * F * e);
+    t.a = cv.take<char>(cap * F * f4);
+    t.cc = cv.take<char>(cap * F * f4);
     t.hh = cv.take<char>(cap * F * e);
-    t.yp = cv.take<char>(cap * H * e);
+    t.yp = cv.take<char>(cap * H * f4);
     if (bwd) {
         t.dyp = cv.take<char>(cap * H * e);
-        t.dh = cv.take<char>(cap * F * e);
+        t.dh = cv.take<char>(cap * F * f4);
         t.da = cv.take<char>(cap * F * e);
         t.dc = cv.take<char>(cap * F * e);
         t.dxp = cv.take<char>(cap * H * e);
@@ -95,11 +100,11 @@ void moe_forward(Context* c, const void* x, const void* gate, const void* w1s, c
     permute_map(c, t.idx, T, E, k, moe_align(dtype), t.rows_cap, t.counts, t.off, t.row_of, t.src_of);
     i64 rows = t.rows_cap;  // padded rows beyond off[E] are never touched by the grouped GEMMs
     permute_rows(c, x, t.src_of, rows, H, k, t.xp, dtype);
-    grouped(c, dtype, false, rows, F, H, (int)E, t.off, t.xp, w1s, t.a, false);
-    grouped(c, dtype, false, rows, F, H, (int)E, t.off, t.xp, w3s, t.cc, false);
-    swiglu_act(c, t.a, t.cc, t.hh, rows, F, F, F, dtype);
-    grouped(c, dtype, false, rows, H, F, (int)E, t.off, t.hh, w2s, t.yp, false);
-    if (y) unpermute_rows(c, t.yp, t.row_of, t.w, T, k, H, y, dtype, false);
+    grouped(c, dtype, false, rows, F, H, (int)E, t.off, t.xp, w1s, t.a, false, CATNN_F32);
+    grouped(c, dtype, false, rows, F, H, (int)E, t.off, t.xp, w3s, t.cc, false, CATNN_F32);
+    swiglu_act(c, t.a, t.cc, t.hh, rows, F, F, F, dtype, CATNN_F32);
+    grouped(c, dtype, false, rows, H, F, (int)E, t.off, t.hh, w2s, t.yp, false, CATNN_F32);
+    if (y) unpermute_rows(c, t.yp, t.row_of, t.w, T, k, H, y, dtype, false, CATNN_F32);
 }
 
 }  // namespace
@@ -223,10 +228,10 @@ int catnn_moe_bwd(catnn_ctx* h, const void* x, const void* gate, const void* w1s
     MoeTemps t = moe_temps(c, T, hidden, mid, E, k, dtype, true);
     moe_forward(c, x, gate, w1s, w3s, w2s, nullptr, T, hidden, mid, E, k, dtype, t);
     i64 rows = t.rows_cap, H = hidden, F = mid;
-    unpermute_bwd(c, t.yp, t.src_of, rows, t.w, dy, k, H, t.dwt, t.dyp, dtype);
-    grouped(c, dtype, true, rows, F, H, (int)E, t.off, t.dyp, w2s, t.dh, false);      // dh = dyp · w2ᵀ
-    grouped_wgrad(c, dtype, rows, H, F, (int)E, t.off, t.hh, t.dyp, dw2s);            // dw2 = hᵀ · dyp
-    swiglu_act_bwd(c, t.a, t.cc, t.dh, t.da, t.dc, rows, F, F, F, dtype);
+    unpermute_bwd(c, t.yp, t.src_of, rows, t.w, dy, k, H, t.dwt, t.dyp, dtype, CATNN_F32);
+    grouped(c, dtype, true, rows, F, H, (int)E, t.off, t.dyp, w2s, t.dh, false, CATNN_F32);  // dh = dyp · w2ᵀ
+    grouped_wgrad(c, dtype, rows, H, F, (int)E, t.off, t.hh, t.dyp, dw2s);                   // dw2 = hᵀ · dyp
+    swiglu_act_bwd(c, t.a, t.cc, t.dh, t.da, t.dc, rows, F, F, F, dtype, CATNN_F32);
     grouped(c, dtype, true, rows, H, F, (int)E, t.off, t.da, w1s, t.dxp, false);      // dxp = da · w1ᵀ
     grouped(c, dtype, true, rows, H, F, (int)E, t.off, t.dc, w3s, t.dxp, true);       //     + dc · w3ᵀ
     grouped_wgrad(c, dtype, rows, F, H, (int)E, t.off, t.xp, t.da, dw1s);             // dw1 = xpᵀ · da

@@ -177,8 +177,8 @@ void permute_rows(Context* c, const void* x, const int32_t* src_of, i64 rows, i6
 // y[t] (+)= Σ_j w[t,j] · yp[row_of[t,j]], slots in order (moe.rs:212-219:
 // out starts at 0 and adds w·y per slot; with accumulate the finished sum
 // is then added to y, as x + moe(x) does).
-template <typename T>
-__global__ void k_unpermute(const T* __restrict__ yp, const int32_t* __restrict__ row_of, const float* __restrict__ w,
+template <typename TI, typename T>
+__global__ void k_unpermute(const TI* __restrict__ yp, const int32_t* __restrict__ row_of, const float* __restrict__ w,
                             i64 Tn, int k, i64 hidden, T* __restrict__ y, int acc) {
     i64 t = blockIdx.y;
     for (i64 i = blockIdx.x * (i64)blockDim.x + threadIdx.x; i < hidden; i += (i64)gridDim.x * blockDim.x) {
@@ -193,20 +193,25 @@ __global__ void k_unpermute(const T* __restrict__ yp, const int32_t* __restrict_
 }
 
 void unpermute_rows(Context* c, const void* yp, const int32_t* row_of, const float* w, i64 T, i64 k, i64 hidden, void* y,
-                    int dtype, bool accumulate) {
+                    int dtype, bool accumulate, int yp_dtype) {
     if (T <= 0 || hidden <= 0) return;
+    if (yp_dtype < 0) yp_dtype = dtype;
     CATNN_CHECK(T <= 2147483647ll, CATNN_ERR_SHAPE, "unpermute: too many tokens");
     dim3 grid(cdiv(hidden, 256), (unsigned)T);
-    if (dtype == CATNN_BF16)
+    if (dtype == CATNN_BF16 && yp_dtype == CATNN_BF16)
         k_unpermute<<<grid, 256, 0, c->stream>>>((const bf16*)yp, row_of, w, T, (int)k, hidden, (bf16*)y, accumulate);
+    else if (dtype == CATNN_BF16)
+        k_unpermute<<<grid, 256, 0, c->stream>>>((const float*)yp, row_of, w, T, (int)k, hidden, (bf16*)y, accumulate);
+    else if (yp_dtype == CATNN_BF16)
+        k_unpermute<<<grid, 256, 0, c->stream>>>((const bf16*)yp, row_of, w, T, (int)k, hidden, (float*)y, accumulate);
     else k_unpermute<<<grid, 256, 0, c->stream>>>((const float*)yp, row_of, w, T, (int)k, hidden, (float*)y, accumulate);
     launched(c);
 }
 
 // Per sorted row r (pair p = src_of[r], token t = p/k):
 // dw[p] = <yp[r], dy[t]> (adjoint.rs:504), dyp[r] = w[p]·dy[t]; zeros on padding rows.
-template <typename T>
-__global__ void k_unpermute_bwd(const T* __restrict__ yp, const int32_t* __restrict__ src_of, const float* __restrict__ w,
+template <typename TY, typename T>
+__global__ void k_unpermute_bwd(const TY* __restrict__ yp, const int32_t* __restrict__ src_of, const float* __restrict__ w,
                                 const T* __restrict__ dy, i64 rows, int k, i64 hidden, float* __restrict__ dw,
                                 T* __restrict__ dyp) {
     i64 r = blockIdx.x * 4 + (threadIdx.x >> 5);
@@ -242,9 +247,13 @@ __global__ void k_permute_bwd(const T* __restrict__ dxp, const int32_t* __restri
 }
 
 void unpermute_bwd(Context* c, const void* yp, const int32_t* src_of, i64 rows, const float* w, const void* dy, i64 k,
-                   i64 hidden, float* dw, void* dyp, int dtype) {
+                   i64 hidden, float* dw, void* dyp, int dtype, int yp_dtype) {
     if (rows <= 0) return;
-    if (dtype == CATNN_BF16)
+    if (yp_dtype < 0) yp_dtype = dtype;
+    if (dtype == CATNN_BF16 && yp_dtype == CATNN_F32)
+        k_unpermute_bwd<<<cdiv(rows, 4), 128, 0, c->stream>>>((const float*)yp, src_of, w, (const bf16*)dy, rows, (int)k,
+                                                               hidden, dw, (bf16*)dyp);
+    else if (dtype == CATNN_BF16)
         k_unpermute_bwd<<<cdiv(rows, 4), 128, 0, c->stream>>>((const bf16*)yp, src_of, w, (const bf16*)dy, rows, (int)k,
                                                                hidden, dw, (bf16*)dyp);
     else
@@ -289,8 +298,8 @@ __device__ __forceinline__ float silu_grad_f(float x) {
 
 // h = silu(a) ⊙ c. a, c: [rows, F] views with leading dimension lda
 // (a fused [a | c] buffer passes cc = a + F and lda = 2F).
-template <typename T>
-__global__ void k_swiglu(const T* __restrict__ a, const T* __restrict__ cc, T* __restrict__ h, i64 rows, i64 F, i64 lda,
+template <typename TI, typename T>
+__global__ void k_swiglu(const TI* __restrict__ a, const TI* __restrict__ cc, T* __restrict__ h, i64 rows, i64 F, i64 lda,
                          i64 ldh) {
     i64 n = rows * F;
     for (i64 i = blockIdx.x * (i64)blockDim.x + threadIdx.x; i < n; i += (i64)gridDim.x * blockDim.x) {
@@ -301,8 +310,8 @@ __global__ void k_swiglu(const T* __restrict__ a, const T* __restrict__ cc, T* _
 }
 
 // adjoint.rs:239-242: da = dh·c·silu'(a), dc = dh·silu(a).
-template <typename T>
-__global__ void k_swiglu_bwd(const T* __restrict__ a, const T* __restrict__ cc, const T* __restrict__ dh,
+template <typename TI, typename TG, typename T>
+__global__ void k_swiglu_bwd(const TI* __restrict__ a, const TI* __restrict__ cc, const TG* __restrict__ dh,
                              T* __restrict__ da, T* __restrict__ dc, i64 rows, i64 F, i64 lda, i64 ldd) {
     i64 n = rows * F;
     for (i64 i = blockIdx.x * (i64)blockDim.x + threadIdx.x; i < n; i += (i64)gridDim.x * blockDim.x) {
@@ -313,24 +322,32 @@ __global__ void k_swiglu_bwd(const T* __restrict__ a, const T* __restrict__ cc, 
     }
 }
 
-void swiglu_act(Context* c, const void* a, const void* cc, void* h, i64 rows, i64 F, i64 lda, i64 ldh, int dtype) {
+void swiglu_act(Context* c, const void* a, const void* cc, void* h, i64 rows, i64 F, i64 lda, i64 ldh, int dtype,
+                int in_dtype) {
     i64 n = rows * F;
     if (n <= 0) return;
+    if (in_dtype < 0) in_dtype = dtype;
     int grid = (int)((n + 255) / 256);
     if (grid > c->sm_count * 8) grid = c->sm_count * 8;
-    if (dtype == CATNN_BF16)
+    if (dtype == CATNN_BF16 && in_dtype == CATNN_F32)
+        k_swiglu<<<grid, 256, 0, c->stream>>>((const float*)a, (const float*)cc, (bf16*)h, rows, F, lda, ldh);
+    else if (dtype == CATNN_BF16)
         k_swiglu<<<grid, 256, 0, c->stream>>>((const bf16*)a, (const bf16*)cc, (bf16*)h, rows, F, lda, ldh);
     else k_swiglu<<<grid, 256, 0, c->stream>>>((const float*)a, (const float*)cc, (float*)h, rows, F, lda, ldh);
     launched(c);
 }
 
 void swiglu_act_bwd(Context* c, const void* a, const void* cc, const void* dh, void* da, void* dc, i64 rows, i64 F,
-                    i64 lda, i64 ldd, int dtype) {
+                    i64 lda, i64 ldd, int dtype, int in_dtype) {
     i64 n = rows * F;
     if (n <= 0) return;
+    if (in_dtype < 0) in_dtype = dtype;
     int grid = (int)((n + 255) / 256);
     if (grid > c->sm_count * 8) grid = c->sm_count * 8;
-    if (dtype == CATNN_BF16)
+    if (dtype == CATNN_BF16 && in_dtype == CATNN_F32)
+        k_swiglu_bwd<<<grid, 256, 0, c->stream>>>((const float*)a, (const float*)cc, (const float*)dh, (bf16*)da,
+                                                   (bf16*)dc, rows, F, lda, ldd);
+    else if (dtype == CATNN_BF16)
         k_swiglu_bwd<<<grid, 256, 0, c->stream>>>((const bf16*)a, (const bf16*)cc, (const bf16*)dh, (bf16*)da, (bf16*)dc,
                                                    rows, F, lda, ldd);
     else

@@ -108,12 +108,13 @@ void router_topk(Context* c, const float* logits, i64 T, i64 E, i64 k, int32_t* 
 void permute_map(Context* c, const int32_t* idx, i64 T, i64 E, i64 k, int align, i64 rows_cap, int32_t* counts,
                  int32_t* offsets, int32_t* row_of, int32_t* src_of);
 void permute_rows(Context* c, const void* x, const int32_t* src_of, i64 rows, i64 hidden, i64 k, void* xp, int dtype);
+// yp_dtype (default: dtype) lets an fp32 expert output feed a bf16 result.
 void unpermute_rows(Context* c, const void* yp, const int32_t* row_of, const float* w, i64 T, i64 k, i64 hidden,
-                    void* y, int dtype, bool accumulate);
+                    void* y, int dtype, bool accumulate, int yp_dtype = -1);
 // Over sorted rows r (pair p = src_of[r], token t = p/k):
 // d_w[p] = <yp[r], dy[t]>; dyp[r] = w[p]*dy[t]; zeros on padding rows.
 void unpermute_bwd(Context* c, const void* yp, const int32_t* src_of, i64 rows, const float* w, const void* dy, i64 k,
-                   i64 hidden, float* dw, void* dyp, int dtype);
+                   i64 hidden, float* dw, void* dyp, int dtype, int yp_dtype = -1);
 // dx[t] (+)= Σ_j dxp[row_of[t,j]].
 void permute_bwd(Context* c, const void* dxp, const int32_t* row_of, i64 T, i64 k, i64 hidden, void* dx,
                  int dtype, bool accumulate);
@@ -122,9 +123,11 @@ void router_ste(Context* c, const int32_t* idx, const float* w, const float* dw,
                 float* dlogits);
 // h = silu(a) * c with a, c read from one [rows, 2F] buffer ([a | c]) or
 // separate buffers; and its adjoint.
+// in_dtype (default: dtype) is the storage of a, c (and dh): fp32 pre-activations
+// may feed bf16 outputs.
 void swiglu_act(Context* c, const void* a, const void* cc, void* h, i64 rows, i64 F, i64 lda, i64 ldh,
-                int dtype);
+                int dtype, int in_dtype = -1);
 void swiglu_act_bwd(Context* c, const void* a, const void* cc, const void* dh, void* da, void* dc, i64 rows,
-                    i64 F, i64 lda, i64 ldd, int dtype);
+                    i64 F, i64 lda, i64 ldd, int dtype, int in_dtype = -1);
 
 }  // namespace catnn

@@ -68,15 +68,17 @@ def test_elementwise():
 def test_softmax_and_ce(rows, last):
     r = rng(rows + last)
     z = (r.standard_normal((rows, last)) * 4).astype(np.float32)
-    close_f32(ops.softmax_last(dev(z)), O.softmax_last(z), what="softmax")
+    close_f32(ops.softmax_last(dev(z)), O.softmax_last(z), what="softmax", exact=O.softmax_last(z, f64=True))
     y = O.softmax_last(z)
     dy = r.standard_normal((rows, last)).astype(np.float32)
-    close_f32(ops.softmax_backward(dev(y), dev(dy)), O.softmax_backward(y, dy), what="softmax'")
+    close_f32(ops.softmax_backward(dev(y), dev(dy)), O.softmax_backward(y, dy), what="softmax'",
+              exact=O.softmax_backward(y, dy, f64=True))
     tg = r.integers(0, last, rows)
     loss, d = ops.cross_entropy(dev(z), dev(tg, torch.int32))
     rl, rd = O.cross_entropy(z, tg)
-    close_f32(loss, np.float32(rl), what="ce loss")
-    close_f32(d, rd, what="dlogits")
+    rl64, rd64 = O.cross_entropy(z, tg, f64=True)
+    close_f32(loss, np.float32(rl), what="ce loss", exact=rl64)
+    close_f32(d, rd, what="dlogits", exact=rd64)
 
 
 def test_ce_rejects_bad_target():
@@ -336,8 +338,11 @@ def test_moe_bf16_grouped_tensor_core():
     w2s = bf16_round((r.standard_normal((E, F, H)) / np.sqrt(F)).astype(np.float32))
     dy = bf16_round(r.standard_normal((T, H)).astype(np.float32))
     args = [dev(a, torch.bfloat16) for a in (x, gate, w1s, w3s, w2s)]
-    close_bf16(ops.moe(*args, k), O.moe(x, gate, w1s, w3s, w2s, k), what="moe bf16")
+    # Block-level band: h is rounded to bf16 before the W2 GEMM and the k
+    # slot outputs are summed (and can cancel), so the floor is 4e-3 of the
+    # output scale instead of 1e-3 (one bf16 ulp at 0.5 is 2e-3).
+    close_bf16(ops.moe(*args, k), O.moe(x, gate, w1s, w3s, w2s, k), what="moe bf16", atol=4e-3)
     got = ops.moe_backward(*args, dev(dy, torch.bfloat16), k)
     ref = O.moe_backward(x, gate, w1s, w3s, w2s, dy, k)
     for name, g, rr in zip(("dx", "dgate", "dw1", "dw3", "dw2"), got, ref):
-        close_bf16(g, rr, what=f"moe bf16 {name}")
+        close_bf16(g, rr, what=f"moe bf16 {name}", atol=4e-3)
