@@ -67,6 +67,15 @@ SIGNATURES = {
     "catnn_sgd": [VP, VP, VP, I64, F32, VP],
     "catnn_adam": [VP, VP, VP, VP, VP, I64, U64, F32, F32, F32, F32, I32, VP],
     "catnn_mlp_step": [VP, VP, VP, VP, VP, VP, VP, VP, I32, I64, I64, I64, I64, VP, VP, VP, VP, VP],
+    "catnn_moe_trainer_create": [VP, VP, PP],
+    "catnn_moe_trainer_destroy": [VP],
+    "catnn_moe_trainer_param_count": [VP, C.POINTER(I64)],
+    "catnn_moe_trainer_set_params": [VP, VP],
+    "catnn_moe_trainer_get_params": [VP, VP],
+    "catnn_moe_trainer_get_grads": [VP, VP],
+    "catnn_moe_trainer_step": [VP, VP, VP, I32],
+    "catnn_moe_trainer_step_host": [VP, VP, VP, I32],
+    "catnn_moe_trainer_check": [VP],
 }
 
 _RESTYPE = {"catnn_last_error": C.c_char_p}

@@ -22,6 +22,7 @@ struct SgemmArgs {
     const float* bias;
     int act;
     int accumulate;
+    const float* resid;  // fp32 [M, ldc] added before the activation
     // grouping (offsets == nullptr: single GEMM)
     const int32_t* offsets;
     int group_mode;  // 0: rows of A/C split by group, B_g = B + g*strideB; 1: K split (wgrad), C_g = C + g*strideC
@@ -108,6 +109,7 @@ __global__ void __launch_bounds__(256) k_sgemm(SgemmArgs a) {
             if (gn >= N) continue;
             float v = acc[i][j];
             if (a.bias) v += a.bias[gn];
+            if (a.resid) v += a.resid[gm * a.ldc + gn];
             if (a.act == CATNN_ACT_RELU) v = fmaxf(v, 0.f);
             else if (a.act == CATNN_ACT_GELU) v = gelu_dev(v);
             if (a.c_bf16) {
@@ -136,9 +138,9 @@ static void launch_sgemm(Context* c, bool ta, bool tb, const SgemmArgs& a, i64 m
 }
 
 void gemm_f32(Context* c, bool ta, bool tb, i64 M, i64 N, i64 K, const float* A, i64 lda, const float* B, i64 ldb,
-              void* C, i64 ldc, int c_dtype, const float* bias, int act, bool accumulate) {
+              void* C, i64 ldc, int c_dtype, const float* bias, int act, bool accumulate, const float* resid) {
     if (M <= 0 || N <= 0) return;
-    SgemmArgs a{M, N, K, A, lda, B, ldb, C, ldc, c_dtype == CATNN_BF16, bias, act, accumulate ? 1 : 0,
+    SgemmArgs a{M, N, K, A, lda, B, ldb, C, ldc, c_dtype == CATNN_BF16, bias, act, accumulate ? 1 : 0, resid,
                 nullptr, 0, 0, 0};
     launch_sgemm<float>(c, ta, tb, a, M, N, 1);
 }
@@ -146,9 +148,9 @@ void gemm_f32(Context* c, bool ta, bool tb, i64 M, i64 N, i64 K, const float* A,
 // CUDA-core bf16 GEMM for shapes the TMA path does not take (tiny N such
 // as the router's E, or unaligned pitches).
 void gemm_bf16_simt(Context* c, bool ta, bool tb, i64 M, i64 N, i64 K, const bf16* A, i64 lda, const bf16* B, i64 ldb,
-                    void* C, i64 ldc, int c_dtype, const float* bias, int act, bool accumulate) {
+                    void* C, i64 ldc, int c_dtype, const float* bias, int act, bool accumulate, const float* resid) {
     if (M <= 0 || N <= 0) return;
-    SgemmArgs a{M, N, K, A, lda, B, ldb, C, ldc, c_dtype == CATNN_BF16, bias, act, accumulate ? 1 : 0,
+    SgemmArgs a{M, N, K, A, lda, B, ldb, C, ldc, c_dtype == CATNN_BF16, bias, act, accumulate ? 1 : 0, resid,
                 nullptr, 0, 0, 0};
     launch_sgemm<bf16>(c, ta, tb, a, M, N, 1);
 }
@@ -158,26 +160,29 @@ void gemm_grouped_f32(Context* c, bool ta_rows, bool tb, i64 total_rows, i64 N, 
                       i64 ldc, i64 strideC, bool accumulate) {
     if (groups <= 0 || N <= 0) return;
     if (!ta_rows) {
-        SgemmArgs a{0, N, K, A, lda, B, ldb, C, ldc, 0, nullptr, 0, accumulate ? 1 : 0, offsets, 0, strideB, 0};
+        SgemmArgs a{0, N, K, A, lda, B, ldb, C, ldc, 0, nullptr, 0, accumulate ? 1 : 0, nullptr, offsets, 0, strideB, 0};
         launch_sgemm<float>(c, false, tb, a, total_rows, N, groups);
     } else {
         // C_g[K, N] = A_gᵀ · B_g over the group's rows; here K is A's width.
-        SgemmArgs a{K, N, 0, A, lda, B, ldb, C, ldc, 0, nullptr, 0, accumulate ? 1 : 0, offsets, 1, 0, strideC};
+        SgemmArgs a{K, N, 0, A, lda, B, ldb, C, ldc, 0, nullptr, 0, accumulate ? 1 : 0, nullptr, offsets, 1, 0, strideC};
         launch_sgemm<float>(c, true, false, a, K, N, groups);
     }
 }
 
 void gemm(Context* c, bool ta, bool tb, i64 M, i64 N, i64 K, const void* A, i64 lda, const void* B, i64 ldb,
-          void* C, i64 ldc, int dtype, int c_dtype, const float* bias, int act, bool accumulate) {
+          void* C, i64 ldc, int dtype, int c_dtype, const float* bias, int act, bool accumulate, const float* resid) {
     check_dtype(dtype);
     check_dtype(c_dtype);
     CATNN_CHECK(M >= 0 && N >= 0 && K >= 0, CATNN_ERR_SHAPE, "gemm: negative size");
     CATNN_CHECK(!(accumulate && act != CATNN_ACT_NONE), CATNN_ERR_INVALID, "gemm: accumulate with an activation");
+    CATNN_CHECK(!resid || c_dtype == CATNN_F32, CATNN_ERR_DTYPE, "gemm: a residual input needs an fp32 output");
     if (M == 0 || N == 0) return;
     if (dtype == CATNN_F32)
-        gemm_f32(c, ta, tb, M, N, K, (const float*)A, lda, (const float*)B, ldb, C, ldc, c_dtype, bias, act, accumulate);
+        gemm_f32(c, ta, tb, M, N, K, (const float*)A, lda, (const float*)B, ldb, C, ldc, c_dtype, bias, act, accumulate,
+                 resid);
     else
-        gemm_bf16_tc(c, ta, tb, M, N, K, (const bf16*)A, lda, (const bf16*)B, ldb, C, ldc, c_dtype, bias, act, accumulate);
+        gemm_bf16_tc(c, ta, tb, M, N, K, (const bf16*)A, lda, (const bf16*)B, ldb, C, ldc, c_dtype, bias, act, accumulate,
+                     resid);
 }
 
 }  // namespace catnn

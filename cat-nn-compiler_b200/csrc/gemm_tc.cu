@@ -30,6 +30,7 @@ struct TcArgs {
     long long ldc, c_group_stride;
     int c_bf16, vec_ok;
     const float* bias;
+    const float* resid;  // fp32 [M, ldc] added before the activation (C must be fp32)
     int act, accumulate;
     int* status;
 };
@@ -254,6 +255,7 @@ __global__ void __launch_bounds__(192, 1)
                     float x = ti.klen > 0 ? __uint_as_float(r[i]) : 0.f;
                     int col = col0 + i;
                     if (a.bias && col < a.N) x += a.bias[col];
+                    if (a.resid && col < a.N) x += a.resid[crow + col];
                     v[i] = x;
                 }
                 bool full_chunk = a.vec_ok && (col0 + 32 <= a.N);
@@ -394,14 +396,14 @@ static bool tc_ok(const void* A, i64 lda, const void* B, i64 ldb) {
 }
 
 void gemm_bf16_simt(Context* c, bool ta, bool tb, i64 M, i64 N, i64 K, const bf16* A, i64 lda, const bf16* B, i64 ldb,
-                    void* C, i64 ldc, int c_dtype, const float* bias, int act, bool accumulate);
+                    void* C, i64 ldc, int c_dtype, const float* bias, int act, bool accumulate, const float* resid);
 
 void gemm_bf16_tc(Context* c, bool ta, bool tb, i64 M, i64 N, i64 K, const bf16* A, i64 lda, const bf16* B, i64 ldb,
-                  void* C, i64 ldc, int c_dtype, const float* bias, int act, bool accumulate) {
+                  void* C, i64 ldc, int c_dtype, const float* bias, int act, bool accumulate, const float* resid) {
     if (M <= 0 || N <= 0) return;
     // Tiny or unaligned problems (e.g. the router's N = E) use the CUDA-core kernel.
     if (N < 16 || K < 16 || !tc_ok(A, lda, B, ldb) || M * N < 128 * 64) {
-        gemm_bf16_simt(c, ta, tb, M, N, K, A, lda, B, ldb, C, ldc, c_dtype, bias, act, accumulate);
+        gemm_bf16_simt(c, ta, tb, M, N, K, A, lda, B, ldb, C, ldc, c_dtype, bias, act, accumulate, resid);
         return;
     }
     CATNN_CHECK(M < (1ll << 31) && N < (1ll << 31) && K < (1ll << 31), CATNN_ERR_SHAPE, "gemm: dimension too large");
@@ -416,6 +418,7 @@ void gemm_bf16_tc(Context* c, bool ta, bool tb, i64 M, i64 N, i64 K, const bf16*
     a.c_bf16 = c_dtype == CATNN_BF16;
     a.vec_ok = aligned16(C) && ((ldc * (a.c_bf16 ? 2 : 4)) % 16 == 0);
     a.bias = bias;
+    a.resid = resid;
     a.act = act;
     a.accumulate = accumulate ? 1 : 0;
     const int BN = N <= 128 ? 128 : 256;

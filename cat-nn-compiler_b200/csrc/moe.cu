@@ -179,7 +179,7 @@ void permute_rows(Context* c, const void* x, const int32_t* src_of, i64 rows, i6
 // is then added to y, as x + moe(x) does).
 template <typename TI, typename T>
 __global__ void k_unpermute(const TI* __restrict__ yp, const int32_t* __restrict__ row_of, const float* __restrict__ w,
-                            i64 Tn, int k, i64 hidden, T* __restrict__ y, int acc) {
+                            i64 Tn, int k, i64 hidden, T* __restrict__ y, int acc, const T* __restrict__ resid) {
     i64 t = blockIdx.y;
     for (i64 i = blockIdx.x * (i64)blockDim.x + threadIdx.x; i < hidden; i += (i64)gridDim.x * blockDim.x) {
         float s = 0.f;
@@ -188,31 +188,38 @@ __global__ void k_unpermute(const TI* __restrict__ yp, const int32_t* __restrict
             s = __fadd_rn(s, __fmul_rn(w[t * k + j], ld(yp + (i64)r * hidden + i)));
         }
         if (acc) s = __fadd_rn(ld(y + t * hidden + i), s);
+        if (resid) s = __fadd_rn(ld(resid + t * hidden + i), s);
         st(y + t * hidden + i, s);
     }
 }
 
 void unpermute_rows(Context* c, const void* yp, const int32_t* row_of, const float* w, i64 T, i64 k, i64 hidden, void* y,
-                    int dtype, bool accumulate, int yp_dtype) {
+                    int dtype, bool accumulate, int yp_dtype, const void* resid) {
     if (T <= 0 || hidden <= 0) return;
     if (yp_dtype < 0) yp_dtype = dtype;
     CATNN_CHECK(T <= 2147483647ll, CATNN_ERR_SHAPE, "unpermute: too many tokens");
     dim3 grid(cdiv(hidden, 256), (unsigned)T);
+    int acc = accumulate ? 1 : 0;
     if (dtype == CATNN_BF16 && yp_dtype == CATNN_BF16)
-        k_unpermute<<<grid, 256, 0, c->stream>>>((const bf16*)yp, row_of, w, T, (int)k, hidden, (bf16*)y, accumulate);
+        k_unpermute<<<grid, 256, 0, c->stream>>>((const bf16*)yp, row_of, w, T, (int)k, hidden, (bf16*)y, acc,
+                                                 (const bf16*)resid);
     else if (dtype == CATNN_BF16)
-        k_unpermute<<<grid, 256, 0, c->stream>>>((const float*)yp, row_of, w, T, (int)k, hidden, (bf16*)y, accumulate);
+        k_unpermute<<<grid, 256, 0, c->stream>>>((const float*)yp, row_of, w, T, (int)k, hidden, (bf16*)y, acc,
+                                                 (const bf16*)resid);
     else if (yp_dtype == CATNN_BF16)
-        k_unpermute<<<grid, 256, 0, c->stream>>>((const bf16*)yp, row_of, w, T, (int)k, hidden, (float*)y, accumulate);
-    else k_unpermute<<<grid, 256, 0, c->stream>>>((const float*)yp, row_of, w, T, (int)k, hidden, (float*)y, accumulate);
+        k_unpermute<<<grid, 256, 0, c->stream>>>((const bf16*)yp, row_of, w, T, (int)k, hidden, (float*)y, acc,
+                                                 (const float*)resid);
+    else
+        k_unpermute<<<grid, 256, 0, c->stream>>>((const float*)yp, row_of, w, T, (int)k, hidden, (float*)y, acc,
+                                                 (const float*)resid);
     launched(c);
 }
 
 // Per sorted row r (pair p = src_of[r], token t = p/k):
 // dw[p] = <yp[r], dy[t]> (adjoint.rs:504), dyp[r] = w[p]·dy[t]; zeros on padding rows.
-template <typename TY, typename T>
+template <typename TY, typename TG, typename T>
 __global__ void k_unpermute_bwd(const TY* __restrict__ yp, const int32_t* __restrict__ src_of, const float* __restrict__ w,
-                                const T* __restrict__ dy, i64 rows, int k, i64 hidden, float* __restrict__ dw,
+                                const TG* __restrict__ dy, i64 rows, int k, i64 hidden, float* __restrict__ dw,
                                 T* __restrict__ dyp) {
     i64 r = blockIdx.x * 4 + (threadIdx.x >> 5);
     int lane = threadIdx.x & 31;
@@ -234,8 +241,8 @@ __global__ void k_unpermute_bwd(const TY* __restrict__ yp, const int32_t* __rest
 }
 
 // dx[t] (+)= Σ_j dxp[row_of[t,j]] in slot order.
-template <typename T>
-__global__ void k_permute_bwd(const T* __restrict__ dxp, const int32_t* __restrict__ row_of, i64 Tn, int k, i64 hidden,
+template <typename TI, typename T>
+__global__ void k_permute_bwd(const TI* __restrict__ dxp, const int32_t* __restrict__ row_of, i64 Tn, int k, i64 hidden,
                               T* __restrict__ dx, int acc) {
     i64 t = blockIdx.y;
     for (i64 i = blockIdx.x * (i64)blockDim.x + threadIdx.x; i < hidden; i += (i64)gridDim.x * blockDim.x) {
@@ -247,26 +254,34 @@ __global__ void k_permute_bwd(const T* __restrict__ dxp, const int32_t* __restri
 }
 
 void unpermute_bwd(Context* c, const void* yp, const int32_t* src_of, i64 rows, const float* w, const void* dy, i64 k,
-                   i64 hidden, float* dw, void* dyp, int dtype, int yp_dtype) {
+                   i64 hidden, float* dw, void* dyp, int dtype, int yp_dtype, int dy_dtype) {
     if (rows <= 0) return;
     if (yp_dtype < 0) yp_dtype = dtype;
-    if (dtype == CATNN_BF16 && yp_dtype == CATNN_F32)
-        k_unpermute_bwd<<<cdiv(rows, 4), 128, 0, c->stream>>>((const float*)yp, src_of, w, (const bf16*)dy, rows, (int)k,
-                                                               hidden, dw, (bf16*)dyp);
-    else if (dtype == CATNN_BF16)
-        k_unpermute_bwd<<<cdiv(rows, 4), 128, 0, c->stream>>>((const bf16*)yp, src_of, w, (const bf16*)dy, rows, (int)k,
-                                                               hidden, dw, (bf16*)dyp);
-    else
-        k_unpermute_bwd<<<cdiv(rows, 4), 128, 0, c->stream>>>((const float*)yp, src_of, w, (const float*)dy, rows, (int)k,
-                                                               hidden, dw, (float*)dyp);
+    if (dy_dtype < 0) dy_dtype = dtype;
+    dim3 g(cdiv(rows, 4));
+#define UPB(TY, TG, T) \
+    k_unpermute_bwd<<<g, 128, 0, c->stream>>>((const TY*)yp, src_of, w, (const TG*)dy, rows, (int)k, hidden, dw, (T*)dyp)
+    if (dtype == CATNN_BF16) {
+        if (yp_dtype == CATNN_F32 && dy_dtype == CATNN_F32) UPB(float, float, bf16);
+        else if (yp_dtype == CATNN_F32) UPB(float, bf16, bf16);
+        else if (dy_dtype == CATNN_F32) UPB(bf16, float, bf16);
+        else UPB(bf16, bf16, bf16);
+    } else {
+        CATNN_CHECK(yp_dtype == CATNN_F32 && dy_dtype == CATNN_F32, CATNN_ERR_DTYPE, "unpermute_bwd: fp32 path");
+        UPB(float, float, float);
+    }
+#undef UPB
     launched(c);
 }
 
 void permute_bwd(Context* c, const void* dxp, const int32_t* row_of, i64 T, i64 k, i64 hidden, void* dx, int dtype,
-                 bool accumulate) {
+                 bool accumulate, int out_dtype) {
     if (T <= 0 || hidden <= 0) return;
+    if (out_dtype < 0) out_dtype = dtype;
     dim3 grid(cdiv(hidden, 256), (unsigned)T);
-    if (dtype == CATNN_BF16)
+    if (dtype == CATNN_BF16 && out_dtype == CATNN_F32)
+        k_permute_bwd<<<grid, 256, 0, c->stream>>>((const bf16*)dxp, row_of, T, (int)k, hidden, (float*)dx, accumulate);
+    else if (dtype == CATNN_BF16)
         k_permute_bwd<<<grid, 256, 0, c->stream>>>((const bf16*)dxp, row_of, T, (int)k, hidden, (bf16*)dx, accumulate);
     else k_permute_bwd<<<grid, 256, 0, c->stream>>>((const float*)dxp, row_of, T, (int)k, hidden, (float*)dx, accumulate);
     launched(c);

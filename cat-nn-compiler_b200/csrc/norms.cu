@@ -354,3 +354,101 @@ void rmsnorm_bwd(Context* c, const void* x, const float* w, const void* dy, void
 }
 
 }  // namespace catnn
+
+// ------------------------------------------------ mixed-storage RMSNorm
+// The training step keeps the residual stream in fp32 and feeds the
+// GEMMs bf16: the forward reads fp32 x and writes bf16 xn; the backward
+// reads fp32 x, a gradient in either storage, adds the residual gradient
+// and writes the fp32 stream plus (optionally) a bf16 copy for the next GEMM.
+namespace catnn {
+
+template <typename TX, typename TY>
+__global__ void k_rms_fwd_mx(const TX* __restrict__ x, const float* __restrict__ w, TY* __restrict__ y, i64 last,
+                             float eps) {
+    __shared__ float red[32];
+    const TX* in = x + blockIdx.x * last;
+    float s = 0.f;
+    for (i64 i = threadIdx.x; i < last; i += blockDim.x) {
+        float v = ld(in + i);
+        s += v * v;
+    }
+    float inv = 1.0f / sqrtf(block_sum(s, red) / (float)last + eps);
+    for (i64 i = threadIdx.x; i < last; i += blockDim.x) st(y + blockIdx.x * last + i, ld(in + i) * inv * w[i]);
+}
+
+template <typename TX, typename TG, typename TC>
+__global__ void k_rms_bwd_mx(const TX* __restrict__ x, const float* __restrict__ w, const TG* __restrict__ dy,
+                             const float* __restrict__ dres, float* __restrict__ dx, TC* __restrict__ copy,
+                             float* __restrict__ invs, i64 last, float eps) {
+    __shared__ float red[32];
+    i64 o = blockIdx.x * last;
+    float n = (float)last;
+    float s = 0.f, di = 0.f;
+    for (i64 i = threadIdx.x; i < last; i += blockDim.x) {
+        float v = ld(x + o + i);
+        s += v * v;
+        di += ld(dy + o + i) * v * w[i];
+    }
+    float ms = block_sum(s, red) / n;
+    di = block_sum(di, red);
+    float inv = 1.0f / sqrtf(ms + eps);
+    float dms = di * -0.5f * powf(ms + eps, -1.5f);
+    for (i64 i = threadIdx.x; i < last; i += blockDim.x) {
+        float v = ld(x + o + i);
+        float r = ld(dy + o + i) * inv * w[i] + dms * (2.0f * v / n);
+        if (dres) r += dres[o + i];
+        dx[o + i] = r;
+        if (copy) st(copy + o + i, r);
+    }
+    if (threadIdx.x == 0) invs[blockIdx.x] = inv;
+}
+
+template <typename TX, typename TG>
+__global__ void k_rms_cols_mx(const TX* __restrict__ x, const TG* __restrict__ dy, const float* __restrict__ invs, i64 rows,
+                              i64 last, float* __restrict__ pw) {
+    i64 j = blockIdx.x * (i64)blockDim.x + threadIdx.x;
+    if (j >= last) return;
+    i64 r0 = (i64)blockIdx.y * NCOL_ROWS, r1 = min(rows, r0 + NCOL_ROWS);
+    float sw = 0.f;
+    for (i64 r = r0; r < r1; ++r) sw += ld(dy + r * last + j) * ld(x + r * last + j) * invs[r];
+    pw[(i64)blockIdx.y * last + j] = sw;
+}
+
+void rmsnorm_fwd_mixed(Context* c, const void* x, int x_dtype, const float* w, void* y, int y_dtype, i64 rows, i64 last,
+                       float eps) {
+    if (rows <= 0 || last <= 0) return;
+    int t = row_threads(last);
+    if (x_dtype == CATNN_F32 && y_dtype == CATNN_BF16)
+        k_rms_fwd_mx<<<rows, t, 0, c->stream>>>((const float*)x, w, (bf16*)y, last, eps);
+    else if (x_dtype == CATNN_F32 && y_dtype == CATNN_F32)
+        k_rms_fwd_mx<<<rows, t, 0, c->stream>>>((const float*)x, w, (float*)y, last, eps);
+    else if (x_dtype == CATNN_BF16 && y_dtype == CATNN_BF16)
+        k_rms_fwd_mx<<<rows, t, 0, c->stream>>>((const bf16*)x, w, (bf16*)y, last, eps);
+    else throw Error(CATNN_ERR_UNSUPPORTED, "rmsnorm_fwd_mixed: dtype pair");
+    launched(c);
+}
+
+void rmsnorm_bwd_mixed(Context* c, const float* x, const float* w, const void* dy, int g_dtype, const float* dres, float* dx,
+                       void* copy, int copy_dtype, float* dw, bool dw_acc, i64 rows, i64 last, float eps) {
+    if (rows <= 0 || last <= 0) return;
+    int chunks = cdiv(rows, NCOL_ROWS);
+    float* invs = (float*)c->scratch_for((size_t)rows * 4 + (size_t)chunks * last * 4);
+    float* pw = invs + rows;
+    int t = row_threads(last);
+    dim3 gc(cdiv(last, 128), chunks);
+    if (g_dtype == CATNN_BF16) {
+        if (copy_dtype == CATNN_BF16 || !copy)
+            k_rms_bwd_mx<<<rows, t, 0, c->stream>>>(x, w, (const bf16*)dy, dres, dx, (bf16*)copy, invs, last, eps);
+        else k_rms_bwd_mx<<<rows, t, 0, c->stream>>>(x, w, (const bf16*)dy, dres, dx, (float*)copy, invs, last, eps);
+        if (dw) k_rms_cols_mx<<<gc, 128, 0, c->stream>>>(x, (const bf16*)dy, invs, rows, last, pw);
+    } else {
+        if (copy_dtype == CATNN_BF16 || !copy)
+            k_rms_bwd_mx<<<rows, t, 0, c->stream>>>(x, w, (const float*)dy, dres, dx, (bf16*)copy, invs, last, eps);
+        else k_rms_bwd_mx<<<rows, t, 0, c->stream>>>(x, w, (const float*)dy, dres, dx, (float*)copy, invs, last, eps);
+        if (dw) k_rms_cols_mx<<<gc, 128, 0, c->stream>>>(x, (const float*)dy, invs, rows, last, pw);
+    }
+    if (dw) k_cols_final<<<cdiv(last, 128), 128, 0, c->stream>>>(pw, chunks, last, dw, dw_acc ? 1 : 0);
+    launched(c, dw ? 3 : 1);
+}
+
+}  // namespace catnn

@@ -33,14 +33,18 @@ inline void check_dtype(int dtype) {
 
 // ---- dense (gemm.cu / gemm_tc.cu)
 // C = act(op(A)op(B) + bias) (+C). See catnn_gemm in catnn_b200.h.
+// resid (fp32 [M, ldc], optional) is added before the activation; it needs
+// an fp32 C (the residual stream: x_out = x_in + A·B in one pass).
 void gemm(Context* c, bool ta, bool tb, i64 M, i64 N, i64 K, const void* A, i64 lda, const void* B,
-          i64 ldb, void* C, i64 ldc, int dtype, int c_dtype, const float* bias, int act, bool accumulate);
+          i64 ldb, void* C, i64 ldc, int dtype, int c_dtype, const float* bias, int act, bool accumulate,
+          const float* resid = nullptr);
 void gemm_f32(Context* c, bool ta, bool tb, i64 M, i64 N, i64 K, const float* A, i64 lda, const float* B,
-              i64 ldb, void* C, i64 ldc, int c_dtype, const float* bias, int act, bool accumulate);
+              i64 ldb, void* C, i64 ldc, int c_dtype, const float* bias, int act, bool accumulate,
+              const float* resid = nullptr);
 // bf16 operands on tcgen05 tensor cores, fp32 accumulation in TMEM.
 void gemm_bf16_tc(Context* c, bool ta, bool tb, i64 M, i64 N, i64 K, const bf16* A, i64 lda,
                   const bf16* B, i64 ldb, void* C, i64 ldc, int c_dtype, const float* bias, int act,
-                  bool accumulate);
+                  bool accumulate, const float* resid = nullptr);
 // Grouped variant: for each group g, rows [off[g], off[g+1]) of A (and C)
 // against B_g = B + g*strideB. A is [rows,K] row-major; B_g is [K,N]
 // (tb=0) or [N,K] (tb=1). Offsets live on the device.
@@ -86,6 +90,14 @@ void rmsnorm_fwd(Context* c, const void* x, const float* w, void* y, i64 rows, i
 void rmsnorm_bwd(Context* c, const void* x, const float* w, const void* dy, void* dx, float* dw, i64 rows,
                  i64 last, float eps, int dtype, bool dw_accumulate, const void* dres = nullptr);
 
+// Mixed storage: fp32 residual stream in, bf16 (or fp32) normalized out.
+void rmsnorm_fwd_mixed(Context* c, const void* x, int x_dtype, const float* w, void* y, int y_dtype, i64 rows, i64 last,
+                       float eps);
+// dx (fp32) = rmsnorm adjoint of dy (g_dtype) at x (fp32) + dres (fp32, optional);
+// copy (optional, copy_dtype) receives dx too; dw (+)= Σ dy·x·inv.
+void rmsnorm_bwd_mixed(Context* c, const float* x, const float* w, const void* dy, int g_dtype, const float* dres, float* dx,
+                       void* copy, int copy_dtype, float* dw, bool dw_acc, i64 rows, i64 last, float eps);
+
 // ---- embedding / attention (attention.cu)
 void embedding_fwd(Context* c, const uint32_t* ids, i64 n, const void* table, i64 vocab, i64 hidden, void* y,
                    int dtype, int* err);
@@ -109,15 +121,16 @@ void permute_map(Context* c, const int32_t* idx, i64 T, i64 E, i64 k, int align,
                  int32_t* offsets, int32_t* row_of, int32_t* src_of);
 void permute_rows(Context* c, const void* x, const int32_t* src_of, i64 rows, i64 hidden, i64 k, void* xp, int dtype);
 // yp_dtype (default: dtype) lets an fp32 expert output feed a bf16 result.
+// resid (optional, y's storage): y = resid + Σ_j w·yp, the residual add of x + moe(x).
 void unpermute_rows(Context* c, const void* yp, const int32_t* row_of, const float* w, i64 T, i64 k, i64 hidden,
-                    void* y, int dtype, bool accumulate, int yp_dtype = -1);
+                    void* y, int dtype, bool accumulate, int yp_dtype = -1, const void* resid = nullptr);
 // Over sorted rows r (pair p = src_of[r], token t = p/k):
 // d_w[p] = <yp[r], dy[t]>; dyp[r] = w[p]*dy[t]; zeros on padding rows.
 void unpermute_bwd(Context* c, const void* yp, const int32_t* src_of, i64 rows, const float* w, const void* dy, i64 k,
-                   i64 hidden, float* dw, void* dyp, int dtype, int yp_dtype = -1);
+                   i64 hidden, float* dw, void* dyp, int dtype, int yp_dtype = -1, int dy_dtype = -1);
 // dx[t] (+)= Σ_j dxp[row_of[t,j]].
 void permute_bwd(Context* c, const void* dxp, const int32_t* row_of, i64 T, i64 k, i64 hidden, void* dx,
-                 int dtype, bool accumulate);
+                 int dtype, bool accumulate, int out_dtype = -1);
 // Router STE: dlogits[t, idx[t,j]] = w*(g - <w,g>), zero elsewhere.
 void router_ste(Context* c, const int32_t* idx, const float* w, const float* dw, i64 T, i64 E, i64 k,
                 float* dlogits);

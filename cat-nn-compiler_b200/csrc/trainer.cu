@@ -1,0 +1,489 @@
+// The MoE decoder training step on one GPU: forward with saved
+// activations, fused cross-entropy, backward, optimizer — all device
+// kernels of this library launched on the context stream, no host sync
+// inside a step. Layout choices:
+//  - residual stream fp32 (x_in, x_mid per layer); every tensor that feeds a
+//    GEMM is stored in the shadow dtype (bf16 on the tensor-core path);
+//  - fused QKV weight [d, (H+2Hkv)·hd] and fused expert weight
+//    W13_e = [w1_e | w3_e] ([d, 2F]) so one GEMM produces both SwiGLU inputs;
+//  - expert rows padded to 128 so every expert GEMM tile is single-expert;
+//  - weight gradients land in fp32 directly from the GEMM epilogue.
+#include <cstring>
+
+#include "trainer.cuh"
+
+namespace catnn {
+
+static i64 al128(i64 n) { return (n + 127) / 128 * 128; }
+
+void MoeTrainer::plan_params() {
+    i64 o = 0;
+    auto take = [&](i64 n) {
+        i64 r = o;
+        o += al128(n);
+        return r;
+    };
+    o_embed = take(V * d);
+    lo.resize(L);
+    for (i64 l = 0; l < L; ++l) {
+        lo[l].rms_attn = take(d);
+        lo[l].wqkv = take(d * qkvd);
+        lo[l].wo = take(qd * d);
+        lo[l].rms_moe = take(d);
+        lo[l].gate = take(d * E);
+        lo[l].w13 = take(E * d * 2 * F);
+        lo[l].w2 = take(E * F * d);
+    }
+    o_final = take(d);
+    o_lm = take(V * d);
+    n_params = o;
+}
+
+i64 MoeTrainer::packed_count() const {
+    i64 layer = d + d * qd + 2 * d * kd + qd * d + d + d * E + 2 * E * d * F + E * F * d;
+    return V * d + L * layer + d + V * d;
+}
+
+// Packed (reference) order, per layer: rms_attn, wq, wk, wv, wo, rms_moe,
+// gate, w1[E], w3[E], w2[E] — the oracle's MixLayout.
+void MoeTrainer::import_packed(const float* pk, float* dst) {
+    cudaStream_t s = c->stream;
+    auto cp = [&](float* to, const float* from, i64 n) {
+        CUDA_OK(cudaMemcpyAsync(to, from, n * 4, cudaMemcpyDeviceToDevice, s));
+    };
+    auto cp2 = [&](float* to, i64 to_ld, const float* from, i64 from_ld, i64 cols, i64 rows) {
+        CUDA_OK(cudaMemcpy2DAsync(to, to_ld * 4, from, from_ld * 4, cols * 4, rows, cudaMemcpyDeviceToDevice, s));
+    };
+    const float* p = pk;
+    cp(dst + o_embed, p, V * d);
+    p += V * d;
+    for (i64 l = 0; l < L; ++l) {
+        const LayerOff& q = lo[l];
+        cp(dst + q.rms_attn, p, d); p += d;
+        cp2(dst + q.wqkv, qkvd, p, qd, qd, d); p += d * qd;
+        cp2(dst + q.wqkv + qd, qkvd, p, kd, kd, d); p += d * kd;
+        cp2(dst + q.wqkv + qd + kd, qkvd, p, kd, kd, d); p += d * kd;
+        cp(dst + q.wo, p, qd * d); p += qd * d;
+        cp(dst + q.rms_moe, p, d); p += d;
+        cp(dst + q.gate, p, d * E); p += d * E;
+        cp2(dst + q.w13, 2 * F, p, F, F, E * d); p += E * d * F;
+        cp2(dst + q.w13 + F, 2 * F, p, F, F, E * d); p += E * d * F;
+        cp(dst + q.w2, p, E * F * d); p += E * F * d;
+    }
+    cp(dst + o_final, p, d); p += d;
+    cp(dst + o_lm, p, V * d);
+}
+
+void MoeTrainer::export_packed(const float* src, float* pk) {
+    cudaStream_t s = c->stream;
+    auto cp = [&](float* to, const float* from, i64 n) {
+        CUDA_OK(cudaMemcpyAsync(to, from, n * 4, cudaMemcpyDeviceToDevice, s));
+    };
+    auto cp2 = [&](float* to, i64 to_ld, const float* from, i64 from_ld, i64 cols, i64 rows) {
+        CUDA_OK(cudaMemcpy2DAsync(to, to_ld * 4, from, from_ld * 4, cols * 4, rows, cudaMemcpyDeviceToDevice, s));
+    };
+    float* p = pk;
+    cp(p, src + o_embed, V * d);
+    p += V * d;
+    for (i64 l = 0; l < L; ++l) {
+        const LayerOff& q = lo[l];
+        cp(p, src + q.rms_attn, d); p += d;
+        cp2(p, qd, src + q.wqkv, qkvd, qd, d); p += d * qd;
+        cp2(p, kd, src + q.wqkv + qd, qkvd, kd, d); p += d * kd;
+        cp2(p, kd, src + q.wqkv + qd + kd, qkvd, kd, d); p += d * kd;
+        cp(p, src + q.wo, qd * d); p += qd * d;
+        cp(p, src + q.rms_moe, d); p += d;
+        cp(p, src + q.gate, d * E); p += d * E;
+        cp2(p, F, src + q.w13, 2 * F, F, E * d); p += E * d * F;
+        cp2(p, F, src + q.w13 + F, 2 * F, F, E * d); p += E * d * F;
+        cp(p, src + q.w2, E * F * d); p += E * F * d;
+    }
+    cp(p, src + o_final, d); p += d;
+    cp(p, src + o_lm, V * d);
+}
+
+void MoeTrainer::alloc() {
+    size_t e = dsize(dt);
+    // parameters: P, G (+ Mo, Vo for Adam) fp32, shadow in dt
+    size_t pb = (size_t)n_params * 4;
+    size_t ptot = pb * (opt == 1 ? 4 : 2) + (dt == CATNN_BF16 ? (size_t)n_params * e : 0) + 4096;
+    CUDA_OK(cudaMalloc(&param_block, ptot));
+    CUDA_OK(cudaMemsetAsync(param_block, 0, ptot, c->stream));
+    Carver pc(param_block);
+    P = pc.take<float>(n_params);
+    G = pc.take<float>(n_params);
+    if (opt == 1) {
+        Mo = pc.take<float>(n_params);
+        Vo = pc.take<float>(n_params);
+    }
+    Sh = dt == CATNN_BF16 ? (void*)pc.take<char>(n_params * e) : (void*)P;
+
+    // activations + scratch
+    std::vector<size_t> sz;
+    auto add = [&](size_t b) { sz.push_back(b); };
+    for (i64 l = 0; l < L; ++l) {
+        add(T * d * 4); add(T * d * 4); add(B * H * S * 4); add(T * E * 4); add(T * K * 4);
+        add(T * d * e); add(T * qkvd * e); add(T * qd * e); add(T * d * e); add(cap * d * e);
+        add(cap * 2 * F * e); add(cap * F * e); add(cap * d * e);
+        add(T * K * 4); add(E * 4); add((E + 1) * 4); add(T * K * 4); add(cap * 4);
+    }
+    add(T * d * 4); add(T * d * e); add((size_t)T * V * e); add(T * 4); add(T * 4); add(64);
+    add(T * d * 4); add(T * d * 4); add(T * d * 4); add(T * E * 4); add(T * K * 4);
+    add(T * d * e); add(cap * d * e); add(cap * F * e); add(cap * 2 * F * e); add(cap * d * e); add(T * qkvd * e);
+    add(T * qd * e); add(T * d * e); add(T * E * e); add(T * d * e);
+    size_t tot = 0;
+    for (size_t b : sz) tot += (b + 255) / 256 * 256;
+    tot += 4096;
+    CUDA_OK(cudaMalloc(&act_block, tot));
+    Carver ac(act_block);
+    acts.resize(L);
+    for (i64 l = 0; l < L; ++l) {
+        Act& a = acts[l];
+        a.x_in = ac.take<float>(T * d);
+        a.x_mid = ac.take<float>(T * d);
+        a.lse = ac.take<float>(B * H * S);
+        a.logits = ac.take<float>(T * E);
+        a.w = ac.take<float>(T * K);
+        a.xn = ac.take<char>(T * d * e);
+        a.qkv = ac.take<char>(T * qkvd * e);
+        a.ctx = ac.take<char>(T * qd * e);
+        a.xm = ac.take<char>(T * d * e);
+        a.xp = ac.take<char>(cap * d * e);
+        a.ac = ac.take<char>(cap * 2 * F * e);
+        a.h = ac.take<char>(cap * F * e);
+        a.yp = ac.take<char>(cap * d * e);
+        a.idx = ac.take<int32_t>(T * K);
+        a.counts = ac.take<int32_t>(E);
+        a.off = ac.take<int32_t>(E + 1);
+        a.row_of = ac.take<int32_t>(T * K);
+        a.src_of = ac.take<int32_t>(cap);
+    }
+    x_last = ac.take<float>(T * d);
+    xf = ac.take<char>(T * d * e);
+    lg = ac.take<char>((size_t)T * V * e);
+    tokens = ac.take<uint32_t>(T);
+    targets = ac.take<uint32_t>(T);
+    loss = ac.take<float>(16);
+    dx = ac.take<float>(T * d);
+    dxmid = ac.take<float>(T * d);
+    dxm = ac.take<float>(T * d);
+    dlog = ac.take<float>(T * E);
+    dwts = ac.take<float>(T * K);
+    dxmid_lp = ac.take<char>(T * d * e);
+    dyp = ac.take<char>(cap * d * e);
+    dh = ac.take<char>(cap * F * e);
+    dac = ac.take<char>(cap * 2 * F * e);
+    dxp = ac.take<char>(cap * d * e);
+    dqkv = ac.take<char>(T * qkvd * e);
+    dctx = ac.take<char>(T * qd * e);
+    dxn = ac.take<char>(T * d * e);
+    dlog_lp = ac.take<char>(T * E * e);
+    dxf = ac.take<char>(T * d * e);
+    CUDA_OK(cudaMallocHost(&h_tokens, T * 4));
+    CUDA_OK(cudaMallocHost(&h_loss, 64));
+}
+
+void MoeTrainer::release() {
+    if (param_block) cudaFree(param_block);
+    if (act_block) cudaFree(act_block);
+    if (h_tokens) cudaFreeHost(h_tokens);
+    if (h_loss) cudaFreeHost(h_loss);
+    param_block = act_block = nullptr;
+    h_tokens = nullptr;
+    h_loss = nullptr;
+}
+
+// train.rs:274-275: targets[i] = tokens[(i+1) % n] % vocab.
+__global__ void k_next_token(const uint32_t* __restrict__ tok, uint32_t* __restrict__ tg, i64 n, i64 vocab) {
+    i64 i = blockIdx.x * (i64)blockDim.x + threadIdx.x;
+    if (i < n) tg[i] = tok[(i + 1) % n] % (uint32_t)vocab;
+}
+
+// Expert GEMM over the sorted rows (bf16: tcgen05 grouped; fp32: CUDA cores).
+static void expert_gemm(Context* c, int dt, bool tb, i64 rows, i64 N, i64 Kd, int E, const int32_t* off, const void* A,
+                        i64 lda, const void* B, void* C, i64 ldc, int c_dtype) {
+    i64 strideB = N * Kd;
+    if (dt == CATNN_BF16)
+        gemm_grouped_bf16_tc(c, tb, rows, N, Kd, E, off, (const bf16*)A, lda, (const bf16*)B, strideB, tb ? Kd : N, C, ldc,
+                             c_dtype, CATNN_ACT_NONE, false);
+    else
+        gemm_grouped_f32(c, false, tb, rows, N, Kd, E, off, (const float*)A, lda, (const float*)B, strideB, tb ? Kd : N,
+                         (float*)C, ldc, 0, false);
+}
+
+static void expert_wgrad(Context* c, int dt, i64 rows, i64 N, i64 Kd, int E, const int32_t* off, const void* A, i64 lda,
+                         const void* D, i64 ldd, float* dB) {
+    if (dt == CATNN_BF16)
+        gemm_grouped_wgrad_bf16_tc(c, rows, N, Kd, E, off, (const bf16*)A, lda, (const bf16*)D, ldd, dB, Kd * N, CATNN_F32,
+                                   false);
+    else
+        gemm_grouped_f32(c, true, false, rows, N, Kd, E, off, (const float*)A, lda, (const float*)D, 0, ldd, dB, N, Kd * N,
+                         false);
+}
+
+void MoeTrainer::forward() {
+    int* err = c->status + 10;
+    k_next_token<<<cdiv(T, 256), 256, 0, c->stream>>>(tokens, targets, T, V);
+    launched(c);
+    embedding_fwd(c, tokens, T, P + o_embed, V, d, acts[0].x_in, CATNN_F32, err);
+    const int align = dt == CATNN_BF16 ? 128 : 1;
+    for (i64 l = 0; l < L; ++l) {
+        Act& a = acts[l];
+        const LayerOff& q = lo[l];
+        float* x_out = l + 1 < L ? acts[l + 1].x_in : x_last;
+        char* qkv = (char*)a.qkv;
+        size_t e = dsize(dt);
+        // attention half: x_mid = x_in + attn(rmsnorm(x_in))   (moe.rs:303-316)
+        rmsnorm_fwd_mixed(c, a.x_in, CATNN_F32, P + q.rms_attn, a.xn, dt, T, d, eps);
+        gemm(c, false, false, T, qkvd, d, a.xn, d, W(q.wqkv), qkvd, a.qkv, qkvd, dt, dt, nullptr, 0, false);
+        rope(c, qkv, B, S, H, hd, theta, false, dt, qkvd, 0);
+        rope(c, qkv, B, S, Hkv, hd, theta, false, dt, qkvd, qd);
+        attention_fwd(c, qkv, qkv + qd * e, qkv + (qd + kd) * e, a.ctx, a.lse, B, S, H, Hkv, hd, true, window, dt, qkvd,
+                      qkvd);
+        gemm(c, false, false, T, d, qd, a.ctx, qd, W(q.wo), d, a.x_mid, d, dt, CATNN_F32, nullptr, 0, false, a.x_in);
+        // MoE half: x_out = x_mid + moe(rmsnorm(x_mid))   (moe.rs:317-319)
+        rmsnorm_fwd_mixed(c, a.x_mid, CATNN_F32, P + q.rms_moe, a.xm, dt, T, d, eps);
+        gemm(c, false, false, T, E, d, a.xm, d, W(q.gate), E, a.logits, E, dt, CATNN_F32, nullptr, 0, false);
+        router_topk(c, a.logits, T, E, K, a.idx, a.w);
+        permute_map(c, a.idx, T, E, K, align, cap, a.counts, a.off, a.row_of, a.src_of);
+        permute_rows(c, a.xm, a.src_of, cap, d, K, a.xp, dt);
+        expert_gemm(c, dt, false, cap, 2 * F, d, (int)E, a.off, a.xp, d, W(q.w13), a.ac, 2 * F, dt);
+        swiglu_act(c, a.ac, (char*)a.ac + F * e, a.h, cap, F, 2 * F, F, dt);
+        expert_gemm(c, dt, false, cap, d, F, (int)E, a.off, a.h, F, W(q.w2), a.yp, d, dt);
+        unpermute_rows(c, a.yp, a.row_of, a.w, T, K, d, x_out, CATNN_F32, false, dt, a.x_mid);
+    }
+    // final norm, LM head, fused cross-entropy (dlogits overwrite logits)
+    rmsnorm_fwd_mixed(c, x_last, CATNN_F32, P + o_final, xf, dt, T, d, eps);
+    gemm(c, false, true, T, V, d, xf, d, W(o_lm), d, lg, V, dt, dt, nullptr, 0, false);
+    xent_fwdbwd(c, lg, targets, T, V, loss, lg, dt, c->status + 9);
+}
+
+void MoeTrainer::backward() {
+    size_t e = dsize(dt);
+    // LM head adjoint (adjoint.rs:903-913) and the final norm
+    gemm(c, false, false, T, d, V, lg, V, W(o_lm), d, dxf, d, dt, dt, nullptr, 0, false);
+    gemm(c, true, false, V, d, T, lg, V, xf, d, G + o_lm, d, dt, CATNN_F32, nullptr, 0, false);
+    rmsnorm_bwd_mixed(c, x_last, P + o_final, dxf, dt, nullptr, dx, nullptr, dt, G + o_final, false, T, d, eps);
+    for (i64 l = L - 1; l >= 0; --l) {
+        Act& a = acts[l];
+        const LayerOff& q = lo[l];
+        char* qkv = (char*)a.qkv;
+        char* dq = (char*)dqkv;
+        // MoE adjoint (adjoint.rs:471-526), batched by expert
+        unpermute_bwd(c, a.yp, a.src_of, cap, a.w, dx, K, d, dwts, dyp, dt, dt, CATNN_F32);
+        expert_gemm(c, dt, true, cap, F, d, (int)E, a.off, dyp, d, W(q.w2), dh, F, dt);
+        expert_wgrad(c, dt, cap, d, F, (int)E, a.off, a.h, F, dyp, d, G + q.w2);
+        swiglu_act_bwd(c, a.ac, (char*)a.ac + F * e, dh, dac, (char*)dac + F * e, cap, F, 2 * F, 2 * F, dt);
+        expert_gemm(c, dt, true, cap, d, 2 * F, (int)E, a.off, dac, 2 * F, W(q.w13), dxp, d, dt);
+        expert_wgrad(c, dt, cap, 2 * F, d, (int)E, a.off, a.xp, d, dac, 2 * F, G + q.w13);
+        permute_bwd(c, dxp, a.row_of, T, K, d, dxm, dt, false, CATNN_F32);
+        // router straight-through adjoint (adjoint.rs:255-284)
+        router_ste(c, a.idx, a.w, dwts, T, E, K, dlog);
+        const void* dl = dlog;
+        if (dt == CATNN_BF16) {
+            cast(c, dlog, CATNN_F32, dlog_lp, CATNN_BF16, T * E);
+            dl = dlog_lp;
+        }
+        gemm(c, false, true, T, d, E, dl, E, W(q.gate), E, dxm, d, dt, CATNN_F32, nullptr, 0, true);
+        gemm(c, true, false, d, E, T, a.xm, d, dl, E, G + q.gate, E, dt, CATNN_F32, nullptr, 0, false);
+        // residual around the MoE: dx_mid = dx + rmsnorm'(dxm)   (train.rs:327-330)
+        rmsnorm_bwd_mixed(c, a.x_mid, P + q.rms_moe, dxm, CATNN_F32, dx, dxmid, dxmid_lp, dt, G + q.rms_moe, false, T, d,
+                          eps);
+        // attention adjoint (adjoint.rs:287-439)
+        gemm(c, false, true, T, qd, d, dxmid_lp, d, W(q.wo), d, dctx, qd, dt, dt, nullptr, 0, false);
+        gemm(c, true, false, qd, d, T, a.ctx, qd, dxmid_lp, d, G + q.wo, d, dt, CATNN_F32, nullptr, 0, false);
+        attention_bwd(c, qkv, qkv + qd * e, qkv + (qd + kd) * e, a.ctx, a.lse, dctx, dq, dq + qd * e, dq + (qd + kd) * e,
+                      B, S, H, Hkv, hd, true, window, dt, qkvd, qkvd);
+        rope(c, dq, B, S, H, hd, theta, true, dt, qkvd, 0);
+        rope(c, dq, B, S, Hkv, hd, theta, true, dt, qkvd, qd);
+        gemm(c, false, true, T, d, qkvd, dqkv, qkvd, W(q.wqkv), qkvd, dxn, d, dt, dt, nullptr, 0, false);
+        gemm(c, true, false, d, qkvd, T, a.xn, d, dqkv, qkvd, G + q.wqkv, qkvd, dt, CATNN_F32, nullptr, 0, false);
+        // residual around attention: dx_in = dx_mid + rmsnorm'(dxn)   (train.rs:348-351)
+        rmsnorm_bwd_mixed(c, a.x_in, P + q.rms_attn, dxn, dt, dxmid, dx, nullptr, dt, G + q.rms_attn, false, T, d, eps);
+    }
+    embedding_bwd(c, tokens, T, dx, G + o_embed, V, d, CATNN_F32);
+}
+
+void MoeTrainer::update() {
+    bf16* sh = dt == CATNN_BF16 ? (bf16*)Sh : nullptr;
+    if (opt == 0) {
+        sgd(c, P, G, n_params, lr, sh);
+    } else {
+        ++t_step;
+        adam(c, P, G, Mo, Vo, n_params, t_step, lr, b1, b2, aeps, CATNN_F32, sh);
+    }
+}
+
+void MoeTrainer::step(const uint32_t* tokens_dev, float* loss_dev, bool upd) {
+    if (tokens_dev != tokens) CUDA_OK(cudaMemcpyAsync(tokens, tokens_dev, T * 4, cudaMemcpyDeviceToDevice, c->stream));
+    forward();
+    backward();
+    if (upd) update();
+    if (loss_dev && loss_dev != loss) CUDA_OK(cudaMemcpyAsync(loss_dev, loss, 4, cudaMemcpyDeviceToDevice, c->stream));
+}
+
+}  // namespace catnn
+
+using namespace catnn;
+
+struct catnn_moe_trainer {
+    MoeTrainer t;
+};
+
+namespace {
+
+MoeTrainer& tr(catnn_moe_trainer* h) {
+    CATNN_CHECK(h != nullptr, CATNN_ERR_INVALID, "null catnn_moe_trainer");
+    bind(h->t.c);
+    return h->t;
+}
+
+void configure(MoeTrainer& t, const catnn_moe_config* cf) {
+    CATNN_CHECK(cf != nullptr, CATNN_ERR_INVALID, "null config");
+    t.V = cf->vocab;
+    t.d = cf->hidden;
+    t.F = cf->mid;
+    t.L = cf->layers;
+    t.H = cf->heads;
+    t.Hkv = cf->kv_heads;
+    t.E = cf->experts;
+    t.K = cf->top_k;
+    t.window = cf->window;
+    t.B = cf->batch;
+    t.S = cf->seq;
+    t.eps = cf->rms_eps;
+    t.theta = cf->rope_theta;
+    t.dt = cf->dtype;
+    t.opt = cf->optimizer;
+    t.lr = cf->lr;
+    t.b1 = cf->beta1;
+    t.b2 = cf->beta2;
+    t.aeps = cf->adam_eps;
+    check_dtype(t.dt);
+    CATNN_CHECK(t.V > 0 && t.d > 0 && t.F > 0 && t.L > 0 && t.B > 0 && t.S > 0, CATNN_ERR_SHAPE, "moe config: sizes");
+    CATNN_CHECK(t.H > 0 && t.d % t.H == 0, CATNN_ERR_SHAPE, "hidden not divisible by heads");
+    CATNN_CHECK(t.Hkv > 0 && t.H % t.Hkv == 0, CATNN_ERR_SHAPE, "heads not divisible by kv heads");
+    CATNN_CHECK(t.E >= 1 && t.E <= 32 && t.K >= 1 && t.K <= t.E, CATNN_ERR_SHAPE, "need 1 <= top_k <= experts <= 32");
+    CATNN_CHECK(t.opt == 0 || t.opt == 1, CATNN_ERR_INVALID, "optimizer: 0 = SGD, 1 = Adam");
+    t.hd = t.d / t.H;
+    CATNN_CHECK(t.hd % 2 == 0 && t.hd <= 128, CATNN_ERR_SHAPE, "head_dim must be even and <= 128");
+    t.T = t.B * t.S;
+    t.qd = t.H * t.hd;
+    t.kd = t.Hkv * t.hd;
+    t.qkvd = t.qd + 2 * t.kd;
+    const i64 align = t.dt == CATNN_BF16 ? 128 : 1;
+    t.cap = t.T * t.K + t.E * (align - 1);
+    if (t.dt == CATNN_BF16)
+        CATNN_CHECK(t.d % 64 == 0 && t.F % 64 == 0, CATNN_ERR_SHAPE, "bf16 path: hidden and mid must be multiples of 64");
+}
+
+}  // namespace
+
+extern "C" {
+
+int catnn_moe_trainer_create(catnn_ctx* h, const catnn_moe_config* cf, catnn_moe_trainer** out) {
+    ABI_BEGIN
+    Context* c = unwrap(h);
+    CATNN_CHECK(out != nullptr, CATNN_ERR_INVALID, "null out");
+    catnn_moe_trainer* t = new catnn_moe_trainer();
+    try {
+        t->t.c = c;
+        configure(t->t, cf);
+        t->t.plan_params();
+        t->t.alloc();
+    } catch (...) {
+        t->t.release();
+        delete t;
+        throw;
+    }
+    *out = t;
+    ABI_END
+}
+
+int catnn_moe_trainer_destroy(catnn_moe_trainer* h) {
+    ABI_BEGIN
+    if (!h) return CATNN_OK;
+    bind(h->t.c);
+    cudaStreamSynchronize(h->t.c->stream);
+    h->t.release();
+    delete h;
+    ABI_END
+}
+
+int catnn_moe_trainer_param_count(const catnn_moe_config* cf, int64_t* out) {
+    ABI_BEGIN
+    CATNN_CHECK(out != nullptr, CATNN_ERR_INVALID, "null out");
+    MoeTrainer t;
+    configure(t, cf);
+    *out = t.packed_count();
+    ABI_END
+}
+
+int catnn_moe_trainer_set_params(catnn_moe_trainer* h, const float* packed) {
+    ABI_BEGIN
+    MoeTrainer& t = tr(h);
+    CATNN_CHECK(packed != nullptr, CATNN_ERR_INVALID, "null params");
+    t.import_packed(packed, t.P);
+    if (t.dt == CATNN_BF16) cast(t.c, t.P, CATNN_F32, t.Sh, CATNN_BF16, t.n_params);
+    if (t.opt == 1) {
+        CUDA_OK(cudaMemsetAsync(t.Mo, 0, t.n_params * 4, t.c->stream));
+        CUDA_OK(cudaMemsetAsync(t.Vo, 0, t.n_params * 4, t.c->stream));
+        t.t_step = 0;
+    }
+    ABI_END
+}
+
+int catnn_moe_trainer_get_params(catnn_moe_trainer* h, float* packed) {
+    ABI_BEGIN
+    MoeTrainer& t = tr(h);
+    CATNN_CHECK(packed != nullptr, CATNN_ERR_INVALID, "null out");
+    t.export_packed(t.P, packed);
+    ABI_END
+}
+
+int catnn_moe_trainer_get_grads(catnn_moe_trainer* h, float* packed) {
+    ABI_BEGIN
+    MoeTrainer& t = tr(h);
+    CATNN_CHECK(packed != nullptr, CATNN_ERR_INVALID, "null out");
+    t.export_packed(t.G, packed);
+    ABI_END
+}
+
+int catnn_moe_trainer_step(catnn_moe_trainer* h, const uint32_t* tokens, float* loss, int update) {
+    ABI_BEGIN
+    MoeTrainer& t = tr(h);
+    CATNN_CHECK(tokens != nullptr, CATNN_ERR_INVALID, "null tokens");
+    t.step(tokens, loss, update != 0);
+    ABI_END
+}
+
+int catnn_moe_trainer_step_host(catnn_moe_trainer* h, const uint32_t* tokens_host, float* loss_host, int update) {
+    ABI_BEGIN
+    MoeTrainer& t = tr(h);
+    CATNN_CHECK(tokens_host != nullptr && loss_host != nullptr, CATNN_ERR_INVALID, "null tokens/loss");
+    // host -> pinned staging -> device, step, loss back to the host
+    std::memcpy(t.h_tokens, tokens_host, t.T * 4);
+    CUDA_OK(cudaMemcpyAsync(t.tokens, t.h_tokens, t.T * 4, cudaMemcpyHostToDevice, t.c->stream));
+    t.step(t.tokens, nullptr, update != 0);
+    CUDA_OK(cudaMemcpyAsync(t.h_loss, t.loss, 4, cudaMemcpyDeviceToHost, t.c->stream));
+    CUDA_OK(cudaStreamSynchronize(t.c->stream));
+    *loss_host = *t.h_loss;
+    ABI_END
+}
+
+int catnn_moe_trainer_check(catnn_moe_trainer* h) {
+    ABI_BEGIN
+    MoeTrainer& t = tr(h);
+    int v[16];
+    CUDA_OK(cudaMemcpyAsync(v, t.c->status, sizeof(v), cudaMemcpyDeviceToHost, t.c->stream));
+    CUDA_OK(cudaStreamSynchronize(t.c->stream));
+    if (v[8] || v[9] || v[10]) {
+        CUDA_OK(cudaMemsetAsync(t.c->status + 8, 0, 3 * 4, t.c->stream));
+        throw Error(CATNN_ERR_SHAPE, v[10] ? "token id >= vocab" : (v[9] ? "ce target out of range"
+                                                                         : "router produced an invalid expert"));
+    }
+    if (v[0] || v[1] || v[2] || v[3]) throw Error(CATNN_ERR_TIMEOUT, "a bounded device wait ran out (GEMM pipeline)");
+    ABI_END
+}
+
+}  // extern "C"

@@ -1,0 +1,70 @@
+// Native training step for the Mixtral-style MoE decoder (the reference's
+// train::mixtral_step, crates/catnn-compile/src/train.rs:261-356, with
+// residual adds, next-token cross-entropy and an SGD or Adam update).
+#pragma once
+#include <vector>
+
+#include "ops.cuh"
+
+struct catnn_moe_config;
+
+namespace catnn {
+
+struct Comm;  // expert-parallel communicator (comm.cu); null on one GPU
+
+struct MoeTrainer {
+    Context* c = nullptr;
+    Comm* comm = nullptr;
+    // shapes
+    i64 V, d, F, L, H, Hkv, hd, E, K, window, B, S, T, qd, kd, qkvd, cap;
+    float eps;
+    double theta;
+    int dt;  // activation / weight-shadow storage (CATNN_F32 or CATNN_BF16)
+    int opt;  // 0 SGD, 1 Adam
+    float lr, b1, b2, aeps;
+    uint64_t t_step = 0;
+
+    // parameters: fp32 master P, gradients G, Adam moments Mo/Vo, and the
+    // storage-dtype shadow S the GEMMs read (S == P on the fp32 path).
+    struct LayerOff {
+        i64 rms_attn, wqkv, wo, rms_moe, gate, w13, w2;
+    };
+    std::vector<LayerOff> lo;
+    i64 o_embed, o_final, o_lm, n_params;
+    float *P = nullptr, *G = nullptr, *Mo = nullptr, *Vo = nullptr;
+    void* Sh = nullptr;
+    void* param_block = nullptr;
+
+    // saved activations per layer
+    struct Act {
+        float *x_in, *x_mid, *lse, *logits, *w;
+        void *xn, *qkv, *ctx, *xm, *xp, *ac, *h, *yp;
+        int32_t *idx, *counts, *off, *row_of, *src_of;
+    };
+    std::vector<Act> acts;
+    float* x_last = nullptr;
+    void *xf = nullptr, *lg = nullptr;
+    uint32_t *tokens = nullptr, *targets = nullptr;
+    float* loss = nullptr;
+    // backward scratch (reused across layers)
+    float *dx, *dxmid, *dxm, *dlog, *dwts;
+    void *dxmid_lp, *dyp, *dh, *dac, *dxp, *dqkv, *dctx, *dxn, *dlog_lp, *dxf;
+    void* act_block = nullptr;
+    // host staging for the host-buffer step
+    uint32_t* h_tokens = nullptr;
+    float* h_loss = nullptr;
+
+    void plan_params();
+    void alloc();
+    void release();
+    const void* W(i64 off) const { return (const char*)Sh + off * dsize(dt); }
+    void forward();
+    void backward();
+    void update();
+    void step(const uint32_t* tokens_dev, float* loss_dev, bool upd);
+    void import_packed(const float* packed, float* dst);
+    void export_packed(const float* src, float* packed);
+    i64 packed_count() const;
+};
+
+}  // namespace catnn

@@ -249,6 +249,47 @@ int catnn_mlp_step(catnn_ctx* ctx, const float* w1, const float* b1, const float
                    int64_t din, int64_t hid, int64_t dout, float* loss, float* dw1, float* db1,
                    float* dw2, float* db2);
 
+/* ------------------------------------------------------------ MoE decoder trainer */
+/* Shapes and optimizer of a Mixtral-style decoder (the fields of
+ * MixtralConfig, crates/catnn-core/src/spec/mixtral.rs:28-51, plus the step's
+ * batch/seq and the update rule). window <= 0: no sliding window.
+ * optimizer: 0 = SGD (Sgd::put), 1 = Adam (Adam::put). */
+typedef struct catnn_moe_config {
+    int64_t vocab, hidden, mid, layers, heads, kv_heads, experts, top_k, window, batch, seq;
+    float rms_eps;
+    double rope_theta;
+    int dtype;
+    int optimizer;
+    float lr, beta1, beta2, adam_eps;
+} catnn_moe_config;
+
+typedef struct catnn_moe_trainer catnn_moe_trainer;
+
+/* Allocates parameters (fp32 master + optimizer state + bf16 shadow),
+ * activations and scratch on the context's device. */
+int catnn_moe_trainer_create(catnn_ctx* ctx, const catnn_moe_config* cfg, catnn_moe_trainer** out);
+int catnn_moe_trainer_destroy(catnn_moe_trainer* t);
+/* Element count of the packed fp32 parameter vector: embed [V,d]; per layer
+ * rms_attn, wq, wk, wv, wo, rms_moe, gate, w1[E], w3[E], w2[E]; final norm;
+ * LM head [V,d] — the MixtralWeights fields (moe.rs:227-244) in order. */
+int catnn_moe_trainer_param_count(const catnn_moe_config* cfg, int64_t* out);
+/* Load parameters from / export parameters or last gradients to a packed
+ * fp32 device vector. Loading resets the optimizer state. */
+int catnn_moe_trainer_set_params(catnn_moe_trainer* t, const float* packed_dev);
+int catnn_moe_trainer_get_params(catnn_moe_trainer* t, float* packed_dev);
+int catnn_moe_trainer_get_grads(catnn_moe_trainer* t, float* packed_dev);
+/* One training step on device token ids [batch*seq]: forward with residual
+ * adds, next-token cross-entropy (targets[i] = tokens[(i+1) % n] % vocab),
+ * backward, and the update when update != 0. loss_dev (optional) receives
+ * the mean loss. Asynchronous. train::mixtral_step + apply_grads_sgd
+ * (crates/catnn-compile/src/train.rs:261-356, :403) / Adam::put. */
+int catnn_moe_trainer_step(catnn_moe_trainer* t, const uint32_t* tokens_dev, float* loss_dev, int update);
+/* The same step from host token ids to a host loss (copies inside; synchronous). */
+int catnn_moe_trainer_step_host(catnn_moe_trainer* t, const uint32_t* tokens_host, float* loss_host, int update);
+/* Synchronizes and reports device-side errors of earlier steps (token id or
+ * target out of range, a bounded wait that ran out). */
+int catnn_moe_trainer_check(catnn_moe_trainer* t);
+
 #ifdef __cplusplus
 }
 #endif

@@ -76,3 +76,26 @@ def test_ir_errors_match_reference():
         eval_gpu(IrNode("m", OpenOp.mix()), [x, x])
     assert adjoint_needs_output(OpenOp.softmax())
     assert not adjoint_needs_output(OpenOp.relu())
+
+
+def test_packed_layout_matches_oracle_and_abi(libpath):
+    """The packed parameter order crossing the ABI is the oracle's MixLayout."""
+    import ctypes as C
+    import torch
+    from catnn_b200 import _lib
+    from catnn_b200.train import MoeConfig, packed_layout
+    from oracle import oracle as O
+    for args in ((32, 32, 64, 2, 4, 2, 4, 2), (32000, 1024, 3584, 4, 16, 16, 8, 2), (1024, 256, 512, 2, 4, 4, 8, 2)):
+        dt = torch.bfloat16 if args[1] % 64 == 0 else torch.float32  # bf16 path needs 64-multiples
+        cfg = MoeConfig.make(*args, batch=1, seq=8, dtype=dt)
+        ours = packed_layout(cfg)
+        ref = O.MixCfg(*args).layout()
+        for k in ("embed", "final_norm", "lm_head", "total", "layer0", "layer_stride", "rms_attn", "wq", "wk", "wv",
+                  "wo", "rms_moe", "gate", "w1", "w3", "w2"):
+            assert ours[k] == ref[k], (args, k, ours[k], ref[k])
+        n = C.c_int64()
+        _lib.call("catnn_moe_trainer_param_count", C.byref(cfg), C.byref(n))
+        assert n.value == ref["total"]
+    # config 5: about 435 M parameters (SURVEY: ≈434.7 M with n_kv = 16)
+    big = O.MixCfg(32000, 1024, 3584, 4, 16, 16, 8, 2).layout()["total"]
+    assert 4.3e8 < big < 4.4e8

@@ -1,0 +1,125 @@
+"""End-to-end parity of the native MoE decoder training step against the
+oracle's train::mixtral_step (train.rs:261-356): loss, every packed
+gradient, and multi-step trajectories (SGD and Adam).
+
+- fp32 path at the reference's own tiny fixture (MixtralConfig::tiny, seed
+  7, tokens 1..8, B=2, S=4) and at a reduced mixtral-tiny shape;
+- bf16 tensor-core path at a reduced shape of the benchmark config, against
+  the fp32 oracle at the bf16 tolerance (rtol 2e-2, atol 1e-3·scale).
+"""
+import numpy as np
+import pytest
+import torch
+
+from gpu_util import close_bf16, close_f32
+from oracle import oracle as O
+
+pytestmark = pytest.mark.gpu
+
+from catnn_b200.train import MoeConfig, MoeTrainer, init_params, packed_layout  # noqa: E402
+
+
+def ocfg(c):
+    return O.MixCfg(c.vocab, c.hidden, c.mid, c.layers, c.heads, c.kv_heads, c.experts, c.top_k, c.rms_eps, c.rope_theta,
+                    c.window or None)
+
+
+def groups(cfg):
+    """(name, slice) per parameter tensor of the packed vector."""
+    L = packed_layout(cfg)
+    out = [("embed", slice(0, L["layer0"]))]
+    names = ["rms_attn", "wq", "wk", "wv", "wo", "rms_moe", "gate", "w1", "w3", "w2"]
+    for l in range(cfg.layers):
+        base = L["layer0"] + l * L["layer_stride"]
+        for i, n in enumerate(names):
+            end = L[names[i + 1]] if i + 1 < len(names) else L["layer_stride"]
+            out.append((f"L{l}.{n}", slice(base + L[n], base + end)))
+    out.append(("final_norm", slice(L["final_norm"], L["lm_head"])))
+    out.append(("lm_head", slice(L["lm_head"], L["total"])))
+    return out
+
+
+def run_compare(cfg, P, tokens, close, steps=1, lr=None):
+    tr = MoeTrainer(cfg)
+    tr.set_params(P)
+    tok = torch.as_tensor(tokens.astype(np.int32)).cuda()
+    loss = torch.zeros(1, device="cuda")
+    oc = ocfg(cfg)
+    Pref = P.copy()
+    m = np.zeros_like(P)
+    v = np.zeros_like(P)
+    for s in range(steps):
+        tr.step(tok, update=False, loss_out=loss)
+        torch.cuda.synchronize()
+        tr.check()
+        rl, rg = O.mixtral_step(oc, Pref, tokens, cfg.batch, cfg.seq)
+        close(loss, np.float32(rl), what=f"loss step {s}")
+        g = tr.grads().cpu().numpy()
+        for name, sl in groups(cfg):
+            close(g[sl], rg[sl], what=f"grad {name} step {s}")
+        tr.step(tok, update=True, loss_out=loss)  # same step again, now with the update
+        torch.cuda.synchronize()
+        if cfg.optimizer == 0:
+            Pref = O.sgd_put(Pref, rg, cfg.lr)
+        else:
+            Pref, m, v, _ = O.adam_put(Pref, rg, m, v, s, cfg.lr, cfg.beta1, cfg.beta2, cfg.adam_eps)
+        close(tr.params().cpu().numpy(), Pref, what=f"params after step {s}")
+    tr.close()
+
+
+def test_tiny_fixture_fp32():
+    """MixtralConfig::tiny with seeded LCG weights (moe.rs:247), seed 7, tokens 1..8."""
+    cfg = MoeConfig.make(32, 32, 64, 2, 4, 2, 4, 2, batch=2, seq=4, window=8, rope_theta=1e4, dtype=torch.float32,
+                         optimizer="sgd", lr=0.02)
+    P = O.mixtral_seeded(ocfg(cfg), 7)
+    run_compare(cfg, P, np.arange(1, 9), lambda g, r, what: close_f32(g, r, rtol=1e-4, floor=1e-5, what=what), steps=3)
+
+
+def test_mixtral_tiny_shape_fp32():
+    """Reduced config 4 (mixtral-tiny: d256 h4 E8 top-2 F512 V1024), fp32 path, SGD lr 0.05."""
+    cfg = MoeConfig.make(1024, 256, 512, 2, 4, 4, 8, 2, batch=2, seq=64, rope_theta=1e4, dtype=torch.float32,
+                         optimizer="sgd", lr=0.05)
+    P = init_params(cfg, 3)
+    tokens = np.random.default_rng(3).integers(0, 1024, cfg.batch * cfg.seq)
+    run_compare(cfg, P, tokens, lambda g, r, what: close_f32(g, r, rtol=1e-4, floor=1e-5, what=what), steps=2)
+
+
+def test_moe_sweep_shape_bf16_adam():
+    """Reduced config 5 (bf16 compute, fp32 master, Adam) against the fp32 oracle."""
+    cfg = MoeConfig.make(2048, 256, 512, 2, 4, 4, 8, 2, batch=2, seq=128, rope_theta=1e6, dtype=torch.bfloat16,
+                         optimizer="adam", lr=1e-3)
+    P = init_params(cfg, 4)
+    tokens = np.random.default_rng(4).integers(0, 2048, cfg.batch * cfg.seq)
+    run_compare(cfg, P, tokens, lambda g, r, what: close_bf16(g, r, what=what, atol=4e-3), steps=2)
+
+
+def test_host_step_matches_device_step():
+    cfg = MoeConfig.make(512, 128, 256, 1, 2, 2, 4, 2, batch=2, seq=64, dtype=torch.bfloat16, optimizer="adam")
+    P = init_params(cfg, 5)
+    tokens = np.random.default_rng(5).integers(0, 512, 128)
+    a, b = MoeTrainer(cfg), MoeTrainer(cfg)
+    a.set_params(P)
+    b.set_params(P)
+    la = [a.step_host(tokens) for _ in range(3)]
+    tok = torch.as_tensor(tokens.astype(np.int32)).cuda()
+    loss = torch.zeros(1, device="cuda")
+    lb = []
+    for _ in range(3):
+        b.step(tok, loss_out=loss)
+        lb.append(float(loss))
+    assert la == lb, (la, lb)  # deterministic: same kernels, same order
+    assert la[-1] < la[0]
+    a.close()
+    b.close()
+
+
+def test_bad_token_is_reported():
+    cfg = MoeConfig.make(64, 128, 256, 1, 2, 2, 4, 2, batch=1, seq=64, dtype=torch.bfloat16)
+    tr = MoeTrainer(cfg)
+    tr.set_params(init_params(cfg, 6))
+    tok = torch.full((64,), 64, dtype=torch.int32, device="cuda")
+    tr.step(tok, update=False)
+    from catnn_b200.errors import ShapeMismatch
+    with pytest.raises(ShapeMismatch):
+        tr.check()
+    tr.close()
