@@ -1,0 +1,359 @@
+#!/usr/bin/env python
+"""Benchmark: Mixtral-style MoE training step on B200.
+
+Workload (one step): 4 layers, d_model 1024, 16 heads (MHA, head_dim 64),
+8 experts top-2 with SwiGLU FFN 1024->3584->1024, RMSNorm, vocab 32000,
+global batch 8 x seq 2048 = 16384 tokens; bf16 compute, fp32 master weights,
+Adam; synthetic token ids uniform in [0, 32000), weights N(0, 0.02), seed 4.
+Metric: training tokens/s over the whole job (all ranks).
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+N > 1 runs one process per GPU (torchrun): the global batch is split over
+ranks (data parallel) with the expert-parallel token exchange and gradient
+all-reduce of the trainer over NCCL. Rank 0 prints one JSON line.
+"""
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "cat-nn-compiler_b200"))
+sys.path.insert(0, ROOT)
+
+CFG = dict(vocab=32000, hidden=1024, mid=3584, layers=4, heads=16, kv_heads=16, experts=8, top_k=2,
+           global_batch=8, seq=2048, rope_theta=1e6, rms_eps=1e-5, lr=1e-4, seed=4)
+METRIC = "MoE train tokens/s (config 5: 4L d1024 h16 E8 top-2 F3584 V32000, seq 2048, global batch 8)"
+
+
+def parse():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=10)
+    p.add_argument("--warmup", type=int, default=3)
+    p.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    return p.parse_args()
+
+
+def peaks():
+    try:
+        return json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json"))), "measured"
+    except Exception:
+        return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}, "fallback"
+
+
+def step_flops(cfg, tokens):
+    """Algorithmic FLOPs of one training step (forward x3), per SURVEY §8(d)."""
+    d, F, V, S, L, k = cfg["hidden"], cfg["mid"], cfg["vocab"], cfg["seq"], cfg["layers"], cfg["top_k"]
+    E = cfg["experts"]
+    per_tok = L * (8 * d * d + 2 * d * (S + 1) + k * 6 * d * F + 2 * d * E) + 2 * d * V
+    return 3 * per_tok * tokens
+
+
+class Clocks:
+    """nvidia-smi sampling during the timed region (clocks + throttle reasons)."""
+
+    def __init__(self, gpu_index):
+        self.proc = None
+        self.path = f"/tmp/catnn_clocks_{os.getpid()}.csv"
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={gpu_index}",
+                 "--query-gpu=clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+                 "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+                 "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        self.proc.wait()
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in open(self.path):
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 8:
+                continue
+            try:
+                sm.append(float(f[0]))
+                mx.append(float(f[1]))
+            except ValueError:
+                continue
+            for n, v in zip(names, f[4:8]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        os.unlink(self.path)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def traffic_from_profile():
+    """DRAM bytes per launch of the dominant kernel from the committed ncu
+    summary (profiles/gemm_grouped_w13.json), scaled to this launch."""
+    try:
+        j = json.load(open(os.path.join(ROOT, "profiles", "gemm_grouped_w13.json")))
+        return j.get("dram_bytes_per_launch_full_size")
+    except Exception:
+        return None
+
+
+def cpu_baseline_port(P_host, cfg, seconds_budget=20.0):
+    """The oracle (C++ restatement of train::mixtral_step) on a bounded
+    sample at config-5 widths: one sequence of a few tokens, single thread."""
+    import numpy as np
+    from oracle import oracle as O
+    oc = O.MixCfg(cfg["vocab"], cfg["hidden"], cfg["mid"], cfg["layers"], cfg["heads"], cfg["kv_heads"], cfg["experts"],
+                  cfg["top_k"], cfg["rms_eps"], cfg["rope_theta"], None)
+    r = np.random.default_rng(cfg["seed"])
+    S = 4
+    tok = r.integers(0, cfg["vocab"], S)
+    t0 = time.perf_counter()
+    O.mixtral_step(oc, P_host, tok, 1, S)
+    dt = time.perf_counter() - t0
+    return {"value": S / dt, "unit": "tokens/s", "cores": 1, "kind": "port",
+            "sample": f"oracle mixtral_step (train.rs:261 restated), 1 sequence x {S} tokens at config-5 widths "
+                      f"(4 layers, d1024, F3584, V32000), full forward+backward, {dt:.1f} s, 1 thread"}
+
+
+def run_ours(args):
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    from catnn_b200 import ops
+    from catnn_b200.train import MoeConfig, MoeTrainer
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE {world}")
+    torch.cuda.set_device(local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=torch.device("cuda", local))
+    cfg = dict(CFG)
+    B = cfg["global_batch"] // world
+    T_local = B * cfg["seq"]
+    T_global = cfg["global_batch"] * cfg["seq"]
+    mc = MoeConfig.make(cfg["vocab"], cfg["hidden"], cfg["mid"], cfg["layers"], cfg["heads"], cfg["kv_heads"],
+                        cfg["experts"], cfg["top_k"], batch=B, seq=cfg["seq"], rope_theta=cfg["rope_theta"],
+                        rms_eps=cfg["rms_eps"], dtype=torch.bfloat16, optimizer="adam", lr=cfg["lr"])
+    tr = MoeTrainer(mc, device=local)
+    # weights N(0, 0.02), norms 1; identical on every rank (same seed)
+    g = torch.Generator(device=f"cuda:{local}").manual_seed(cfg["seed"])
+    P = torch.randn(tr.n_params, generator=g, device=f"cuda:{local}") * 0.02
+    from catnn_b200.train import packed_layout
+    L = packed_layout(mc)
+    h = cfg["hidden"]
+    for l in range(cfg["layers"]):
+        base = L["layer0"] + l * L["layer_stride"]
+        P[base + L["rms_attn"]:base + L["rms_attn"] + h] = 1.0
+        P[base + L["rms_moe"]:base + L["rms_moe"] + h] = 1.0
+    P[L["final_norm"]:L["final_norm"] + h] = 1.0
+    tr.set_params(P)
+    gt = torch.Generator(device=f"cuda:{local}").manual_seed(cfg["seed"] + 1000 * rank)
+    tokens = torch.randint(0, cfg["vocab"], (T_local,), generator=gt, device=f"cuda:{local}", dtype=torch.int32)
+    loss = torch.zeros(1, device=f"cuda:{local}")
+    ctx = ops.context(local)
+    stream = torch.cuda.current_stream(local)
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local])
+        torch.cuda.synchronize(local)
+
+    for _ in range(args.warmup):
+        tr.step(tokens, update=True, loss_out=loss)
+    barrier()
+    tr.check()
+    clocks = Clocks(local)
+    launches0 = ctx.launch_count()
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        tr.step(tokens, update=True, loss_out=loss)
+    e1.record(stream)
+    barrier()
+    ms = e0.elapsed_time(e1) / args.steps
+    launches = (ctx.launch_count() - launches0) // max(args.steps, 1)
+    clk = clocks.stop()
+    tr.check()
+    last_loss = float(loss)
+    # max over ranks
+    t = torch.tensor([ms], device=f"cuda:{local}")
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t)
+
+    # end to end through the public host-buffer call: host tokens -> device,
+    # step, loss -> host, every step
+    host_tok = tokens.cpu().numpy().astype(np.uint32)
+    barrier()
+    e0.record(stream)
+    for _ in range(args.steps):
+        tr.step_host(host_tok, update=True)
+    e1.record(stream)
+    barrier()
+    e2e_ms = e0.elapsed_time(e1) / args.steps
+    t = torch.tensor([e2e_ms], device=f"cuda:{local}")
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    e2e_ms = float(t)
+
+    # dominant kernel: the grouped expert GEMM (W13 forward shape), timed live
+    pk, pk_kind = peaks()
+    E, k, F, d = cfg["experts"], cfg["top_k"], cfg["mid"], cfg["hidden"]
+    rng = np.random.default_rng(cfg["seed"])
+    counts = np.bincount(rng.integers(0, E, T_local * k), minlength=E)
+    padded = -(-counts // 128) * 128
+    offs = np.concatenate([[0], np.cumsum(padded)]).astype(np.int32)
+    rows = int(offs[-1])
+    A = torch.randn(rows, d, device=f"cuda:{local}", dtype=torch.bfloat16)
+    Bw = torch.randn(E, d, 2 * F, device=f"cuda:{local}", dtype=torch.bfloat16)
+    C = torch.empty(rows, 2 * F, device=f"cuda:{local}", dtype=torch.bfloat16)
+    off_t = torch.as_tensor(offs).to(f"cuda:{local}")
+    for _ in range(3):
+        ops.grouped_gemm(A, Bw, off_t, out=C)
+    torch.cuda.synchronize(local)
+    reps = 20
+    e0.record(stream)
+    for _ in range(reps):
+        ops.grouped_gemm(A, Bw, off_t, out=C)
+    e1.record(stream)
+    torch.cuda.synchronize(local)
+    kms = e0.elapsed_time(e1) / reps
+    kflops = 2.0 * int(counts.sum()) * 2 * F * d
+    achieved = kflops / (kms * 1e-3) / 1e12
+    peak = pk.get("bf16_tflops", 1590.0)
+
+    out = {
+        "metric": METRIC,
+        "value": T_global / (ms * 1e-3),
+        "unit": "tokens/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": ms,
+        "higher_is_better": True,
+        "scaling": "strong",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic (token ids uniform [0,32000), weights N(0,0.02), seed 4)",
+        "config": {"workload": "config5_moe_train_step", "global_batch": cfg["global_batch"], "seq_len": cfg["seq"],
+                   "tokens_per_step": T_global, "layers": 4, "d_model": 1024, "heads": 16, "experts": 8, "top_k": 2,
+                   "ffn": 3584, "vocab": 32000, "optimizer": "adam (fp32 master)",
+                   "parallelism": f"dp{world}+ep{world}" if world > 1 else "single",
+                   "l2": "inputs larger than L2 (per-step working set > 10 GB, no flush needed)"},
+        "e2e": {"value": T_global / (e2e_ms * 1e-3), "unit": "tokens/s", "h2d_bytes_per_step": T_global * 4,
+                "d2h_bytes_per_step": 4 * world},
+        "gpu_launches": int(launches),
+        "tflops_per_step": step_flops(cfg, T_global) / 1e12,
+        "model_tflops_achieved": step_flops(cfg, T_global) / (ms * 1e-3) / 1e12,
+        "loss_last": last_loss,
+        "roofline": {"bound": "tensor", "kernel": "k_gemm_tc grouped (expert W13 forward, rows=%d, N=%d, K=%d)"
+                     % (rows, 2 * F, d), "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                     "frac": achieved / peak, "peak_source": f"{pk_kind} bf16_tflops (burst, kernel timed alone)",
+                     "traffic": traffic_from_profile(), "launch_ms": kms},
+        "clocks": clk,
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        P_host = tr.params().cpu().numpy()
+        out["cpu_baseline"] = cpu_baseline_port(P_host, cfg)
+    tr.close()
+    if world > 1:
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(out), flush=True)
+
+
+def _ref_worker(args):
+    """One bounded sample of the reference step (oracle restatement)."""
+    seed, S = args
+    import numpy as np
+    from oracle import oracle as O
+    P = _SHARED["P"]
+    cfg = CFG
+    oc = O.MixCfg(cfg["vocab"], cfg["hidden"], cfg["mid"], cfg["layers"], cfg["heads"], cfg["kv_heads"], cfg["experts"],
+                  cfg["top_k"], cfg["rms_eps"], cfg["rope_theta"], None)
+    tok = np.random.default_rng(seed).integers(0, cfg["vocab"], S)
+    t0 = time.perf_counter()
+    O.mixtral_step(oc, P, tok, 1, S)
+    return time.perf_counter() - t0
+
+
+_SHARED = {}
+
+
+def run_reference(args):
+    """The reference's CPU path (its train::mixtral_step restated in C++ —
+    Rust is not available here) on the host cores: one independent sample per
+    worker process, all workers in parallel; tokens/s = tokens done / time."""
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    import multiprocessing as mp
+
+    import numpy as np
+    cfg = CFG
+    from oracle import oracle as O
+    oc = O.MixCfg(cfg["vocab"], cfg["hidden"], cfg["mid"], cfg["layers"], cfg["heads"], cfg["kv_heads"], cfg["experts"],
+                  cfg["top_k"], cfg["rms_eps"], cfg["rope_theta"], None)
+    n = oc.layout()["total"]
+    r = np.random.default_rng(cfg["seed"])
+    P = (r.standard_normal(n, dtype=np.float32) * 0.02).astype(np.float32)
+    _SHARED["P"] = P  # shared copy-on-write with the forked workers (no CUDA in this process)
+    try:
+        avail = os.sysconf("SC_AVPHYS_PAGES") * os.sysconf("SC_PAGE_SIZE")
+    except (ValueError, OSError):
+        avail = 64 << 30
+    cores = os.cpu_count() or 1
+    workers = max(1, min(cores, 32, int((avail - (8 << 30)) // (3 << 30))))
+    S = 2  # tokens per worker sample: each step is a bounded slice of the workload
+    ctx = mp.get_context("fork")
+    with ctx.Pool(workers) as pool:
+        for i in range(min(args.warmup, 1)):
+            pool.map(_ref_worker, [(1000 + w, S) for w in range(workers)])
+        times = []
+        t0 = time.perf_counter()
+        for s in range(args.steps):
+            ts = time.perf_counter()
+            pool.map(_ref_worker, [(s * 100 + w, S) for w in range(workers)])
+            times.append(time.perf_counter() - ts)
+        wall = time.perf_counter() - t0
+    tok_done = args.steps * workers * S
+    value = tok_done / wall
+    out = {"metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+           "warmup": args.warmup, "ms_per_step": wall / args.steps * 1e3, "higher_is_better": True,
+           "scaling": "strong", "vs_baseline": None, "dtype": "f32", "impl": "reference",
+           "data": "synthetic (token ids uniform [0,32000), weights N(0,0.02), seed 4)",
+           "config": {"workload": "config5_moe_train_step", "global_batch": 8, "seq_len": 2048,
+                      "parallelism": f"{workers} CPU processes"},
+           "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": workers, "kind": "port",
+                            "sample": f"each step: {workers} processes x 1 sequence of {S} tokens through the oracle's "
+                                      f"train::mixtral_step at config-5 widths (full forward+backward)"},
+           "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(out), flush=True)
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -422,6 +422,20 @@ def moe_unpermute(yp, row_of, w, tokens, k):
     return y
 
 
+def grouped_gemm(a, b, offsets, trans_b=False, out=None, out_dtype=None):
+    """Per-expert GEMM over expert-sorted rows (catnn_grouped_gemm):
+    rows [off[g], off[g+1]) of a [rows, K] times b[g] ([K,N], or [N,K] with trans_b)."""
+    _same(a, b)
+    rows, k = a.shape
+    g = b.shape[0]
+    n = b.shape[1] if trans_b else b.shape[2]
+    if out is None:
+        out = torch.empty(rows, n, dtype=out_dtype or a.dtype, device=a.device)
+    _lib.call("catnn_grouped_gemm", _h(a), int(trans_b), rows, n, k, g, _p(offsets), _p(a), _p(b), _p(out), _dt(a),
+              _dt(out))
+    return out
+
+
 def swiglu(x, w1, w3, w2):
     """moe::swiglu (moe.rs:159)."""
     _same(x, w1, w3, w2)

@@ -153,6 +153,19 @@ int catnn_moe_unpermute(catnn_ctx* h, const void* yp, const int32_t* row_of, con
     ABI_END
 }
 
+int catnn_grouped_gemm(catnn_ctx* h, int trans_b, int64_t rows, int64_t N, int64_t K, int64_t groups,
+                       const int32_t* offsets, const void* A, const void* B, void* C, int dtype, int c_dtype) {
+    ABI_BEGIN
+    Context* c = unwrap(h);
+    check_dtype(dtype);
+    check_dtype(c_dtype);
+    need(offsets && A && B && C, "grouped_gemm arguments");
+    shape(rows >= 0 && N > 0 && K > 0 && groups >= 1 && groups <= 1024, "grouped_gemm: sizes");
+    CATNN_CHECK(dtype == CATNN_BF16 || c_dtype == CATNN_F32, CATNN_ERR_DTYPE, "fp32 grouped gemm writes fp32");
+    grouped(c, dtype, trans_b != 0, rows, N, K, (int)groups, offsets, A, B, C, false, c_dtype);
+    ABI_END
+}
+
 int catnn_swiglu_fwd(catnn_ctx* h, const void* x, const void* w1, const void* w3, const void* w2, void* y, int64_t T,
                      int64_t hidden, int64_t mid, int dtype) {
     ABI_BEGIN

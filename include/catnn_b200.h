@@ -211,6 +211,14 @@ int catnn_moe_permute(catnn_ctx* ctx, const void* x, const int32_t* src_of, int6
 /* y[t] = Σ_j w[t,j] · yp[row_of[t·k+j]] in j order (moe.rs:217-219). */
 int catnn_moe_unpermute(catnn_ctx* ctx, const void* yp, const int32_t* row_of, const float* w,
                         int64_t T, int64_t k, int64_t hidden, void* y, int dtype);
+/* Expert GEMM over expert-sorted rows: for each group g, rows
+ * [offsets[g], offsets[g+1]) of A [rows, K] times op(B_g), B_g = B + g·K·N
+ * stored [K,N] (trans_b=0) or [N,K] (trans_b=1), into the same rows of
+ * C [rows, N]. offsets: device int32 [groups+1]; on the bf16 path each
+ * group's row count is a multiple of 128 (catnn_moe_permute_map, align 128).
+ * The per-expert products moe::moe computes token by token (moe.rs:207-221). */
+int catnn_grouped_gemm(catnn_ctx* ctx, int trans_b, int64_t rows, int64_t N, int64_t K, int64_t groups,
+                       const int32_t* offsets, const void* A, const void* B, void* C, int dtype, int c_dtype);
 /* SwiGLU expert w2(silu(x·w1) ⊙ (x·w3)) on x [T,hidden]. moe::swiglu (moe.rs:159). */
 int catnn_swiglu_fwd(catnn_ctx* ctx, const void* x, const void* w1, const void* w3, const void* w2,
                      void* y, int64_t T, int64_t hidden, int64_t mid, int dtype);

@@ -53,7 +53,15 @@ def close_bf16(got, ref, what="", atol=ATOL_BF16):
     err = np.abs(got.astype(np.float64) - ref)
     bound = RTOL_BF16 * np.abs(ref) + atol * scale
     bad = err > bound
-    assert not bad.any(), f"{what}: {int(bad.sum())}/{ref.size} out of tolerance; max err {err.max():.3e}"
+    i = int(np.argmax(err - bound)) if ref.size else 0
+    assert not bad.any(), (f"{what}: {int(bad.sum())}/{ref.size} out of tolerance; max err {err.max():.3e}, scale "
+                           f"{scale:.3e}, worst got {got.reshape(-1)[i]:.5e} ref {ref.reshape(-1)[i]:.5e}")
+
+
+def rel_l2(got, ref):
+    got = host(got) if torch.is_tensor(got) else np.asarray(got, np.float32)
+    ref = np.asarray(ref, np.float64).reshape(got.shape)
+    return float(np.linalg.norm(got - ref) / max(np.linalg.norm(ref), 1e-30))
 
 
 def bf16_round(a):

