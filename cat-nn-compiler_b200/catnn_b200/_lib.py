@@ -77,6 +77,7 @@ SIGNATURES = {
     "catnn_moe_trainer_step": [VP, VP, VP, I32],
     "catnn_moe_trainer_step_host": [VP, VP, VP, I32],
     "catnn_moe_trainer_check": [VP],
+    "catnn_moe_trainer_activation": [VP, I32, I64, VP],
 }
 
 _RESTYPE = {"catnn_last_error": C.c_char_p}

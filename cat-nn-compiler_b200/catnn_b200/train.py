@@ -93,7 +93,10 @@ class MoeTrainer:
         self.ctx.bind()
 
     def set_params(self, packed):
-        t = torch.as_tensor(np.ascontiguousarray(packed, np.float32)).to(f"cuda:{self.device}")
+        if torch.is_tensor(packed):
+            t = packed.detach().to(device=f"cuda:{self.device}", dtype=torch.float32).contiguous()
+        else:
+            t = torch.as_tensor(np.ascontiguousarray(packed, np.float32)).to(f"cuda:{self.device}")
         assert t.numel() == self.n_params, (t.numel(), self.n_params)
         self._bind()
         _lib.call("catnn_moe_trainer_set_params", self.handle, C.c_void_p(t.data_ptr()))
@@ -125,6 +128,19 @@ class MoeTrainer:
         self._bind()
         _lib.call("catnn_moe_trainer_step_host", self.handle, tok.ctypes.data_as(C.c_void_p), C.byref(loss), int(update))
         return float(loss.value)
+
+    ACTIVATIONS = {"x_in": 0, "x_mid": 1, "xm": 2, "ctx": 3, "router_logits": 4, "x_last": 5, "xf": 6}
+
+    def activation(self, name, layer=0):
+        """A saved activation of the last step, as an fp32 tensor."""
+        c = self.cfg
+        T, d = c.batch * c.seq, c.hidden
+        cols = {"router_logits": c.experts}.get(name, d)
+        out = torch.empty(T, cols, dtype=torch.float32, device=f"cuda:{self.device}")
+        self._bind()
+        _lib.call("catnn_moe_trainer_activation", self.handle, self.ACTIVATIONS[name], layer, C.c_void_p(out.data_ptr()))
+        torch.cuda.synchronize(self.device)
+        return out
 
     def check(self):
         self._bind()

@@ -126,6 +126,7 @@ void MoeTrainer::alloc() {
         add(T * d * e); add(T * qkvd * e); add(T * qd * e); add(T * d * e); add(cap * d * e);
         add(cap * 2 * F * e); add(cap * F * e); add(cap * d * e);
         add(T * K * 4); add(E * 4); add((E + 1) * 4); add(T * K * 4); add(cap * 4);
+        if (dt == CATNN_BF16) add(T * d * 4);
     }
     add(T * d * 4); add(T * d * e); add((size_t)T * V * e); add(T * 4); add(T * 4); add(64);
     add(T * d * 4); add(T * d * 4); add(T * d * 4); add(T * E * 4); add(T * K * 4);
@@ -157,6 +158,7 @@ void MoeTrainer::alloc() {
         a.off = ac.take<int32_t>(E + 1);
         a.row_of = ac.take<int32_t>(T * K);
         a.src_of = ac.take<int32_t>(cap);
+        a.xm32 = dt == CATNN_BF16 ? ac.take<float>(T * d) : (float*)a.xm;
     }
     x_last = ac.take<float>(T * d);
     xf = ac.take<char>(T * d * e);
@@ -242,8 +244,12 @@ void MoeTrainer::forward() {
                       qkvd);
         gemm(c, false, false, T, d, qd, a.ctx, qd, W(q.wo), d, a.x_mid, d, dt, CATNN_F32, nullptr, 0, false, a.x_in);
         // MoE half: x_out = x_mid + moe(rmsnorm(x_mid))   (moe.rs:317-319)
+        // The router runs in fp32 on every path (fp32 normalized input, fp32
+        // master gate): top-k decisions then match the reference's f32 logits
+        // instead of flipping near ties on bf16-rounded inputs.
         rmsnorm_fwd_mixed(c, a.x_mid, CATNN_F32, P + q.rms_moe, a.xm, dt, T, d, eps);
-        gemm(c, false, false, T, E, d, a.xm, d, W(q.gate), E, a.logits, E, dt, CATNN_F32, nullptr, 0, false);
+        if (dt == CATNN_BF16) rmsnorm_fwd_mixed(c, a.x_mid, CATNN_F32, P + q.rms_moe, a.xm32, CATNN_F32, T, d, eps);
+        gemm(c, false, false, T, E, d, a.xm32, d, P + q.gate, E, a.logits, E, CATNN_F32, CATNN_F32, nullptr, 0, false);
         router_topk(c, a.logits, T, E, K, a.idx, a.w);
         permute_map(c, a.idx, T, E, K, align, cap, a.counts, a.off, a.row_of, a.src_of);
         permute_rows(c, a.xm, a.src_of, cap, d, K, a.xp, dt);
@@ -279,13 +285,8 @@ void MoeTrainer::backward() {
         permute_bwd(c, dxp, a.row_of, T, K, d, dxm, dt, false, CATNN_F32);
         // router straight-through adjoint (adjoint.rs:255-284)
         router_ste(c, a.idx, a.w, dwts, T, E, K, dlog);
-        const void* dl = dlog;
-        if (dt == CATNN_BF16) {
-            cast(c, dlog, CATNN_F32, dlog_lp, CATNN_BF16, T * E);
-            dl = dlog_lp;
-        }
-        gemm(c, false, true, T, d, E, dl, E, W(q.gate), E, dxm, d, dt, CATNN_F32, nullptr, 0, true);
-        gemm(c, true, false, d, E, T, a.xm, d, dl, E, G + q.gate, E, dt, CATNN_F32, nullptr, 0, false);
+        gemm(c, false, true, T, d, E, dlog, E, P + q.gate, E, dxm, d, CATNN_F32, CATNN_F32, nullptr, 0, true);
+        gemm(c, true, false, d, E, T, a.xm32, d, dlog, E, G + q.gate, E, CATNN_F32, CATNN_F32, nullptr, 0, false);
         // residual around the MoE: dx_mid = dx + rmsnorm'(dxm)   (train.rs:327-330)
         rmsnorm_bwd_mixed(c, a.x_mid, P + q.rms_moe, dxm, CATNN_F32, dx, dxmid, dxmid_lp, dt, G + q.rms_moe, false, T, d,
                           eps);
@@ -468,6 +469,25 @@ int catnn_moe_trainer_step_host(catnn_moe_trainer* h, const uint32_t* tokens_hos
     CUDA_OK(cudaMemcpyAsync(t.h_loss, t.loss, 4, cudaMemcpyDeviceToHost, t.c->stream));
     CUDA_OK(cudaStreamSynchronize(t.c->stream));
     *loss_host = *t.h_loss;
+    ABI_END
+}
+
+int catnn_moe_trainer_activation(catnn_moe_trainer* h, int which, int64_t layer, float* out) {
+    ABI_BEGIN
+    MoeTrainer& t = tr(h);
+    CATNN_CHECK(out != nullptr, CATNN_ERR_INVALID, "null out");
+    CATNN_CHECK(which == 5 || which == 6 || (layer >= 0 && layer < t.L), CATNN_ERR_INVALID, "layer out of range");
+    const MoeTrainer::Act* a = which < 5 ? &t.acts[layer] : nullptr;
+    switch (which) {
+        case 0: CUDA_OK(cudaMemcpyAsync(out, a->x_in, t.T * t.d * 4, cudaMemcpyDeviceToDevice, t.c->stream)); break;
+        case 1: CUDA_OK(cudaMemcpyAsync(out, a->x_mid, t.T * t.d * 4, cudaMemcpyDeviceToDevice, t.c->stream)); break;
+        case 2: cast(t.c, a->xm, t.dt, out, CATNN_F32, t.T * t.d); break;
+        case 3: cast(t.c, a->ctx, t.dt, out, CATNN_F32, t.T * t.qd); break;
+        case 4: CUDA_OK(cudaMemcpyAsync(out, a->logits, t.T * t.E * 4, cudaMemcpyDeviceToDevice, t.c->stream)); break;
+        case 5: CUDA_OK(cudaMemcpyAsync(out, t.x_last, t.T * t.d * 4, cudaMemcpyDeviceToDevice, t.c->stream)); break;
+        case 6: cast(t.c, t.xf, t.dt, out, CATNN_F32, t.T * t.d); break;
+        default: throw Error(CATNN_ERR_INVALID, "activation: which in 0..6");
+    }
     ABI_END
 }
 

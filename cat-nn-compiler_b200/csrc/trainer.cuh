@@ -39,6 +39,7 @@ struct MoeTrainer {
     struct Act {
         float *x_in, *x_mid, *lse, *logits, *w;
         void *xn, *qkv, *ctx, *xm, *xp, *ac, *h, *yp;
+        float* xm32;  // fp32 router input (bf16 path; == xm on the fp32 path)
         int32_t *idx, *counts, *off, *row_of, *src_of;
     };
     std::vector<Act> acts;

@@ -294,6 +294,13 @@ int catnn_moe_trainer_get_grads(catnn_moe_trainer* t, float* packed_dev);
 int catnn_moe_trainer_step(catnn_moe_trainer* t, const uint32_t* tokens_dev, float* loss_dev, int update);
 /* The same step from host token ids to a host loss (copies inside; synchronous). */
 int catnn_moe_trainer_step_host(catnn_moe_trainer* t, const uint32_t* tokens_host, float* loss_host, int update);
+/* Copies a saved activation of the last step to out (fp32): which = 0 x_in
+ * [T,d] (input of `layer`), 1 x_mid [T,d], 2 normalized MoE input [T,d],
+ * 3 attention context [T,H·hd], 4 router logits [T,E], 5 final residual
+ * [T,d], 6 final normalized [T,d] (layer ignored for 5 and 6). The
+ * device-resident counterpart of the activations coord::ensure_act
+ * rematerializes (crates/catnn-rt/src/coord.rs:436-473). */
+int catnn_moe_trainer_activation(catnn_moe_trainer* t, int which, int64_t layer, float* out);
 /* Synchronizes and reports device-side errors of earlier steps (token id or
  * target out of range, a bounded wait that ran out). */
 int catnn_moe_trainer_check(catnn_moe_trainer* t);

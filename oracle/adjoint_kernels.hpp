@@ -151,12 +151,17 @@ void swiglu_backward(const T* x, const T* w1, const T* w3, const T* w2, const T*
 // subset dlogits = w * (g - <w, g>); dx, dgate from linear_backward.
 template <typename T>
 void router_backward_ste(const T* x, const T* gate, const T* d_weights, T* dx, T* dgate,
-                         i64 tokens, i64 hidden, i64 n_exp, i64 k) {
+                         i64 tokens, i64 hidden, i64 n_exp, i64 k, const int64_t* forced = nullptr) {
     std::vector<T> logits(tokens * n_exp), dlog(tokens * n_exp, (T)0), w(k);
     std::vector<int64_t> idx(k);
     matmul_seq(x, gate, logits.data(), tokens, hidden, n_exp);
     for (i64 t = 0; t < tokens; ++t) {
-        topk_softmax(logits.data() + t * n_exp, n_exp, k, idx.data(), w.data());
+        if (forced) {
+            for (i64 i = 0; i < k; ++i) idx[i] = forced[t * k + i];
+            softmax_selected(logits.data() + t * n_exp, k, idx.data(), w.data());
+        } else {
+            topk_softmax(logits.data() + t * n_exp, n_exp, k, idx.data(), w.data());
+        }
         T dot = 0;
         for (i64 kk = 0; kk < k; ++kk) dot += w[kk] * d_weights[t * k + kk];
         for (i64 kk = 0; kk < k; ++kk)
@@ -172,10 +177,10 @@ void router_backward_ste(const T* x, const T* gate, const T* d_weights, T* dx, T
 template <typename T>
 void moe_backward(const T* x, const T* gate, const T* w1s, const T* w3s, const T* w2s, const T* dy,
                   T* dx, T* dgate, T* dw1s, T* dw3s, T* dw2s, i64 tokens, i64 hidden, i64 mid,
-                  i64 n_exp, i64 k) {
+                  i64 n_exp, i64 k, const int64_t* forced = nullptr) {
     std::vector<int64_t> idx(tokens * k);
     std::vector<T> wts(tokens * k), logits(tokens * n_exp), dwts(tokens * k);
-    route(x, gate, tokens, hidden, n_exp, k, idx.data(), wts.data(), logits.data());
+    route(x, gate, tokens, hidden, n_exp, k, idx.data(), wts.data(), logits.data(), forced);
     std::fill(dx, dx + tokens * hidden, (T)0);
     std::fill(dw1s, dw1s + n_exp * hidden * mid, (T)0);
     std::fill(dw3s, dw3s + n_exp * hidden * mid, (T)0);
@@ -210,7 +215,7 @@ void moe_backward(const T* x, const T* gate, const T* w1s, const T* w3s, const T
         }
     }
     std::vector<T> dxg(tokens * hidden);
-    router_backward_ste(x, gate, dwts.data(), dxg.data(), dgate, tokens, hidden, n_exp, k);
+    router_backward_ste(x, gate, dwts.data(), dxg.data(), dgate, tokens, hidden, n_exp, k, forced);
     for (i64 i = 0; i < tokens * hidden; ++i) dx[i] += dxg[i];
 }
 

@@ -159,12 +159,35 @@ template <typename T> void topk_softmax(const T* logits, i64 n, i64 k, int64_t* 
     for (i64 i = 0; i < kk; ++i) w[i] *= inv;
 }
 
+// Frozen routing (the held-fixed indices of fd64.rs:550-600, topk_fixed /
+// route_idx): the k experts are given, the weights are the softmax over
+// their logits exactly as topk_softmax computes it.
+template <typename T> void softmax_selected(const T* logits, i64 k, const int64_t* idx, T* w) {
+    T mx = -INFINITY;
+    for (i64 i = 0; i < k; ++i) mx = tmax(mx, logits[idx[i]]);
+    T sum = 0;
+    for (i64 i = 0; i < k; ++i) {
+        w[i] = std::exp(logits[idx[i]] - mx);
+        sum += w[i];
+    }
+    T inv = (T)1.0 / tmax(sum, (T)1e-30);
+    for (i64 i = 0; i < k; ++i) w[i] *= inv;
+}
+
 // moe.rs:177-195 — logits = x·gate (linear_seq), then topk_softmax per row.
+// forced (optional, [tokens, k]) replaces the top-k selection.
 template <typename T>
 void route(const T* x, const T* gate, i64 tokens, i64 hidden, i64 n_exp, i64 k, int64_t* idx,
-           T* w, T* logits) {
+           T* w, T* logits, const int64_t* forced = nullptr) {
     matmul_seq(x, gate, logits, tokens, hidden, n_exp);
-    for (i64 t = 0; t < tokens; ++t) topk_softmax(logits + t * n_exp, n_exp, k, idx + t * k, w + t * k);
+    for (i64 t = 0; t < tokens; ++t) {
+        if (forced) {
+            for (i64 i = 0; i < k; ++i) idx[t * k + i] = forced[t * k + i];
+            softmax_selected(logits + t * n_exp, k, idx + t * k, w + t * k);
+        } else {
+            topk_softmax(logits + t * n_exp, n_exp, k, idx + t * k, w + t * k);
+        }
+    }
 }
 
 // moe.rs:197-223 — per token, per slot: out += w_tk * swiglu_e(x_t).
@@ -172,10 +195,10 @@ void route(const T* x, const T* gate, i64 tokens, i64 hidden, i64 n_exp, i64 k, 
 // w2s [E, mid, hidden].
 template <typename T>
 void moe(const T* x, const T* gate, const T* w1s, const T* w3s, const T* w2s, T* y, i64 tokens,
-         i64 hidden, i64 mid, i64 n_exp, i64 k) {
+         i64 hidden, i64 mid, i64 n_exp, i64 k, const int64_t* forced = nullptr) {
     std::vector<int64_t> idx(tokens * k);
     std::vector<T> wts(tokens * k), logits(tokens * n_exp), ye(hidden);
-    route(x, gate, tokens, hidden, n_exp, k, idx.data(), wts.data(), logits.data());
+    route(x, gate, tokens, hidden, n_exp, k, idx.data(), wts.data(), logits.data(), forced);
     std::fill(y, y + tokens * hidden, (T)0);
     for (i64 t = 0; t < tokens; ++t)
         for (i64 kk = 0; kk < k; ++kk) {

@@ -493,6 +493,23 @@ def mixtral_step(cfg, P, tokens, batch, seq, f64=False):
     return float(loss.value), G
 
 
+def mixtral_step_frozen(cfg, P, tokens, batch, seq, forced):
+    """mixtral_step with every layer's routing held fixed to `forced`
+    ([layers, batch*seq, top_k] expert indices) — fd64.rs's frozen-index
+    methodology for comparing across the discontinuous top-k."""
+    a, P = cfg.arr(), _arr(P)
+    tok = np.ascontiguousarray(tokens, np.uint32)
+    fz = np.ascontiguousarray(forced, np.int64)
+    assert fz.shape == (cfg.layers, batch * seq, cfg.top_k), fz.shape
+    G = np.empty_like(P)
+    loss = C.c_float()
+    rc = lib().orc_mixtral_step_frozen(_p(a), C.c_float(cfg.eps), C.c_double(cfg.theta), _p(P), _p(tok), I64(batch),
+                                       I64(seq), _p(fz), C.byref(loss), _p(G))
+    if rc:
+        raise ValueError("shape mismatch in mixtral step")
+    return float(loss.value), G
+
+
 def mlp_step(w1, b1, w2, b2, x, labels=None, y_mse=None):
     """train.rs:71 mlp_step; CE on labels when given, else MSE on y_mse."""
     w1, b1, w2, b2, x = (_arr(a) for a in (w1, b1, w2, b2, x))

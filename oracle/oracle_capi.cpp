@@ -151,6 +151,11 @@ int orc_mixtral_step(const i64* c, float eps, double theta, const float* P, cons
 int orc64_mixtral_step(const i64* c, float eps, double theta, const double* P, const uint32_t* tok, i64 b, i64 s, double* loss, double* G) {
     return orc::mixtral_step(mkcfg(c, eps, theta), P, tok, b, s, loss, G);
 }
+// forced: [layers][b*s][top_k] routing indices held fixed
+int orc_mixtral_step_frozen(const i64* c, float eps, double theta, const float* P, const uint32_t* tok, i64 b, i64 s,
+                            const int64_t* forced, float* loss, float* G) {
+    return orc::mixtral_step(mkcfg(c, eps, theta), P, tok, b, s, loss, G, forced);
+}
 int orc_mlp_step(const float* w1, const float* b1, const float* w2, const float* b2, const float* x, const float* y_mse,
                  const uint32_t* labels, int ce, i64 batch, i64 din, i64 hid, i64 dout, float* loss, float* dw1, float* db1,
                  float* dw2, float* db2) {

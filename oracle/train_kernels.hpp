@@ -143,8 +143,11 @@ int mixtral_forward(const MixCfg& c, const T* P, const uint32_t* tokens, i64 bat
 // train.rs:261-356 — mixtral_step without checkpointing (the rematerialized
 // path is bit-identical in the reference, train.rs:826). Targets are the
 // next token with wrap-around, mod vocab. G receives the packed gradients.
+// forced (optional, [layers][batch*seq][top_k]) freezes the routing of each
+// layer (the fd64.rs methodology for checks across a discontinuous top-k).
 template <typename T>
-int mixtral_step(const MixCfg& c, const T* P, const uint32_t* tokens, i64 batch, i64 seq, T* loss, T* G) {
+int mixtral_step(const MixCfg& c, const T* P, const uint32_t* tokens, i64 batch, i64 seq, T* loss, T* G,
+                 const int64_t* forced = nullptr) {
     MixLayout L(c);
     i64 h = c.hidden, n = batch * seq, hd = c.hidden / c.heads;
     std::vector<uint32_t> targets(n);
@@ -161,7 +164,8 @@ int mixtral_step(const MixCfg& c, const T* P, const uint32_t* tokens, i64 batch,
             c.heads, c.kv_heads, hd, c.theta, c.window);
         add(x.data(), attn.data(), x.data(), n * h);
         rmsnorm(x.data(), Lp + L.rms_moe, xm.data(), n, h, (T)c.eps);
-        moe(xm.data(), Lp + L.gate, Lp + L.w1, Lp + L.w3, Lp + L.w2, tmp.data(), n, h, c.mid, c.experts, c.top_k);
+        moe(xm.data(), Lp + L.gate, Lp + L.w1, Lp + L.w3, Lp + L.w2, tmp.data(), n, h, c.mid, c.experts, c.top_k,
+            forced ? forced + l * n * c.top_k : nullptr);
         add(x.data(), tmp.data(), x.data(), n * h);
         s_xn.push_back(xn);
         s_xm.push_back(xm);
@@ -182,7 +186,8 @@ int mixtral_step(const MixCfg& c, const T* P, const uint32_t* tokens, i64 batch,
         T* Gl = G + L.layer0 + l * L.layer_stride;
         add(xs[l].data(), s_attn[l].data(), xmid.data(), n * h);
         moe_backward(s_xm[l].data(), Lp + L.gate, Lp + L.w1, Lp + L.w3, Lp + L.w2, dx.data(), dxm.data(),
-                     Gl + L.gate, Gl + L.w1, Gl + L.w3, Gl + L.w2, n, h, c.mid, c.experts, c.top_k);
+                     Gl + L.gate, Gl + L.w1, Gl + L.w3, Gl + L.w2, n, h, c.mid, c.experts, c.top_k,
+                     forced ? forced + l * n * c.top_k : nullptr);
         rmsnorm_backward(xmid.data(), Lp + L.rms_moe, dxm.data(), dxmid.data(), Gl + L.rms_moe, n, h, (T)c.eps);
         add(dx.data(), dxmid.data(), dxmid.data(), n * h);  // dx_mid = dx + dxmid_moe
         gqa_backward(s_xn[l].data(), Lp + L.wq, Lp + L.wk, Lp + L.wv, Lp + L.wo, dxmid.data(), dxn.data(),

@@ -26,12 +26,13 @@ def host(t):
     return t.detach().float().cpu().numpy()
 
 
-def close_f32(got, ref, rtol=RTOL_F32, floor=RTOL_F32, what="", exact=None):
+def close_f32(got, ref, rtol=RTOL_F32, floor=RTOL_F32, what="", exact=None, scale=None):
     got = host(got) if torch.is_tensor(got) else np.asarray(got, np.float32)
     ref = np.asarray(ref, np.float32)
     assert got.shape == ref.shape or got.size == ref.size, (what, got.shape, ref.shape)
     got = got.reshape(ref.shape)
-    scale = float(np.max(np.abs(ref))) if ref.size else 0.0
+    if scale is None:
+        scale = float(np.max(np.abs(ref))) if ref.size else 0.0
     err = np.abs(got.astype(np.float64) - ref.astype(np.float64))
     bound = rtol * np.abs(ref) + floor * max(scale, 1e-30)
     bad = err > bound
