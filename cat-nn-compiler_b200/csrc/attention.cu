@@ -305,11 +305,23 @@ __global__ void __launch_bounds__(128) k_attn_fwd(AttnArgs a) {
     }
 }
 
+bool attention_tc_ok(i64 hd, i64 q_stride, i64 kv_stride, const void* q, const void* k, const void* v);
+void attention_fwd_tc(Context* c, const void* q, const void* k, const void* v, void* o, float* lse, i64 b, i64 s, i64 h,
+                      i64 hkv, i64 hd, bool causal, i64 window, i64 q_stride, i64 kv_stride);
+void attention_bwd_tc(Context* c, const void* q, const void* k, const void* v, const void* o, const float* lse,
+                      const void* dout, void* dq, void* dk, void* dv, i64 b, i64 s, i64 h, i64 hkv, i64 hd, bool causal,
+                      i64 window, i64 q_stride, i64 kv_stride);
+
 void attention_fwd(Context* c, const void* q, const void* k, const void* v, void* o, float* lse, i64 b, i64 s, i64 h,
                    i64 hkv, i64 hd, bool causal, i64 window, int dtype, i64 q_stride, i64 kv_stride) {
     if (b <= 0 || s <= 0 || h <= 0) return;
     CATNN_CHECK(hd > 0 && hd <= HDMAX, CATNN_ERR_UNSUPPORTED, "attention: head_dim must be in [1, 128]");
     CATNN_CHECK(hkv > 0 && h % hkv == 0, CATNN_ERR_SHAPE, "attention: n_heads must be a multiple of n_kv_heads");
+    if (dtype == CATNN_BF16 && attention_tc_ok(hd, q_stride ? q_stride : h * hd, kv_stride ? kv_stride : hkv * hd, q, k, v)) {
+        attention_fwd_tc(c, q, k, v, o, lse, b, s, h, hkv, hd, causal, window, q_stride ? q_stride : h * hd,
+                         kv_stride ? kv_stride : hkv * hd);
+        return;
+    }
     AttnArgs a{};
     a.q = q; a.k = k; a.v = v; a.out = o; a.lse = lse;
     a.b = b; a.s = s; a.h = h; a.hkv = hkv; a.hd = hd;
@@ -536,6 +548,11 @@ void attention_bwd(Context* c, const void* q, const void* k, const void* v, cons
     if (b <= 0 || s <= 0 || h <= 0) return;
     CATNN_CHECK(hd > 0 && hd <= HDMAX, CATNN_ERR_UNSUPPORTED, "attention: head_dim must be in [1, 128]");
     CATNN_CHECK(hkv > 0 && h % hkv == 0, CATNN_ERR_SHAPE, "attention: n_heads must be a multiple of n_kv_heads");
+    if (dtype == CATNN_BF16 && attention_tc_ok(hd, q_stride ? q_stride : h * hd, kv_stride ? kv_stride : hkv * hd, q, k, v)) {
+        attention_bwd_tc(c, q, k, v, o, lse, dout, dq, dk, dv, b, s, h, hkv, hd, causal, window,
+                         q_stride ? q_stride : h * hd, kv_stride ? kv_stride : hkv * hd);
+        return;
+    }
     float* dsum = (float*)c->scratch_for((size_t)b * h * s * 4);
     AttnArgs a{};
     a.q = q; a.k = k; a.v = v; a.o = o; a.dout = dout; a.dq = dq; a.dk = dk; a.dv = dv;

@@ -346,3 +346,31 @@ def test_moe_bf16_grouped_tensor_core():
     ref = O.moe_backward(x, gate, w1s, w3s, w2s, dy, k)
     for name, g, rr in zip(("dx", "dgate", "dw1", "dw3", "dw2"), got, ref):
         close_bf16(g, rr, what=f"moe bf16 {name}", atol=4e-3)
+
+
+@pytest.mark.parametrize("b,s,h,kv,hd,causal,window", [(2, 200, 4, 4, 64, True, None), (1, 130, 4, 2, 64, True, 48),
+                                                        (2, 96, 2, 2, 128, True, None), (1, 64, 2, 2, 64, False, None),
+                                                        (1, 257, 2, 1, 128, True, 100)])
+def test_attention_core_bf16_tensor_core(b, s, h, kv, hd, causal, window):
+    """Flash attention (mma.sync) vs the fp32 attention core (itself checked
+    against the oracle's GQA above) on the same bf16 inputs."""
+    r = rng(s + hd)
+    q = bf16_round(r.standard_normal((b, s, h, hd)).astype(np.float32))
+    k = bf16_round(r.standard_normal((b, s, kv, hd)).astype(np.float32))
+    v = bf16_round(r.standard_normal((b, s, kv, hd)).astype(np.float32))
+    do = bf16_round(r.standard_normal((b, s, h * hd)).astype(np.float32))
+    o32, l32 = ops.attention_core(dev(q), dev(k), dev(v), causal, window)
+    o16, l16 = ops.attention_core(dev(q, torch.bfloat16), dev(k, torch.bfloat16), dev(v, torch.bfloat16), causal, window)
+    close_bf16(o16, host(o32), what="fa fwd o")
+    close_f32(l16, host(l32), rtol=1e-3, floor=1e-4, what="fa fwd lse")
+    if causal:  # moe.rs:100-133 is the causal core; compare with the oracle directly too
+        close_bf16(o16, O.gqa_core(q, k, v, window), what="fa fwd vs oracle")
+    g32 = ops.attention_core_backward(dev(q), dev(k), dev(v), o32, l32, dev(do), causal, window)
+    g16 = ops.attention_core_backward(dev(q, torch.bfloat16), dev(k, torch.bfloat16), dev(v, torch.bfloat16), o16, l16,
+                                      dev(do, torch.bfloat16), causal, window)
+    from gpu_util import rel_l2
+    # dS = P ∘ (dP - D) is rounded to bf16 before the dS·K and dSᵀ·Q products
+    # (as every bf16 flash attention does) and dP - D cancels: block floor 4e-3.
+    for name, a16, a32 in zip(("dq", "dk", "dv"), g16, g32):
+        assert rel_l2(a16, host(a32)) < 1e-2, (name, rel_l2(a16, host(a32)))
+        close_bf16(a16, host(a32), what=f"fa bwd {name}", atol=4e-3)
