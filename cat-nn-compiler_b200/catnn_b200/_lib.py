@@ -42,6 +42,7 @@ SIGNATURES = {
     "catnn_softmax_fwd": [VP, VP, VP, I64, I64, I32],
     "catnn_softmax_bwd": [VP, VP, VP, VP, I64, I64, I32],
     "catnn_xent_fwdbwd": [VP, VP, VP, I64, I64, VP, VP, I32, I32],
+    "catnn_xent_fwdbwd_noalloc": [VP, VP, VP, I64, I64, VP, VP, I32, I32],
     "catnn_mse_fwdbwd": [VP, VP, VP, I64, VP, VP],
     "catnn_layernorm_fwd": [VP, VP, VP, VP, VP, I64, I64, F32, I32],
     "catnn_layernorm_bwd": [VP, VP, VP, VP, VP, VP, VP, I64, I64, F32, I32],

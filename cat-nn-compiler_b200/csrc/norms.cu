@@ -4,6 +4,8 @@
 // order (deterministic run to run). Weight-vector gradients (dgamma,
 // dbeta, dw) are column reductions done in row chunks, then chunk order:
 // no atomics, so every run gives the same bits.
+#include <mutex>
+
 #include "ops.cuh"
 
 namespace catnn {
@@ -452,3 +454,68 @@ void rmsnorm_bwd_mixed(Context* c, const float* x, const float* w, const void* d
 }
 
 }  // namespace catnn
+
+// ------------------------------------------- cross-entropy without allocation
+// Some callers cannot allocate device memory while they run a step: a
+// runtime that has planned every byte of a device's memory ahead of time
+// (catnn's fixed code/buffer/scratch budgets), or a host thread that must
+// not synchronize the device, which a cudaMalloc may do. For them, this
+// variant of catnn_xent_fwdbwd keeps its per-row loss scratch in a
+// fixed-size array compiled into the library instead of the context's
+// grow-on-demand scratch buffer. Every device that loads the library holds
+// the array (256 KB) until the process exits.
+namespace catnn {
+
+static __device__ __align__(256) float g_xent_row_loss[CATNN_XENT_NOALLOC_MAX_ROWS];
+
+// Device address of g_xent_row_loss for each device, resolved once with
+// that device current (the host-side symbol is only a stand-in).
+static float* g_xent_row_loss_ptr[64] = {nullptr};
+static std::mutex g_xent_row_loss_mu;
+
+static float* xent_row_loss_buffer(int device) {
+    CATNN_CHECK(device >= 0 && device < 64, CATNN_ERR_INVALID, "device index out of range");
+    std::lock_guard<std::mutex> lock(g_xent_row_loss_mu);
+    if (!g_xent_row_loss_ptr[device]) {
+        void* p = nullptr;
+        CUDA_OK(cudaGetSymbolAddress(&p, g_xent_row_loss));
+        g_xent_row_loss_ptr[device] = (float*)p;
+    }
+    return g_xent_row_loss_ptr[device];
+}
+
+}  // namespace catnn
+
+extern "C" int catnn_xent_fwdbwd_noalloc(catnn_ctx* h, const void* logits, const uint32_t* targets, int64_t rows,
+                                         int64_t vocab, float* loss, void* dlogits, int dtype, int check) {
+    ABI_BEGIN
+    using namespace catnn;
+    Context* c = unwrap(h);  // makes the context's device current
+    check_dtype(dtype);
+    CATNN_CHECK(rows >= 1 && vocab >= 1, CATNN_ERR_SHAPE, "cross_entropy: empty logits");
+    CATNN_CHECK(rows <= CATNN_XENT_NOALLOC_MAX_ROWS, CATNN_ERR_SHAPE,
+                "catnn_xent_fwdbwd_noalloc: " + std::to_string(rows) + " rows exceed its fixed limit of " +
+                    std::to_string(CATNN_XENT_NOALLOC_MAX_ROWS) + " (use catnn_xent_fwdbwd)");
+    CATNN_CHECK(logits && targets && loss && dlogits, CATNN_ERR_INVALID, "null argument");
+    float* rl = xent_row_loss_buffer(c->device);
+    int t = row_threads(vocab);
+    int* err = c->status + 9;
+    // every row r < rows writes rl[r] before the reduction reads it, so the
+    // array needs no clearing between calls
+    if (dtype == CATNN_BF16)
+        k_xent_rows<<<rows, t, 0, c->stream>>>((const bf16*)logits, targets, vocab, rows, (bf16*)dlogits, rl, err);
+    else
+        k_xent_rows<<<rows, t, 0, c->stream>>>((const float*)logits, targets, vocab, rows, (float*)dlogits, rl, err);
+    k_sum_rows_mean<<<1, 1024, 0, c->stream>>>(rl, rows, loss);
+    launched(c, 2);
+    if (check) {
+        int v = 0;
+        CUDA_OK(cudaMemcpyAsync(&v, err, 4, cudaMemcpyDeviceToHost, c->stream));
+        CUDA_OK(cudaStreamSynchronize(c->stream));
+        if (v) {
+            CUDA_OK(cudaMemsetAsync(err, 0, 4, c->stream));
+            throw Error(CATNN_ERR_SHAPE, "ce targets: a target is >= the number of classes");
+        }
+    }
+    ABI_END
+}

@@ -125,6 +125,19 @@ int catnn_softmax_bwd(catnn_ctx* ctx, const void* y, const void* dy, void* dx, i
  * check != 0). adjoint::cross_entropy (adjoint.rs:123). */
 int catnn_xent_fwdbwd(catnn_ctx* ctx, const void* logits, const uint32_t* targets, int64_t rows,
                       int64_t vocab, float* loss, void* dlogits, int dtype, int check);
+/* catnn_xent_fwdbwd for callers that cannot allocate device memory during
+ * a step (a runtime with a fixed memory plan, or a thread that must not
+ * block on the allocator). Same arguments, same results; its per-row scratch
+ * is a fixed array inside the library (CATNN_XENT_NOALLOC_MAX_ROWS floats per
+ * device, held until exit), so rows above that limit are rejected with
+ * CATNN_ERR_SHAPE. It calls no allocator. The first call on a device looks
+ * up that array's device address; make it before any stream capture.
+ * Calls share the array: two calls whose kernels overlap on the GPU (other
+ * streams, other contexts of the device) race. No counterpart in the
+ * reference: its CPU kernels allocate on the host per call. */
+#define CATNN_XENT_NOALLOC_MAX_ROWS 65536
+int catnn_xent_fwdbwd_noalloc(catnn_ctx* ctx, const void* logits, const uint32_t* targets, int64_t rows,
+                              int64_t vocab, float* loss, void* dlogits, int dtype, int check);
 /* Mean squared error, d = 2(p - t)/n. adjoint::mse_loss (adjoint.rs:106). fp32. */
 int catnn_mse_fwdbwd(catnn_ctx* ctx, const float* pred, const float* target, int64_t n, float* loss, float* d);
 
