@@ -37,6 +37,9 @@ def parse():
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--impl", default="ours", choices=["ours", "reference"])
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--kernel-only", action="store_true",
+                   help="run only the dominant kernel (grouped expert GEMM, W13 forward shape) for profiling")
+    p.add_argument("--reps", type=int, default=20)
     return p.parse_args()
 
 
@@ -122,6 +125,47 @@ def cpu_baseline_port(P_host, cfg, seconds_budget=20.0):
     return {"value": S / dt, "unit": "tokens/s", "cores": 1, "kind": "port",
             "sample": f"oracle mixtral_step (train.rs:261 restated), 1 sequence x {S} tokens at config-5 widths "
                       f"(4 layers, d1024, F3584, V32000), full forward+backward, {dt:.1f} s, 1 thread"}
+
+
+def dominant_kernel(local, T_local, warm, reps):
+    """The grouped expert GEMM at the config-5 W13 forward shape (routed rows
+    x 7168 x 1024, experts padded to 128 rows), timed with CUDA events on the
+    launching stream. Returns (ms per launch, algorithmic FLOPs, rows, F, d)."""
+    import numpy as np
+    import torch
+    from catnn_b200 import ops
+    cfg = CFG
+    E, k, F, d = cfg["experts"], cfg["top_k"], cfg["mid"], cfg["hidden"]
+    rng = np.random.default_rng(cfg["seed"])
+    counts = np.bincount(rng.integers(0, E, T_local * k), minlength=E)
+    padded = -(-counts // 128) * 128
+    offs = np.concatenate([[0], np.cumsum(padded)]).astype(np.int32)
+    rows = int(offs[-1])
+    dev = f"cuda:{local}"
+    A = torch.randn(rows, d, device=dev, dtype=torch.bfloat16)
+    Bw = torch.randn(E, d, 2 * F, device=dev, dtype=torch.bfloat16)
+    C = torch.empty(rows, 2 * F, device=dev, dtype=torch.bfloat16)
+    off_t = torch.as_tensor(offs).to(dev)
+    for _ in range(warm):
+        ops.grouped_gemm(A, Bw, off_t, out=C)
+    torch.cuda.synchronize(local)
+    stream = torch.cuda.current_stream(local)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(reps):
+        ops.grouped_gemm(A, Bw, off_t, out=C)
+    e1.record(stream)
+    torch.cuda.synchronize(local)
+    return e0.elapsed_time(e1) / reps, 2.0 * int(counts.sum()) * 2 * F * d, rows, F, d
+
+
+def run_kernel_only(args):
+    import torch
+    torch.cuda.set_device(0)
+    T = CFG["global_batch"] * CFG["seq"]
+    ms, flops, rows, F, d = dominant_kernel(0, T, 1, args.reps)
+    print(json.dumps({"kernel": "k_gemm_tc grouped W13 forward", "rows": rows, "N": 2 * F, "K": d, "ms": ms,
+                      "tflops": flops / (ms * 1e-3) / 1e12}), flush=True)
 
 
 def run_ours(args):
@@ -213,27 +257,7 @@ def run_ours(args):
 
     # dominant kernel: the grouped expert GEMM (W13 forward shape), timed live
     pk, pk_kind = peaks()
-    E, k, F, d = cfg["experts"], cfg["top_k"], cfg["mid"], cfg["hidden"]
-    rng = np.random.default_rng(cfg["seed"])
-    counts = np.bincount(rng.integers(0, E, T_local * k), minlength=E)
-    padded = -(-counts // 128) * 128
-    offs = np.concatenate([[0], np.cumsum(padded)]).astype(np.int32)
-    rows = int(offs[-1])
-    A = torch.randn(rows, d, device=f"cuda:{local}", dtype=torch.bfloat16)
-    Bw = torch.randn(E, d, 2 * F, device=f"cuda:{local}", dtype=torch.bfloat16)
-    C = torch.empty(rows, 2 * F, device=f"cuda:{local}", dtype=torch.bfloat16)
-    off_t = torch.as_tensor(offs).to(f"cuda:{local}")
-    for _ in range(3):
-        ops.grouped_gemm(A, Bw, off_t, out=C)
-    torch.cuda.synchronize(local)
-    reps = 20
-    e0.record(stream)
-    for _ in range(reps):
-        ops.grouped_gemm(A, Bw, off_t, out=C)
-    e1.record(stream)
-    torch.cuda.synchronize(local)
-    kms = e0.elapsed_time(e1) / reps
-    kflops = 2.0 * int(counts.sum()) * 2 * F * d
+    kms, kflops, rows, F, d = dominant_kernel(local, T_local, 3, args.reps)
     achieved = kflops / (kms * 1e-3) / 1e12
     peak = pk.get("bf16_tflops", 1590.0)
 
@@ -349,7 +373,9 @@ def run_reference(args):
 
 def main():
     args = parse()
-    if args.impl == "reference":
+    if args.kernel_only:
+        run_kernel_only(args)
+    elif args.impl == "reference":
         run_reference(args)
     else:
         run_ours(args)
