@@ -115,22 +115,36 @@ __global__ void k_rope_table(float2* __restrict__ tab, i64 s, i64 hd, double the
     }
 }
 
+// Element pair (2i, 2i+1) of one head as one 4-byte (bf16) or 8-byte (fp32) access.
+template <typename T> struct Pair;
+template <> struct Pair<float> {
+    static __device__ __forceinline__ float2 get(const float* p) { return *(const float2*)p; }
+    static __device__ __forceinline__ void put(float* p, float a, float b) { *(float2*)p = make_float2(a, b); }
+};
+template <> struct Pair<bf16> {
+    static __device__ __forceinline__ float2 get(const bf16* p) { return __bfloat1622float2(*(const __nv_bfloat162*)p); }
+    static __device__ __forceinline__ void put(bf16* p, float a, float b) {
+        *(__nv_bfloat162*)p = __floats2bfloat162_rn(a, b);
+    }
+};
+
+// CTAs stride over token rows, threads over the (head, pair) slots of a row.
 template <typename T>
-__global__ void k_rope(T* __restrict__ x, const float2* __restrict__ tab, i64 b, i64 s, i64 heads, i64 hd, int inverse,
-                       i64 row_stride, i64 col_off) {
-    i64 half = hd / 2;
-    i64 total = b * s * heads * half;
-    for (i64 idx = blockIdx.x * (i64)blockDim.x + threadIdx.x; idx < total; idx += (i64)gridDim.x * blockDim.x) {
-        i64 i = idx % half;
-        i64 h = (idx / half) % heads;
-        i64 tok = idx / (half * heads);
-        i64 pos = tok % s;
-        float2 cs_sn = tab[pos * half + i];
-        float cs = cs_sn.x, sn = inverse ? -cs_sn.y : cs_sn.y;
-        T* p = x + tok * row_stride + col_off + h * hd + 2 * i;
-        float a = ld(p), bb = ld(p + 1);
-        st(p, __fsub_rn(__fmul_rn(a, cs), __fmul_rn(bb, sn)));
-        st(p + 1, __fadd_rn(__fmul_rn(a, sn), __fmul_rn(bb, cs)));
+__global__ void __launch_bounds__(256) k_rope(T* __restrict__ x, const float2* __restrict__ tab, i64 b, i64 s, int heads,
+                                              int hd, int inverse, i64 row_stride, i64 col_off) {
+    const int half = hd / 2, slots = heads * half;
+    for (i64 tok = blockIdx.x; tok < b * s; tok += gridDim.x) {
+        const float2* trow = tab + (tok % s) * half;
+        T* xr = x + tok * row_stride + col_off;
+        for (int j = threadIdx.x; j < slots; j += blockDim.x) {
+            int h = j / half, i = j - h * half;
+            float2 cs_sn = trow[i];
+            float cs = cs_sn.x, sn = inverse ? -cs_sn.y : cs_sn.y;
+            T* p = xr + h * hd + 2 * i;
+            float2 v = Pair<T>::get(p);
+            Pair<T>::put(p, __fsub_rn(__fmul_rn(v.x, cs), __fmul_rn(v.y, sn)),
+                         __fadd_rn(__fmul_rn(v.x, sn), __fmul_rn(v.y, cs)));
+        }
     }
 }
 
@@ -159,12 +173,16 @@ void rope(Context* c, void* x, i64 b, i64 s, i64 heads, i64 hd, double theta, bo
     if (b * s * heads * (hd / 2) <= 0) return;
     if (row_stride == 0) row_stride = heads * hd;
     const float2* tab = rope_table(c, s, hd, theta);
-    i64 total = b * s * heads * (hd / 2);
-    int grid = (int)((total + 255) / 256);
-    if (grid > c->sm_count * 16) grid = c->sm_count * 16;
+    CATNN_CHECK(hd % 2 == 0 && row_stride % 2 == 0 && col_off % 2 == 0 && heads * hd <= (1 << 30), CATNN_ERR_SHAPE,
+                "rope: head dim, row stride and column offset must be even");
+    CATNN_CHECK(aligned_to(x, dtype == CATNN_BF16 ? 4 : 8), CATNN_ERR_INVALID, "rope: misaligned tensor");
+    int grid = (int)std::min<i64>(b * s, (i64)c->sm_count * 16);
     if (dtype == CATNN_BF16)
-        k_rope<<<grid, 256, 0, c->stream>>>((bf16*)x, tab, b, s, heads, hd, inverse ? 1 : 0, row_stride, col_off);
-    else k_rope<<<grid, 256, 0, c->stream>>>((float*)x, tab, b, s, heads, hd, inverse ? 1 : 0, row_stride, col_off);
+        k_rope<<<grid, 256, 0, c->stream>>>((bf16*)x, tab, b, s, (int)heads, (int)hd, inverse ? 1 : 0, row_stride,
+                                            col_off);
+    else
+        k_rope<<<grid, 256, 0, c->stream>>>((float*)x, tab, b, s, (int)heads, (int)hd, inverse ? 1 : 0, row_stride,
+                                            col_off);
     launched(c);
 }
 

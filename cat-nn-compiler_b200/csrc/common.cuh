@@ -139,4 +139,62 @@ template <> __device__ __forceinline__ void st<__nv_bfloat16>(__nv_bfloat16* p, 
 
 typedef __nv_bfloat16 bf16;
 
+// V consecutive elements in one (or two) 16-byte accesses: the streaming
+// kernels' loads and stores. The caller guarantees alignment of
+// V * sizeof(T) bytes (checked on the host with vec_ok).
+template <typename T, int V>
+__device__ __forceinline__ void ldv(const T* p, float (&o)[V]) {
+    if constexpr (V == 1) {
+        o[0] = ld(p);
+    } else if constexpr (sizeof(T) == 4) {
+        static_assert(V % 4 == 0, "fp32 vectors are multiples of 4");
+#pragma unroll
+        for (int j = 0; j < V; j += 4) {
+            float4 t = *(const float4*)((const float*)p + j);
+            o[j] = t.x; o[j + 1] = t.y; o[j + 2] = t.z; o[j + 3] = t.w;
+        }
+    } else if constexpr (V == 8) {
+        uint4 t = *(const uint4*)p;
+        const __nv_bfloat162* h = (const __nv_bfloat162*)&t;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            float2 f = __bfloat1622float2(h[j]);
+            o[2 * j] = f.x; o[2 * j + 1] = f.y;
+        }
+    } else {
+        static_assert(V == 4, "bf16 vectors are 4 or 8 wide");
+        uint2 t = *(const uint2*)p;
+        const __nv_bfloat162* h = (const __nv_bfloat162*)&t;
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+            float2 f = __bfloat1622float2(h[j]);
+            o[2 * j] = f.x; o[2 * j + 1] = f.y;
+        }
+    }
+}
+template <typename T, int V>
+__device__ __forceinline__ void stv(T* p, const float (&v)[V]) {
+    if constexpr (V == 1) {
+        st(p, v[0]);
+    } else if constexpr (sizeof(T) == 4) {
+#pragma unroll
+        for (int j = 0; j < V; j += 4) *(float4*)((float*)p + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+    } else if constexpr (V == 8) {
+        uint4 t;
+        __nv_bfloat162* h = (__nv_bfloat162*)&t;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) h[j] = __floats2bfloat162_rn(v[2 * j], v[2 * j + 1]);
+        *(uint4*)p = t;
+    } else {
+        uint2 t;
+        __nv_bfloat162* h = (__nv_bfloat162*)&t;
+#pragma unroll
+        for (int j = 0; j < 2; ++j) h[j] = __floats2bfloat162_rn(v[2 * j], v[2 * j + 1]);
+        *(uint2*)p = t;
+    }
+}
+
+// Host check: pointer aligned to `bytes` (nullptr passes).
+inline bool aligned_to(const void* p, size_t bytes) { return ((uintptr_t)p % bytes) == 0; }
+
 }  // namespace catnn

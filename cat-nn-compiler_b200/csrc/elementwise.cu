@@ -4,6 +4,8 @@
 // the storage type allows, each product and sum rounded separately
 // (__fmul_rn/__fadd_rn) so that SGD, Adam, add and mul are bit-identical to
 // the reference's f32 arithmetic.
+#include <type_traits>
+
 #include "ops.cuh"
 
 namespace catnn {
@@ -174,22 +176,39 @@ void sgd(Context* c, float* p, const float* g, i64 n, float lr, bf16* shadow) {
 // optim.rs:95-119, one thread per parameter, separate roundings:
 // m = b1*m + (1-b1)*g; v = b2*v + ((1-b2)*g)*g;
 // p = p - (lr*(m/max(b1t,1e-30))) / (sqrt(v/max(b2t,1e-30)) + eps).
-template <typename G>
-__global__ void k_adam(float* __restrict__ p, const G* __restrict__ g, float* __restrict__ m, float* __restrict__ v,
-                       i64 n, float lr, float b1, float omb1, float b2, float omb2, float b1t, float b2t, float eps,
-                       bf16* __restrict__ sh) {
-    float d1 = fmaxf(b1t, 1e-30f), d2 = fmaxf(b2t, 1e-30f);
-    for (i64 i = blockIdx.x * (i64)blockDim.x + threadIdx.x; i < n; i += (i64)gridDim.x * blockDim.x) {
-        float gi = ld(g + i);
-        float mi = __fadd_rn(__fmul_rn(b1, m[i]), __fmul_rn(omb1, gi));
-        float vi = __fadd_rn(__fmul_rn(b2, v[i]), __fmul_rn(__fmul_rn(omb2, gi), gi));
-        m[i] = mi;
-        v[i] = vi;
+struct AdamK {
+    float lr, b1, omb1, b2, omb2, d1, d2, eps;
+    __device__ __forceinline__ float step(float& p, float gi, float& m, float& v) const {
+        float mi = __fadd_rn(__fmul_rn(b1, m), __fmul_rn(omb1, gi));
+        float vi = __fadd_rn(__fmul_rn(b2, v), __fmul_rn(__fmul_rn(omb2, gi), gi));
+        m = mi;
+        v = vi;
         float mhat = __fdiv_rn(mi, d1), vhat = __fdiv_rn(vi, d2);
         float upd = __fdiv_rn(__fmul_rn(lr, mhat), __fadd_rn(__fsqrt_rn(vhat), eps));
-        float pv = __fsub_rn(p[i], upd);
-        p[i] = pv;
-        if (sh) sh[i] = __float2bfloat16_rn(pv);
+        p = __fsub_rn(p, upd);
+        return p;
+    }
+};
+
+// V = 4: p, m, v and an fp32 gradient as float4, a bf16 gradient and the
+// shadow as 8-byte groups; the host sends the n % 4 tail through V = 1.
+template <typename G, int V>
+__global__ void __launch_bounds__(256) k_adam(float* __restrict__ p, const G* __restrict__ g, float* __restrict__ m,
+                                              float* __restrict__ v, i64 n, AdamK k, bf16* __restrict__ sh) {
+    const i64 nv = n / V;
+    for (i64 i = blockIdx.x * (i64)blockDim.x + threadIdx.x; i < nv; i += (i64)gridDim.x * blockDim.x) {
+        const i64 o = i * V;
+        float pv[V], gv[V], mv[V], vv[V];
+        ldv<float, V>(p + o, pv);
+        ldv<G, V>(g + o, gv);
+        ldv<float, V>(m + o, mv);
+        ldv<float, V>(v + o, vv);
+#pragma unroll
+        for (int j = 0; j < V; ++j) k.step(pv[j], gv[j], mv[j], vv[j]);
+        stv<float, V>(m + o, mv);
+        stv<float, V>(v + o, vv);
+        stv<float, V>(p + o, pv);
+        if (sh) stv<bf16, V>(sh + o, pv);
     }
 }
 
@@ -212,11 +231,21 @@ void adam(Context* c, float* p, const void* g, float* m, float* v, i64 n, uint64
     volatile float one = 1.0f;
     float b1t = one - powi_f32(b1, t), b2t = one - powi_f32(b2, t);
     float omb1 = one - b1, omb2 = one - b2;
-    if (g_dtype == CATNN_BF16)
-        k_adam<<<ew_grid(c, n), 256, 0, c->stream>>>(p, (const bf16*)g, m, v, n, lr, b1, omb1, b2, omb2, b1t, b2t, eps, shadow);
-    else
-        k_adam<<<ew_grid(c, n), 256, 0, c->stream>>>(p, (const float*)g, m, v, n, lr, b1, omb1, b2, omb2, b1t, b2t, eps, shadow);
-    launched(c);
+    AdamK k{lr, b1, omb1, b2, omb2, std::max(b1t, 1e-30f), std::max(b2t, 1e-30f), eps};
+    const int gs = g_dtype == CATNN_BF16 ? 2 : 4;
+    const bool vec = aligned_to(p, 16) && aligned_to(m, 16) && aligned_to(v, 16) && aligned_to(g, 4 * gs) &&
+                     aligned_to(shadow, 8);
+    i64 head = vec ? n / 4 * 4 : 0;
+    auto run = [&](auto gp) {
+        using G = std::remove_const_t<std::remove_pointer_t<decltype(gp)>>;
+        if (head > 0) k_adam<G, 4><<<ew_grid(c, head / 4), 256, 0, c->stream>>>(p, gp, m, v, head, k, shadow);
+        if (n > head)
+            k_adam<G, 1><<<ew_grid(c, n - head), 256, 0, c->stream>>>(p + head, gp + head, m + head, v + head, n - head, k,
+                                                                   shadow ? shadow + head : nullptr);
+    };
+    if (g_dtype == CATNN_BF16) run((const bf16*)g);
+    else run((const float*)g);
+    launched(c, (head > 0) + (n > head));
 }
 
 }  // namespace catnn

@@ -7,6 +7,9 @@
 // dense GEMM over its rows. Rows of an expert are in token order and each
 // expert's row block is padded to `align` rows (zeros) so tensor-core tiles
 // never straddle two experts.
+#include <initializer_list>
+#include <utility>
+
 #include "ops.cuh"
 
 namespace catnn {
@@ -312,62 +315,115 @@ __device__ __forceinline__ float silu_grad_f(float x) {
 }
 
 // h = silu(a) ⊙ c. a, c: [rows, F] views with leading dimension lda
-// (a fused [a | c] buffer passes cc = a + F and lda = 2F).
-template <typename TI, typename T>
-__global__ void k_swiglu(const TI* __restrict__ a, const TI* __restrict__ cc, T* __restrict__ h, i64 rows, i64 F, i64 lda,
-                         i64 ldh) {
-    i64 n = rows * F;
-    for (i64 i = blockIdx.x * (i64)blockDim.x + threadIdx.x; i < n; i += (i64)gridDim.x * blockDim.x) {
-        i64 r = i / F, f = i % F;
-        float av = ld(a + r * lda + f), cv = ld(cc + r * lda + f);
-        st(h + r * ldh + f, silu_f(av) * cv);
+// (a fused [a | c] buffer passes cc = a + F and lda = 2F). CTAs stride over
+// rows, threads over V-wide column vectors (16-byte accesses when aligned).
+template <typename TI, typename T, int V>
+__global__ void __launch_bounds__(256) k_swiglu(const TI* __restrict__ a, const TI* __restrict__ cc, T* __restrict__ h,
+                                                i64 rows, i64 F, i64 lda, i64 ldh) {
+    for (i64 r = blockIdx.x; r < rows; r += gridDim.x) {
+        const TI* ar = a + r * lda;
+        const TI* cr = cc + r * lda;
+        T* hr = h + r * ldh;
+        for (i64 f = (i64)threadIdx.x * V; f < F; f += (i64)blockDim.x * V) {
+            float av[V], cv[V], o[V];
+            ldv<TI, V>(ar + f, av);
+            ldv<TI, V>(cr + f, cv);
+#pragma unroll
+            for (int j = 0; j < V; ++j) o[j] = silu_f(av[j]) * cv[j];
+            stv<T, V>(hr + f, o);
+        }
     }
 }
 
 // adjoint.rs:239-242: da = dh·c·silu'(a), dc = dh·silu(a).
-template <typename TI, typename TG, typename T>
-__global__ void k_swiglu_bwd(const TI* __restrict__ a, const TI* __restrict__ cc, const TG* __restrict__ dh,
-                             T* __restrict__ da, T* __restrict__ dc, i64 rows, i64 F, i64 lda, i64 ldd) {
-    i64 n = rows * F;
-    for (i64 i = blockIdx.x * (i64)blockDim.x + threadIdx.x; i < n; i += (i64)gridDim.x * blockDim.x) {
-        i64 r = i / F, f = i % F;
-        float av = ld(a + r * lda + f), cv = ld(cc + r * lda + f), g = ld(dh + r * F + f);
-        st(da + r * ldd + f, g * cv * silu_grad_f(av));
-        st(dc + r * ldd + f, g * silu_f(av));
+template <typename TI, typename TG, typename T, int V>
+__global__ void __launch_bounds__(256) k_swiglu_bwd(const TI* __restrict__ a, const TI* __restrict__ cc,
+                                                    const TG* __restrict__ dh, T* __restrict__ da, T* __restrict__ dc,
+                                                    i64 rows, i64 F, i64 lda, i64 ldd) {
+    for (i64 r = blockIdx.x; r < rows; r += gridDim.x) {
+        const TI* ar = a + r * lda;
+        const TI* cr = cc + r * lda;
+        const TG* gr = dh + r * F;
+        for (i64 f = (i64)threadIdx.x * V; f < F; f += (i64)blockDim.x * V) {
+            float av[V], cv[V], g[V], oa[V], oc[V];
+            ldv<TI, V>(ar + f, av);
+            ldv<TI, V>(cr + f, cv);
+            ldv<TG, V>(gr + f, g);
+#pragma unroll
+            for (int j = 0; j < V; ++j) {
+                oa[j] = g[j] * cv[j] * silu_grad_f(av[j]);
+                oc[j] = g[j] * silu_f(av[j]);
+            }
+            stv<T, V>(da + r * ldd + f, oa);
+            stv<T, V>(dc + r * ldd + f, oc);
+        }
     }
+}
+
+// Vector width for a row-strided stream: 8 when every tensor is bf16, 4
+// otherwise, 1 when a pitch, width or base pointer breaks the alignment.
+static int swiglu_vec(bool all_bf16, i64 F, std::initializer_list<i64> pitches,
+                      std::initializer_list<std::pair<const void*, int>> ptrs) {
+    int v = all_bf16 ? 8 : 4;
+    if (F % v) return 1;
+    for (i64 p : pitches)
+        if (p % v) return 1;
+    for (auto& q : ptrs)
+        if (!aligned_to(q.first, (size_t)v * q.second)) return 1;
+    return v;
+}
+
+static int row_grid(Context* c, i64 rows) { return (int)std::min<i64>(rows, (i64)c->sm_count * 16); }
+
+template <typename TI, typename T>
+static void launch_swiglu(Context* c, const void* a, const void* cc, void* h, i64 rows, i64 F, i64 lda, i64 ldh,
+                          int v) {
+    int g = row_grid(c, rows);
+    auto A = (const TI*)a;
+    auto Cc = (const TI*)cc;
+    auto H = (T*)h;
+    if (v == 8) k_swiglu<TI, T, 8><<<g, 256, 0, c->stream>>>(A, Cc, H, rows, F, lda, ldh);
+    else if (v == 4) k_swiglu<TI, T, 4><<<g, 256, 0, c->stream>>>(A, Cc, H, rows, F, lda, ldh);
+    else k_swiglu<TI, T, 1><<<g, 256, 0, c->stream>>>(A, Cc, H, rows, F, lda, ldh);
 }
 
 void swiglu_act(Context* c, const void* a, const void* cc, void* h, i64 rows, i64 F, i64 lda, i64 ldh, int dtype,
                 int in_dtype) {
-    i64 n = rows * F;
-    if (n <= 0) return;
+    if (rows * F <= 0) return;
     if (in_dtype < 0) in_dtype = dtype;
-    int grid = (int)((n + 255) / 256);
-    if (grid > c->sm_count * 8) grid = c->sm_count * 8;
-    if (dtype == CATNN_BF16 && in_dtype == CATNN_F32)
-        k_swiglu<<<grid, 256, 0, c->stream>>>((const float*)a, (const float*)cc, (bf16*)h, rows, F, lda, ldh);
-    else if (dtype == CATNN_BF16)
-        k_swiglu<<<grid, 256, 0, c->stream>>>((const bf16*)a, (const bf16*)cc, (bf16*)h, rows, F, lda, ldh);
-    else k_swiglu<<<grid, 256, 0, c->stream>>>((const float*)a, (const float*)cc, (float*)h, rows, F, lda, ldh);
+    int is = in_dtype == CATNN_BF16 ? 2 : 4, os = dtype == CATNN_BF16 ? 2 : 4;
+    int v = swiglu_vec(is == 2 && os == 2, F, {lda, ldh}, {{a, is}, {cc, is}, {h, os}});
+    if (dtype == CATNN_BF16 && in_dtype == CATNN_F32) launch_swiglu<float, bf16>(c, a, cc, h, rows, F, lda, ldh, v);
+    else if (dtype == CATNN_BF16) launch_swiglu<bf16, bf16>(c, a, cc, h, rows, F, lda, ldh, v);
+    else launch_swiglu<float, float>(c, a, cc, h, rows, F, lda, ldh, v);
     launched(c);
+}
+
+template <typename TI, typename TG, typename T>
+static void launch_swiglu_bwd(Context* c, const void* a, const void* cc, const void* dh, void* da, void* dc, i64 rows,
+                              i64 F, i64 lda, i64 ldd, int v) {
+    int g = row_grid(c, rows);
+    auto A = (const TI*)a;
+    auto Cc = (const TI*)cc;
+    auto G = (const TG*)dh;
+    auto DA = (T*)da;
+    auto DC = (T*)dc;
+    if (v == 8) k_swiglu_bwd<TI, TG, T, 8><<<g, 256, 0, c->stream>>>(A, Cc, G, DA, DC, rows, F, lda, ldd);
+    else if (v == 4) k_swiglu_bwd<TI, TG, T, 4><<<g, 256, 0, c->stream>>>(A, Cc, G, DA, DC, rows, F, lda, ldd);
+    else k_swiglu_bwd<TI, TG, T, 1><<<g, 256, 0, c->stream>>>(A, Cc, G, DA, DC, rows, F, lda, ldd);
 }
 
 void swiglu_act_bwd(Context* c, const void* a, const void* cc, const void* dh, void* da, void* dc, i64 rows, i64 F,
                     i64 lda, i64 ldd, int dtype, int in_dtype) {
-    i64 n = rows * F;
-    if (n <= 0) return;
+    if (rows * F <= 0) return;
     if (in_dtype < 0) in_dtype = dtype;
-    int grid = (int)((n + 255) / 256);
-    if (grid > c->sm_count * 8) grid = c->sm_count * 8;
+    int is = in_dtype == CATNN_BF16 ? 2 : 4, os = dtype == CATNN_BF16 ? 2 : 4;
+    // dh has the input's type (fp32 intermediates with fp32 inputs)
+    int v = swiglu_vec(is == 2 && os == 2, F, {lda, ldd}, {{a, is}, {cc, is}, {dh, is}, {da, os}, {dc, os}});
     if (dtype == CATNN_BF16 && in_dtype == CATNN_F32)
-        k_swiglu_bwd<<<grid, 256, 0, c->stream>>>((const float*)a, (const float*)cc, (const float*)dh, (bf16*)da,
-                                                   (bf16*)dc, rows, F, lda, ldd);
-    else if (dtype == CATNN_BF16)
-        k_swiglu_bwd<<<grid, 256, 0, c->stream>>>((const bf16*)a, (const bf16*)cc, (const bf16*)dh, (bf16*)da, (bf16*)dc,
-                                                   rows, F, lda, ldd);
-    else
-        k_swiglu_bwd<<<grid, 256, 0, c->stream>>>((const float*)a, (const float*)cc, (const float*)dh, (float*)da,
-                                                   (float*)dc, rows, F, lda, ldd);
+        launch_swiglu_bwd<float, float, bf16>(c, a, cc, dh, da, dc, rows, F, lda, ldd, v);
+    else if (dtype == CATNN_BF16) launch_swiglu_bwd<bf16, bf16, bf16>(c, a, cc, dh, da, dc, rows, F, lda, ldd, v);
+    else launch_swiglu_bwd<float, float, float>(c, a, cc, dh, da, dc, rows, F, lda, ldd, v);
     launched(c);
 }
 

@@ -65,7 +65,9 @@ void softmax_bwd(Context* c, const void* y, const void* dy, void* dx, i64 rows, 
 // then dlogits = p / rows with 1/rows taken off at the target, and the row
 // loss -ln(max(p_t, 1e-30)) into a per-row buffer that a single CTA sums in
 // row order.
-template <typename T>
+// V-wide accesses along the row (16 bytes when aligned); the running
+// (max, sum) pair is rescaled once per vector.
+template <typename T, int V>
 __global__ void k_xent_rows(const T* __restrict__ logits, const uint32_t* __restrict__ tg, i64 vocab, i64 rows,
                             T* __restrict__ dlog, float* __restrict__ row_loss, int* __restrict__ err) {
     __shared__ float red[32];
@@ -75,14 +77,18 @@ __global__ void k_xent_rows(const T* __restrict__ logits, const uint32_t* __rest
     T* out = dlog + r * vocab;
     // online max/sum per thread, then merge
     float m = -INFINITY, s = 0.f;
-    for (i64 i = threadIdx.x; i < vocab; i += blockDim.x) {
-        float v = ld(in + i);
-        if (v > m) {
-            s = s * expf(m - v) + 1.0f;
-            m = v;
-        } else {
-            s += expf(v - m);
+    for (i64 i = (i64)threadIdx.x * V; i < vocab; i += (i64)blockDim.x * V) {
+        float x[V];
+        ldv<T, V>(in + i, x);
+        float lm = x[0];
+#pragma unroll
+        for (int j = 1; j < V; ++j) lm = fmaxf(lm, x[j]);
+        if (lm > m) {
+            s = s * expf(m - lm);
+            m = lm;
         }
+#pragma unroll
+        for (int j = 0; j < V; ++j) s += expf(x[j] - m);
     }
     float gm = block_max(m, red);
     float sc = (m == -INFINITY) ? 0.f : s * expf(m - gm);
@@ -92,21 +98,46 @@ __global__ void k_xent_rows(const T* __restrict__ logits, const uint32_t* __rest
         sh_s = gs;
     }
     __syncthreads();
-    float inv = 1.0f / fmaxf(sh_s, 1e-30f);
-    float fr = (float)rows;
-    uint32_t t = tg[r];
-    bool bad = (i64)t >= vocab;
+    const float inv = 1.0f / fmaxf(sh_s, 1e-30f);
+    const float rinv = 1.0f / (float)rows;
+    const uint32_t t = tg[r];
+    const bool bad = (i64)t >= vocab;
     if (bad && threadIdx.x == 0 && err) atomicExch(err, 1);
-    for (i64 i = threadIdx.x; i < vocab; i += blockDim.x) {
-        float p = expf(ld(in + i) - sh_m) * inv;
-        float d = p / fr;
-        if (i == (i64)t) {
-            d = d - 1.0f / fr;
-            row_loss[r] = -logf(fmaxf(p, 1e-30f));
+    for (i64 i = (i64)threadIdx.x * V; i < vocab; i += (i64)blockDim.x * V) {
+        float x[V], o[V];
+        ldv<T, V>(in + i, x);
+#pragma unroll
+        for (int j = 0; j < V; ++j) {
+            float p = expf(x[j] - sh_m) * inv;
+            float d = p * rinv;
+            if (i + j == (i64)t) {
+                d = d - rinv;
+                row_loss[r] = -logf(fmaxf(p, 1e-30f));
+            }
+            o[j] = d;
         }
-        st(out + i, d);
+        stv<T, V>(out + i, o);
     }
     if (bad && threadIdx.x == 0) row_loss[r] = 0.f;
+}
+
+// One CTA per row; vector width by dtype and alignment of both row tensors.
+static void launch_xent_rows(Context* c, const void* logits, const uint32_t* targets, i64 rows, i64 vocab,
+                             void* dlogits, int dtype, float* rl, int* err) {
+    int t = row_threads(vocab);
+    int v = dtype == CATNN_BF16 ? 8 : 4;
+    if (vocab % v || !aligned_to(logits, 16) || !aligned_to(dlogits, 16)) v = 1;
+    if (dtype == CATNN_BF16) {
+        auto x = (const bf16*)logits;
+        auto d = (bf16*)dlogits;
+        if (v == 8) k_xent_rows<bf16, 8><<<rows, t, 0, c->stream>>>(x, targets, vocab, rows, d, rl, err);
+        else k_xent_rows<bf16, 1><<<rows, t, 0, c->stream>>>(x, targets, vocab, rows, d, rl, err);
+    } else {
+        auto x = (const float*)logits;
+        auto d = (float*)dlogits;
+        if (v == 4) k_xent_rows<float, 4><<<rows, t, 0, c->stream>>>(x, targets, vocab, rows, d, rl, err);
+        else k_xent_rows<float, 1><<<rows, t, 0, c->stream>>>(x, targets, vocab, rows, d, rl, err);
+    }
 }
 
 __global__ void k_sum_rows_mean(const float* __restrict__ v, i64 n, float* __restrict__ out) {
@@ -122,11 +153,7 @@ void xent_fwdbwd(Context* c, const void* logits, const uint32_t* targets, i64 ro
                  void* dlogits, int dtype, int* err) {
     if (rows <= 0 || vocab <= 0) return;
     float* rl = (float*)c->scratch_for(rows * 4);
-    int t = row_threads(vocab);
-    if (dtype == CATNN_BF16)
-        k_xent_rows<<<rows, t, 0, c->stream>>>((const bf16*)logits, targets, vocab, rows, (bf16*)dlogits, rl, err);
-    else
-        k_xent_rows<<<rows, t, 0, c->stream>>>((const float*)logits, targets, vocab, rows, (float*)dlogits, rl, err);
+    launch_xent_rows(c, logits, targets, rows, vocab, dlogits, dtype, rl, err);
     k_sum_rows_mean<<<1, 1024, 0, c->stream>>>(rl, rows, loss);
     launched(c, 2);
 }
@@ -498,14 +525,10 @@ extern "C" int catnn_xent_fwdbwd_noalloc(catnn_ctx* h, const void* logits, const
                     std::to_string(CATNN_XENT_NOALLOC_MAX_ROWS) + " (use catnn_xent_fwdbwd)");
     CATNN_CHECK(logits && targets && loss && dlogits, CATNN_ERR_INVALID, "null argument");
     float* rl = xent_row_loss_buffer(c->device);
-    int t = row_threads(vocab);
     int* err = c->status + 9;
     // every row r < rows writes rl[r] before the reduction reads it, so the
     // array needs no clearing between calls
-    if (dtype == CATNN_BF16)
-        k_xent_rows<<<rows, t, 0, c->stream>>>((const bf16*)logits, targets, vocab, rows, (bf16*)dlogits, rl, err);
-    else
-        k_xent_rows<<<rows, t, 0, c->stream>>>((const float*)logits, targets, vocab, rows, (float*)dlogits, rl, err);
+    launch_xent_rows(c, logits, targets, rows, vocab, dlogits, dtype, rl, err);
     k_sum_rows_mean<<<1, 1024, 0, c->stream>>>(rl, rows, loss);
     launched(c, 2);
     if (check) {

@@ -238,8 +238,8 @@ void MoeTrainer::forward() {
         // attention half: x_mid = x_in + attn(rmsnorm(x_in))   (moe.rs:303-316)
         rmsnorm_fwd_mixed(c, a.x_in, CATNN_F32, P + q.rms_attn, a.xn, dt, T, d, eps);
         gemm(c, false, false, T, qkvd, d, a.xn, d, W(q.wqkv), qkvd, a.qkv, qkvd, dt, dt, nullptr, 0, false);
-        rope(c, qkv, B, S, H, hd, theta, false, dt, qkvd, 0);
-        rope(c, qkv, B, S, Hkv, hd, theta, false, dt, qkvd, qd);
+        // q and k heads sit side by side at the front of each qkv row: one pass rotates both
+        rope(c, qkv, B, S, H + Hkv, hd, theta, false, dt, qkvd, 0);
         attention_fwd(c, qkv, qkv + qd * e, qkv + (qd + kd) * e, a.ctx, a.lse, B, S, H, Hkv, hd, true, window, dt, qkvd,
                       qkvd);
         gemm(c, false, false, T, d, qd, a.ctx, qd, W(q.wo), d, a.x_mid, d, dt, CATNN_F32, nullptr, 0, false, a.x_in);
@@ -295,8 +295,7 @@ void MoeTrainer::backward() {
         gemm(c, true, false, qd, d, T, a.ctx, qd, dxmid_lp, d, G + q.wo, d, dt, CATNN_F32, nullptr, 0, false);
         attention_bwd(c, qkv, qkv + qd * e, qkv + (qd + kd) * e, a.ctx, a.lse, dctx, dq, dq + qd * e, dq + (qd + kd) * e,
                       B, S, H, Hkv, hd, true, window, dt, qkvd, qkvd);
-        rope(c, dq, B, S, H, hd, theta, true, dt, qkvd, 0);
-        rope(c, dq, B, S, Hkv, hd, theta, true, dt, qkvd, qd);
+        rope(c, dq, B, S, H + Hkv, hd, theta, true, dt, qkvd, 0);
         gemm(c, false, true, T, d, qkvd, dqkv, qkvd, W(q.wqkv), qkvd, dxn, d, dt, dt, nullptr, 0, false);
         gemm(c, true, false, d, qkvd, T, a.xn, d, dqkv, qkvd, G + q.wqkv, qkvd, dt, CATNN_F32, nullptr, 0, false);
         // residual around attention: dx_in = dx_mid + rmsnorm'(dxn)   (train.rs:348-351)

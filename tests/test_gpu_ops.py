@@ -39,6 +39,33 @@ def test_linear_fwd_bwd_f32(m, k, n):
     close_f32(gb, rb, what="db")
 
 
+@pytest.mark.parametrize("T,d,E", [(16384, 1024, 8), (1000, 260, 5), (300, 64, 16), (257, 96, 32), (4096, 33, 3)])
+def test_router_shaped_gemm_f32(T, d, E):
+    """The MoE gate's three fp32 GEMMs at router shapes (N or K = experts):
+    logits = x·gate, dx += dlog·gateᵀ, dgate = xᵀ·dlog — the narrow-N,
+    short-K and split-K kernels — against the oracle's f32 linear with an
+    exact f64 fallback (rtol 1e-5 band)."""
+    r = rng(T + d + E)
+    x = r.standard_normal((T, d)).astype(np.float32)
+    gate = (r.standard_normal((d, E)) / np.sqrt(d)).astype(np.float32)
+    dlog = r.standard_normal((T, E)).astype(np.float32)
+    dx0 = r.standard_normal((T, d)).astype(np.float32)
+    X, G, DL = dev(x), dev(gate), dev(dlog)
+    lg = ops.gemm(X, G)
+    close_f32(lg, O.linear(x, gate), what="logits", exact=x.astype(np.float64) @ gate)
+    lgt = ops.gemm(X, dev(np.ascontiguousarray(gate.T)), trans_b=True)
+    close_f32(lgt, O.linear(x, gate), what="logits (gate stored [E, d])", exact=x.astype(np.float64) @ gate)
+    dx = dev(dx0)
+    ops.gemm(DL, G, trans_b=True, out=dx, accumulate=True)
+    ex = dx0 + dlog.astype(np.float64) @ gate.T.astype(np.float64)
+    close_f32(dx, ex.astype(np.float32), what="dx += dlog·gateᵀ", exact=ex)
+    dg = ops.gemm(X, DL, trans_a=True)
+    exg = x.T.astype(np.float64) @ dlog
+    close_f32(dg, O.linear(np.ascontiguousarray(x.T), dlog), what="dgate", exact=exg)
+    dg2 = ops.gemm(X, DL, trans_a=True)
+    assert torch.equal(dg, dg2), "split-K weight gradient must be deterministic"
+
+
 def test_linear_kat_identity():
     y = ops.linear(dev([[1.0, 2.0]]), dev([[1.0, 0.0], [0.0, 1.0]]))
     assert host(y).tolist() == [[1.0, 2.0]]
