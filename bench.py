@@ -33,7 +33,7 @@ METRIC = "MoE train tokens/s (config 5: 4L d1024 h16 E8 top-2 F3584 V32000, seq 
 def parse():
     p = argparse.ArgumentParser()
     p.add_argument("--gpus", type=int, default=1)
-    p.add_argument("--steps", type=int, default=10)
+    p.add_argument("--steps", type=int, default=30)
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--impl", default="ours", choices=["ours", "reference"])
     p.add_argument("--no-cpu-baseline", action="store_true")
@@ -127,17 +127,18 @@ def cpu_baseline_port(P_host, cfg, seconds_budget=20.0):
                       f"(4 layers, d1024, F3584, V32000), full forward+backward, {dt:.1f} s, 1 thread"}
 
 
-def dominant_kernel(local, T_local, warm, reps):
-    """The grouped expert GEMM at the config-5 W13 forward shape (routed rows
-    x 7168 x 1024, experts padded to 128 rows), timed with CUDA events on the
-    launching stream. Returns (ms per launch, algorithmic FLOPs, rows, F, d)."""
+def dominant_kernel(local, pairs, E, warm, reps):
+    """The grouped expert GEMM at this rank's config-5 W13 forward shape
+    (`pairs` routed rows over E local experts, each padded to 128 rows, x 7168
+    x 1024), timed with CUDA events on the launching stream. Returns (ms per
+    launch, algorithmic FLOPs, rows, F, d)."""
     import numpy as np
     import torch
     from catnn_b200 import ops
     cfg = CFG
-    E, k, F, d = cfg["experts"], cfg["top_k"], cfg["mid"], cfg["hidden"]
+    F, d = cfg["mid"], cfg["hidden"]
     rng = np.random.default_rng(cfg["seed"])
-    counts = np.bincount(rng.integers(0, E, T_local * k), minlength=E)
+    counts = np.bincount(rng.integers(0, E, pairs), minlength=E)
     padded = -(-counts // 128) * 128
     offs = np.concatenate([[0], np.cumsum(padded)]).astype(np.int32)
     rows = int(offs[-1])
@@ -163,7 +164,7 @@ def run_kernel_only(args):
     import torch
     torch.cuda.set_device(0)
     T = CFG["global_batch"] * CFG["seq"]
-    ms, flops, rows, F, d = dominant_kernel(0, T, 1, args.reps)
+    ms, flops, rows, F, d = dominant_kernel(0, T * CFG["top_k"], CFG["experts"], 1, args.reps)
     print(json.dumps({"kernel": "k_gemm_tc grouped W13 forward", "rows": rows, "N": 2 * F, "K": d, "ms": ms,
                       "tflops": flops / (ms * 1e-3) / 1e12}), flush=True)
 
@@ -189,10 +190,17 @@ def run_ours(args):
     B = cfg["global_batch"] // world
     T_local = B * cfg["seq"]
     T_global = cfg["global_batch"] * cfg["seq"]
+    # the global batch on every rank: each trains its sequences and owns
+    # experts/world experts (data + expert parallel; world 1: one GPU)
     mc = MoeConfig.make(cfg["vocab"], cfg["hidden"], cfg["mid"], cfg["layers"], cfg["heads"], cfg["kv_heads"],
-                        cfg["experts"], cfg["top_k"], batch=B, seq=cfg["seq"], rope_theta=cfg["rope_theta"],
-                        rms_eps=cfg["rms_eps"], dtype=torch.bfloat16, optimizer="adam", lr=cfg["lr"])
-    tr = MoeTrainer(mc, device=local)
+                        cfg["experts"], cfg["top_k"], batch=cfg["global_batch"], seq=cfg["seq"],
+                        rope_theta=cfg["rope_theta"], rms_eps=cfg["rms_eps"], dtype=torch.bfloat16, optimizer="adam",
+                        lr=cfg["lr"])
+    comm = None
+    if world > 1:
+        from catnn_b200.dist import Comm
+        comm = Comm.from_process_group(local)
+    tr = MoeTrainer(mc, device=local, comm=comm)
     # weights N(0, 0.02), norms 1; identical on every rank (same seed)
     g = torch.Generator(device=f"cuda:{local}").manual_seed(cfg["seed"])
     P = torch.randn(tr.n_params, generator=g, device=f"cuda:{local}") * 0.02
@@ -205,8 +213,8 @@ def run_ours(args):
         P[base + L["rms_moe"]:base + L["rms_moe"] + h] = 1.0
     P[L["final_norm"]:L["final_norm"] + h] = 1.0
     tr.set_params(P)
-    gt = torch.Generator(device=f"cuda:{local}").manual_seed(cfg["seed"] + 1000 * rank)
-    tokens = torch.randint(0, cfg["vocab"], (T_local,), generator=gt, device=f"cuda:{local}", dtype=torch.int32)
+    gt = torch.Generator(device=f"cuda:{local}").manual_seed(cfg["seed"] + 1000)
+    tokens = torch.randint(0, cfg["vocab"], (T_global,), generator=gt, device=f"cuda:{local}", dtype=torch.int32)
     loss = torch.zeros(1, device=f"cuda:{local}")
     ctx = ops.context(local)
     stream = torch.cuda.current_stream(local)
@@ -257,7 +265,8 @@ def run_ours(args):
 
     # dominant kernel: the grouped expert GEMM (W13 forward shape), timed live
     pk, pk_kind = peaks()
-    kms, kflops, rows, F, d = dominant_kernel(local, T_local, 3, args.reps)
+    kms, kflops, rows, F, d = dominant_kernel(local, T_global * cfg["top_k"] // world, cfg["experts"] // world, 3,
+                                              args.reps)
     achieved = kflops / (kms * 1e-3) / 1e12
     peak = pk.get("bf16_tflops", 1590.0)
 
@@ -279,7 +288,7 @@ def run_ours(args):
                    "ffn": 3584, "vocab": 32000, "optimizer": "adam (fp32 master)",
                    "parallelism": f"dp{world}+ep{world}" if world > 1 else "single",
                    "l2": "inputs larger than L2 (per-step working set > 10 GB, no flush needed)"},
-        "e2e": {"value": T_global / (e2e_ms * 1e-3), "unit": "tokens/s", "h2d_bytes_per_step": T_global * 4,
+        "e2e": {"value": T_global / (e2e_ms * 1e-3), "unit": "tokens/s", "h2d_bytes_per_step": T_global * 4 * world,
                 "d2h_bytes_per_step": 4 * world},
         "gpu_launches": int(launches),
         "tflops_per_step": step_flops(cfg, T_global) / 1e12,
@@ -295,6 +304,8 @@ def run_ours(args):
         P_host = tr.params().cpu().numpy()
         out["cpu_baseline"] = cpu_baseline_port(P_host, cfg)
     tr.close()
+    if comm is not None:
+        comm.close()
     if world > 1:
         dist.destroy_process_group()
     if rank == 0:

@@ -79,6 +79,18 @@ SIGNATURES = {
     "catnn_moe_trainer_step_host": [VP, VP, VP, I32],
     "catnn_moe_trainer_check": [VP],
     "catnn_moe_trainer_activation": [VP, I32, I64, VP],
+    "catnn_moe_trainer_create_ep": [VP, VP, VP, PP],
+    "catnn_comm_unique_id": [VP],
+    "catnn_comm_create": [VP, I32, I32, VP, PP],
+    "catnn_comm_destroy": [VP],
+    "catnn_comm_rank": [VP, C.POINTER(I32), C.POINTER(I32)],
+    "catnn_comm_set_timeout_ms": [VP, I64],
+    "catnn_comm_allreduce": [VP, VP, I64, I32],
+    "catnn_comm_all_to_all": [VP, VP, C.POINTER(I64), VP, C.POINTER(I64)],
+    "catnn_comm_barrier": [VP],
+    "catnn_comm_signal": [VP, I32, U64],
+    "catnn_comm_wait": [VP, I32, U64],
+    "catnn_comm_check": [VP],
 }
 
 _RESTYPE = {"catnn_last_error": C.c_char_p}

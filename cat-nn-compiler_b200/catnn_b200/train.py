@@ -66,14 +66,26 @@ def init_params(cfg, seed, std=0.02):
 
 
 class MoeTrainer:
-    def __init__(self, cfg, device=0):
+    """The native trainer on one GPU, or — given a ``dist.Comm`` — one rank of
+    the data-parallel + expert-parallel trainer (catnn_moe_trainer_create_ep):
+    ``cfg.batch`` is then the global batch, steps take the global token
+    array, and ``params()`` / ``grads()`` fill the replicated entries and this
+    rank's experts of the packed vector (other experts' entries are zero)."""
+
+    def __init__(self, cfg, device=0, comm=None):
         self.cfg = cfg
         self.device = device
+        self.comm = comm
         self.ctx = ops.context(device)
         h = C.c_void_p()
         with torch.cuda.device(device):
-            _lib.call("catnn_moe_trainer_create", self.ctx.bind(), C.byref(cfg), C.byref(h))
+            if comm is None:
+                _lib.call("catnn_moe_trainer_create", self.ctx.bind(), C.byref(cfg), C.byref(h))
+            else:
+                _lib.call("catnn_moe_trainer_create_ep", self.ctx.bind(), C.byref(cfg), comm.handle, C.byref(h))
         self.handle = h
+        self.world = comm.world if comm is not None else 1
+        self.rank = comm.rank if comm is not None else 0
         n = C.c_int64()
         _lib.call("catnn_moe_trainer_param_count", C.byref(cfg), C.byref(n))
         self.n_params = int(n.value)
@@ -103,7 +115,7 @@ class MoeTrainer:
         torch.cuda.synchronize(self.device)
 
     def _get(self, name):
-        out = torch.empty(self.n_params, dtype=torch.float32, device=f"cuda:{self.device}")
+        out = torch.zeros(self.n_params, dtype=torch.float32, device=f"cuda:{self.device}")
         self._bind()
         _lib.call(name, self.handle, C.c_void_p(out.data_ptr()))
         return out
@@ -134,7 +146,7 @@ class MoeTrainer:
     def activation(self, name, layer=0):
         """A saved activation of the last step, as an fp32 tensor."""
         c = self.cfg
-        T, d = c.batch * c.seq, c.hidden
+        T, d = c.batch // self.world * c.seq, c.hidden
         cols = {"router_logits": c.experts}.get(name, d)
         out = torch.empty(T, cols, dtype=torch.float32, device=f"cuda:{self.device}")
         self._bind()

@@ -1,0 +1,60 @@
+// Communicator of one rank in a single-node group: NCCL for the bulk
+// collectives (gradient allreduce, generic all-to-all) and peer-mapped
+// device memory (CUDA IPC over NVLink) for the fused MoE dispatch/combine
+// kernels, which read and write the other ranks' buffers directly and
+// synchronise through epoch flags with bounded waits.
+//
+// The reference models expert parallelism as E/EP experts per rank with an
+// activation all-to-all whose remote fraction is (EP-1)/EP
+// (crates/catnn-compile/src/spark_place.rs:119-131,196) and runs device
+// handlers one worker per device (crates/catnn-rt/src/dist.rs:441-517).
+#pragma once
+#include <vector>
+
+#include "ops.cuh"
+
+namespace catnn {
+
+// Status slot set by a device wait that ran out of time (and the epoch it waited for).
+constexpr int COMM_STATUS_SLOT = 12;
+constexpr int COMM_MAX_WORLD = 8;
+
+struct NcclFns;
+
+struct Comm {
+    Context* c = nullptr;
+    int rank = 0, world = 1;
+    void* nccl = nullptr;  // ncclComm_t
+    const NcclFns* fn = nullptr;
+    // Peer-mapped allocations: base[p] is rank p's copy as seen from this
+    // process (base[rank] is the local pointer).
+    struct Mapped {
+        void* base[COMM_MAX_WORLD] = {};
+        size_t bytes = 0;
+    };
+    std::vector<Mapped> maps;
+    // flags[src] in each rank's flag block: the last epoch rank src signalled.
+    uint64_t* flag_block = nullptr;           // local, world x uint64
+    uint64_t** flag_ptrs_dev = nullptr;       // device [world] -> each rank's flag block
+    uint64_t epoch = 0;
+    int64_t timeout_ns = 10ll * 1000 * 1000 * 1000;
+
+    // Exchange an IPC handle of `local` (the base of a cudaMalloc block of
+    // `bytes`, same size on every rank) and map the peers' blocks. Collective.
+    Mapped map(void* local, size_t bytes);
+    // Pointer q inside mapped block m, translated to rank p's copy.
+    template <typename T>
+    T* at(const Mapped& m, int p, T* q) const {
+        return (T*)((char*)m.base[p] + ((char*)q - (char*)m.base[rank]));
+    }
+    // Device barrier: every rank signals every rank, then waits (bounded)
+    // for all signals of this epoch. Enqueued on the context stream.
+    void barrier();
+    void allreduce_sum(void* buf, i64 n, int dtype);
+    void release();
+};
+
+// The communicator behind a catnn_comm handle (binds its context).
+Comm* comm_of(catnn_comm* h);
+
+}  // namespace catnn

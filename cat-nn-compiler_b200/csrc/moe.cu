@@ -319,7 +319,8 @@ __device__ __forceinline__ float silu_grad_f(float x) {
 // rows, threads over V-wide column vectors (16-byte accesses when aligned).
 template <typename TI, typename T, int V>
 __global__ void __launch_bounds__(256) k_swiglu(const TI* __restrict__ a, const TI* __restrict__ cc, T* __restrict__ h,
-                                                i64 rows, i64 F, i64 lda, i64 ldh) {
+                                                i64 rows, i64 F, i64 lda, i64 ldh, const int32_t* __restrict__ rows_dev) {
+    if (rows_dev && *rows_dev < rows) rows = *rows_dev;
     for (i64 r = blockIdx.x; r < rows; r += gridDim.x) {
         const TI* ar = a + r * lda;
         const TI* cr = cc + r * lda;
@@ -339,7 +340,9 @@ __global__ void __launch_bounds__(256) k_swiglu(const TI* __restrict__ a, const 
 template <typename TI, typename TG, typename T, int V>
 __global__ void __launch_bounds__(256) k_swiglu_bwd(const TI* __restrict__ a, const TI* __restrict__ cc,
                                                     const TG* __restrict__ dh, T* __restrict__ da, T* __restrict__ dc,
-                                                    i64 rows, i64 F, i64 lda, i64 ldd) {
+                                                    i64 rows, i64 F, i64 lda, i64 ldd,
+                                                    const int32_t* __restrict__ rows_dev) {
+    if (rows_dev && *rows_dev < rows) rows = *rows_dev;
     for (i64 r = blockIdx.x; r < rows; r += gridDim.x) {
         const TI* ar = a + r * lda;
         const TI* cr = cc + r * lda;
@@ -377,53 +380,53 @@ static int row_grid(Context* c, i64 rows) { return (int)std::min<i64>(rows, (i64
 
 template <typename TI, typename T>
 static void launch_swiglu(Context* c, const void* a, const void* cc, void* h, i64 rows, i64 F, i64 lda, i64 ldh,
-                          int v) {
+                          int v, const int32_t* rows_dev) {
     int g = row_grid(c, rows);
     auto A = (const TI*)a;
     auto Cc = (const TI*)cc;
     auto H = (T*)h;
-    if (v == 8) k_swiglu<TI, T, 8><<<g, 256, 0, c->stream>>>(A, Cc, H, rows, F, lda, ldh);
-    else if (v == 4) k_swiglu<TI, T, 4><<<g, 256, 0, c->stream>>>(A, Cc, H, rows, F, lda, ldh);
-    else k_swiglu<TI, T, 1><<<g, 256, 0, c->stream>>>(A, Cc, H, rows, F, lda, ldh);
+    if (v == 8) k_swiglu<TI, T, 8><<<g, 256, 0, c->stream>>>(A, Cc, H, rows, F, lda, ldh, rows_dev);
+    else if (v == 4) k_swiglu<TI, T, 4><<<g, 256, 0, c->stream>>>(A, Cc, H, rows, F, lda, ldh, rows_dev);
+    else k_swiglu<TI, T, 1><<<g, 256, 0, c->stream>>>(A, Cc, H, rows, F, lda, ldh, rows_dev);
 }
 
 void swiglu_act(Context* c, const void* a, const void* cc, void* h, i64 rows, i64 F, i64 lda, i64 ldh, int dtype,
-                int in_dtype) {
+                int in_dtype, const int32_t* rows_dev) {
     if (rows * F <= 0) return;
     if (in_dtype < 0) in_dtype = dtype;
     int is = in_dtype == CATNN_BF16 ? 2 : 4, os = dtype == CATNN_BF16 ? 2 : 4;
     int v = swiglu_vec(is == 2 && os == 2, F, {lda, ldh}, {{a, is}, {cc, is}, {h, os}});
-    if (dtype == CATNN_BF16 && in_dtype == CATNN_F32) launch_swiglu<float, bf16>(c, a, cc, h, rows, F, lda, ldh, v);
-    else if (dtype == CATNN_BF16) launch_swiglu<bf16, bf16>(c, a, cc, h, rows, F, lda, ldh, v);
-    else launch_swiglu<float, float>(c, a, cc, h, rows, F, lda, ldh, v);
+    if (dtype == CATNN_BF16 && in_dtype == CATNN_F32) launch_swiglu<float, bf16>(c, a, cc, h, rows, F, lda, ldh, v, rows_dev);
+    else if (dtype == CATNN_BF16) launch_swiglu<bf16, bf16>(c, a, cc, h, rows, F, lda, ldh, v, rows_dev);
+    else launch_swiglu<float, float>(c, a, cc, h, rows, F, lda, ldh, v, rows_dev);
     launched(c);
 }
 
 template <typename TI, typename TG, typename T>
 static void launch_swiglu_bwd(Context* c, const void* a, const void* cc, const void* dh, void* da, void* dc, i64 rows,
-                              i64 F, i64 lda, i64 ldd, int v) {
+                              i64 F, i64 lda, i64 ldd, int v, const int32_t* rows_dev) {
     int g = row_grid(c, rows);
     auto A = (const TI*)a;
     auto Cc = (const TI*)cc;
     auto G = (const TG*)dh;
     auto DA = (T*)da;
     auto DC = (T*)dc;
-    if (v == 8) k_swiglu_bwd<TI, TG, T, 8><<<g, 256, 0, c->stream>>>(A, Cc, G, DA, DC, rows, F, lda, ldd);
-    else if (v == 4) k_swiglu_bwd<TI, TG, T, 4><<<g, 256, 0, c->stream>>>(A, Cc, G, DA, DC, rows, F, lda, ldd);
-    else k_swiglu_bwd<TI, TG, T, 1><<<g, 256, 0, c->stream>>>(A, Cc, G, DA, DC, rows, F, lda, ldd);
+    if (v == 8) k_swiglu_bwd<TI, TG, T, 8><<<g, 256, 0, c->stream>>>(A, Cc, G, DA, DC, rows, F, lda, ldd, rows_dev);
+    else if (v == 4) k_swiglu_bwd<TI, TG, T, 4><<<g, 256, 0, c->stream>>>(A, Cc, G, DA, DC, rows, F, lda, ldd, rows_dev);
+    else k_swiglu_bwd<TI, TG, T, 1><<<g, 256, 0, c->stream>>>(A, Cc, G, DA, DC, rows, F, lda, ldd, rows_dev);
 }
 
 void swiglu_act_bwd(Context* c, const void* a, const void* cc, const void* dh, void* da, void* dc, i64 rows, i64 F,
-                    i64 lda, i64 ldd, int dtype, int in_dtype) {
+                    i64 lda, i64 ldd, int dtype, int in_dtype, const int32_t* rows_dev) {
     if (rows * F <= 0) return;
     if (in_dtype < 0) in_dtype = dtype;
     int is = in_dtype == CATNN_BF16 ? 2 : 4, os = dtype == CATNN_BF16 ? 2 : 4;
     // dh has the input's type (fp32 intermediates with fp32 inputs)
     int v = swiglu_vec(is == 2 && os == 2, F, {lda, ldd}, {{a, is}, {cc, is}, {dh, is}, {da, os}, {dc, os}});
     if (dtype == CATNN_BF16 && in_dtype == CATNN_F32)
-        launch_swiglu_bwd<float, float, bf16>(c, a, cc, dh, da, dc, rows, F, lda, ldd, v);
-    else if (dtype == CATNN_BF16) launch_swiglu_bwd<bf16, bf16, bf16>(c, a, cc, dh, da, dc, rows, F, lda, ldd, v);
-    else launch_swiglu_bwd<float, float, float>(c, a, cc, dh, da, dc, rows, F, lda, ldd, v);
+        launch_swiglu_bwd<float, float, bf16>(c, a, cc, dh, da, dc, rows, F, lda, ldd, v, rows_dev);
+    else if (dtype == CATNN_BF16) launch_swiglu_bwd<bf16, bf16, bf16>(c, a, cc, dh, da, dc, rows, F, lda, ldd, v, rows_dev);
+    else launch_swiglu_bwd<float, float, float>(c, a, cc, dh, da, dc, rows, F, lda, ldd, v, rows_dev);
     launched(c);
 }
 

@@ -68,7 +68,7 @@ void softmax_bwd(Context* c, const void* y, const void* dy, void* dx, i64 rows, 
 // V-wide accesses along the row (16 bytes when aligned); the running
 // (max, sum) pair is rescaled once per vector.
 template <typename T, int V>
-__global__ void k_xent_rows(const T* __restrict__ logits, const uint32_t* __restrict__ tg, i64 vocab, i64 rows,
+__global__ void k_xent_rows(const T* __restrict__ logits, const uint32_t* __restrict__ tg, i64 vocab, i64 denom,
                             T* __restrict__ dlog, float* __restrict__ row_loss, int* __restrict__ err) {
     __shared__ float red[32];
     __shared__ float sh_m, sh_s;
@@ -99,7 +99,7 @@ __global__ void k_xent_rows(const T* __restrict__ logits, const uint32_t* __rest
     }
     __syncthreads();
     const float inv = 1.0f / fmaxf(sh_s, 1e-30f);
-    const float rinv = 1.0f / (float)rows;
+    const float rinv = 1.0f / (float)denom;
     const uint32_t t = tg[r];
     const bool bad = (i64)t >= vocab;
     if (bad && threadIdx.x == 0 && err) atomicExch(err, 1);
@@ -123,38 +123,39 @@ __global__ void k_xent_rows(const T* __restrict__ logits, const uint32_t* __rest
 
 // One CTA per row; vector width by dtype and alignment of both row tensors.
 static void launch_xent_rows(Context* c, const void* logits, const uint32_t* targets, i64 rows, i64 vocab,
-                             void* dlogits, int dtype, float* rl, int* err) {
+                             void* dlogits, int dtype, float* rl, int* err, i64 denom) {
     int t = row_threads(vocab);
     int v = dtype == CATNN_BF16 ? 8 : 4;
     if (vocab % v || !aligned_to(logits, 16) || !aligned_to(dlogits, 16)) v = 1;
     if (dtype == CATNN_BF16) {
         auto x = (const bf16*)logits;
         auto d = (bf16*)dlogits;
-        if (v == 8) k_xent_rows<bf16, 8><<<rows, t, 0, c->stream>>>(x, targets, vocab, rows, d, rl, err);
-        else k_xent_rows<bf16, 1><<<rows, t, 0, c->stream>>>(x, targets, vocab, rows, d, rl, err);
+        if (v == 8) k_xent_rows<bf16, 8><<<rows, t, 0, c->stream>>>(x, targets, vocab, denom, d, rl, err);
+        else k_xent_rows<bf16, 1><<<rows, t, 0, c->stream>>>(x, targets, vocab, denom, d, rl, err);
     } else {
         auto x = (const float*)logits;
         auto d = (float*)dlogits;
-        if (v == 4) k_xent_rows<float, 4><<<rows, t, 0, c->stream>>>(x, targets, vocab, rows, d, rl, err);
-        else k_xent_rows<float, 1><<<rows, t, 0, c->stream>>>(x, targets, vocab, rows, d, rl, err);
+        if (v == 4) k_xent_rows<float, 4><<<rows, t, 0, c->stream>>>(x, targets, vocab, denom, d, rl, err);
+        else k_xent_rows<float, 1><<<rows, t, 0, c->stream>>>(x, targets, vocab, denom, d, rl, err);
     }
 }
 
-__global__ void k_sum_rows_mean(const float* __restrict__ v, i64 n, float* __restrict__ out) {
+__global__ void k_sum_rows_mean(const float* __restrict__ v, i64 n, float* __restrict__ out, i64 denom) {
     __shared__ float red[32];
     float s = 0.f;
     // fixed assignment: thread t sums elements t, t+B, ... in order
     for (i64 i = threadIdx.x; i < n; i += blockDim.x) s += v[i];
     s = block_sum(s, red);
-    if (threadIdx.x == 0) *out = s / (float)n;
+    if (threadIdx.x == 0) *out = s / (float)denom;
 }
 
 void xent_fwdbwd(Context* c, const void* logits, const uint32_t* targets, i64 rows, i64 vocab, float* loss,
-                 void* dlogits, int dtype, int* err) {
+                 void* dlogits, int dtype, int* err, i64 denom) {
     if (rows <= 0 || vocab <= 0) return;
+    if (denom <= 0) denom = rows;
     float* rl = (float*)c->scratch_for(rows * 4);
-    launch_xent_rows(c, logits, targets, rows, vocab, dlogits, dtype, rl, err);
-    k_sum_rows_mean<<<1, 1024, 0, c->stream>>>(rl, rows, loss);
+    launch_xent_rows(c, logits, targets, rows, vocab, dlogits, dtype, rl, err, denom);
+    k_sum_rows_mean<<<1, 1024, 0, c->stream>>>(rl, rows, loss, denom);
     launched(c, 2);
 }
 
@@ -528,8 +529,8 @@ extern "C" int catnn_xent_fwdbwd_noalloc(catnn_ctx* h, const void* logits, const
     int* err = c->status + 9;
     // every row r < rows writes rl[r] before the reduction reads it, so the
     // array needs no clearing between calls
-    launch_xent_rows(c, logits, targets, rows, vocab, dlogits, dtype, rl, err);
-    k_sum_rows_mean<<<1, 1024, 0, c->stream>>>(rl, rows, loss);
+    launch_xent_rows(c, logits, targets, rows, vocab, dlogits, dtype, rl, err, rows);
+    k_sum_rows_mean<<<1, 1024, 0, c->stream>>>(rl, rows, loss, rows);
     launched(c, 2);
     if (check) {
         int v = 0;

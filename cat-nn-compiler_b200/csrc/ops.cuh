@@ -77,9 +77,11 @@ void adam(Context* c, float* p, const void* g, float* m, float* v, i64 n, uint64
 void softmax_fwd(Context* c, const void* x, void* y, i64 rows, i64 last, int dtype);
 void softmax_bwd(Context* c, const void* y, const void* dy, void* dx, i64 rows, i64 last, int dtype);
 // loss: device fp32 scalar (written, not accumulated). err: device int set
-// to 1 when a target is out of range (may be null).
+// to 1 when a target is out of range (may be null). denom (0: rows) is the
+// count the mean divides by — the global token count when the rows are one
+// rank's share of a batch.
 void xent_fwdbwd(Context* c, const void* logits, const uint32_t* targets, i64 rows, i64 vocab, float* loss,
-                 void* dlogits, int dtype, int* err);
+                 void* dlogits, int dtype, int* err, i64 denom = 0);
 void mse_fwdbwd(Context* c, const float* pred, const float* target, i64 n, float* loss, float* d);
 void layernorm_fwd(Context* c, const void* x, const float* g, const float* b, void* y, i64 rows, i64 last,
                    float eps, int dtype);
@@ -138,9 +140,11 @@ void router_ste(Context* c, const int32_t* idx, const float* w, const float* dw,
 // separate buffers; and its adjoint.
 // in_dtype (default: dtype) is the storage of a, c (and dh): fp32 pre-activations
 // may feed bf16 outputs.
+// rows_dev (optional, device int): only the first min(rows, *rows_dev) rows
+// are computed (the rows an expert-parallel rank actually received).
 void swiglu_act(Context* c, const void* a, const void* cc, void* h, i64 rows, i64 F, i64 lda, i64 ldh,
-                int dtype, int in_dtype = -1);
+                int dtype, int in_dtype = -1, const int32_t* rows_dev = nullptr);
 void swiglu_act_bwd(Context* c, const void* a, const void* cc, const void* dh, void* da, void* dc, i64 rows,
-                    i64 F, i64 lda, i64 ldd, int dtype, int in_dtype = -1);
+                    i64 F, i64 lda, i64 ldd, int dtype, int in_dtype = -1, const int32_t* rows_dev = nullptr);
 
 }  // namespace catnn

@@ -10,6 +10,7 @@
 //  - weight gradients land in fp32 directly from the GEMM epilogue.
 #include <cstring>
 
+#include "moe_ep.cuh"
 #include "trainer.cuh"
 
 namespace catnn {
@@ -31,11 +32,15 @@ void MoeTrainer::plan_params() {
         lo[l].wo = take(qd * d);
         lo[l].rms_moe = take(d);
         lo[l].gate = take(d * E);
-        lo[l].w13 = take(E * d * 2 * F);
-        lo[l].w2 = take(E * F * d);
     }
     o_final = take(d);
     o_lm = take(V * d);
+    o_loss = take(1);
+    n_rep = o;
+    for (i64 l = 0; l < L; ++l) {
+        lo[l].w13 = take(El * d * 2 * F);
+        lo[l].w2 = take(El * F * d);
+    }
     n_params = o;
 }
 
@@ -66,9 +71,10 @@ void MoeTrainer::import_packed(const float* pk, float* dst) {
         cp(dst + q.wo, p, qd * d); p += qd * d;
         cp(dst + q.rms_moe, p, d); p += d;
         cp(dst + q.gate, p, d * E); p += d * E;
-        cp2(dst + q.w13, 2 * F, p, F, F, E * d); p += E * d * F;
-        cp2(dst + q.w13 + F, 2 * F, p, F, F, E * d); p += E * d * F;
-        cp(dst + q.w2, p, E * F * d); p += E * F * d;
+        // this rank's experts [e0, e0 + El) of w1[E], w3[E], w2[E]
+        cp2(dst + q.w13, 2 * F, p + e0 * d * F, F, F, El * d); p += E * d * F;
+        cp2(dst + q.w13 + F, 2 * F, p + e0 * d * F, F, F, El * d); p += E * d * F;
+        cp(dst + q.w2, p + e0 * F * d, El * F * d); p += E * F * d;
     }
     cp(dst + o_final, p, d); p += d;
     cp(dst + o_lm, p, V * d);
@@ -94,9 +100,9 @@ void MoeTrainer::export_packed(const float* src, float* pk) {
         cp(p, src + q.wo, qd * d); p += qd * d;
         cp(p, src + q.rms_moe, d); p += d;
         cp(p, src + q.gate, d * E); p += d * E;
-        cp2(p, F, src + q.w13, 2 * F, F, E * d); p += E * d * F;
-        cp2(p, F, src + q.w13 + F, 2 * F, F, E * d); p += E * d * F;
-        cp(p, src + q.w2, E * F * d); p += E * F * d;
+        cp2(p + e0 * d * F, F, src + q.w13, 2 * F, F, El * d); p += E * d * F;
+        cp2(p + e0 * d * F, F, src + q.w13 + F, 2 * F, F, El * d); p += E * d * F;
+        cp(p + e0 * F * d, src + q.w2, El * F * d); p += E * F * d;
     }
     cp(p, src + o_final, d); p += d;
     cp(p, src + o_lm, V * d);
@@ -127,8 +133,10 @@ void MoeTrainer::alloc() {
         add(cap * 2 * F * e); add(cap * F * e); add(cap * d * e);
         add(T * K * 4); add(E * 4); add((E + 1) * 4); add(T * K * 4); add(cap * 4);
         if (dt == CATNN_BF16) add(T * d * 4);
+        if (ep) { add(world * E * 4); add(ep_plan_len(E, El) * 4); add(T * K * 4); }
     }
-    add(T * d * 4); add(T * d * e); add((size_t)T * V * e); add(T * 4); add(T * 4); add(64);
+    if (ep) add(T * K * 4);
+    add(T * d * 4); add(T * d * e); add((size_t)T * V * e); add(Tg * 4); add(T * 4); add(64);
     add(T * d * 4); add(T * d * 4); add(T * d * 4); add(T * E * 4); add(T * K * 4);
     add(T * d * e); add(cap * d * e); add(cap * F * e); add(cap * 2 * F * e); add(cap * d * e); add(T * qkvd * e);
     add(T * qd * e); add(T * d * e); add(T * E * e); add(T * d * e);
@@ -159,11 +167,17 @@ void MoeTrainer::alloc() {
         a.row_of = ac.take<int32_t>(T * K);
         a.src_of = ac.take<int32_t>(cap);
         a.xm32 = dt == CATNN_BF16 ? ac.take<float>(T * d) : (float*)a.xm;
+        if (ep) {
+            a.cnt_all = ac.take<int32_t>(world * E);
+            a.plan = ac.take<int32_t>(ep_plan_len(E, El));
+            a.dest = ac.take<int32_t>(T * K);
+        }
     }
+    if (ep) src1 = ac.take<int32_t>(T * K);
     x_last = ac.take<float>(T * d);
     xf = ac.take<char>(T * d * e);
     lg = ac.take<char>((size_t)T * V * e);
-    tokens = ac.take<uint32_t>(T);
+    tokens = ac.take<uint32_t>(Tg);
     targets = ac.take<uint32_t>(T);
     loss = ac.take<float>(16);
     dx = ac.take<float>(T * d);
@@ -181,11 +195,43 @@ void MoeTrainer::alloc() {
     dxn = ac.take<char>(T * d * e);
     dlog_lp = ac.take<char>(T * E * e);
     dxf = ac.take<char>(T * d * e);
-    CUDA_OK(cudaMallocHost(&h_tokens, T * 4));
+    CUDA_OK(cudaMallocHost(&h_tokens, Tg * 4));
     CUDA_OK(cudaMallocHost(&h_loss, 64));
+    act_bytes = tot;
+    if (ep) {
+        // every buffer a peer reads or writes lives in act_block: map it once
+        CUDA_OK(cudaMemsetAsync(act_block, 0, tot, c->stream));
+        CUDA_OK(cudaStreamSynchronize(c->stream));
+        comm->map(act_block, tot);
+        map_id = (int)comm->maps.size() - 1;
+    }
+}
+
+template <typename Q>
+PeerTab MoeTrainer::tab(Q* local) const {
+    PeerTab t{};
+    for (int p = 0; p < world; ++p) t.p[p] = (void*)comm->at(comm->maps[map_id], p, (char*)local);
+    return t;
 }
 
 void MoeTrainer::release() {
+    if (ep && map_id >= 0 && comm) {
+        // close this rank's mappings of the peers' arenas; only when every
+        // rank has done so may any rank free its own (collective)
+        cudaStreamSynchronize(c->stream);
+        Comm::Mapped& m = comm->maps[map_id];
+        for (int p = 0; p < world; ++p)
+            if (p != rank && m.base[p]) {
+                cudaIpcCloseMemHandle(m.base[p]);
+                m.base[p] = nullptr;
+            }
+        try {
+            comm->barrier();
+        } catch (...) {
+        }
+        cudaStreamSynchronize(c->stream);
+        map_id = -1;
+    }
     if (param_block) cudaFree(param_block);
     if (act_block) cudaFree(act_block);
     if (h_tokens) cudaFreeHost(h_tokens);
@@ -195,10 +241,12 @@ void MoeTrainer::release() {
     h_loss = nullptr;
 }
 
-// train.rs:274-275: targets[i] = tokens[(i+1) % n] % vocab.
-__global__ void k_next_token(const uint32_t* __restrict__ tok, uint32_t* __restrict__ tg, i64 n, i64 vocab) {
+// train.rs:274-275: targets[i] = tokens[(i+1) % n] % vocab over the global
+// token array (n tokens); this rank's targets are those of tokens off .. off+m-1.
+__global__ void k_next_token(const uint32_t* __restrict__ tok, uint32_t* __restrict__ tg, i64 off, i64 m, i64 n,
+                             i64 vocab) {
     i64 i = blockIdx.x * (i64)blockDim.x + threadIdx.x;
-    if (i < n) tg[i] = tok[(i + 1) % n] % (uint32_t)vocab;
+    if (i < m) tg[i] = tok[(off + i + 1) % n] % (uint32_t)vocab;
 }
 
 // Expert GEMM over the sorted rows (bf16: tcgen05 grouped; fp32: CUDA cores).
@@ -225,9 +273,9 @@ static void expert_wgrad(Context* c, int dt, i64 rows, i64 N, i64 Kd, int E, con
 
 void MoeTrainer::forward() {
     int* err = c->status + 10;
-    k_next_token<<<cdiv(T, 256), 256, 0, c->stream>>>(tokens, targets, T, V);
+    k_next_token<<<cdiv(T, 256), 256, 0, c->stream>>>(tokens, targets, tok_off, T, Tg, V);
     launched(c);
-    embedding_fwd(c, tokens, T, P + o_embed, V, d, acts[0].x_in, CATNN_F32, err);
+    embedding_fwd(c, tokens + tok_off, T, P + o_embed, V, d, acts[0].x_in, CATNN_F32, err);
     const int align = dt == CATNN_BF16 ? 128 : 1;
     for (i64 l = 0; l < L; ++l) {
         Act& a = acts[l];
@@ -251,17 +299,37 @@ void MoeTrainer::forward() {
         if (dt == CATNN_BF16) rmsnorm_fwd_mixed(c, a.x_mid, CATNN_F32, P + q.rms_moe, a.xm32, CATNN_F32, T, d, eps);
         gemm(c, false, false, T, E, d, a.xm32, d, P + q.gate, E, a.logits, E, CATNN_F32, CATNN_F32, nullptr, 0, false);
         router_topk(c, a.logits, T, E, K, a.idx, a.w);
-        permute_map(c, a.idx, T, E, K, align, cap, a.counts, a.off, a.row_of, a.src_of);
-        permute_rows(c, a.xm, a.src_of, cap, d, K, a.xp, dt);
-        expert_gemm(c, dt, false, cap, 2 * F, d, (int)E, a.off, a.xp, d, W(q.w13), a.ac, 2 * F, dt);
-        swiglu_act(c, a.ac, (char*)a.ac + F * e, a.h, cap, F, 2 * F, F, dt);
-        expert_gemm(c, dt, false, cap, d, F, (int)E, a.off, a.h, F, W(q.w2), a.yp, d, dt);
-        unpermute_rows(c, a.yp, a.row_of, a.w, T, K, d, x_out, CATNN_F32, false, dt, a.x_mid);
+        if (!ep) {
+            permute_map(c, a.idx, T, E, K, align, cap, a.counts, a.off, a.row_of, a.src_of);
+            permute_rows(c, a.xm, a.src_of, cap, d, K, a.xp, dt);
+            expert_gemm(c, dt, false, cap, 2 * F, d, (int)E, a.off, a.xp, d, W(q.w13), a.ac, 2 * F, dt);
+            swiglu_act(c, a.ac, (char*)a.ac + F * e, a.h, cap, F, 2 * F, F, dt);
+            expert_gemm(c, dt, false, cap, d, F, (int)E, a.off, a.h, F, W(q.w2), a.yp, d, dt);
+            unpermute_rows(c, a.yp, a.row_of, a.w, T, K, d, x_out, CATNN_F32, false, dt, a.x_mid);
+        } else {
+            // local counts and within-expert ranks (align 1), published to every rank
+            permute_map(c, a.idx, T, E, K, 1, T * K, a.counts, a.off, a.row_of, src1);
+            ep_publish_counts(c, a.counts, tab(a.cnt_all), rank, world, (int)E);
+            comm->barrier();
+            ep_plan(c, a.cnt_all, rank, world, (int)E, (int)El, align, a.plan, cap);
+            // rows straight into the owners' receive buffers
+            ep_dispatch(c, a.xm, a.idx, a.row_of, a.off, a.plan, tab(a.xp), tab(a.src_of), a.dest, T, (int)K, d,
+                        (int)El, align, rank, world, cap, dt);
+            comm->barrier();
+            expert_gemm(c, dt, false, cap, 2 * F, d, (int)El, a.plan, a.xp, d, W(q.w13), a.ac, 2 * F, dt);
+            swiglu_act(c, a.ac, (char*)a.ac + F * e, a.h, cap, F, 2 * F, F, dt, -1, a.plan + El);
+            expert_gemm(c, dt, false, cap, d, F, (int)El, a.plan, a.h, F, W(q.w2), a.yp, d, dt);
+            comm->barrier();
+            // weighted sum read from the owners' expert outputs
+            ep_combine(c, tab(a.yp), a.idx, a.dest, a.w, T, (int)K, d, (int)El, world, cap, x_out, a.x_mid, dt);
+        }
     }
     // final norm, LM head, fused cross-entropy (dlogits overwrite logits)
     rmsnorm_fwd_mixed(c, x_last, CATNN_F32, P + o_final, xf, dt, T, d, eps);
     gemm(c, false, true, T, V, d, xf, d, W(o_lm), d, lg, V, dt, dt, nullptr, 0, false);
-    xent_fwdbwd(c, lg, targets, T, V, loss, lg, dt, c->status + 9);
+    // mean over the GLOBAL token count: the ranks' gradients then sum to the
+    // one-GPU gradient, and so do their losses
+    xent_fwdbwd(c, lg, targets, T, V, loss, lg, dt, c->status + 9, Tg);
 }
 
 void MoeTrainer::backward() {
@@ -276,13 +344,27 @@ void MoeTrainer::backward() {
         char* qkv = (char*)a.qkv;
         char* dq = (char*)dqkv;
         // MoE adjoint (adjoint.rs:471-526), batched by expert
-        unpermute_bwd(c, a.yp, a.src_of, cap, a.w, dx, K, d, dwts, dyp, dt, dt, CATNN_F32);
-        expert_gemm(c, dt, true, cap, F, d, (int)E, a.off, dyp, d, W(q.w2), dh, F, dt);
-        expert_wgrad(c, dt, cap, d, F, (int)E, a.off, a.h, F, dyp, d, G + q.w2);
-        swiglu_act_bwd(c, a.ac, (char*)a.ac + F * e, dh, dac, (char*)dac + F * e, cap, F, 2 * F, 2 * F, dt);
-        expert_gemm(c, dt, true, cap, d, 2 * F, (int)E, a.off, dac, 2 * F, W(q.w13), dxp, d, dt);
-        expert_wgrad(c, dt, cap, 2 * F, d, (int)E, a.off, a.xp, d, dac, 2 * F, G + q.w13);
-        permute_bwd(c, dxp, a.row_of, T, K, d, dxm, dt, false, CATNN_F32);
+        const int ng = ep ? (int)El : (int)E;
+        const int32_t* goff = ep ? a.plan : a.off;
+        if (!ep) {
+            unpermute_bwd(c, a.yp, a.src_of, cap, a.w, dx, K, d, dwts, dyp, dt, dt, CATNN_F32);
+        } else {
+            comm->barrier();  // every rank's dx for this layer is final
+            ep_unpermute_bwd(c, a.yp, a.src_of, a.plan, tab(a.w), tab(dx), tab(dwts), cap, T * K, (int)K, d, (int)El,
+                             world, dyp, dt);
+        }
+        expert_gemm(c, dt, true, cap, F, d, ng, goff, dyp, d, W(q.w2), dh, F, dt);
+        expert_wgrad(c, dt, cap, d, F, ng, goff, a.h, F, dyp, d, G + q.w2);
+        swiglu_act_bwd(c, a.ac, (char*)a.ac + F * e, dh, dac, (char*)dac + F * e, cap, F, 2 * F, 2 * F, dt, -1,
+                       ep ? a.plan + El : nullptr);
+        expert_gemm(c, dt, true, cap, d, 2 * F, ng, goff, dac, 2 * F, W(q.w13), dxp, d, dt);
+        expert_wgrad(c, dt, cap, 2 * F, d, ng, goff, a.xp, d, dac, 2 * F, G + q.w13);
+        if (!ep) {
+            permute_bwd(c, dxp, a.row_of, T, K, d, dxm, dt, false, CATNN_F32);
+        } else {
+            comm->barrier();  // owners' dxp rows and the dwts they wrote are final
+            ep_permute_bwd(c, tab(dxp), a.idx, a.dest, T, (int)K, d, (int)El, world, cap, dxm, dt);
+        }
         // router straight-through adjoint (adjoint.rs:255-284)
         router_ste(c, a.idx, a.w, dwts, T, E, K, dlog);
         gemm(c, false, true, T, d, E, dlog, E, P + q.gate, E, dxm, d, CATNN_F32, CATNN_F32, nullptr, 0, true);
@@ -301,7 +383,7 @@ void MoeTrainer::backward() {
         // residual around attention: dx_in = dx_mid + rmsnorm'(dxn)   (train.rs:348-351)
         rmsnorm_bwd_mixed(c, a.x_in, P + q.rms_attn, dxn, dt, dxmid, dx, nullptr, dt, G + q.rms_attn, false, T, d, eps);
     }
-    embedding_bwd(c, tokens, T, dx, G + o_embed, V, d, CATNN_F32);
+    embedding_bwd(c, tokens + tok_off, T, dx, G + o_embed, V, d, CATNN_F32);
 }
 
 void MoeTrainer::update() {
@@ -315,9 +397,17 @@ void MoeTrainer::update() {
 }
 
 void MoeTrainer::step(const uint32_t* tokens_dev, float* loss_dev, bool upd) {
-    if (tokens_dev != tokens) CUDA_OK(cudaMemcpyAsync(tokens, tokens_dev, T * 4, cudaMemcpyDeviceToDevice, c->stream));
+    if (tokens_dev != tokens) CUDA_OK(cudaMemcpyAsync(tokens, tokens_dev, Tg * 4, cudaMemcpyDeviceToDevice, c->stream));
     forward();
     backward();
+    if (ep) {
+        // replicated gradients and the loss (parked in the gradient slot
+        // o_loss) summed over ranks in one NCCL allreduce; expert gradients
+        // are already complete on their owners
+        CUDA_OK(cudaMemcpyAsync(G + o_loss, loss, 4, cudaMemcpyDeviceToDevice, c->stream));
+        comm->allreduce_sum(G, n_rep, CATNN_F32);
+        CUDA_OK(cudaMemcpyAsync(loss, G + o_loss, 4, cudaMemcpyDeviceToDevice, c->stream));
+    }
     if (upd) update();
     if (loss_dev && loss_dev != loss) CUDA_OK(cudaMemcpyAsync(loss_dev, loss, 4, cudaMemcpyDeviceToDevice, c->stream));
 }
@@ -338,8 +428,11 @@ MoeTrainer& tr(catnn_moe_trainer* h) {
     return h->t;
 }
 
-void configure(MoeTrainer& t, const catnn_moe_config* cf) {
+void configure(MoeTrainer& t, const catnn_moe_config* cf, int rank = 0, int world = 1) {
     CATNN_CHECK(cf != nullptr, CATNN_ERR_INVALID, "null config");
+    t.rank = rank;
+    t.world = world;
+    t.ep = world > 1;
     t.V = cf->vocab;
     t.d = cf->hidden;
     t.F = cf->mid;
@@ -367,12 +460,25 @@ void configure(MoeTrainer& t, const catnn_moe_config* cf) {
     CATNN_CHECK(t.opt == 0 || t.opt == 1, CATNN_ERR_INVALID, "optimizer: 0 = SGD, 1 = Adam");
     t.hd = t.d / t.H;
     CATNN_CHECK(t.hd % 2 == 0 && t.hd <= 128, CATNN_ERR_SHAPE, "head_dim must be even and <= 128");
+    CATNN_CHECK(t.B % world == 0, CATNN_ERR_SHAPE,
+                "expert parallel: batch " + std::to_string(t.B) + " not divisible by " + std::to_string(world) + " ranks");
+    CATNN_CHECK(t.E % world == 0, CATNN_ERR_SHAPE,
+                "expert parallel: experts " + std::to_string(t.E) + " not divisible by " + std::to_string(world) + " ranks");
+    t.Bg = t.B;
+    t.Tg = t.B * t.S;
+    t.B = t.Bg / world;
     t.T = t.B * t.S;
+    t.tok_off = (i64)rank * t.T;
+    t.El = t.E / world;
+    t.e0 = (i64)rank * t.El;
     t.qd = t.H * t.hd;
     t.kd = t.Hkv * t.hd;
     t.qkvd = t.qd + 2 * t.kd;
     const i64 align = t.dt == CATNN_BF16 ? 128 : 1;
-    t.cap = t.T * t.K + t.E * (align - 1);
+    // worst case: every pair of the global batch that can reach this rank's
+    // experts (a token's top-k experts are distinct) does, plus padding
+    t.cap = t.Tg * std::min(t.K, t.El) + t.El * (align - 1);
+    CATNN_CHECK(t.Tg * t.K < (1ll << 31), CATNN_ERR_SHAPE, "too many (token, slot) pairs");
     if (t.dt == CATNN_BF16)
         CATNN_CHECK(t.d % 64 == 0 && t.F % 64 == 0, CATNN_ERR_SHAPE, "bf16 path: hidden and mid must be multiples of 64");
 }
@@ -389,6 +495,28 @@ int catnn_moe_trainer_create(catnn_ctx* h, const catnn_moe_config* cf, catnn_moe
     try {
         t->t.c = c;
         configure(t->t, cf);
+        t->t.plan_params();
+        t->t.alloc();
+    } catch (...) {
+        t->t.release();
+        delete t;
+        throw;
+    }
+    *out = t;
+    ABI_END
+}
+
+int catnn_moe_trainer_create_ep(catnn_ctx* h, const catnn_moe_config* cf, catnn_comm* cm, catnn_moe_trainer** out) {
+    ABI_BEGIN
+    Context* c = unwrap(h);
+    CATNN_CHECK(out != nullptr, CATNN_ERR_INVALID, "null out");
+    Comm* comm = comm_of(cm);
+    CATNN_CHECK(comm->c == c, CATNN_ERR_INVALID, "trainer and communicator must share the context");
+    catnn_moe_trainer* t = new catnn_moe_trainer();
+    try {
+        t->t.c = c;
+        t->t.comm = comm;
+        configure(t->t, cf, comm->rank, comm->world);
         t->t.plan_params();
         t->t.alloc();
     } catch (...) {
@@ -462,8 +590,8 @@ int catnn_moe_trainer_step_host(catnn_moe_trainer* h, const uint32_t* tokens_hos
     MoeTrainer& t = tr(h);
     CATNN_CHECK(tokens_host != nullptr && loss_host != nullptr, CATNN_ERR_INVALID, "null tokens/loss");
     // host -> pinned staging -> device, step, loss back to the host
-    std::memcpy(t.h_tokens, tokens_host, t.T * 4);
-    CUDA_OK(cudaMemcpyAsync(t.tokens, t.h_tokens, t.T * 4, cudaMemcpyHostToDevice, t.c->stream));
+    std::memcpy(t.h_tokens, tokens_host, t.Tg * 4);
+    CUDA_OK(cudaMemcpyAsync(t.tokens, t.h_tokens, t.Tg * 4, cudaMemcpyHostToDevice, t.c->stream));
     t.step(t.tokens, nullptr, update != 0);
     CUDA_OK(cudaMemcpyAsync(t.h_loss, t.loss, 4, cudaMemcpyDeviceToHost, t.c->stream));
     CUDA_OK(cudaStreamSynchronize(t.c->stream));
@@ -502,6 +630,12 @@ int catnn_moe_trainer_check(catnn_moe_trainer* h) {
                                                                          : "router produced an invalid expert"));
     }
     if (v[0] || v[1] || v[2] || v[3]) throw Error(CATNN_ERR_TIMEOUT, "a bounded device wait ran out (GEMM pipeline)");
+    if (v[EP_STATUS_SLOT]) throw Error(CATNN_ERR_INVALID, "expert-parallel receive buffer overflow");
+    if (v[COMM_STATUS_SLOT]) {
+        CUDA_OK(cudaMemsetAsync(t.c->status + COMM_STATUS_SLOT, 0, 8, t.c->stream));
+        throw Error(CATNN_ERR_TIMEOUT, "a device wait for another rank ran out (epoch " +
+                                           std::to_string(v[COMM_STATUS_SLOT + 1]) + ")");
+    }
     ABI_END
 }
 

@@ -10,12 +10,19 @@ struct catnn_moe_config;
 
 namespace catnn {
 
-struct Comm;  // expert-parallel communicator (comm.cu); null on one GPU
+struct Comm;     // expert-parallel communicator (comm.cu); null on one GPU
+struct PeerTab;  // moe_ep.cuh
 
 struct MoeTrainer {
     Context* c = nullptr;
     Comm* comm = nullptr;
-    // shapes
+    // group: this rank trains tokens [tok_off, tok_off + T) of the global
+    // batch (Tg tokens) and owns experts [e0, e0 + El)
+    int rank = 0, world = 1;
+    bool ep = false;
+    i64 Bg, Tg, tok_off, El, e0;
+    // shapes (B, T: this rank's sequences and tokens; cap: expert rows this
+    // rank can receive, padding included)
     i64 V, d, F, L, H, Hkv, hd, E, K, window, B, S, T, qd, kd, qkvd, cap;
     float eps;
     double theta;
@@ -30,7 +37,9 @@ struct MoeTrainer {
         i64 rms_attn, wqkv, wo, rms_moe, gate, w13, w2;
     };
     std::vector<LayerOff> lo;
-    i64 o_embed, o_final, o_lm, n_params;
+    // replicated parameters (and the loss slot) come first: [0, n_rep) is
+    // what the gradient allreduce sums; this rank's experts follow
+    i64 o_embed, o_final, o_lm, o_loss, n_rep, n_params;
     float *P = nullptr, *G = nullptr, *Mo = nullptr, *Vo = nullptr;
     void* Sh = nullptr;
     void* param_block = nullptr;
@@ -41,6 +50,9 @@ struct MoeTrainer {
         void *xn, *qkv, *ctx, *xm, *xp, *ac, *h, *yp;
         float* xm32;  // fp32 router input (bf16 path; == xm on the fp32 path)
         int32_t *idx, *counts, *off, *row_of, *src_of;
+        // expert parallel: counts of every rank [world][E], the layer plan
+        // (moe_ep.cuh) and each local pair's row in its owner's buffer
+        int32_t *cnt_all = nullptr, *plan = nullptr, *dest = nullptr;
     };
     std::vector<Act> acts;
     float* x_last = nullptr;
@@ -51,6 +63,11 @@ struct MoeTrainer {
     float *dx, *dxmid, *dxm, *dlog, *dwts;
     void *dxmid_lp, *dyp, *dh, *dac, *dxp, *dqkv, *dctx, *dxn, *dlog_lp, *dxf;
     void* act_block = nullptr;
+    size_t act_bytes = 0;
+    int32_t* src1 = nullptr;  // local align-1 map's row sources (expert parallel)
+    int map_id = -1;          // act_block's entry in comm->maps
+    template <typename Q>
+    PeerTab tab(Q* local) const;
     // host staging for the host-buffer step
     uint32_t* h_tokens = nullptr;
     float* h_loss = nullptr;

@@ -318,6 +318,56 @@ int catnn_moe_trainer_activation(catnn_moe_trainer* t, int which, int64_t layer,
  * target out of range, a bounded wait that ran out). */
 int catnn_moe_trainer_check(catnn_moe_trainer* t);
 
+/* ------------------------------------------------------------ multi-GPU (one node) */
+/* One rank of a group of 1..8 processes, one GPU each. The reference runs
+ * one device handler per device and moves tensors between them on the host
+ * (crates/catnn-rt/src/dist.rs:441-517, transfer.rs); it models expert
+ * parallelism as E/EP experts per rank with an activation all-to-all
+ * (crates/catnn-compile/src/spark_place.rs:119-131,196). Here NCCL carries
+ * the bulk collectives and CUDA IPC peer mappings over NVLink carry the
+ * fused expert dispatch/combine. Device waits are bounded (default 10 s,
+ * catnn_comm_set_timeout_ms); a wait that runs out makes the next
+ * catnn_comm_check / catnn_moe_trainer_check return CATNN_ERR_TIMEOUT. */
+typedef struct catnn_comm catnn_comm;
+#define CATNN_COMM_ID_BYTES 128
+/* Rank 0 creates the group id (CATNN_COMM_ID_BYTES bytes) and sends it to
+ * every rank over any host channel. */
+int catnn_comm_unique_id(void* id_out);
+/* Collective over all ranks. world == 1 needs no id (id may be NULL). */
+int catnn_comm_create(catnn_ctx* ctx, int rank, int world, const void* id, catnn_comm** out);
+int catnn_comm_destroy(catnn_comm* comm);
+int catnn_comm_rank(catnn_comm* comm, int* rank, int* world);
+int catnn_comm_set_timeout_ms(catnn_comm* comm, int64_t ms);
+/* In-place sum over ranks of n elements (CATNN_F32 or CATNN_BF16), on the context stream. */
+int catnn_comm_allreduce(catnn_comm* comm, void* buf, int64_t n, int dtype);
+/* Bytes send[off_p .. off_p + send_bytes[p]) go to rank p, which receives
+ * them at recv + (sum of recv_bytes before this rank); counts are host arrays of world entries. */
+int catnn_comm_all_to_all(catnn_comm* comm, const void* send, const int64_t* send_bytes, void* recv,
+                          const int64_t* recv_bytes);
+/* Device barrier on peer flags (bounded waits). */
+int catnn_comm_barrier(catnn_comm* comm);
+/* Point-to-point flag primitives under the barrier: signal sets this
+ * rank's flag at `peer` to epoch (synchronous); wait enqueues a bounded wait
+ * until peer's flag at this rank reaches epoch. For diagnostics and tests. */
+int catnn_comm_signal(catnn_comm* comm, int peer, uint64_t epoch);
+int catnn_comm_wait(catnn_comm* comm, int peer, uint64_t epoch);
+/* Synchronizes; CATNN_ERR_TIMEOUT if a device wait gave up (and clears it). */
+int catnn_comm_check(catnn_comm* comm);
+
+/* Data-parallel + expert-parallel trainer over the ranks of comm.
+ * cfg->batch is the GLOBAL batch: rank r trains sequences
+ * [r*batch/world, (r+1)*batch/world) and owns experts
+ * [r*experts/world, (r+1)*experts/world) of every layer; all other
+ * parameters are replicated and their gradients summed over ranks (NCCL).
+ * Needs batch % world == 0 and experts % world == 0. Steps take the GLOBAL
+ * token array [batch*seq] on every rank and report the global mean loss;
+ * set_params reads the full packed vector; get_params / get_grads write the
+ * replicated parameters and this rank's experts into a full packed vector
+ * and leave the other experts' entries untouched. activation() returns this
+ * rank's rows. With world == 1 it is the single-GPU trainer. */
+int catnn_moe_trainer_create_ep(catnn_ctx* ctx, const catnn_moe_config* cfg, catnn_comm* comm,
+                                catnn_moe_trainer** out);
+
 #ifdef __cplusplus
 }
 #endif

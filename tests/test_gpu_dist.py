@@ -1,0 +1,158 @@
+"""The communicator and the data-parallel + expert-parallel trainer on GPUs.
+
+One GPU: the communicator's barrier, its bounded wait (a flag that nothing
+sets runs out and comes back as DeviceTimeout, the context staying usable),
+the degenerate collectives, and an expert-parallel trainer over a one-rank
+group that must equal the single-GPU trainer bit for bit.
+
+Two GPUs (skipped with fewer): ranks run tests/ep_worker.py under torchrun;
+their loss, gradients (replicated ones from every rank, expert ones from
+each owner) and parameters after two update steps (SGD on the fp32 path,
+Adam on the bf16 path) are compared with the
+single-GPU trainer on the same global batch. The fp32 path must agree to
+rtol 1e-5 (the gradient sums run in another order across ranks); the bf16
+path to the bf16 band (rel-L2 <= 2e-2)."""
+import os
+import subprocess
+import sys
+
+import numpy as np
+import pytest
+import torch
+
+from gpu_util import close_f32, rel_l2
+
+pytestmark = pytest.mark.gpu
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _lib():
+    import catnn_b200
+    catnn_b200.load()
+
+
+from catnn_b200 import dist as D  # noqa: E402
+from catnn_b200.errors import DeviceTimeout  # noqa: E402
+from catnn_b200.train import MoeTrainer, init_params  # noqa: E402
+
+sys.path.insert(0, HERE)
+import ep_worker as W  # noqa: E402
+
+
+def test_comm_one_rank_barrier_and_bounded_wait():
+    comm = D.Comm(0, 1, 0)
+    comm.barrier()
+    comm.check()
+    comm.signal(0, 1000)
+    comm.wait(0, 1000)
+    comm.check()
+    comm.set_timeout_ms(200)
+    comm.wait(0, 1001)  # nothing ever sets epoch 1001: the wait gives up
+    with pytest.raises(DeviceTimeout):
+        comm.check()
+    comm.check()  # the status was cleared; the context still works
+    x = torch.arange(8, dtype=torch.float32, device="cuda")
+    comm.allreduce(x)
+    recv = torch.empty_like(x)
+    comm.all_to_all(x, [32], recv, [32])
+    torch.cuda.synchronize()
+    assert torch.equal(recv, torch.arange(8, dtype=torch.float32, device="cuda"))
+    comm.close()
+
+
+@pytest.mark.parametrize("name", ["f32", "bf16"])
+def test_ep_trainer_one_rank_equals_single_gpu(name):
+    cfg = W.config(name)
+    P = init_params(cfg, seed=3)
+    tok = torch.as_tensor(W.tokens(cfg).astype(np.int32)).cuda()
+    a = MoeTrainer(cfg, 0)
+    a.set_params(P)
+    comm = D.Comm(0, 1, 0)
+    b = MoeTrainer(cfg, 0, comm=comm)
+    b.set_params(P)
+    la, lb = torch.zeros(1, device="cuda"), torch.zeros(1, device="cuda")
+    for upd in (False, True, True):
+        a.step(tok, update=upd, loss_out=la)
+        b.step(tok, update=upd, loss_out=lb)
+        assert torch.equal(la, lb)
+    assert torch.equal(a.params(), b.params())
+    assert torch.equal(a.grads(), b.grads())
+    a.close()
+    b.close()
+    comm.close()
+
+
+def _single(name, steps=2):
+    cfg = W.config(name)
+    tr = MoeTrainer(cfg, 0)
+    tr.set_params(init_params(cfg, seed=3))
+    tok = torch.as_tensor(W.tokens(cfg).astype(np.int32)).cuda()
+    loss = torch.zeros(1, device="cuda")
+    tr.step(tok, update=False, loss_out=loss)
+    out = {"loss0": loss.cpu().numpy(), "grads0": tr.grads().cpu().numpy()}
+    losses = []
+    for _ in range(steps):
+        tr.step(tok, update=True, loss_out=loss)
+        losses.append(float(loss.item()))
+    out["losses"] = np.array(losses, np.float32)
+    out["params"] = tr.params().cpu().numpy()
+    out["x_last"] = tr.activation("x_last").cpu().numpy()
+    tr.close()
+    return cfg, out
+
+
+def _expert_mask(cfg, world, rank):
+    """Entries of the packed vector that hold rank's experts."""
+    from catnn_b200.train import packed_layout
+    L = packed_layout(cfg)
+    E, h, F = cfg.experts, cfg.hidden, cfg.mid
+    El = E // world
+    m = np.zeros(L["total"], bool)
+    for l in range(cfg.layers):
+        base = L["layer0"] + l * L["layer_stride"]
+        for name, per in (("w1", h * F), ("w3", h * F), ("w2", F * h)):
+            o = base + L[name] + rank * El * per
+            m[o:o + El * per] = True
+    return m
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+@pytest.mark.parametrize("name", ["f32", "bf16"])
+def test_ep_two_ranks_match_single_gpu(name, tmp_path):
+    world = 2
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", f"--nproc-per-node={world}",
+           "--master-addr=127.0.0.1", "--master-port=29541", os.path.join(HERE, "ep_worker.py"), "--config", name,
+           "--out", str(tmp_path)]
+    r = subprocess.run(cmd, env=env, capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
+    cfg, ref = _single(name)
+    ranks = [dict(np.load(tmp_path / f"rank{q}.npz")) for q in range(world)]
+    masks = [_expert_mask(cfg, world, q) for q in range(world)]
+    anyexp = np.any(masks, axis=0)
+
+    def merged(key):
+        v = ranks[0][key].copy()
+        # replicated entries agree bit for bit across ranks (same allreduce result, same update)
+        for q in range(1, world):
+            assert np.array_equal(ranks[q][key][~anyexp], v[~anyexp]), key
+        for q in range(world):
+            v[masks[q]] = ranks[q][key][masks[q]]
+        return v
+
+    g, p = merged("grads0"), merged("params")
+    x_last = np.concatenate([ranks[q]["x_last"] for q in range(world)])
+    if name == "f32":
+        close_f32(ranks[0]["loss0"], ref["loss0"], what="loss")
+        close_f32(ranks[0]["losses"], ref["losses"], what="losses after SGD steps")
+        gscale = float(np.abs(ref["grads0"]).max())
+        close_f32(g, ref["grads0"], floor=1e-4, scale=gscale, what="gradients")
+        close_f32(p, ref["params"], floor=1e-4, what="parameters after 2 SGD steps")
+        close_f32(x_last, ref["x_last"], what="final residual")
+    else:
+        assert abs(float(ranks[0]["loss0"][0]) - float(ref["loss0"][0])) <= 2e-2 * abs(float(ref["loss0"][0]))
+        assert rel_l2(g, ref["grads0"]) <= 2e-2
+        assert rel_l2(p, ref["params"]) <= 2e-2
+        assert rel_l2(x_last, ref["x_last"]) <= 2e-2
