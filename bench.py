@@ -99,12 +99,20 @@ class Clocks:
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
-def traffic_from_profile():
-    """DRAM bytes per launch of the dominant kernel from the committed ncu
-    summary (profiles/gemm_grouped_w13.json), scaled to this launch."""
+def gemm_bytes(rows, E, F, d):
+    """Algorithmic bytes of one grouped W13 launch: A [rows, d], B [E, d, 2F], C [rows, 2F], bf16."""
+    return 2 * (rows * d + E * d * 2 * F + rows * 2 * F)
+
+
+def traffic_from_profile(rows, E, F, d):
+    """DRAM bytes per launch of the dominant kernel: the committed ncu
+    capture at the one-GPU shape (profiles/gemm_grouped_w13.json), scaled by
+    this launch's algorithmic bytes over the captured launch's (traffic
+    grows with the rows and the local experts)."""
     try:
         j = json.load(open(os.path.join(ROOT, "profiles", "gemm_grouped_w13.json")))
-        return j.get("dram_bytes_per_launch_full_size")
+        full = j["dram_bytes_per_launch_full_size"]
+        return int(full * gemm_bytes(rows, E, F, d) / j["algorithmic_bytes_per_launch"])
     except Exception:
         return None
 
@@ -297,7 +305,8 @@ def run_ours(args):
         "roofline": {"bound": "tensor", "kernel": "k_gemm_tc grouped (expert W13 forward, rows=%d, N=%d, K=%d)"
                      % (rows, 2 * F, d), "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                      "frac": achieved / peak, "peak_source": f"{pk_kind} bf16_tflops (burst, kernel timed alone)",
-                     "traffic": traffic_from_profile(), "launch_ms": kms},
+                     "traffic": traffic_from_profile(rows, cfg["experts"] // world, F, d),
+                     "algorithmic_bytes": gemm_bytes(rows, cfg["experts"] // world, F, d), "launch_ms": kms},
         "clocks": clk,
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:

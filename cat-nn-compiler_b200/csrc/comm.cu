@@ -197,8 +197,35 @@ void Comm::allreduce_sum(void* buf, i64 n, int dtype) {
     NCCL_OK(fn, fn->allReduce(buf, buf, (size_t)n, nccl_type(dtype), ncclSum, nc(*this), c->stream));
 }
 
+void Comm::allreduce_overlapped(float* buf, i64 n) {
+    if (world == 1 || n <= 0) return;
+    if (!side) {
+        int lo = 0, hi = 0;
+        CUDA_OK(cudaDeviceGetStreamPriorityRange(&lo, &hi));
+        CUDA_OK(cudaStreamCreateWithPriority(&side, cudaStreamNonBlocking, hi));
+        CUDA_OK(cudaEventCreateWithFlags(&ev_ready, cudaEventDisableTiming));
+        CUDA_OK(cudaEventCreateWithFlags(&ev_done, cudaEventDisableTiming));
+    }
+    CUDA_OK(cudaEventRecord(ev_ready, c->stream));
+    CUDA_OK(cudaStreamWaitEvent(side, ev_ready, 0));
+    NCCL_OK(fn, fn->allReduce(buf, buf, (size_t)n, ncclFloat32, ncclSum, nc(*this), side));
+}
+
+void Comm::join_overlapped() {
+    if (!side) return;
+    CUDA_OK(cudaEventRecord(ev_done, side));
+    CUDA_OK(cudaStreamWaitEvent(c->stream, ev_done, 0));
+}
+
 void Comm::release() {
     if (c) cudaStreamSynchronize(c->stream);
+    if (side) {
+        cudaStreamSynchronize(side);
+        cudaEventDestroy(ev_ready);
+        cudaEventDestroy(ev_done);
+        cudaStreamDestroy(side);
+        side = nullptr;
+    }
     for (auto& m : maps)
         for (int p = 0; p < world; ++p)
             if (p != rank && m.base[p]) cudaIpcCloseMemHandle(m.base[p]);

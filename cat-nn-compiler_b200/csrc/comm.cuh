@@ -51,6 +51,13 @@ struct Comm {
     // for all signals of this epoch. Enqueued on the context stream.
     void barrier();
     void allreduce_sum(void* buf, i64 n, int dtype);
+    // fp32 sum of n elements on the communication stream, after the work
+    // enqueued so far on the context stream; join_overlapped makes the
+    // context stream wait for every such allreduce.
+    void allreduce_overlapped(float* buf, i64 n);
+    void join_overlapped();
+    cudaStream_t side = nullptr;
+    cudaEvent_t ev_ready = nullptr, ev_done = nullptr;
     void release();
 };
 

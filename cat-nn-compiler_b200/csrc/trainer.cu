@@ -338,6 +338,12 @@ void MoeTrainer::backward() {
     gemm(c, false, false, T, d, V, lg, V, W(o_lm), d, dxf, d, dt, dt, nullptr, 0, false);
     gemm(c, true, false, V, d, T, lg, V, xf, d, G + o_lm, d, dt, CATNN_F32, nullptr, 0, false);
     rmsnorm_bwd_mixed(c, x_last, P + o_final, dxf, dt, nullptr, dx, nullptr, dt, G + o_final, false, T, d, eps);
+    if (ep) {
+        // the loss rides in the gradient slot o_loss; final norm, LM head and
+        // loss are summed over ranks while the layers' adjoints run
+        CUDA_OK(cudaMemcpyAsync(G + o_loss, loss, 4, cudaMemcpyDeviceToDevice, c->stream));
+        comm->allreduce_overlapped(G + o_final, n_rep - o_final);
+    }
     for (i64 l = L - 1; l >= 0; --l) {
         Act& a = acts[l];
         const LayerOff& q = lo[l];
@@ -382,8 +388,11 @@ void MoeTrainer::backward() {
         gemm(c, true, false, d, qkvd, T, a.xn, d, dqkv, qkvd, G + q.wqkv, qkvd, dt, CATNN_F32, nullptr, 0, false);
         // residual around attention: dx_in = dx_mid + rmsnorm'(dxn)   (train.rs:348-351)
         rmsnorm_bwd_mixed(c, a.x_in, P + q.rms_attn, dxn, dt, dxmid, dx, nullptr, dt, G + q.rms_attn, false, T, d, eps);
+        // this layer's replicated gradients [rms_attn .. gate] are final
+        if (ep) comm->allreduce_overlapped(G + q.rms_attn, q.gate + d * E - q.rms_attn);
     }
     embedding_bwd(c, tokens + tok_off, T, dx, G + o_embed, V, d, CATNN_F32);
+    if (ep) comm->allreduce_overlapped(G + o_embed, V * d);
 }
 
 void MoeTrainer::update() {
@@ -401,11 +410,12 @@ void MoeTrainer::step(const uint32_t* tokens_dev, float* loss_dev, bool upd) {
     forward();
     backward();
     if (ep) {
-        // replicated gradients and the loss (parked in the gradient slot
-        // o_loss) summed over ranks in one NCCL allreduce; expert gradients
-        // are already complete on their owners
-        CUDA_OK(cudaMemcpyAsync(G + o_loss, loss, 4, cudaMemcpyDeviceToDevice, c->stream));
-        comm->allreduce_sum(G, n_rep, CATNN_F32);
+        // replicated gradients and the loss were summed over ranks bucket by
+        // bucket during the backward pass (expert gradients are complete on
+        // their owners); the update waits for the last bucket. That bucket
+        // completes only once every rank has finished its backward pass, so
+        // no rank's next dispatch can overwrite a buffer a peer still reads.
+        comm->join_overlapped();
         CUDA_OK(cudaMemcpyAsync(loss, G + o_loss, 4, cudaMemcpyDeviceToDevice, c->stream));
     }
     if (upd) update();
