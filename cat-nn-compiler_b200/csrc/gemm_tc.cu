@@ -33,18 +33,24 @@ struct TcArgs {
     const float* resid;  // fp32 [M, ldc] added before the activation (C must be fp32)
     int act, accumulate;
     int* status;
+    // split-K: ksplit > 1 cuts each tile's K range into ksplit slices whose
+    // fp32 partial sums go to part[slice] (no epilogue); k_splitk_reduce
+    // then adds the slices in order and applies the epilogue.
+    int ksplit, kchunk;
+    float* part;
+    long long c_group_stride_part;  // elements between two slices of part
 };
 
 static constexpr int BM = 128, BK = 64;
 
 struct TileInfo {
-    int g, m0, n0, kstart, klen, mlimit, arow0;
+    int g, m0, n0, kstart, klen, mlimit, arow0, ks;
 };
 
 // Total tiles and the t-th tile of the static schedule. Groups are few
 // (experts), so a linear scan is cheaper than a device-side prefix sum.
 template <int BN>
-__device__ __forceinline__ int total_tiles(const TcArgs& a) {
+__device__ __forceinline__ int base_tiles(const TcArgs& a) {
     int nt = (a.N + BN - 1) / BN;
     if (a.mode == 0) return ((a.M + BM - 1) / BM) * nt;
     if (a.mode == 2) return a.groups * ((a.M + BM - 1) / BM) * nt;
@@ -52,10 +58,36 @@ __device__ __forceinline__ int total_tiles(const TcArgs& a) {
     for (int g = 0; g < a.groups; ++g) tot += ((a.offsets[g + 1] - a.offsets[g] + BM - 1) / BM) * nt;
     return tot;
 }
+template <int BN>
+__device__ __forceinline__ int total_tiles(const TcArgs& a) {
+    return base_tiles<BN>(a) * a.ksplit;
+}
 
 template <int BN>
+__device__ __forceinline__ TileInfo tile_at_base(const TcArgs& a, int t);
+
+// Tile t of the schedule: the K slice is the slowest index, so the tiles
+// running at the same time share their operands' K slice in L2.
+template <int BN>
 __device__ __forceinline__ TileInfo tile_at(const TcArgs& a, int t) {
+    if (a.ksplit <= 1) return tile_at_base<BN>(a, t);
+    int nb = base_tiles<BN>(a);
+    int ks = t / nb;
+    TileInfo ti = tile_at_base<BN>(a, t - ks * nb);
+    // mode 2 cuts each group's own row range; modes 0 and 1 share one chunk
+    int chunk = a.mode == 2 ? ((ti.klen + a.ksplit - 1) / a.ksplit + BK - 1) / BK * BK : a.kchunk;
+    int k0 = ks * chunk;
+    int len = ti.klen - k0;
+    ti.kstart += k0;
+    ti.klen = len < 0 ? 0 : (len < chunk ? len : chunk);
+    ti.ks = ks;
+    return ti;
+}
+
+template <int BN>
+__device__ __forceinline__ TileInfo tile_at_base(const TcArgs& a, int t) {
     TileInfo ti;
+    ti.ks = 0;
     int nt = (a.N + BN - 1) / BN;
     if (a.mode == 0) {
         ti.g = 0;
@@ -163,14 +195,14 @@ __global__ void __launch_bounds__(192, 1)
                 tc::mbar_arrive_expect_tx(&full[s], STAGE_BYTES);
                 int k = ti.kstart + kb * BK;
                 if (!A_MN) {
-                    tc::tma_load_2d(sA, &mapA, kb * BK, ti.arow0 + ti.m0, &full[s]);
+                    tc::tma_load_2d(sA, &mapA, k, ti.arow0 + ti.m0, &full[s]);
                 } else {
 #pragma unroll
                     for (int j = 0; j < BM / 64; ++j) tc::tma_load_2d(sA + j * 8192, &mapA, ti.m0 + 64 * j, k, &full[s]);
                 }
                 if (!B_MN) {
                     int brow = (a.mode == 1 ? ti.g * a.b_group_rows : 0) + ti.n0;
-                    tc::tma_load_2d(sB, &mapB, kb * BK, brow, &full[s]);
+                    tc::tma_load_2d(sB, &mapB, k, brow, &full[s]);
                 } else {
                     int brow = (a.mode == 1 ? ti.g * a.b_group_rows : 0) + k;
 #pragma unroll
@@ -249,6 +281,29 @@ __global__ void __launch_bounds__(192, 1)
                 tc::tmem_ld32(tmem_base + ((uint32_t)(q * 32) << 16) + acc * BN + cc * 32, r);
                 tc::tmem_ld_wait();
                 if (!rv) continue;
+                if (a.ksplit > 1) {
+                    // raw fp32 partial of this K slice: part[ks] is [rows, N] with
+                    // rows = M (mode 0), total rows (mode 1), groups·M (mode 2)
+                    long long prow = a.mode == 0 ? row : (a.mode == 1 ? ti.arow0 + row : (long long)ti.g * a.M + row);
+                    float* p = a.part + (long long)ti.ks * a.c_group_stride_part + prow * a.N + col0;
+                    bool vec = (a.N % 4 == 0) && (col0 + 32 <= a.N);
+                    if (vec) {
+#pragma unroll
+                        for (int i4 = 0; i4 < 8; ++i4) {
+                            float4 w;
+                            w.x = ti.klen > 0 ? __uint_as_float(r[i4 * 4 + 0]) : 0.f;
+                            w.y = ti.klen > 0 ? __uint_as_float(r[i4 * 4 + 1]) : 0.f;
+                            w.z = ti.klen > 0 ? __uint_as_float(r[i4 * 4 + 2]) : 0.f;
+                            w.w = ti.klen > 0 ? __uint_as_float(r[i4 * 4 + 3]) : 0.f;
+                            *(float4*)(p + i4 * 4) = w;
+                        }
+                    } else {
+#pragma unroll
+                        for (int i = 0; i < 32; ++i)
+                            if (col0 + i < a.N) p[i] = ti.klen > 0 ? __uint_as_float(r[i]) : 0.f;
+                    }
+                    continue;
+                }
                 float v[32];
 #pragma unroll
                 for (int i = 0; i < 32; ++i) {
@@ -281,7 +336,9 @@ __global__ void __launch_bounds__(192, 1)
                             *(uint4*)(p + i4 * 8) = pk;
                         }
                     } else {
-                        for (int i = 0; i < 32 && col0 + i < a.N; ++i) {
+#pragma unroll
+                        for (int i = 0; i < 32; ++i) {
+                            if (col0 + i >= a.N) continue;
                             float x = v[i];
                             if (a.accumulate) x += __bfloat162float(p[i]);
                             p[i] = __float2bfloat16_rn(act_apply(x, a.act));
@@ -302,7 +359,9 @@ __global__ void __launch_bounds__(192, 1)
                             *(float4*)(p + i4 * 4) = w;
                         }
                     } else {
-                        for (int i = 0; i < 32 && col0 + i < a.N; ++i) {
+#pragma unroll
+                        for (int i = 0; i < 32; ++i) {
+                            if (col0 + i >= a.N) continue;
                             float x = v[i];
                             if (a.accumulate) x += p[i];
                             p[i] = act_apply(x, a.act);
@@ -320,6 +379,43 @@ __global__ void __launch_bounds__(192, 1)
     if (warp == 1) {
         tc::tc_fence_after();
         tc::tmem_dealloc(tmem_base, TMEM_COLS);
+    }
+}
+
+// Split-K epilogue: C = epilogue(Σ_slices part[slice]) with the slices added
+// in order (deterministic), then bias, residual, accumulate and activation
+// as in k_gemm_tc. One thread per element of the partial rows.
+__global__ void k_splitk_reduce(TcArgs a, long long prows) {
+    const long long n = prows * a.N;
+    int lo = 0, hi = 0;
+    if (a.mode == 1) {
+        lo = a.offsets[0];
+        hi = a.offsets[a.groups];
+    }
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
+        long long prow = i / a.N;
+        int col = (int)(i - prow * a.N);
+        if (a.mode == 1 && (prow < lo || prow >= hi)) continue;
+        float v = a.part[i];
+        for (int k = 1; k < a.ksplit; ++k) v += a.part[(long long)k * a.c_group_stride_part + i];
+        long long off;
+        if (a.mode == 2) {
+            long long g = prow / a.M, row = prow - g * a.M;
+            off = g * a.c_group_stride + row * a.ldc + col;
+        } else {
+            off = prow * a.ldc + col;
+        }
+        if (a.bias) v += a.bias[col];
+        if (a.resid) v += a.resid[off];
+        if (a.c_bf16) {
+            bf16* p = (bf16*)a.C + off;
+            if (a.accumulate) v += __bfloat162float(*p);
+            *p = __float2bfloat16_rn(act_apply(v, a.act));
+        } else {
+            float* p = (float*)a.C + off;
+            if (a.accumulate) v += *p;
+            *p = act_apply(v, a.act);
+        }
     }
 }
 
@@ -377,17 +473,61 @@ static void dispatch_tc(Context* c, bool a_mn, bool b_mn, const CUtensorMap& ma,
 
 static bool aligned16(const void* p) { return ((uintptr_t)p & 15) == 0; }
 
+// K slices for a launch of `tiles` output tiles over a K range of klen:
+// only when the tiles leave SMs idle; the count minimises
+// ceil(tiles·s / SMs) / s (time in tile-waves) plus a small charge for the
+// partial sums' round trip. Slices stay multiples of BK.
+static int pick_ksplit(Context* c, i64 tiles, i64 klen, int* kchunk) {
+    *kchunk = 0;
+    if (tiles <= 0 || tiles >= c->sm_count || klen < 4 * BK) return 1;
+    int best = 1;
+    double best_cost = 1.0 * cdiv(tiles, c->sm_count);
+    for (int s = 2; s <= 16 && (i64)s * 2 * BK <= klen; ++s) {
+        double cost = (double)cdiv(tiles * s, c->sm_count) / s + 0.08;
+        if (cost < best_cost - 1e-9) {
+            best_cost = cost;
+            best = s;
+        }
+    }
+    if (best > 1) {
+        i64 ch = cdiv(cdiv(klen, best), BK) * BK;
+        *kchunk = (int)ch;
+        best = (int)cdiv(klen, ch);
+    }
+    return best;
+}
+
 // Builds both maps for op(A) [M(or rows), K] and op(B) [K, N] and launches.
+// part_rows: rows of one split-K partial slice (0: no split-K).
 static void run_tc(Context* c, TcArgs a, bool a_mn, bool b_mn, const bf16* A, i64 a_rows, i64 a_cols, i64 lda,
-                   const bf16* B, i64 b_rows, i64 b_cols, i64 ldb, int grid_bound) {
+                   const bf16* B, i64 b_rows, i64 b_cols, i64 ldb, int grid_bound, i64 base_tiles = 0,
+                   i64 klen = 0, i64 part_rows = 0) {
     const int BN = a.N <= 128 ? 128 : 256;
     CUtensorMap ma = make_map(A, a_rows, a_cols, lda, 64, a_mn ? 64 : BM);
     CUtensorMap mb = make_map(B, b_rows, b_cols, ldb, 64, b_mn ? 64 : BN);
     a.status = c->status;
+    a.ksplit = 1;
+    if (part_rows > 0) {
+        int kchunk = 0;
+        int ks = pick_ksplit(c, base_tiles, klen, &kchunk);
+        if (ks > 1) {
+            a.ksplit = ks;
+            a.kchunk = kchunk;
+            a.c_group_stride_part = part_rows * a.N;
+            a.part = (float*)c->scratch_for((size_t)ks * part_rows * a.N * 4);
+            grid_bound = (int)std::min<i64>((i64)grid_bound * ks, (i64)c->sm_count);
+        }
+    }
     int grid = grid_bound < c->sm_count ? grid_bound : c->sm_count;
     if (grid < 1) grid = 1;
     if (BN == 128) dispatch_tc<128, 6>(c, a_mn, b_mn, ma, mb, a, grid);
     else dispatch_tc<256, 4>(c, a_mn, b_mn, ma, mb, a, grid);
+    if (a.ksplit > 1) {
+        i64 n = part_rows * a.N;
+        int g = (int)std::min<i64>(cdiv(n, 256), (i64)c->sm_count * 8);
+        k_splitk_reduce<<<g, 256, 0, c->stream>>>(a, part_rows);
+        launched(c);
+    }
 }
 
 // Shapes the TMA path accepts: 16-byte aligned bases and row pitches.
@@ -425,7 +565,7 @@ void gemm_bf16_tc(Context* c, bool ta, bool tb, i64 M, i64 N, i64 K, const bf16*
     int tiles = cdiv(M, BM) * cdiv(N, BN);
     // op(A): ta=0 -> A [M,K] K-major; ta=1 -> A [K,M] MN-major.
     // op(B): tb=1 -> B [N,K] K-major; tb=0 -> B [K,N] MN-major.
-    run_tc(c, a, ta, !tb, A, ta ? K : M, ta ? M : K, lda, B, tb ? N : K, tb ? K : N, ldb, tiles);
+    run_tc(c, a, ta, !tb, A, ta ? K : M, ta ? M : K, lda, B, tb ? N : K, tb ? K : N, ldb, tiles, tiles, K, M);
 }
 
 void gemm_grouped_bf16_tc(Context* c, bool tb, i64 total_rows, i64 N, i64 K, int groups, const int32_t* offsets,
@@ -452,7 +592,10 @@ void gemm_grouped_bf16_tc(Context* c, bool tb, i64 total_rows, i64 N, i64 K, int
     a.accumulate = accumulate ? 1 : 0;
     const int BN = N <= 128 ? 128 : 256;
     int bound = (cdiv(total_rows, BM) + groups) * cdiv(N, BN);
-    run_tc(c, a, false, !tb, A, total_rows, K, lda, B, (i64)groups * (tb ? N : K), tb ? K : N, ldb, bound);
+    // the tile count depends on the device offsets: the split is sized for
+    // the host-side bound of the rows
+    run_tc(c, a, false, !tb, A, total_rows, K, lda, B, (i64)groups * (tb ? N : K), tb ? K : N, ldb, bound,
+           cdiv(total_rows, BM) * cdiv(N, BN), K, total_rows);
 }
 
 void gemm_grouped_wgrad_bf16_tc(Context* c, i64 total_rows, i64 N, i64 K, int groups, const int32_t* offsets,
@@ -477,7 +620,9 @@ void gemm_grouped_wgrad_bf16_tc(Context* c, i64 total_rows, i64 N, i64 K, int gr
     const int BN = N <= 128 ? 128 : 256;
     int tiles = groups * cdiv(K, BM) * cdiv(N, BN);
     // A_g: rows of X [rows, K] read MN-major (M = K); D_g: rows of [rows, N] read MN-major.
-    run_tc(c, a, true, true, A, total_rows, K, lda, D, total_rows, N, ldd, tiles);
+    // Split-K slices each group's rows; the chunk is sized for the mean group.
+    run_tc(c, a, true, true, A, total_rows, K, lda, D, total_rows, N, ldd, tiles, tiles, cdiv(total_rows, groups),
+           (i64)groups * K);
 }
 
 }  // namespace catnn

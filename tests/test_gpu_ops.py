@@ -355,6 +355,45 @@ def test_gemm_bf16_bias_act_accumulate():
     close_bf16(c0, ref2.astype(np.float32), what="accumulate")
 
 
+@pytest.mark.parametrize("ta,tb", [(False, False), (True, False), (False, True)])
+def test_gemm_bf16_split_k(ta, tb):
+    """Few output tiles over a long K: the K range is cut into slices whose
+    fp32 partials are added in slice order (bit-identical run to run), with
+    bias, activation and accumulate applied once after the sum."""
+    r = rng(31 + 2 * ta + tb)
+    M, N, K = 256, 384, 4096
+    a = bf16_round((r.standard_normal((K, M) if ta else (M, K)) / np.sqrt(K)).astype(np.float32))
+    b = bf16_round(r.standard_normal((N, K) if tb else (K, N)).astype(np.float32))
+    bias = r.standard_normal(N).astype(np.float32)
+    ref = (a.T if ta else a).astype(np.float64) @ (b.T if tb else b).astype(np.float64) + bias
+    A, B = dev(a, torch.bfloat16), dev(b, torch.bfloat16)
+    c1 = ops.gemm(A, B, ta, tb, out_dtype=torch.float32, bias=dev(bias), act="relu")
+    close_bf16(c1, np.maximum(ref, 0).astype(np.float32), what="split-K bias+relu")
+    c2 = ops.gemm(A, B, ta, tb, out_dtype=torch.float32, bias=dev(bias), act="relu")
+    assert torch.equal(c1, c2)
+    c0 = dev(r.standard_normal((M, N)).astype(np.float32))
+    ref2 = host(c0) + (ref - bias)
+    ops.gemm(A, B, ta, tb, out=c0, accumulate=True)
+    close_bf16(c0, ref2.astype(np.float32), what="split-K accumulate")
+    cb = ops.gemm(A, B, ta, tb, out_dtype=torch.bfloat16)
+    close_bf16(cb, (ref - bias).astype(np.float32), what="split-K bf16 out")
+
+
+@pytest.mark.parametrize("tb", [False, True])
+def test_grouped_gemm_bf16_split_k(tb):
+    """Two experts of 256 rows against K = 4096: M-grouped tiles cut in K."""
+    r = rng(41 + tb)
+    E, R, N, K = 2, 256, 512, 4096
+    a = bf16_round((r.standard_normal((E * R, K)) / np.sqrt(K)).astype(np.float32))
+    b = bf16_round(r.standard_normal((E, N, K) if tb else (E, K, N)).astype(np.float32))
+    off = torch.tensor([0, R, 2 * R], dtype=torch.int32, device="cuda")
+    out = ops.grouped_gemm(dev(a, torch.bfloat16), dev(b, torch.bfloat16), off, trans_b=tb, out_dtype=torch.float32)
+    for g in range(E):
+        bg = b[g].T if tb else b[g]
+        ref = a[g * R:(g + 1) * R].astype(np.float64) @ bg.astype(np.float64)
+        close_bf16(out[g * R:(g + 1) * R], ref.astype(np.float32), what=f"grouped split-K expert {g}")
+
+
 def test_moe_bf16_grouped_tensor_core():
     r = rng(22)
     T, H, F, E, k = 512, 128, 256, 4, 2
