@@ -133,6 +133,7 @@ __global__ void k_colsum_partial(const T* __restrict__ x, i64 rows, i64 cols, fl
     if (j >= cols) return;
     i64 r1 = r0 + COLSUM_ROWS < rows ? r0 + COLSUM_ROWS : rows;
     float s = 0.f;
+#pragma unroll 8
     for (i64 r = r0; r < r1; ++r) s = __fadd_rn(s, ld(x + r * cols + j));
     part[(i64)blockIdx.y * cols + j] = s;
 }
@@ -140,6 +141,7 @@ __global__ void k_colsum_final(const float* __restrict__ part, int chunks, i64 c
     i64 j = blockIdx.x * (i64)blockDim.x + threadIdx.x;
     if (j >= cols) return;
     float s = 0.f;
+#pragma unroll 8
     for (int ch = 0; ch < chunks; ++ch) s = __fadd_rn(s, part[(i64)ch * cols + j]);
     out[j] = acc ? __fadd_rn(out[j], s) : s;
 }

@@ -384,37 +384,54 @@ __global__ void __launch_bounds__(192, 1)
 
 // Split-K epilogue: C = epilogue(Σ_slices part[slice]) with the slices added
 // in order (deterministic), then bias, residual, accumulate and activation
-// as in k_gemm_tc. One thread per element of the partial rows.
-__global__ void k_splitk_reduce(TcArgs a, long long prows) {
-    const long long n = prows * a.N;
-    int lo = 0, hi = 0;
+// as in k_gemm_tc. CTAs stride over partial rows, threads over columns.
+__global__ void __launch_bounds__(256) k_splitk_reduce(TcArgs a, long long prows) {
+    int lo = 0, hi = 0x7fffffff;
     if (a.mode == 1) {
         lo = a.offsets[0];
         hi = a.offsets[a.groups];
     }
-    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
-        long long prow = i / a.N;
-        int col = (int)(i - prow * a.N);
-        if (a.mode == 1 && (prow < lo || prow >= hi)) continue;
-        float v = a.part[i];
-        for (int k = 1; k < a.ksplit; ++k) v += a.part[(long long)k * a.c_group_stride_part + i];
-        long long off;
+    const bool vec = (a.N % 4) == 0;
+    for (long long prow = blockIdx.x; prow < prows; prow += gridDim.x) {
+        if (prow < lo || prow >= hi) continue;
+        long long obase;
         if (a.mode == 2) {
             long long g = prow / a.M, row = prow - g * a.M;
-            off = g * a.c_group_stride + row * a.ldc + col;
+            obase = g * a.c_group_stride + row * a.ldc;
         } else {
-            off = prow * a.ldc + col;
+            obase = prow * a.ldc;
         }
-        if (a.bias) v += a.bias[col];
-        if (a.resid) v += a.resid[off];
-        if (a.c_bf16) {
-            bf16* p = (bf16*)a.C + off;
-            if (a.accumulate) v += __bfloat162float(*p);
-            *p = __float2bfloat16_rn(act_apply(v, a.act));
-        } else {
-            float* p = (float*)a.C + off;
-            if (a.accumulate) v += *p;
-            *p = act_apply(v, a.act);
+        const float* src = a.part + prow * a.N;
+        const int step = vec ? 4 : 1;
+        for (int col = threadIdx.x * step; col < a.N; col += blockDim.x * step) {
+            float v[4];
+            int nv = vec ? 4 : 1;
+            if (vec) {
+                float4 t = *(const float4*)(src + col);
+                v[0] = t.x; v[1] = t.y; v[2] = t.z; v[3] = t.w;
+                for (int k = 1; k < a.ksplit; ++k) {
+                    float4 u = *(const float4*)(src + (long long)k * a.c_group_stride_part + col);
+                    v[0] += u.x; v[1] += u.y; v[2] += u.z; v[3] += u.w;
+                }
+            } else {
+                v[0] = src[col];
+                for (int k = 1; k < a.ksplit; ++k) v[0] += src[(long long)k * a.c_group_stride_part + col];
+            }
+            for (int j = 0; j < nv; ++j) {
+                float x = v[j];
+                long long off = obase + col + j;
+                if (a.bias) x += a.bias[col + j];
+                if (a.resid) x += a.resid[off];
+                if (a.c_bf16) {
+                    bf16* p = (bf16*)a.C + off;
+                    if (a.accumulate) x += __bfloat162float(*p);
+                    *p = __float2bfloat16_rn(act_apply(x, a.act));
+                } else {
+                    float* p = (float*)a.C + off;
+                    if (a.accumulate) x += *p;
+                    *p = act_apply(x, a.act);
+                }
+            }
         }
     }
 }
@@ -473,19 +490,26 @@ static void dispatch_tc(Context* c, bool a_mn, bool b_mn, const CUtensorMap& ma,
 
 static bool aligned16(const void* p) { return ((uintptr_t)p & 15) == 0; }
 
-// K slices for a launch of `tiles` output tiles over a K range of klen:
-// only when the tiles leave SMs idle; the count minimises
-// ceil(tiles·s / SMs) / s (time in tile-waves) plus a small charge for the
-// partial sums' round trip. Slices stay multiples of BK.
-static int pick_ksplit(Context* c, i64 tiles, i64 klen, int* kchunk) {
+// K slices for a launch of `tiles` BM x BN output tiles over a K range of
+// klen, writing part_elems outputs: only when the tiles leave SMs idle. The
+// count minimises an estimate of the time — tile waves x (tile FLOPs / s) at
+// a per-SM rate of 4 TFLOP/s, plus for s > 1 the fp32 partials' round trip
+// through HBM (5 TB/s) and the reduction launch. Slices are multiples of BK.
+static int pick_ksplit(Context* c, i64 tiles, i64 klen, i64 part_elems, int BN, int* kchunk) {
     *kchunk = 0;
     if (tiles <= 0 || tiles >= c->sm_count || klen < 4 * BK) return 1;
+    const double sm_rate = 4e12, hbm = 5e12, launch = 3e-6;
+    auto cost = [&](int s) {
+        double t = (double)cdiv(tiles * s, c->sm_count) * (2.0 * BM * BN * (double)klen / s) / sm_rate;
+        if (s > 1) t += ((double)s * part_elems * 8 + (double)part_elems * 4) / hbm + launch;
+        return t;
+    };
     int best = 1;
-    double best_cost = 1.0 * cdiv(tiles, c->sm_count);
+    double best_cost = cost(1);
     for (int s = 2; s <= 16 && (i64)s * 2 * BK <= klen; ++s) {
-        double cost = (double)cdiv(tiles * s, c->sm_count) / s + 0.08;
-        if (cost < best_cost - 1e-9) {
-            best_cost = cost;
+        double t = cost(s);
+        if (t < best_cost * 0.97) {
+            best_cost = t;
             best = s;
         }
     }
@@ -509,7 +533,7 @@ static void run_tc(Context* c, TcArgs a, bool a_mn, bool b_mn, const bf16* A, i6
     a.ksplit = 1;
     if (part_rows > 0) {
         int kchunk = 0;
-        int ks = pick_ksplit(c, base_tiles, klen, &kchunk);
+        int ks = pick_ksplit(c, base_tiles, klen, part_rows * a.N, BN, &kchunk);
         if (ks > 1) {
             a.ksplit = ks;
             a.kchunk = kchunk;
@@ -523,8 +547,7 @@ static void run_tc(Context* c, TcArgs a, bool a_mn, bool b_mn, const bf16* A, i6
     if (BN == 128) dispatch_tc<128, 6>(c, a_mn, b_mn, ma, mb, a, grid);
     else dispatch_tc<256, 4>(c, a_mn, b_mn, ma, mb, a, grid);
     if (a.ksplit > 1) {
-        i64 n = part_rows * a.N;
-        int g = (int)std::min<i64>(cdiv(n, 256), (i64)c->sm_count * 8);
+        int g = (int)std::min<i64>(part_rows, (i64)c->sm_count * 16);
         k_splitk_reduce<<<g, 256, 0, c->stream>>>(a, part_rows);
         launched(c);
     }

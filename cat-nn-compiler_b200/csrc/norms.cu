@@ -245,6 +245,7 @@ __global__ void k_ln_cols(const T* __restrict__ x, const T* __restrict__ dy, con
     if (j >= last) return;
     i64 r0 = (i64)blockIdx.y * NCOL_ROWS, r1 = min(rows, r0 + NCOL_ROWS);
     float sg = 0.f, sb = 0.f;
+#pragma unroll 8
     for (i64 r = r0; r < r1; ++r) {
         float d = ld(dy + r * last + j);
         float xh = (ld(x + r * last + j) - stats[2 * r]) * stats[2 * r + 1];
@@ -258,6 +259,7 @@ __global__ void k_cols_final(const float* __restrict__ p, int chunks, i64 last, 
     i64 j = blockIdx.x * (i64)blockDim.x + threadIdx.x;
     if (j >= last) return;
     float s = 0.f;
+#pragma unroll 8
     for (int ch = 0; ch < chunks; ++ch) s += p[(i64)ch * last + j];
     out[j] = acc ? out[j] + s : s;
 }
@@ -348,6 +350,7 @@ __global__ void k_rms_cols(const T* __restrict__ x, const T* __restrict__ dy, co
     if (j >= last) return;
     i64 r0 = (i64)blockIdx.y * NCOL_ROWS, r1 = min(rows, r0 + NCOL_ROWS);
     float sw = 0.f;
+#pragma unroll 8
     for (i64 r = r0; r < r1; ++r) sw += ld(dy + r * last + j) * ld(x + r * last + j) * invs[r];
     pw[(i64)blockIdx.y * last + j] = sw;
 }
@@ -440,6 +443,7 @@ __global__ void k_rms_cols_mx(const TX* __restrict__ x, const TG* __restrict__ d
     if (j >= last) return;
     i64 r0 = (i64)blockIdx.y * NCOL_ROWS, r1 = min(rows, r0 + NCOL_ROWS);
     float sw = 0.f;
+#pragma unroll 8
     for (i64 r = r0; r < r1; ++r) sw += ld(dy + r * last + j) * ld(x + r * last + j) * invs[r];
     pw[(i64)blockIdx.y * last + j] = sw;
 }

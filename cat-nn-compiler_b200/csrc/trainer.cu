@@ -232,6 +232,13 @@ void MoeTrainer::release() {
         cudaStreamSynchronize(c->stream);
         map_id = -1;
     }
+    if (us) {
+        cudaStreamSynchronize(us);
+        cudaEventDestroy(ev_u);
+        cudaEventDestroy(ev_u_done);
+        cudaStreamDestroy(us);
+        us = nullptr;
+    }
     if (param_block) cudaFree(param_block);
     if (act_block) cudaFree(act_block);
     if (h_tokens) cudaFreeHost(h_tokens);
@@ -343,6 +350,9 @@ void MoeTrainer::backward() {
         // loss are summed over ranks while the layers' adjoints run
         CUDA_OK(cudaMemcpyAsync(G + o_loss, loss, 4, cudaMemcpyDeviceToDevice, c->stream));
         comm->allreduce_overlapped(G + o_final, n_rep - o_final);
+        update_after_comm(o_final, n_rep - o_final);
+    } else {
+        update_after_main(o_final, n_rep - o_final);
     }
     for (i64 l = L - 1; l >= 0; --l) {
         Act& a = acts[l];
@@ -388,37 +398,91 @@ void MoeTrainer::backward() {
         gemm(c, true, false, d, qkvd, T, a.xn, d, dqkv, qkvd, G + q.wqkv, qkvd, dt, CATNN_F32, nullptr, 0, false);
         // residual around attention: dx_in = dx_mid + rmsnorm'(dxn)   (train.rs:348-351)
         rmsnorm_bwd_mixed(c, a.x_in, P + q.rms_attn, dxn, dt, dxmid, dx, nullptr, dt, G + q.rms_attn, false, T, d, eps);
-        // this layer's replicated gradients [rms_attn .. gate] are final
-        if (ep) comm->allreduce_overlapped(G + q.rms_attn, q.gate + d * E - q.rms_attn);
+        // this layer's replicated gradients [rms_attn .. gate] and its experts are final
+        const i64 rep = q.gate + d * E - q.rms_attn;
+        if (ep) {
+            comm->allreduce_overlapped(G + q.rms_attn, rep);
+            update_after_comm(q.rms_attn, rep);
+        } else {
+            update_after_main(q.rms_attn, rep);
+        }
+        update_after_main(q.w13, q.w2 + El * F * d - q.w13);
     }
     embedding_bwd(c, tokens + tok_off, T, dx, G + o_embed, V, d, CATNN_F32);
-    if (ep) comm->allreduce_overlapped(G + o_embed, V * d);
+    if (ep) {
+        comm->allreduce_overlapped(G + o_embed, V * d);
+        update_after_comm(o_embed, V * d);
+    } else {
+        update_after_main(o_embed, V * d);
+    }
 }
 
-void MoeTrainer::update() {
-    bf16* sh = dt == CATNN_BF16 ? (bf16*)Sh : nullptr;
-    if (opt == 0) {
-        sgd(c, P, G, n_params, lr, sh);
-    } else {
-        ++t_step;
-        adam(c, P, G, Mo, Vo, n_params, t_step, lr, b1, b2, aeps, CATNN_F32, sh);
-    }
+// optim.rs:32-43 (SGD) / :95-119 (Adam) on parameters [off, off + n).
+void MoeTrainer::update_range(i64 off, i64 n) {
+    if (n <= 0) return;
+    bf16* sh = dt == CATNN_BF16 ? (bf16*)Sh + off : nullptr;
+    if (opt == 0) sgd(c, P + off, G + off, n, lr, sh);
+    else adam(c, P + off, G + off, Mo + off, Vo + off, n, t_step, lr, b1, b2, aeps, CATNN_F32, sh);
+}
+
+namespace {
+// Enqueue the launchers' work on another stream for the scope's lifetime.
+struct OnStream {
+    Context* c;
+    cudaStream_t saved;
+    OnStream(Context* ctx, cudaStream_t s) : c(ctx), saved(ctx->stream) { c->stream = s; }
+    ~OnStream() { c->stream = saved; }
+};
+}  // namespace
+
+static void make_update_stream(cudaStream_t* us, cudaEvent_t* a, cudaEvent_t* b) {
+    if (*us) return;
+    int lo = 0, hi = 0;
+    CUDA_OK(cudaDeviceGetStreamPriorityRange(&lo, &hi));
+    CUDA_OK(cudaStreamCreateWithPriority(us, cudaStreamNonBlocking, lo));  // lowest: the backward pass goes first
+    CUDA_OK(cudaEventCreateWithFlags(a, cudaEventDisableTiming));
+    CUDA_OK(cudaEventCreateWithFlags(b, cudaEventDisableTiming));
+}
+
+void MoeTrainer::update_after_main(i64 off, i64 n) {
+    if (!upd_pending || n <= 0) return;
+    make_update_stream(&us, &ev_u, &ev_u_done);
+    CUDA_OK(cudaEventRecord(ev_u, c->stream));
+    CUDA_OK(cudaStreamWaitEvent(us, ev_u, 0));
+    OnStream on(c, us);
+    update_range(off, n);
+}
+
+void MoeTrainer::update_after_comm(i64 off, i64 n) {
+    if (!upd_pending || n <= 0) return;
+    make_update_stream(&us, &ev_u, &ev_u_done);
+    CUDA_OK(cudaEventRecord(ev_u, comm->side));
+    CUDA_OK(cudaStreamWaitEvent(us, ev_u, 0));
+    OnStream on(c, us);
+    update_range(off, n);
+}
+
+void MoeTrainer::join_updates() {
+    if (!us) return;
+    CUDA_OK(cudaEventRecord(ev_u_done, us));
+    CUDA_OK(cudaStreamWaitEvent(c->stream, ev_u_done, 0));
 }
 
 void MoeTrainer::step(const uint32_t* tokens_dev, float* loss_dev, bool upd) {
     if (tokens_dev != tokens) CUDA_OK(cudaMemcpyAsync(tokens, tokens_dev, Tg * 4, cudaMemcpyDeviceToDevice, c->stream));
+    upd_pending = upd;
+    if (upd && opt == 1) ++t_step;
     forward();
-    backward();
+    backward();  // enqueues the gradient allreduces and the updates bucket by bucket
     if (ep) {
-        // replicated gradients and the loss were summed over ranks bucket by
-        // bucket during the backward pass (expert gradients are complete on
-        // their owners); the update waits for the last bucket. That bucket
-        // completes only once every rank has finished its backward pass, so
-        // no rank's next dispatch can overwrite a buffer a peer still reads.
+        // The last allreduce completes only once every rank has finished its
+        // backward pass, so no rank's next dispatch can overwrite a buffer a
+        // peer still reads.
         comm->join_overlapped();
         CUDA_OK(cudaMemcpyAsync(loss, G + o_loss, 4, cudaMemcpyDeviceToDevice, c->stream));
     }
-    if (upd) update();
+    join_updates();
+    upd_pending = false;
     if (loss_dev && loss_dev != loss) CUDA_OK(cudaMemcpyAsync(loss_dev, loss, 4, cudaMemcpyDeviceToDevice, c->stream));
 }
 

@@ -78,7 +78,16 @@ struct MoeTrainer {
     const void* W(i64 off) const { return (const char*)Sh + off * dsize(dt); }
     void forward();
     void backward();
-    void update();
+    // Optimizer updates run on a low-priority side stream, bucket by bucket,
+    // as soon as a bucket's gradients are final (summed over ranks when
+    // replicated), overlapping the rest of the backward pass.
+    bool upd_pending = false;
+    cudaStream_t us = nullptr;
+    cudaEvent_t ev_u = nullptr, ev_u_done = nullptr;
+    void update_range(i64 off, i64 n);          // on the context's current stream
+    void update_after_main(i64 off, i64 n);     // on us, after the work enqueued so far
+    void update_after_comm(i64 off, i64 n);     // on us, after the last allreduce enqueued
+    void join_updates();
     void step(const uint32_t* tokens_dev, float* loss_dev, bool upd);
     void import_packed(const float* packed, float* dst);
     void export_packed(const float* src, float* packed);
