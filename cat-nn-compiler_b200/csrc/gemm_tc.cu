@@ -261,6 +261,7 @@ __global__ void __launch_bounds__(192, 1)
     } else if (warp >= 2) {
         // ---------------- epilogue
         const int q = warp & 3;
+        const bool plain = !a.bias && !a.resid && a.act == CATNN_ACT_NONE && !a.accumulate;
         int it = 0;
         for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++it) {
             TileInfo ti = tile_at<BN>(a, t);
@@ -304,68 +305,102 @@ __global__ void __launch_bounds__(192, 1)
                     }
                     continue;
                 }
-                float v[32];
-#pragma unroll
-                for (int i = 0; i < 32; ++i) {
-                    float x = ti.klen > 0 ? __uint_as_float(r[i]) : 0.f;
-                    int col = col0 + i;
-                    if (a.bias && col < a.N) x += a.bias[col];
-                    if (a.resid && col < a.N) x += a.resid[crow + col];
-                    v[i] = x;
-                }
                 bool full_chunk = a.vec_ok && (col0 + 32 <= a.N);
-                if (a.c_bf16) {
-                    bf16* p = (bf16*)a.C + crow + col0;
-                    if (full_chunk) {
+                if (plain && full_chunk) {
+                    // the common case (no bias, residual, activation or
+                    // accumulate): convert and store, nothing per element else
+                    const bool z = ti.klen <= 0;
+                    if (a.c_bf16) {
+                        bf16* p = (bf16*)a.C + crow + col0;
 #pragma unroll
                         for (int i4 = 0; i4 < 4; ++i4) {
-                            uint4 old;
-                            if (a.accumulate) old = *(const uint4*)(p + i4 * 8);
-                            const bf16* ob = (const bf16*)&old;
                             uint4 pk;
                             __nv_bfloat162* pp = (__nv_bfloat162*)&pk;
 #pragma unroll
-                            for (int j = 0; j < 4; ++j) {
-                                float x0 = v[i4 * 8 + 2 * j], x1 = v[i4 * 8 + 2 * j + 1];
-                                if (a.accumulate) {
-                                    x0 += __bfloat162float(ob[2 * j]);
-                                    x1 += __bfloat162float(ob[2 * j + 1]);
-                                }
-                                pp[j] = __floats2bfloat162_rn(act_apply(x0, a.act), act_apply(x1, a.act));
-                            }
+                            for (int j = 0; j < 4; ++j)
+                                pp[j] = z ? __floats2bfloat162_rn(0.f, 0.f)
+                                          : __floats2bfloat162_rn(__uint_as_float(r[i4 * 8 + 2 * j]),
+                                                                  __uint_as_float(r[i4 * 8 + 2 * j + 1]));
+                            *(uint4*)(p + i4 * 8) = pk;
+                        }
+                    } else {
+                        float* p = (float*)a.C + crow + col0;
+#pragma unroll
+                        for (int i4 = 0; i4 < 8; ++i4) {
+                            uint4 pk = z ? make_uint4(0, 0, 0, 0)
+                                         : make_uint4(r[i4 * 4], r[i4 * 4 + 1], r[i4 * 4 + 2], r[i4 * 4 + 3]);
+                            *(uint4*)(p + i4 * 4) = pk;
+                        }
+                    }
+                    continue;
+                }
+                // General path. Each option is one uniform branch around its
+                // own loop, so a disabled option costs nothing per element.
+                float v[32];
+                const bool z = ti.klen <= 0;
+#pragma unroll
+                for (int i = 0; i < 32; ++i) v[i] = z ? 0.f : __uint_as_float(r[i]);
+                if (a.bias) {
+#pragma unroll
+                    for (int i = 0; i < 32; ++i)
+                        if (full_chunk || col0 + i < a.N) v[i] += a.bias[col0 + i];
+                }
+                if (a.resid) {
+                    const float* rs = a.resid + crow + col0;
+#pragma unroll
+                    for (int i = 0; i < 32; ++i)
+                        if (full_chunk || col0 + i < a.N) v[i] += rs[i];
+                }
+                if (a.c_bf16) {
+                    bf16* p = (bf16*)a.C + crow + col0;
+                    if (a.accumulate) {
+#pragma unroll
+                        for (int i = 0; i < 32; ++i)
+                            if (full_chunk || col0 + i < a.N) v[i] += __bfloat162float(p[i]);
+                    }
+                    if (a.act == CATNN_ACT_RELU) {
+#pragma unroll
+                        for (int i = 0; i < 32; ++i) v[i] = act_apply(v[i], CATNN_ACT_RELU);
+                    } else if (a.act == CATNN_ACT_GELU) {
+#pragma unroll
+                        for (int i = 0; i < 32; ++i) v[i] = act_apply(v[i], CATNN_ACT_GELU);
+                    }
+                    if (full_chunk) {
+#pragma unroll
+                        for (int i4 = 0; i4 < 4; ++i4) {
+                            uint4 pk;
+                            __nv_bfloat162* pp = (__nv_bfloat162*)&pk;
+#pragma unroll
+                            for (int j = 0; j < 4; ++j) pp[j] = __floats2bfloat162_rn(v[i4 * 8 + 2 * j], v[i4 * 8 + 2 * j + 1]);
                             *(uint4*)(p + i4 * 8) = pk;
                         }
                     } else {
 #pragma unroll
-                        for (int i = 0; i < 32; ++i) {
-                            if (col0 + i >= a.N) continue;
-                            float x = v[i];
-                            if (a.accumulate) x += __bfloat162float(p[i]);
-                            p[i] = __float2bfloat16_rn(act_apply(x, a.act));
-                        }
+                        for (int i = 0; i < 32; ++i)
+                            if (col0 + i < a.N) p[i] = __float2bfloat16_rn(v[i]);
                     }
                 } else {
                     float* p = (float*)a.C + crow + col0;
+                    if (a.accumulate) {
+#pragma unroll
+                        for (int i = 0; i < 32; ++i)
+                            if (full_chunk || col0 + i < a.N) v[i] += p[i];
+                    }
+                    if (a.act == CATNN_ACT_RELU) {
+#pragma unroll
+                        for (int i = 0; i < 32; ++i) v[i] = act_apply(v[i], CATNN_ACT_RELU);
+                    } else if (a.act == CATNN_ACT_GELU) {
+#pragma unroll
+                        for (int i = 0; i < 32; ++i) v[i] = act_apply(v[i], CATNN_ACT_GELU);
+                    }
                     if (full_chunk) {
 #pragma unroll
-                        for (int i4 = 0; i4 < 8; ++i4) {
-                            float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
-                            if (a.accumulate) o = *(const float4*)(p + i4 * 4);
-                            float4 w;
-                            w.x = act_apply(v[i4 * 4 + 0] + o.x, a.act);
-                            w.y = act_apply(v[i4 * 4 + 1] + o.y, a.act);
-                            w.z = act_apply(v[i4 * 4 + 2] + o.z, a.act);
-                            w.w = act_apply(v[i4 * 4 + 3] + o.w, a.act);
-                            *(float4*)(p + i4 * 4) = w;
-                        }
+                        for (int i4 = 0; i4 < 8; ++i4)
+                            *(float4*)(p + i4 * 4) = make_float4(v[i4 * 4], v[i4 * 4 + 1], v[i4 * 4 + 2], v[i4 * 4 + 3]);
                     } else {
 #pragma unroll
-                        for (int i = 0; i < 32; ++i) {
-                            if (col0 + i >= a.N) continue;
-                            float x = v[i];
-                            if (a.accumulate) x += p[i];
-                            p[i] = act_apply(x, a.act);
-                        }
+                        for (int i = 0; i < 32; ++i)
+                            if (col0 + i < a.N) p[i] = v[i];
                     }
                 }
             }
