@@ -324,6 +324,9 @@ __global__ void __launch_bounds__(128) k_attn_fwd(AttnArgs a) {
 }
 
 bool attention_tc_ok(i64 hd, i64 q_stride, i64 kv_stride, const void* q, const void* k, const void* v);
+bool attention_fwd_tc5_ok(i64 hd, i64 q_stride, i64 kv_stride, const void* q, const void* k, const void* v);
+void attention_fwd_tc5(Context* c, const void* q, const void* k, const void* v, void* o, float* lse, i64 b, i64 s,
+                       i64 h, i64 hkv, bool causal, i64 window, i64 q_stride, i64 kv_stride);
 void attention_fwd_tc(Context* c, const void* q, const void* k, const void* v, void* o, float* lse, i64 b, i64 s, i64 h,
                       i64 hkv, i64 hd, bool causal, i64 window, i64 q_stride, i64 kv_stride);
 void attention_bwd_tc(Context* c, const void* q, const void* k, const void* v, const void* o, const float* lse,
@@ -335,9 +338,14 @@ void attention_fwd(Context* c, const void* q, const void* k, const void* v, void
     if (b <= 0 || s <= 0 || h <= 0) return;
     CATNN_CHECK(hd > 0 && hd <= HDMAX, CATNN_ERR_UNSUPPORTED, "attention: head_dim must be in [1, 128]");
     CATNN_CHECK(hkv > 0 && h % hkv == 0, CATNN_ERR_SHAPE, "attention: n_heads must be a multiple of n_kv_heads");
-    if (dtype == CATNN_BF16 && attention_tc_ok(hd, q_stride ? q_stride : h * hd, kv_stride ? kv_stride : hkv * hd, q, k, v)) {
-        attention_fwd_tc(c, q, k, v, o, lse, b, s, h, hkv, hd, causal, window, q_stride ? q_stride : h * hd,
-                         kv_stride ? kv_stride : hkv * hd);
+    const i64 qs = q_stride ? q_stride : h * hd, ks = kv_stride ? kv_stride : hkv * hd;
+    if (dtype == CATNN_BF16 && attention_fwd_tc5_ok(hd, qs, ks, q, k, v)) {
+        // tcgen05 + TMEM (head_dim 64)
+        attention_fwd_tc5(c, q, k, v, o, lse, b, s, h, hkv, causal, window, qs, ks);
+        return;
+    }
+    if (dtype == CATNN_BF16 && attention_tc_ok(hd, qs, ks, q, k, v)) {
+        attention_fwd_tc(c, q, k, v, o, lse, b, s, h, hkv, hd, causal, window, qs, ks);
         return;
     }
     AttnArgs a{};

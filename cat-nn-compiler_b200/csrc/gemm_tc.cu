@@ -500,6 +500,12 @@ static CUtensorMap make_map(const void* base, i64 rows, i64 cols, i64 ld, int bo
     return m;
 }
 
+// Shared with the tensor-core attention kernels: a 2-D bf16 load map with
+// 128-byte swizzle over a row-major [rows, cols] matrix (leading dimension ld).
+CUtensorMap tma_map_bf16(const void* base, i64 rows, i64 cols, i64 ld, int box_cols, int box_rows) {
+    return make_map(base, rows, cols, ld, box_cols, box_rows);
+}
+
 template <bool A_MN, bool B_MN, int BN, int STAGES>
 static void launch_tc(Context* c, const CUtensorMap& ma, const CUtensorMap& mb, const TcArgs& a, int grid) {
     constexpr size_t smem = (size_t)STAGES * (BM * BK * 2 + BN * BK * 2) + 1024 + 256;

@@ -140,4 +140,9 @@ __host__ __device__ constexpr uint32_t idesc_bf16(int M, int N, bool a_mn, bool 
 }
 
 }  // namespace tc
+
+// Host: a 2-D bf16 TMA load map, 128-byte swizzle, over a row-major
+// [rows, cols] matrix with leading dimension ld (gemm_tc.cu).
+CUtensorMap tma_map_bf16(const void* base, i64 rows, i64 cols, i64 ld, int box_cols, int box_rows);
+
 }  // namespace catnn

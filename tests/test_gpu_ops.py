@@ -416,10 +416,13 @@ def test_moe_bf16_grouped_tensor_core():
 
 @pytest.mark.parametrize("b,s,h,kv,hd,causal,window", [(2, 200, 4, 4, 64, True, None), (1, 130, 4, 2, 64, True, 48),
                                                         (2, 96, 2, 2, 128, True, None), (1, 64, 2, 2, 64, False, None),
-                                                        (1, 257, 2, 1, 128, True, 100)])
+                                                        (1, 257, 2, 1, 128, True, 100), (1, 1024, 2, 1, 64, True, None),
+                                                        (2, 384, 2, 2, 64, False, None), (1, 600, 4, 2, 64, True, 200)])
 def test_attention_core_bf16_tensor_core(b, s, h, kv, hd, causal, window):
-    """Flash attention (mma.sync) vs the fp32 attention core (itself checked
-    against the oracle's GQA above) on the same bf16 inputs."""
+    """Flash attention on the tensor cores (forward: tcgen05 + TMEM for
+    head_dim 64, mma.sync for 128; backward: mma.sync) vs the fp32 attention
+    core (itself checked against the oracle's GQA above) on the same bf16
+    inputs."""
     r = rng(s + hd)
     q = bf16_round(r.standard_normal((b, s, h, hd)).astype(np.float32))
     k = bf16_round(r.standard_normal((b, s, kv, hd)).astype(np.float32))
