@@ -322,6 +322,488 @@ __global__ void __launch_bounds__(NT, 2)
     }
 }
 
+// ------------------------------------------------------------------ backward
+// dS = P ⊙ (dP - D), D = rowsum(dO ⊙ O), P = 2^(S·scale·log2e - lse·log2e)
+// (the adjoint of the max-subtracted softmax, adjoint.rs:92-104, inside the
+// attention adjoint adjoint.rs:287-439). Two kernels, each deterministic:
+//   k_dkdv  one CTA per 128 keys of a kv head; loops over the query blocks
+//           of every head of its group: Sᵀ = K·Qᵀ, dPᵀ = V·dOᵀ (TMEM),
+//           then dV += Pᵀ·dO and dK += dSᵀ·Q accumulate in TMEM.
+//   k_dq    one CTA per 128 queries; loops over key blocks:
+//           S = Q·Kᵀ, dP = dO·Vᵀ, dQ += dS·K in TMEM.
+// The same shared-memory tile serves as a K-major B operand (for Qᵀ, dOᵀ,
+// Kᵀ, Vᵀ) and as an MN-major B operand (for Q, dO, K): only the descriptor
+// changes. P and dS are written by the compute threads in the A-operand
+// layout (128-byte rows, 16-byte chunks XOR-swizzled by row).
+
+constexpr int BB = 64;                           // the looped block (queries in k_dkdv, keys in k_dq)
+constexpr uint32_t T64 = 64 * HD * 2;            // 8 KB: a 64-row tile
+constexpr uint32_t T128 = 128 * HD * 2;          // 16 KB: a 128-row tile
+constexpr uint32_t QD_STAGE = 2 * T64 + 1024;    // Q, dO and the block's L, D
+constexpr size_t SMEM_DKDV = 2 * T128 + 2 * QD_STAGE + 2 * T128 + 1024 + 512;
+constexpr size_t SMEM_DQ = 2 * T128 + 3 * 2 * T64 + T128 + 1024 + 512;
+
+struct BwdArgs {
+    int b, s, h, hkv;
+    int causal, window;
+    float scale;
+    const float* lse;   // [B, H, S], natural log
+    const float* dsum;  // [B, H, S]
+    bf16 *dq, *dk, *dv;
+    int q_stride, kv_stride;
+    int* status;
+};
+
+__device__ __forceinline__ int bklo(const BwdArgs& a, int i) {
+    if (!a.causal || a.window <= 0) return 0;
+    int l = i - a.window + 1;
+    return l > 0 ? l : 0;
+}
+__device__ __forceinline__ int bkhi(const BwdArgs& a, int i) { return a.causal ? i : a.s - 1; }
+// queries that see key k: [qlo, qhi]
+__device__ __forceinline__ int bqlo(const BwdArgs& a, int k) { return a.causal ? k : 0; }
+__device__ __forceinline__ int bqhi(const BwdArgs& a, int k) {
+    if (!a.causal) return a.s - 1;
+    if (a.window <= 0) return a.s - 1;
+    return min(a.s - 1, k + a.window - 1);
+}
+
+// 16-byte chunk `chunk` (8 bf16) of row r of a 128-byte-row swizzled tile
+__device__ __forceinline__ void st_chunk8(uint32_t row_addr, int r, int chunk, const float (&x)[8]) {
+    uint4 pk;
+    __nv_bfloat162* pp = (__nv_bfloat162*)&pk;
+#pragma unroll
+    for (int t = 0; t < 4; ++t) pp[t] = __floats2bfloat162_rn(x[2 * t], x[2 * t + 1]);
+    asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(row_addr + ((chunk ^ (r & 7)) << 4)), "r"(pk.x),
+                 "r"(pk.y), "r"(pk.z), "r"(pk.w)
+                 : "memory");
+}
+
+__device__ __forceinline__ void ld_row64(uint32_t taddr, uint32_t (&v)[64]) {
+    uint32_t (&v0)[32] = *reinterpret_cast<uint32_t(*)[32]>(&v[0]);
+    uint32_t (&v1)[32] = *reinterpret_cast<uint32_t(*)[32]>(&v[32]);
+    tc::tmem_ld32(taddr, v0);
+    tc::tmem_ld32(taddr + 32, v1);
+}
+
+__global__ void __launch_bounds__(NT, 2)
+    k_dkdv(const __grid_constant__ CUtensorMap mk, const __grid_constant__ CUtensorMap mv,
+           const __grid_constant__ CUtensorMap mq, const __grid_constant__ CUtensorMap mdo, BwdArgs a) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+    uint8_t* sK = smem;
+    uint8_t* sV = sK + T128;
+    uint8_t* sQD = sV + T128;  // 2 stages: Q | dO | L[64] D[64]
+    uint8_t* sP = sQD + 2 * QD_STAGE;
+    uint8_t* sDS = sP + T128;
+    uint64_t* bars = (uint64_t*)(sDS + T128);
+    uint64_t* kv_full = bars;
+    uint64_t* qd_full = kv_full + 1;
+    uint64_t* qd_empty = qd_full + 2;
+    uint64_t* st_full = qd_empty + 2;
+    uint64_t* st_free = st_full + 1;
+    uint64_t* pd_full = st_free + 1;
+    uint64_t* pd_free = pd_full + 1;
+    uint64_t* acc_full = pd_free + 1;
+    uint64_t* drain = acc_full + 1;
+    uint32_t* tmem_slot = (uint32_t*)(drain + 1);
+    constexpr uint32_t C_S = 0, C_DP = 64, C_DV = 128, C_DK = 192;
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int kb = gridDim.x - 1 - blockIdx.x;  // early keys see the most queries: first
+    const int k0 = kb * 128, kvh = blockIdx.y, bi = blockIdx.z;
+    const int grp = a.h / a.hkv;
+    const int klast = min(k0 + 127, a.s - 1);
+    const int qb0 = bqlo(a, k0) / BB, qb1 = bqhi(a, klast) / BB;
+    const int nq = qb1 - qb0 + 1, n = grp * nq;
+    const long long seq_row = (long long)bi * a.s;
+
+    if (threadIdx.x == 0) {
+        tc::mbar_init(kv_full, 1);
+        for (int i = 0; i < 2; ++i) {
+            tc::mbar_init(&qd_full[i], 1);
+            tc::mbar_init(&qd_empty[i], 1);
+        }
+        tc::mbar_init(st_full, 1);
+        tc::mbar_init(st_free, 4);
+        tc::mbar_init(pd_full, 4);
+        tc::mbar_init(pd_free, 1);
+        tc::mbar_init(acc_full, 1);
+        tc::mbar_init(drain, 1);
+        tc::fence_mbar_init();
+    }
+    if (warp == 1) tc::tmem_alloc(tmem_slot, 256);
+    tc::tc_fence_before();
+    __syncthreads();
+    tc::tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0) {
+        // ---------------- producer (whole warp: lane 0 issues TMA, all lanes fill L and D)
+        if (lane == 0) {
+            tc::mbar_arrive_expect_tx(kv_full, 2 * T128);
+            tc::tma_load_2d(sK, &mk, kvh * HD, (int)(seq_row + k0), kv_full);
+            tc::tma_load_2d(sV, &mv, kvh * HD, (int)(seq_row + k0), kv_full);
+        }
+        int last_ph[2] = {-1, -1};
+        int ok = 1;
+        for (int it = 0; it < n; ++it) {
+            const int st = it & 1;
+            if (lane == 0) ok = tc::mbar_wait(&qd_empty[st], ((it >> 1) & 1) ^ 1, a.status, 4);
+            ok = __shfl_sync(0xffffffffu, ok, 0);
+            if (!ok) break;
+            last_ph[st] = (it >> 1) & 1;
+            const int h = kvh * grp + it / nq;
+            const int q0 = (qb0 + it % nq) * BB;
+            uint8_t* stg = sQD + st * QD_STAGE;
+            float* sL = (float*)(stg + 2 * T64);
+            float* sD = sL + 64;
+            const long long lrow = ((long long)bi * a.h + h) * a.s;
+#pragma unroll
+            for (int u = 0; u < 2; ++u) {
+                const int c = lane * 2 + u, q = q0 + c;
+                sL[c] = q < a.s ? a.lse[lrow + q] * LOG2E : INFINITY;
+                sD[c] = q < a.s ? a.dsum[lrow + q] : 0.f;
+            }
+            __syncwarp();
+            if (lane == 0) {
+                tc::mbar_arrive_expect_tx(&qd_full[st], 2 * T64);
+                tc::tma_load_2d(stg, &mq, h * HD, (int)(seq_row + q0), &qd_full[st]);
+                tc::tma_load_2d(stg + T64, &mdo, h * HD, (int)(seq_row + q0), &qd_full[st]);
+            }
+        }
+        if (!ok && lane == 0) {
+            // let the copies in flight land before the CTA exits
+            tc::mbar_wait(kv_full, 0, a.status, 4, 400000000ll, false);
+            for (int i = 0; i < 2; ++i)
+                if (last_ph[i] >= 0) tc::mbar_wait(&qd_full[i], (uint32_t)last_ph[i], a.status, 4, 400000000ll, false);
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            // ---------------- MMA issuer
+            constexpr uint32_t ID_T = tc::idesc_bf16(128, BB, false, false);  // Sᵀ, dPᵀ
+            constexpr uint32_t ID_A = tc::idesc_bf16(128, HD, false, true);   // dV, dK
+            bool ok = tc::mbar_wait(kv_full, 0, a.status, 4);
+            const uint32_t aK = tc::smem_u32(sK), aV = tc::smem_u32(sV);
+            const uint32_t aP = tc::smem_u32(sP), aDS = tc::smem_u32(sDS);
+            for (int it = 0; it < n && ok; ++it) {
+                const int st = it & 1;
+                if (!tc::mbar_wait(&qd_full[st], (it >> 1) & 1, a.status, 4) ||
+                    !tc::mbar_wait(st_free, (it & 1) ^ 1, a.status, 4)) {
+                    ok = false;
+                    break;
+                }
+                tc::tc_fence_after();
+                const uint32_t bQ = tc::smem_u32(sQD + st * QD_STAGE), bO = bQ + T64;
+#pragma unroll
+                for (int kk = 0; kk < HD / 16; ++kk)
+                    tc::mma_bf16(tmem + C_S, tc::sdesc(aK + kk * 32, 16, 1024), tc::sdesc(bQ + kk * 32, 16, 1024), ID_T,
+                                 kk != 0);
+#pragma unroll
+                for (int kk = 0; kk < HD / 16; ++kk)
+                    tc::mma_bf16(tmem + C_DP, tc::sdesc(aV + kk * 32, 16, 1024), tc::sdesc(bO + kk * 32, 16, 1024), ID_T,
+                                 kk != 0);
+                tc::mma_commit(st_full);
+                if (!tc::mbar_wait(pd_full, it & 1, a.status, 4)) {
+                    ok = false;
+                    break;
+                }
+                tc::tc_fence_after();
+#pragma unroll
+                for (int kk = 0; kk < BB / 16; ++kk)
+                    tc::mma_bf16(tmem + C_DV, tc::sdesc(aP + kk * 32, 16, 1024), tc::sdesc(bO + kk * 2048, 8192, 1024),
+                                 ID_A, (it | kk) != 0);
+#pragma unroll
+                for (int kk = 0; kk < BB / 16; ++kk)
+                    tc::mma_bf16(tmem + C_DK, tc::sdesc(aDS + kk * 32, 16, 1024), tc::sdesc(bQ + kk * 2048, 8192, 1024),
+                                 ID_A, (it | kk) != 0);
+                tc::mma_commit(pd_free);
+                tc::mma_commit(&qd_empty[st]);
+            }
+            if (ok) tc::mma_commit(acc_full);
+            tc::mma_commit(drain);
+            tc::mbar_wait(drain, 0, a.status, 4, 400000000ll, false);
+        }
+    } else {
+        // ---------------- compute: thread = key row
+        const int qd = warp & 3;
+        const int r = qd * 32 + lane;
+        const int key = k0 + r;
+        const uint32_t lane_off = (uint32_t)(qd * 32) << 16;
+        const float sc = a.scale * LOG2E;
+        const int qlo = bqlo(a, key), qhi = bqhi(a, key);
+        const uint32_t prow = tc::smem_u32(sP) + r * 128, dsrow = tc::smem_u32(sDS) + r * 128;
+        bool ok = true;
+        for (int it = 0; it < n && ok; ++it) {
+            const int st = it & 1;
+            const int q0 = (qb0 + it % nq) * BB;
+            if (!tc::mbar_wait(st_full, it & 1, a.status, 4)) {
+                ok = false;
+                break;
+            }
+            tc::tc_fence_after();
+            uint32_t s[64], dp[64];
+            ld_row64(tmem + lane_off + C_S, s);
+            ld_row64(tmem + lane_off + C_DP, dp);
+            tc::tmem_ld_wait();
+            tc::tc_fence_before();
+            __syncwarp();
+            if (lane == 0) tc::mbar_arrive(st_free);
+            // no masking when every (query, key) pair of the block is visible
+            const bool full = q0 >= bqlo(a, klast) && q0 + BB - 1 <= bqhi(a, k0) && q0 + BB - 1 < a.s;
+            const float* sL = (const float*)(sQD + st * QD_STAGE + 2 * T64);
+            const float* sD = sL + 64;
+            // the MMAs of the previous block have read P and dS (their commit
+            // precedes the one that filled S and dP: no wait in practice)
+            if (!tc::mbar_wait(pd_free, (it & 1) ^ 1, a.status, 4)) {
+                ok = false;
+                break;
+            }
+#pragma unroll
+            for (int chunk = 0; chunk < 8; ++chunk) {
+                float p[8], ds[8];
+#pragma unroll
+                for (int t = 0; t < 8; ++t) {
+                    const int c = chunk * 8 + t, q = q0 + c;
+                    float pv = ex2(fmaf(__uint_as_float(s[c]), sc, -sL[c]));
+                    if (!full && (q < qlo || q > qhi)) pv = 0.f;
+                    p[t] = pv;
+                    ds[t] = pv * (__uint_as_float(dp[c]) - sD[c]);
+                }
+                st_chunk8(prow, r, chunk, p);
+                st_chunk8(dsrow, r, chunk, ds);
+            }
+            tc::fence_proxy_async();
+            __syncwarp();
+            if (lane == 0) tc::mbar_arrive(pd_full);
+        }
+        if (ok && n > 0 && tc::mbar_wait(acc_full, 0, a.status, 4)) {
+            tc::tc_fence_after();
+            uint32_t dv[64], dk[64];
+            ld_row64(tmem + lane_off + C_DV, dv);
+            ld_row64(tmem + lane_off + C_DK, dk);
+            tc::tmem_ld_wait();
+            if (key < a.s) {
+                const long long off = (seq_row + key) * a.kv_stride + kvh * HD;
+#pragma unroll
+                for (int c = 0; c < 8; ++c) {
+                    uint4 pv, pk;
+                    __nv_bfloat162* a2 = (__nv_bfloat162*)&pv;
+                    __nv_bfloat162* b2 = (__nv_bfloat162*)&pk;
+#pragma unroll
+                    for (int t = 0; t < 4; ++t) {
+                        a2[t] = __floats2bfloat162_rn(__uint_as_float(dv[c * 8 + 2 * t]), __uint_as_float(dv[c * 8 + 2 * t + 1]));
+                        b2[t] = __floats2bfloat162_rn(__uint_as_float(dk[c * 8 + 2 * t]) * a.scale,
+                                                      __uint_as_float(dk[c * 8 + 2 * t + 1]) * a.scale);
+                    }
+                    *(uint4*)(a.dv + off + c * 8) = pv;
+                    *(uint4*)(a.dk + off + c * 8) = pk;
+                }
+            }
+        }
+    }
+    tc::tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc::tc_fence_after();
+        tc::tmem_dealloc(tmem, 256);
+    }
+}
+
+__global__ void __launch_bounds__(NT, 2)
+    k_dq(const __grid_constant__ CUtensorMap mq, const __grid_constant__ CUtensorMap mdo,
+         const __grid_constant__ CUtensorMap mk, const __grid_constant__ CUtensorMap mv, BwdArgs a) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+    uint8_t* sQ = smem;
+    uint8_t* sO = sQ + T128;
+    uint8_t* sKV = sO + T128;  // 3 stages: K | V (64 keys each)
+    uint8_t* sDS = sKV + 3 * 2 * T64;
+    uint64_t* bars = (uint64_t*)(sDS + T128);
+    uint64_t* q_full = bars;
+    uint64_t* kv_full = q_full + 1;
+    uint64_t* kv_empty = kv_full + 3;
+    uint64_t* st_full = kv_empty + 3;
+    uint64_t* st_free = st_full + 1;
+    uint64_t* ds_full = st_free + 1;
+    uint64_t* ds_free = ds_full + 1;
+    uint64_t* acc_full = ds_free + 1;
+    uint64_t* drain = acc_full + 1;
+    uint32_t* tmem_slot = (uint32_t*)(drain + 1);
+    constexpr uint32_t C_S = 0, C_DP = 64, C_DQ = 128;
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int qt = gridDim.x - 1 - blockIdx.x;
+    const int q0 = qt * 128, h = blockIdx.y, bi = blockIdx.z;
+    const int kvh = h / (a.h / a.hkv);
+    const int qlast = min(q0 + 127, a.s - 1);
+    const int j0 = bklo(a, q0) / BB, j1 = min(bkhi(a, qlast), a.s - 1) / BB;
+    const int n = j1 - j0 + 1;
+    const long long seq_row = (long long)bi * a.s;
+
+    if (threadIdx.x == 0) {
+        tc::mbar_init(q_full, 1);
+        for (int i = 0; i < 3; ++i) {
+            tc::mbar_init(&kv_full[i], 1);
+            tc::mbar_init(&kv_empty[i], 1);
+        }
+        tc::mbar_init(st_full, 1);
+        tc::mbar_init(st_free, 4);
+        tc::mbar_init(ds_full, 4);
+        tc::mbar_init(ds_free, 1);
+        tc::mbar_init(acc_full, 1);
+        tc::mbar_init(drain, 1);
+        tc::fence_mbar_init();
+    }
+    if (warp == 1) tc::tmem_alloc(tmem_slot, 256);
+    tc::tc_fence_before();
+    __syncthreads();
+    tc::tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            tc::mbar_arrive_expect_tx(q_full, 2 * T128);
+            tc::tma_load_2d(sQ, &mq, h * HD, (int)(seq_row + q0), q_full);
+            tc::tma_load_2d(sO, &mdo, h * HD, (int)(seq_row + q0), q_full);
+            int last_ph[3] = {-1, -1, -1};
+            bool ok = true;
+            for (int j = 0; j < n; ++j) {
+                const int st = j % 3;
+                const uint32_t ph = (j / 3) & 1;
+                if (!tc::mbar_wait(&kv_empty[st], ph ^ 1, a.status, 4)) {
+                    ok = false;
+                    break;
+                }
+                uint8_t* stg = sKV + st * 2 * T64;
+                tc::mbar_arrive_expect_tx(&kv_full[st], 2 * T64);
+                const int krow = (int)(seq_row + (long long)(j0 + j) * BB);
+                tc::tma_load_2d(stg, &mk, kvh * HD, krow, &kv_full[st]);
+                tc::tma_load_2d(stg + T64, &mv, kvh * HD, krow, &kv_full[st]);
+                last_ph[st] = (int)ph;
+            }
+            if (!ok) {
+                tc::mbar_wait(q_full, 0, a.status, 4, 400000000ll, false);
+                for (int i = 0; i < 3; ++i)
+                    if (last_ph[i] >= 0) tc::mbar_wait(&kv_full[i], (uint32_t)last_ph[i], a.status, 4, 400000000ll, false);
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            constexpr uint32_t ID_S = tc::idesc_bf16(128, BB, false, false);  // S, dP
+            constexpr uint32_t ID_Q = tc::idesc_bf16(128, HD, false, true);   // dQ (K MN-major)
+            bool ok = tc::mbar_wait(q_full, 0, a.status, 4);
+            const uint32_t aQ = tc::smem_u32(sQ), aO = tc::smem_u32(sO), aDS = tc::smem_u32(sDS);
+            for (int j = 0; j < n && ok; ++j) {
+                const int st = j % 3;
+                if (!tc::mbar_wait(&kv_full[st], (j / 3) & 1, a.status, 4) ||
+                    !tc::mbar_wait(st_free, (j & 1) ^ 1, a.status, 4)) {
+                    ok = false;
+                    break;
+                }
+                tc::tc_fence_after();
+                const uint32_t bK = tc::smem_u32(sKV + st * 2 * T64), bV = bK + T64;
+#pragma unroll
+                for (int kk = 0; kk < HD / 16; ++kk)
+                    tc::mma_bf16(tmem + C_S, tc::sdesc(aQ + kk * 32, 16, 1024), tc::sdesc(bK + kk * 32, 16, 1024), ID_S,
+                                 kk != 0);
+#pragma unroll
+                for (int kk = 0; kk < HD / 16; ++kk)
+                    tc::mma_bf16(tmem + C_DP, tc::sdesc(aO + kk * 32, 16, 1024), tc::sdesc(bV + kk * 32, 16, 1024), ID_S,
+                                 kk != 0);
+                tc::mma_commit(st_full);
+                if (!tc::mbar_wait(ds_full, j & 1, a.status, 4)) {
+                    ok = false;
+                    break;
+                }
+                tc::tc_fence_after();
+#pragma unroll
+                for (int kk = 0; kk < BB / 16; ++kk)
+                    tc::mma_bf16(tmem + C_DQ, tc::sdesc(aDS + kk * 32, 16, 1024), tc::sdesc(bK + kk * 2048, 8192, 1024),
+                                 ID_Q, (j | kk) != 0);
+                tc::mma_commit(ds_free);
+                tc::mma_commit(&kv_empty[st]);
+            }
+            if (ok) tc::mma_commit(acc_full);
+            tc::mma_commit(drain);
+            tc::mbar_wait(drain, 0, a.status, 4, 400000000ll, false);
+        }
+    } else {
+        // ---------------- compute: thread = query row
+        const int qd = warp & 3;
+        const int r = qd * 32 + lane;
+        const int row = q0 + r;
+        const uint32_t lane_off = (uint32_t)(qd * 32) << 16;
+        const float sc = a.scale * LOG2E;
+        const long long lrow = ((long long)bi * a.h + h) * a.s;
+        const float L = row < a.s ? a.lse[lrow + row] * LOG2E : INFINITY;
+        const float D = row < a.s ? a.dsum[lrow + row] : 0.f;
+        const int lo = bklo(a, row), hi = min(bkhi(a, row), a.s - 1);
+        const uint32_t dsrow = tc::smem_u32(sDS) + r * 128;
+        bool ok = true;
+        for (int j = 0; j < n && ok; ++j) {
+            const int kb0 = (j0 + j) * BB;
+            if (!tc::mbar_wait(st_full, j & 1, a.status, 4)) {
+                ok = false;
+                break;
+            }
+            tc::tc_fence_after();
+            uint32_t s[64], dp[64];
+            ld_row64(tmem + lane_off + C_S, s);
+            ld_row64(tmem + lane_off + C_DP, dp);
+            tc::tmem_ld_wait();
+            tc::tc_fence_before();
+            __syncwarp();
+            if (lane == 0) tc::mbar_arrive(st_free);
+            const bool full = kb0 >= bklo(a, qlast) && kb0 + BB - 1 <= min(bkhi(a, q0), a.s - 1);
+            if (!tc::mbar_wait(ds_free, (j & 1) ^ 1, a.status, 4)) {
+                ok = false;
+                break;
+            }
+#pragma unroll
+            for (int chunk = 0; chunk < 8; ++chunk) {
+                float ds[8];
+#pragma unroll
+                for (int t = 0; t < 8; ++t) {
+                    const int c = chunk * 8 + t, key = kb0 + c;
+                    float pv = ex2(fmaf(__uint_as_float(s[c]), sc, -L));
+                    if (!full && (key < lo || key > hi)) pv = 0.f;
+                    ds[t] = pv * (__uint_as_float(dp[c]) - D);
+                }
+                st_chunk8(dsrow, r, chunk, ds);
+            }
+            tc::fence_proxy_async();
+            __syncwarp();
+            if (lane == 0) tc::mbar_arrive(ds_full);
+        }
+        if (ok && n > 0 && tc::mbar_wait(acc_full, 0, a.status, 4)) {
+            tc::tc_fence_after();
+            uint32_t dq[64];
+            ld_row64(tmem + lane_off + C_DQ, dq);
+            tc::tmem_ld_wait();
+            if (row < a.s) {
+                bf16* out = a.dq + (seq_row + row) * a.q_stride + h * HD;
+#pragma unroll
+                for (int c = 0; c < 8; ++c) {
+                    uint4 pk;
+                    __nv_bfloat162* b2 = (__nv_bfloat162*)&pk;
+#pragma unroll
+                    for (int t = 0; t < 4; ++t)
+                        b2[t] = __floats2bfloat162_rn(__uint_as_float(dq[c * 8 + 2 * t]) * a.scale,
+                                                      __uint_as_float(dq[c * 8 + 2 * t + 1]) * a.scale);
+                    *(uint4*)(out + c * 8) = pk;
+                }
+            }
+        }
+    }
+    tc::tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc::tc_fence_after();
+        tc::tmem_dealloc(tmem, 256);
+    }
+}
+
 }  // namespace fa5
 
 // The tcgen05 forward applies to head_dim 64 with 16-byte aligned bases and
@@ -360,6 +842,53 @@ void attention_fwd_tc5(Context* c, const void* q, const void* k, const void* v, 
     dim3 grid((unsigned)cdiv(s, BQ), (unsigned)h, (unsigned)b);
     k_fwd<<<grid, NT, SMEM, c->stream>>>(mq, mk, mv, a);
     launched(c);
+}
+
+}  // namespace catnn
+
+namespace catnn {
+
+void attention_bwd_tc5(Context* c, const void* q, const void* k, const void* v, const void* dout, const float* lse,
+                       const float* dsum, void* dq, void* dk, void* dv, i64 b, i64 s, i64 h, i64 hkv, bool causal,
+                       i64 window, i64 q_stride, i64 kv_stride) {
+    using namespace fa5;
+    if (b <= 0 || s <= 0 || h <= 0) return;
+    CATNN_CHECK(b * s < (1ll << 31) && h % hkv == 0, CATNN_ERR_SHAPE, "attention: sizes");
+    CUtensorMap mq64 = tma_map_bf16(q, b * s, h * HD, q_stride, HD, 64);
+    CUtensorMap mq128 = tma_map_bf16(q, b * s, h * HD, q_stride, HD, 128);
+    CUtensorMap mdo64 = tma_map_bf16(dout, b * s, h * HD, h * HD, HD, 64);
+    CUtensorMap mdo128 = tma_map_bf16(dout, b * s, h * HD, h * HD, HD, 128);
+    CUtensorMap mk128 = tma_map_bf16(k, b * s, hkv * HD, kv_stride, HD, 128);
+    CUtensorMap mv128 = tma_map_bf16(v, b * s, hkv * HD, kv_stride, HD, 128);
+    CUtensorMap mk64 = tma_map_bf16(k, b * s, hkv * HD, kv_stride, HD, 64);
+    CUtensorMap mv64 = tma_map_bf16(v, b * s, hkv * HD, kv_stride, HD, 64);
+    BwdArgs a{};
+    a.b = (int)b;
+    a.s = (int)s;
+    a.h = (int)h;
+    a.hkv = (int)hkv;
+    a.causal = causal ? 1 : 0;
+    a.window = (int)window;
+    a.scale = 1.0f / sqrtf((float)HD);
+    a.lse = lse;
+    a.dsum = dsum;
+    a.dq = (bf16*)dq;
+    a.dk = (bf16*)dk;
+    a.dv = (bf16*)dv;
+    a.q_stride = (int)q_stride;
+    a.kv_stride = (int)kv_stride;
+    a.status = c->status;
+    static bool attr[64] = {false};
+    if (!attr[c->device]) {
+        CUDA_OK(cudaFuncSetAttribute(k_dkdv, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_DKDV));
+        CUDA_OK(cudaFuncSetAttribute(k_dq, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_DQ));
+        attr[c->device] = true;
+    }
+    k_dkdv<<<dim3((unsigned)cdiv(s, 128), (unsigned)hkv, (unsigned)b), NT, SMEM_DKDV, c->stream>>>(mk128, mv128, mq64,
+                                                                                                    mdo64, a);
+    k_dq<<<dim3((unsigned)cdiv(s, 128), (unsigned)h, (unsigned)b), NT, SMEM_DQ, c->stream>>>(mq128, mdo128, mk64, mv64,
+                                                                                              a);
+    launched(c, 2);
 }
 
 }  // namespace catnn

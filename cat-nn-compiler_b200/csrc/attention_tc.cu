@@ -512,11 +512,22 @@ __global__ void k_attn_dsum_tc(const T* __restrict__ o, const T* __restrict__ do
     if (lane == 0) dsum[((tok / s) * h + hh) * s + tok % s] = acc;
 }
 
+void attention_bwd_tc5(Context* c, const void* q, const void* k, const void* v, const void* dout, const float* lse,
+                       const float* dsum, void* dq, void* dk, void* dv, i64 b, i64 s, i64 h, i64 hkv, bool causal,
+                       i64 window, i64 q_stride, i64 kv_stride);
+
 void attention_bwd_tc(Context* c, const void* q, const void* k, const void* v, const void* o, const float* lse,
                       const void* dout, void* dq, void* dk, void* dv, i64 b, i64 s, i64 h, i64 hkv, i64 hd, bool causal,
                       i64 window, i64 q_stride, i64 kv_stride) {
     float* dsum = (float*)c->scratch_for((size_t)b * h * s * 4);
     k_attn_dsum_tc<<<cdiv(b * s * h, 4), 128, 0, c->stream>>>((const bf16*)o, (const bf16*)dout, dsum, b, s, h, hd);
+    auto al = [](const void* p) { return ((uintptr_t)p & 15) == 0; };
+    if (hd == 64 && al(dout) && al(dq) && al(dk) && al(dv)) {
+        // tcgen05 + TMEM kernels (q, k, v alignment and pitches were checked by attention_tc_ok)
+        attention_bwd_tc5(c, q, k, v, dout, lse, dsum, dq, dk, dv, b, s, h, hkv, causal, window, q_stride, kv_stride);
+        launched(c);
+        return;
+    }
     fa::Args a = fa_args(q, k, v, b, s, h, hkv, hd, causal, window, q_stride, kv_stride);
     a.o = (const bf16*)o;
     a.dout = (const bf16*)dout;

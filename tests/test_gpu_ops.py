@@ -419,8 +419,8 @@ def test_moe_bf16_grouped_tensor_core():
                                                         (1, 257, 2, 1, 128, True, 100), (1, 1024, 2, 1, 64, True, None),
                                                         (2, 384, 2, 2, 64, False, None), (1, 600, 4, 2, 64, True, 200)])
 def test_attention_core_bf16_tensor_core(b, s, h, kv, hd, causal, window):
-    """Flash attention on the tensor cores (forward: tcgen05 + TMEM for
-    head_dim 64, mma.sync for 128; backward: mma.sync) vs the fp32 attention
+    """Flash attention on the tensor cores (tcgen05 + TMEM for head_dim 64,
+    mma.sync for 128; forward and backward) vs the fp32 attention
     core (itself checked against the oracle's GQA above) on the same bf16
     inputs."""
     r = rng(s + hd)
