@@ -516,12 +516,39 @@ void attention_bwd_tc5(Context* c, const void* q, const void* k, const void* v, 
                        const float* dsum, void* dq, void* dk, void* dv, i64 b, i64 s, i64 h, i64 hkv, bool causal,
                        i64 window, i64 q_stride, i64 kv_stride);
 
+// D = rowsum(O ⊙ dO) for head_dim 64: 8 threads per (token, head) row, one
+// 16-byte load of each operand per thread, a 3-step shuffle sum.
+__global__ void k_attn_dsum64(const bf16* __restrict__ o, const bf16* __restrict__ dout, float* __restrict__ dsum,
+                              i64 rows, i64 s, i64 h) {
+    const i64 row = (blockIdx.x * (i64)blockDim.x + threadIdx.x) >> 3;
+    const int part = threadIdx.x & 7;
+    float acc = 0.f;
+    if (row < rows) {
+        float x[8], y[8];
+        ldv<bf16, 8>(o + row * 64 + part * 8, x);
+        ldv<bf16, 8>(dout + row * 64 + part * 8, y);
+#pragma unroll
+        for (int t = 0; t < 8; ++t) acc = fmaf(x[t], y[t], acc);
+    }
+    acc += __shfl_xor_sync(0xffffffffu, acc, 1);
+    acc += __shfl_xor_sync(0xffffffffu, acc, 2);
+    acc += __shfl_xor_sync(0xffffffffu, acc, 4);
+    if (row < rows && part == 0) {
+        const i64 hh = row % h, tok = row / h;
+        dsum[((tok / s) * h + hh) * s + tok % s] = acc;
+    }
+}
+
 void attention_bwd_tc(Context* c, const void* q, const void* k, const void* v, const void* o, const float* lse,
                       const void* dout, void* dq, void* dk, void* dv, i64 b, i64 s, i64 h, i64 hkv, i64 hd, bool causal,
                       i64 window, i64 q_stride, i64 kv_stride) {
     float* dsum = (float*)c->scratch_for((size_t)b * h * s * 4);
-    k_attn_dsum_tc<<<cdiv(b * s * h, 4), 128, 0, c->stream>>>((const bf16*)o, (const bf16*)dout, dsum, b, s, h, hd);
     auto al = [](const void* p) { return ((uintptr_t)p & 15) == 0; };
+    if (hd == 64 && al(o) && al(dout))
+        k_attn_dsum64<<<cdiv(b * s * h * 8, 256), 256, 0, c->stream>>>((const bf16*)o, (const bf16*)dout, dsum, b * s * h, s,
+                                                                       h);
+    else
+        k_attn_dsum_tc<<<cdiv(b * s * h, 4), 128, 0, c->stream>>>((const bf16*)o, (const bf16*)dout, dsum, b, s, h, hd);
     if (hd == 64 && al(dout) && al(dq) && al(dk) && al(dv)) {
         // tcgen05 + TMEM kernels (q, k, v alignment and pitches were checked by attention_tc_ok)
         attention_bwd_tc5(c, q, k, v, dout, lse, dsum, dq, dk, dv, b, s, h, hkv, causal, window, q_stride, kv_stride);
