@@ -236,14 +236,23 @@ __global__ void k_ln_bwd_rows(const T* __restrict__ x, const float* __restrict__
     }
 }
 
-static const int NCOL_ROWS = 128;
+// Rows per column-partial chunk: 128, or fewer when the rows are few, so
+// that the chunk grid still puts about four CTAs on every SM.
+static int col_chunk_rows(const Context* c, i64 rows, i64 last) {
+    const i64 gx = cdiv(last, 128);
+    const i64 want = cdiv((i64)c->sm_count * 4, gx);
+    i64 cr = cdiv(rows, want);
+    if (cr < 16) cr = 16;
+    if (cr > 128) cr = 128;
+    return (int)cr;
+}
 // Column partials for dgamma (Σ dy·xhat) and dbeta (Σ dy) over a chunk of rows.
 template <typename T>
 __global__ void k_ln_cols(const T* __restrict__ x, const T* __restrict__ dy, const float* __restrict__ stats,
-                          i64 rows, i64 last, float* __restrict__ pg, float* __restrict__ pb) {
+                          i64 rows, i64 last, float* __restrict__ pg, float* __restrict__ pb, int crows) {
     i64 j = blockIdx.x * (i64)blockDim.x + threadIdx.x;
     if (j >= last) return;
-    i64 r0 = (i64)blockIdx.y * NCOL_ROWS, r1 = min(rows, r0 + NCOL_ROWS);
+    i64 r0 = (i64)blockIdx.y * crows, r1 = min(rows, r0 + crows);
     float sg = 0.f, sb = 0.f;
 #pragma unroll 8
     for (i64 r = r0; r < r1; ++r) {
@@ -281,7 +290,8 @@ void layernorm_bwd(Context* c, const void* x, const float* g, const void* dy, vo
         if (db) CUDA_OK(cudaMemsetAsync(db, 0, last * 4, c->stream));
         return;
     }
-    int chunks = cdiv(rows, NCOL_ROWS);
+    const int crows = col_chunk_rows(c, rows, last);
+    int chunks = cdiv(rows, crows);
     size_t need = (size_t)rows * 2 * 4 + (size_t)chunks * last * 4 * 2;
     float* stats = (float*)c->scratch_for(need);
     float* pg = stats + rows * 2;
@@ -290,10 +300,10 @@ void layernorm_bwd(Context* c, const void* x, const float* g, const void* dy, vo
     dim3 gc(cdiv(last, 128), chunks);
     if (dtype == CATNN_BF16) {
         k_ln_bwd_rows<<<rows, t, 0, c->stream>>>((const bf16*)x, g, (const bf16*)dy, (bf16*)dx, stats, last, eps);
-        k_ln_cols<<<gc, 128, 0, c->stream>>>((const bf16*)x, (const bf16*)dy, stats, rows, last, pg, pb);
+        k_ln_cols<<<gc, 128, 0, c->stream>>>((const bf16*)x, (const bf16*)dy, stats, rows, last, pg, pb, crows);
     } else {
         k_ln_bwd_rows<<<rows, t, 0, c->stream>>>((const float*)x, g, (const float*)dy, (float*)dx, stats, last, eps);
-        k_ln_cols<<<gc, 128, 0, c->stream>>>((const float*)x, (const float*)dy, stats, rows, last, pg, pb);
+        k_ln_cols<<<gc, 128, 0, c->stream>>>((const float*)x, (const float*)dy, stats, rows, last, pg, pb, crows);
     }
     if (dg) k_cols_final<<<cdiv(last, 128), 128, 0, c->stream>>>(pg, chunks, last, dg, 0);
     if (db) k_cols_final<<<cdiv(last, 128), 128, 0, c->stream>>>(pb, chunks, last, db, 0);
@@ -345,10 +355,10 @@ __global__ void k_rms_bwd_rows(const T* __restrict__ x, const float* __restrict_
 
 template <typename T>
 __global__ void k_rms_cols(const T* __restrict__ x, const T* __restrict__ dy, const float* __restrict__ invs, i64 rows,
-                           i64 last, float* __restrict__ pw) {
+                           i64 last, float* __restrict__ pw, int crows) {
     i64 j = blockIdx.x * (i64)blockDim.x + threadIdx.x;
     if (j >= last) return;
-    i64 r0 = (i64)blockIdx.y * NCOL_ROWS, r1 = min(rows, r0 + NCOL_ROWS);
+    i64 r0 = (i64)blockIdx.y * crows, r1 = min(rows, r0 + crows);
     float sw = 0.f;
 #pragma unroll 8
     for (i64 r = r0; r < r1; ++r) sw += ld(dy + r * last + j) * ld(x + r * last + j) * invs[r];
@@ -370,17 +380,18 @@ void rmsnorm_bwd(Context* c, const void* x, const float* w, const void* dy, void
         if (dw && !dw_accumulate) CUDA_OK(cudaMemsetAsync(dw, 0, last * 4, c->stream));
         return;
     }
-    int chunks = cdiv(rows, NCOL_ROWS);
+    const int crows = col_chunk_rows(c, rows, last);
+    int chunks = cdiv(rows, crows);
     float* invs = (float*)c->scratch_for((size_t)rows * 4 + (size_t)chunks * last * 4);
     float* pw = invs + rows;
     int t = row_threads(last);
     dim3 gc(cdiv(last, 128), chunks);
     if (dtype == CATNN_BF16) {
         k_rms_bwd_rows<<<rows, t, 0, c->stream>>>((const bf16*)x, w, (const bf16*)dy, (const bf16*)dres, (bf16*)dx, invs, last, eps);
-        if (dw) k_rms_cols<<<gc, 128, 0, c->stream>>>((const bf16*)x, (const bf16*)dy, invs, rows, last, pw);
+        if (dw) k_rms_cols<<<gc, 128, 0, c->stream>>>((const bf16*)x, (const bf16*)dy, invs, rows, last, pw, crows);
     } else {
         k_rms_bwd_rows<<<rows, t, 0, c->stream>>>((const float*)x, w, (const float*)dy, (const float*)dres, (float*)dx, invs, last, eps);
-        if (dw) k_rms_cols<<<gc, 128, 0, c->stream>>>((const float*)x, (const float*)dy, invs, rows, last, pw);
+        if (dw) k_rms_cols<<<gc, 128, 0, c->stream>>>((const float*)x, (const float*)dy, invs, rows, last, pw, crows);
     }
     if (dw) k_cols_final<<<cdiv(last, 128), 128, 0, c->stream>>>(pw, chunks, last, dw, dw_accumulate ? 1 : 0);
     launched(c, dw ? 3 : 1);
@@ -438,10 +449,10 @@ __global__ void k_rms_bwd_mx(const TX* __restrict__ x, const float* __restrict__
 
 template <typename TX, typename TG>
 __global__ void k_rms_cols_mx(const TX* __restrict__ x, const TG* __restrict__ dy, const float* __restrict__ invs, i64 rows,
-                              i64 last, float* __restrict__ pw) {
+                              i64 last, float* __restrict__ pw, int crows) {
     i64 j = blockIdx.x * (i64)blockDim.x + threadIdx.x;
     if (j >= last) return;
-    i64 r0 = (i64)blockIdx.y * NCOL_ROWS, r1 = min(rows, r0 + NCOL_ROWS);
+    i64 r0 = (i64)blockIdx.y * crows, r1 = min(rows, r0 + crows);
     float sw = 0.f;
 #pragma unroll 8
     for (i64 r = r0; r < r1; ++r) sw += ld(dy + r * last + j) * ld(x + r * last + j) * invs[r];
@@ -465,7 +476,8 @@ void rmsnorm_fwd_mixed(Context* c, const void* x, int x_dtype, const float* w, v
 void rmsnorm_bwd_mixed(Context* c, const float* x, const float* w, const void* dy, int g_dtype, const float* dres, float* dx,
                        void* copy, int copy_dtype, float* dw, bool dw_acc, i64 rows, i64 last, float eps) {
     if (rows <= 0 || last <= 0) return;
-    int chunks = cdiv(rows, NCOL_ROWS);
+    const int crows = col_chunk_rows(c, rows, last);
+    int chunks = cdiv(rows, crows);
     float* invs = (float*)c->scratch_for((size_t)rows * 4 + (size_t)chunks * last * 4);
     float* pw = invs + rows;
     int t = row_threads(last);
@@ -474,12 +486,12 @@ void rmsnorm_bwd_mixed(Context* c, const float* x, const float* w, const void* d
         if (copy_dtype == CATNN_BF16 || !copy)
             k_rms_bwd_mx<<<rows, t, 0, c->stream>>>(x, w, (const bf16*)dy, dres, dx, (bf16*)copy, invs, last, eps);
         else k_rms_bwd_mx<<<rows, t, 0, c->stream>>>(x, w, (const bf16*)dy, dres, dx, (float*)copy, invs, last, eps);
-        if (dw) k_rms_cols_mx<<<gc, 128, 0, c->stream>>>(x, (const bf16*)dy, invs, rows, last, pw);
+        if (dw) k_rms_cols_mx<<<gc, 128, 0, c->stream>>>(x, (const bf16*)dy, invs, rows, last, pw, crows);
     } else {
         if (copy_dtype == CATNN_BF16 || !copy)
             k_rms_bwd_mx<<<rows, t, 0, c->stream>>>(x, w, (const float*)dy, dres, dx, (bf16*)copy, invs, last, eps);
         else k_rms_bwd_mx<<<rows, t, 0, c->stream>>>(x, w, (const float*)dy, dres, dx, (float*)copy, invs, last, eps);
-        if (dw) k_rms_cols_mx<<<gc, 128, 0, c->stream>>>(x, (const float*)dy, invs, rows, last, pw);
+        if (dw) k_rms_cols_mx<<<gc, 128, 0, c->stream>>>(x, (const float*)dy, invs, rows, last, pw, crows);
     }
     if (dw) k_cols_final<<<cdiv(last, 128), 128, 0, c->stream>>>(pw, chunks, last, dw, dw_acc ? 1 : 0);
     launched(c, dw ? 3 : 1);
