@@ -16,6 +16,8 @@
 // so no transposed copies of weights or activations are ever made.
 #include <cudaTypedefs.h>
 
+#include <cstring>
+
 #include "ops.cuh"
 #include "tc_prims.cuh"
 
@@ -39,9 +41,13 @@ struct TcArgs {
     int ksplit, kchunk;
     float* part;
     long long c_group_stride_part;  // elements between two slices of part
+    // tma_c: plain full 32-row blocks of C are staged in shared memory and
+    // written by TMA bulk stores of mapC
+    int tma_c;
 };
 
 static constexpr int BM = 128, BK = 64;
+static constexpr uint32_t EPI_STAGE_BYTES = 4 * 8192;
 
 struct TileInfo {
     int g, m0, n0, kstart, klen, mlimit, arow0, ks;
@@ -137,7 +143,8 @@ __device__ __forceinline__ float act_apply(float v, int act) {
 
 template <bool A_MN, bool B_MN, int BN, int STAGES>
 __global__ void __launch_bounds__(192, 1)
-    k_gemm_tc(const __grid_constant__ CUtensorMap mapA, const __grid_constant__ CUtensorMap mapB, TcArgs a) {
+    k_gemm_tc(const __grid_constant__ CUtensorMap mapA, const __grid_constant__ CUtensorMap mapB,
+              const __grid_constant__ CUtensorMap mapC, TcArgs a) {
     constexpr uint32_t A_BYTES = BM * BK * 2;
     constexpr uint32_t B_BYTES = BN * BK * 2;
     constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
@@ -146,7 +153,10 @@ __global__ void __launch_bounds__(192, 1)
 
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
-    uint64_t* full = (uint64_t*)(smem + STAGES * STAGE_BYTES);
+    // epilogue staging for TMA stores: per epilogue warp 8 KB (four 2 KB
+    // bf16 blocks or two 4 KB fp32 blocks of 32 x 32)
+    uint8_t* stage_c = smem + STAGES * STAGE_BYTES;
+    uint64_t* full = (uint64_t*)(stage_c + EPI_STAGE_BYTES);
     uint64_t* empty = full + STAGES;
     uint64_t* tfull = empty + STAGES;
     uint64_t* tempty = tfull + 2;
@@ -263,6 +273,7 @@ __global__ void __launch_bounds__(192, 1)
         const int q = warp & 3;
         const bool plain = !a.bias && !a.resid && a.act == CATNN_ACT_NONE && !a.accumulate;
         int it = 0;
+        uint32_t nst = 0;  // TMA stores issued by this warp (picks the staging buffer)
         for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++it) {
             TileInfo ti = tile_at<BN>(a, t);
             int acc = it & 1;
@@ -274,6 +285,12 @@ __global__ void __launch_bounds__(192, 1)
             if (a.mode == 0) crow = (long long)row * a.ldc;
             else if (a.mode == 1) crow = (long long)(ti.arow0 + row) * a.ldc;
             else crow = (long long)ti.g * a.c_group_stride + (long long)row * a.ldc;
+            // TMA stores for this warp's 32 rows when they are all valid rows of
+            // the output map (warp-uniform; split-K partials keep the direct path)
+            const int row0 = ti.m0 + q * 32;
+            const bool use_tma = a.tma_c && a.ksplit <= 1 && row0 + 32 <= ti.mlimit;
+            const long long ybase =
+                a.mode == 0 ? row0 : (a.mode == 1 ? (long long)ti.arow0 + row0 : (long long)ti.g * a.M + row0);
 #pragma unroll 1
             for (int cc = 0; cc < BN / 32; ++cc) {
                 int col0 = ti.n0 + cc * 32;
@@ -306,6 +323,51 @@ __global__ void __launch_bounds__(192, 1)
                     continue;
                 }
                 bool full_chunk = a.vec_ok && (col0 + 32 <= a.N);
+                if (plain && use_tma) {
+                    // Stage the warp's 32 x 32 block with the store map's swizzle
+                    // (16-byte chunk c of row l at chunk c ^ f(l): conflict-free
+                    // st.shared), then one lane issues an async TMA store: whole
+                    // 64/128-byte row segments, fewer L2 transactions than per-row
+                    // 16-byte stores, no stall of the warp.
+                    const bool z = ti.klen <= 0;
+                    const int nbuf = a.c_bf16 ? 4 : 2;
+                    const uint32_t bbytes = a.c_bf16 ? 2048 : 4096;
+                    const int b = (int)(nst % (uint32_t)nbuf);
+                    const uint32_t sb = tc::smem_u32(stage_c + q * 8192 + b * bbytes);
+                    if (lane == 0) {
+                        if (a.c_bf16) tc::bulk_wait_read<3>();  // this buffer's previous store has read it
+                        else tc::bulk_wait_read<1>();
+                    }
+                    __syncwarp();
+                    if (a.c_bf16) {
+#pragma unroll
+                        for (int c4 = 0; c4 < 4; ++c4) {
+                            uint4 pk;
+                            __nv_bfloat162* pp = (__nv_bfloat162*)&pk;
+#pragma unroll
+                            for (int j = 0; j < 4; ++j)
+                                pp[j] = z ? __floats2bfloat162_rn(0.f, 0.f)
+                                          : __floats2bfloat162_rn(__uint_as_float(r[c4 * 8 + 2 * j]),
+                                                                  __uint_as_float(r[c4 * 8 + 2 * j + 1]));
+                            tc::st_shared_v4(sb + lane * 64 + ((c4 ^ ((lane >> 1) & 3)) << 4), pk);
+                        }
+                    } else {
+#pragma unroll
+                        for (int c8 = 0; c8 < 8; ++c8) {
+                            uint4 pk = z ? make_uint4(0, 0, 0, 0)
+                                         : make_uint4(r[c8 * 4], r[c8 * 4 + 1], r[c8 * 4 + 2], r[c8 * 4 + 3]);
+                            tc::st_shared_v4(sb + lane * 128 + ((c8 ^ (lane & 7)) << 4), pk);
+                        }
+                    }
+                    tc::fence_proxy_async();
+                    __syncwarp();
+                    if (lane == 0) {
+                        tc::tma_store_2d(&mapC, stage_c + q * 8192 + b * bbytes, col0, (int)ybase);
+                        tc::bulk_commit();
+                    }
+                    ++nst;
+                    continue;
+                }
                 if (plain && full_chunk) {
                     // the common case (no bias, residual, activation or
                     // accumulate): convert and store, nothing per element else
@@ -408,6 +470,9 @@ __global__ void __launch_bounds__(192, 1)
             __syncwarp();
             if (lane == 0) tc::mbar_arrive(&tempty[acc]);
         }
+        // the stores must have left shared memory (and landed) before the CTA exits
+        if (lane == 0) tc::bulk_wait_all();
+        __syncwarp();
     }
     tc::tc_fence_before();
     __syncthreads();
@@ -500,6 +565,24 @@ static CUtensorMap make_map(const void* base, i64 rows, i64 cols, i64 ld, int bo
     return m;
 }
 
+// Store map of the epilogue: [rows, cols] with leading dimension ld, box 32
+// x 32; bf16 rows of the box are 64 B (64-byte swizzle), fp32 rows 128 B
+// (128-byte swizzle) — the layouts the epilogue's staging writes follow.
+static CUtensorMap make_store_map(const void* base, i64 rows, i64 cols, i64 ld, bool fp32) {
+    CUtensorMap m;
+    const int es = fp32 ? 4 : 2;
+    cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+    cuuint64_t strides[1] = {(cuuint64_t)(ld * es)};
+    cuuint32_t box[2] = {32, 32};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = encode_fn()(&m, fp32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
+                             const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                             fp32 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
+                             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    CATNN_CHECK(r == CUDA_SUCCESS, CATNN_ERR_CUDA, "cuTensorMapEncodeTiled (store) failed (" + std::to_string((int)r) + ")");
+    return m;
+}
+
 // Shared with the tensor-core attention kernels: a 2-D bf16 load map with
 // 128-byte swizzle over a row-major [rows, cols] matrix (leading dimension ld).
 CUtensorMap tma_map_bf16(const void* base, i64 rows, i64 cols, i64 ld, int box_cols, int box_rows) {
@@ -507,8 +590,10 @@ CUtensorMap tma_map_bf16(const void* base, i64 rows, i64 cols, i64 ld, int box_c
 }
 
 template <bool A_MN, bool B_MN, int BN, int STAGES>
-static void launch_tc(Context* c, const CUtensorMap& ma, const CUtensorMap& mb, const TcArgs& a, int grid) {
-    constexpr size_t smem = (size_t)STAGES * (BM * BK * 2 + BN * BK * 2) + 1024 + 256;
+static void launch_tc(Context* c, const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mc, const TcArgs& a,
+                      int grid) {
+    constexpr size_t smem = (size_t)STAGES * (BM * BK * 2 + BN * BK * 2) + EPI_STAGE_BYTES + 1024 + 256;
+    static_assert(smem <= 232448, "shared memory per CTA");
     static bool attr_set[64] = {false};
     int dev = c->device;
     if (!attr_set[dev]) {
@@ -516,17 +601,17 @@ static void launch_tc(Context* c, const CUtensorMap& ma, const CUtensorMap& mb, 
                                      (int)smem));
         attr_set[dev] = true;
     }
-    k_gemm_tc<A_MN, B_MN, BN, STAGES><<<grid, 192, smem, c->stream>>>(ma, mb, a);
+    k_gemm_tc<A_MN, B_MN, BN, STAGES><<<grid, 192, smem, c->stream>>>(ma, mb, mc, a);
     launched(c);
 }
 
 template <int BN, int STAGES>
 static void dispatch_tc(Context* c, bool a_mn, bool b_mn, const CUtensorMap& ma, const CUtensorMap& mb,
-                        const TcArgs& a, int grid) {
-    if (!a_mn && !b_mn) launch_tc<false, false, BN, STAGES>(c, ma, mb, a, grid);
-    else if (!a_mn && b_mn) launch_tc<false, true, BN, STAGES>(c, ma, mb, a, grid);
-    else if (a_mn && !b_mn) launch_tc<true, false, BN, STAGES>(c, ma, mb, a, grid);
-    else launch_tc<true, true, BN, STAGES>(c, ma, mb, a, grid);
+                        const CUtensorMap& mc, const TcArgs& a, int grid) {
+    if (!a_mn && !b_mn) launch_tc<false, false, BN, STAGES>(c, ma, mb, mc, a, grid);
+    else if (!a_mn && b_mn) launch_tc<false, true, BN, STAGES>(c, ma, mb, mc, a, grid);
+    else if (a_mn && !b_mn) launch_tc<true, false, BN, STAGES>(c, ma, mb, mc, a, grid);
+    else launch_tc<true, true, BN, STAGES>(c, ma, mb, mc, a, grid);
 }
 
 static bool aligned16(const void* p) { return ((uintptr_t)p & 15) == 0; }
@@ -583,10 +668,24 @@ static void run_tc(Context* c, TcArgs a, bool a_mn, bool b_mn, const bf16* A, i6
             grid_bound = (int)std::min<i64>((i64)grid_bound * ks, (i64)c->sm_count);
         }
     }
+    // output map for the plain epilogue's TMA stores (C as one 2-D [rows, N] matrix)
+    CUtensorMap mc;
+    std::memset(&mc, 0, sizeof(mc));
+    a.tma_c = 0;
+    {
+        const int es = a.c_bf16 ? 2 : 4;
+        const i64 crows = a.mode == 2 ? (i64)a.groups * a.M : (i64)a.M;
+        const bool plain = !a.bias && !a.resid && a.act == CATNN_ACT_NONE && !a.accumulate;
+        if (plain && a.ksplit <= 1 && aligned16(a.C) && (a.ldc * es) % 16 == 0 && a.N >= 32 &&
+            (a.mode != 2 || a.c_group_stride == (long long)a.M * a.ldc) && crows < (1ll << 31)) {
+            mc = make_store_map(a.C, crows, a.N, a.ldc, !a.c_bf16);
+            a.tma_c = 1;
+        }
+    }
     int grid = grid_bound < c->sm_count ? grid_bound : c->sm_count;
     if (grid < 1) grid = 1;
-    if (BN == 128) dispatch_tc<128, 6>(c, a_mn, b_mn, ma, mb, a, grid);
-    else dispatch_tc<256, 4>(c, a_mn, b_mn, ma, mb, a, grid);
+    if (BN == 128) dispatch_tc<128, 6>(c, a_mn, b_mn, ma, mb, mc, a, grid);
+    else dispatch_tc<256, 4>(c, a_mn, b_mn, ma, mb, mc, a, grid);
     if (a.ksplit > 1) {
         int g = (int)std::min<i64>(part_rows, (i64)c->sm_count * 16);
         k_splitk_reduce<<<g, 256, 0, c->stream>>>(a, part_rows);
