@@ -128,6 +128,32 @@ template <> struct Pair<bf16> {
     }
 };
 
+// bf16 form: a thread rotates 4 consecutive pairs (one 16-byte load and
+// store); same arithmetic per pair as k_rope.
+__global__ void __launch_bounds__(256) k_rope8(bf16* __restrict__ x, const float2* __restrict__ tab, i64 b, i64 s,
+                                               int heads, int hd, int inverse, i64 row_stride, i64 col_off) {
+    const int half = hd / 2, groups = heads * half / 4;  // 4 pairs per group (half % 4 == 0)
+    for (i64 tok = blockIdx.x; tok < b * s; tok += gridDim.x) {
+        const float2* trow = tab + (tok % s) * half;
+        bf16* xr = x + tok * row_stride + col_off;
+        for (int g = threadIdx.x; g < groups; g += blockDim.x) {
+            const int j0 = g * 4, h = j0 / half, i0 = j0 - h * half;
+            bf16* p = xr + h * hd + 2 * i0;
+            float v[8];
+            ldv<bf16, 8>(p, v);
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                float2 cs_sn = trow[i0 + u];
+                float cs = cs_sn.x, sn = inverse ? -cs_sn.y : cs_sn.y;
+                float a0 = v[2 * u], b0 = v[2 * u + 1];
+                v[2 * u] = __fsub_rn(__fmul_rn(a0, cs), __fmul_rn(b0, sn));
+                v[2 * u + 1] = __fadd_rn(__fmul_rn(a0, sn), __fmul_rn(b0, cs));
+            }
+            stv<bf16, 8>(p, v);
+        }
+    }
+}
+
 // CTAs stride over token rows, threads over the (head, pair) slots of a row.
 template <typename T>
 __global__ void __launch_bounds__(256) k_rope(T* __restrict__ x, const float2* __restrict__ tab, i64 b, i64 s, int heads,
@@ -177,7 +203,10 @@ void rope(Context* c, void* x, i64 b, i64 s, i64 heads, i64 hd, double theta, bo
                 "rope: head dim, row stride and column offset must be even");
     CATNN_CHECK(aligned_to(x, dtype == CATNN_BF16 ? 4 : 8), CATNN_ERR_INVALID, "rope: misaligned tensor");
     int grid = (int)std::min<i64>(b * s, (i64)c->sm_count * 16);
-    if (dtype == CATNN_BF16)
+    if (dtype == CATNN_BF16 && (hd / 2) % 4 == 0 && row_stride % 8 == 0 && col_off % 8 == 0 && aligned_to(x, 16))
+        k_rope8<<<grid, 256, 0, c->stream>>>((bf16*)x, tab, b, s, (int)heads, (int)hd, inverse ? 1 : 0, row_stride,
+                                             col_off);
+    else if (dtype == CATNN_BF16)
         k_rope<<<grid, 256, 0, c->stream>>>((bf16*)x, tab, b, s, (int)heads, (int)hd, inverse ? 1 : 0, row_stride,
                                             col_off);
     else

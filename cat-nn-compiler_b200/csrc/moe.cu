@@ -124,6 +124,119 @@ __global__ void __launch_bounds__(1024) k_permute_map(const int32_t* __restrict_
     for (i64 r = off[E] + tid; r < rows_cap; r += nt) src_of[r] = -1;
 }
 
+// ---- the same stable counting sort across many CTAs (large pair counts)
+// Chunk g of PM_CHUNK pairs: per-expert histogram -> hist[g][E].
+constexpr int PM_CHUNK = 1024, PM_THREADS = 256;
+__global__ void __launch_bounds__(PM_THREADS) k_pm_hist(const int32_t* __restrict__ idx, i64 P, int E,
+                                                        int32_t* __restrict__ hist, int* __restrict__ err) {
+    __shared__ int h[32];
+    if (threadIdx.x < 32) h[threadIdx.x] = 0;
+    __syncthreads();
+    const i64 p0 = (i64)blockIdx.x * PM_CHUNK, p1 = min(P, p0 + PM_CHUNK);
+    for (i64 p = p0 + threadIdx.x; p < p1; p += PM_THREADS) {
+        int e = idx[p];
+        if (e < 0 || e >= E) {
+            atomicExch(err, 1);
+            continue;
+        }
+        atomicAdd(&h[e], 1);
+    }
+    __syncthreads();
+    if (threadIdx.x < E) hist[(i64)blockIdx.x * E + threadIdx.x] = h[threadIdx.x];
+}
+
+// One CTA: per expert, chunk bases in chunk order (hist becomes the base of
+// each chunk's first pair of that expert), counts, padded offsets.
+__global__ void k_pm_scan(int32_t* __restrict__ hist, int G, int E, int align, int32_t* __restrict__ counts,
+                          int32_t* __restrict__ offsets, i64 rows_cap, int* __restrict__ err) {
+    __shared__ int tot[33], off[33];
+    const int e = threadIdx.x;
+    if (e < E) {
+        int run = 0;
+        for (int g = 0; g < G; ++g) {
+            int v = hist[(i64)g * E + e];
+            hist[(i64)g * E + e] = run;
+            run += v;
+        }
+        tot[e] = run;
+        counts[e] = run;
+    }
+    __syncthreads();
+    if (e == 0) {
+        int o = 0;
+        for (int x = 0; x < E; ++x) {
+            off[x] = o;
+            offsets[x] = o;
+            o += (tot[x] + align - 1) / align * align;
+        }
+        off[E] = o;
+        offsets[E] = o;
+        if ((i64)o > rows_cap) atomicExch(err, 2);
+    }
+    __syncthreads();
+    if (e < E)
+        for (int g = 0; g < G; ++g) hist[(i64)g * E + e] += off[e];
+}
+
+// Chunk g places its pairs in pair order: rounds of PM_THREADS pairs, the
+// rank among equal experts inside a warp from __match_any_sync, warps in
+// order through a shared-memory prefix, chunk base from k_pm_scan.
+__global__ void __launch_bounds__(PM_THREADS) k_pm_place(const int32_t* __restrict__ idx, i64 P, int E,
+                                                         const int32_t* __restrict__ base, const int32_t* __restrict__ offsets,
+                                                         i64 rows_cap, int32_t* __restrict__ row_of,
+                                                         int32_t* __restrict__ src_of) {
+    __shared__ int run[32], wcnt[PM_THREADS / 32][32], wpre[PM_THREADS / 32][32];
+    if ((i64)offsets[E] > rows_cap) return;  // flagged by k_pm_scan; nothing is placed
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (threadIdx.x < E) run[threadIdx.x] = base[(i64)blockIdx.x * E + threadIdx.x];
+    const i64 p0 = (i64)blockIdx.x * PM_CHUNK, p1 = min(P, p0 + PM_CHUNK);
+    for (i64 rb = p0; rb < p1; rb += PM_THREADS) {
+        for (int i = threadIdx.x; i < (PM_THREADS / 32) * 32; i += PM_THREADS) (&wcnt[0][0])[i] = 0;
+        __syncthreads();
+        const i64 p = rb + threadIdx.x;
+        int e = p < p1 ? idx[p] : -1;
+        if (e >= E) e = -1;
+        const unsigned same = __match_any_sync(0xffffffffu, e);
+        const int rank = __popc(same & ((1u << lane) - 1u));
+        if (e >= 0 && rank == 0) wcnt[warp][e] = __popc(same);
+        __syncthreads();
+        if (threadIdx.x < E) {
+            int r = run[threadIdx.x];
+            for (int w = 0; w < PM_THREADS / 32; ++w) {
+                wpre[w][threadIdx.x] = r;
+                r += wcnt[w][threadIdx.x];
+            }
+            run[threadIdx.x] = r;
+        }
+        __syncthreads();
+        if (e >= 0) {
+            const int row = wpre[warp][e] + rank;
+            row_of[p] = row;
+            src_of[row] = (int32_t)p;
+        }
+        __syncthreads();
+    }
+}
+
+// src_of = -1 on every padding row and on the rows past the last expert.
+__global__ void k_pm_pad(const int32_t* __restrict__ counts, const int32_t* __restrict__ offsets, int E, i64 rows_cap,
+                         int32_t* __restrict__ src_of) {
+    __shared__ int off[33], cnt[32];
+    if (threadIdx.x <= E) off[threadIdx.x] = offsets[threadIdx.x];
+    if (threadIdx.x < E) cnt[threadIdx.x] = counts[threadIdx.x];
+    __syncthreads();
+    if ((i64)off[E] > rows_cap) return;
+    for (i64 r = blockIdx.x * (i64)blockDim.x + threadIdx.x; r < rows_cap; r += (i64)gridDim.x * blockDim.x) {
+        bool pad = r >= off[E];
+        if (!pad) {
+            int e = 0;
+            while (e + 1 < E && r >= off[e + 1]) ++e;
+            pad = r >= off[e] + cnt[e];
+        }
+        if (pad) src_of[r] = -1;
+    }
+}
+
 void permute_map(Context* c, const int32_t* idx, i64 T, i64 E, i64 k, int align, i64 rows_cap, int32_t* counts,
                  int32_t* offsets, int32_t* row_of, int32_t* src_of) {
     if (T <= 0) {
@@ -135,6 +248,17 @@ void permute_map(Context* c, const int32_t* idx, i64 T, i64 E, i64 k, int align,
     CATNN_CHECK(align >= 1, CATNN_ERR_INVALID, "permute_map: align >= 1");
     i64 P = T * k;
     CATNN_CHECK(P < (1ll << 31), CATNN_ERR_SHAPE, "permute_map: too many pairs");
+    if (P > 4 * PM_CHUNK) {
+        const i64 G = cdiv(P, PM_CHUNK);
+        int32_t* hist = (int32_t*)c->scratch_for((size_t)G * E * 4);
+        k_pm_hist<<<(unsigned)G, PM_THREADS, 0, c->stream>>>(idx, P, (int)E, hist, c->status + 8);
+        k_pm_scan<<<1, 32, 0, c->stream>>>(hist, (int)G, (int)E, align, counts, offsets, rows_cap, c->status + 8);
+        k_pm_place<<<(unsigned)G, PM_THREADS, 0, c->stream>>>(idx, P, (int)E, hist, offsets, rows_cap, row_of, src_of);
+        k_pm_pad<<<(unsigned)std::min<i64>(cdiv(rows_cap, 256), (i64)c->sm_count * 8), 256, 0, c->stream>>>(
+            counts, offsets, (int)E, rows_cap, src_of);
+        launched(c, 4);
+        return;
+    }
     size_t smem = (size_t)(1024 * E + E + 1) * 4;
     static bool attr[64] = {false};
     if (!attr[c->device]) {
@@ -196,10 +320,81 @@ __global__ void k_unpermute(const TI* __restrict__ yp, const int32_t* __restrict
     }
 }
 
+// Vector form of k_unpermute (same arithmetic per element): CTAs stride over
+// tokens, threads over V-wide column groups with 16-byte accesses.
+template <typename TI, typename T, int V>
+__global__ void __launch_bounds__(128) k_unpermute_v(const TI* __restrict__ yp, const int32_t* __restrict__ row_of,
+                                                     const float* __restrict__ w, i64 Tn, int k, i64 hidden,
+                                                     T* __restrict__ y, int acc, const T* __restrict__ resid) {
+    for (i64 t = blockIdx.x; t < Tn; t += gridDim.x) {
+        for (i64 c = (i64)threadIdx.x * V; c < hidden; c += (i64)blockDim.x * V) {
+            float s[V];
+#pragma unroll
+            for (int u = 0; u < V; ++u) s[u] = 0.f;
+            for (int j = 0; j < k; ++j) {
+                const i64 r = row_of[t * k + j];
+                const float wt = w[t * k + j];
+                float v[V];
+                ldv<TI, V>(yp + r * hidden + c, v);
+#pragma unroll
+                for (int u = 0; u < V; ++u) s[u] = __fadd_rn(s[u], __fmul_rn(wt, v[u]));
+            }
+            if (acc) {
+                float o[V];
+                ldv<T, V>(y + t * hidden + c, o);
+#pragma unroll
+                for (int u = 0; u < V; ++u) s[u] = __fadd_rn(o[u], s[u]);
+            }
+            if (resid) {
+                float o[V];
+                ldv<T, V>(resid + t * hidden + c, o);
+#pragma unroll
+                for (int u = 0; u < V; ++u) s[u] = __fadd_rn(o[u], s[u]);
+            }
+            stv<T, V>(y + t * hidden + c, s);
+        }
+    }
+}
+
+// Vector form of k_permute_bwd (same arithmetic per element).
+template <typename TI, typename T, int V>
+__global__ void __launch_bounds__(128) k_permute_bwd_v(const TI* __restrict__ dxp, const int32_t* __restrict__ row_of,
+                                                       i64 Tn, int k, i64 hidden, T* __restrict__ dx, int acc) {
+    for (i64 t = blockIdx.x; t < Tn; t += gridDim.x) {
+        for (i64 c = (i64)threadIdx.x * V; c < hidden; c += (i64)blockDim.x * V) {
+            float s[V];
+#pragma unroll
+            for (int u = 0; u < V; ++u) s[u] = 0.f;
+            for (int j = 0; j < k; ++j) {
+                float v[V];
+                ldv<TI, V>(dxp + (i64)row_of[t * k + j] * hidden + c, v);
+#pragma unroll
+                for (int u = 0; u < V; ++u) s[u] = __fadd_rn(s[u], v[u]);
+            }
+            if (acc) {
+                float o[V];
+                ldv<T, V>(dx + t * hidden + c, o);
+#pragma unroll
+                for (int u = 0; u < V; ++u) s[u] = __fadd_rn(o[u], s[u]);
+            }
+            stv<T, V>(dx + t * hidden + c, s);
+        }
+    }
+}
+
 void unpermute_rows(Context* c, const void* yp, const int32_t* row_of, const float* w, i64 T, i64 k, i64 hidden, void* y,
                     int dtype, bool accumulate, int yp_dtype, const void* resid) {
     if (T <= 0 || hidden <= 0) return;
     if (yp_dtype < 0) yp_dtype = dtype;
+    if (yp_dtype == CATNN_BF16 && dtype == CATNN_F32 && hidden % 8 == 0 && aligned_to(yp, 16) && aligned_to(y, 16) &&
+        aligned_to(resid, 16)) {
+        // the trainer's combine: bf16 expert rows into the fp32 residual stream
+        const int grid = (int)std::min<i64>(T, (i64)c->sm_count * 16);
+        k_unpermute_v<bf16, float, 8><<<grid, 128, 0, c->stream>>>((const bf16*)yp, row_of, w, T, (int)k, hidden,
+                                                                   (float*)y, accumulate ? 1 : 0, (const float*)resid);
+        launched(c);
+        return;
+    }
     CATNN_CHECK(T <= 2147483647ll, CATNN_ERR_SHAPE, "unpermute: too many tokens");
     dim3 grid(cdiv(hidden, 256), (unsigned)T);
     int acc = accumulate ? 1 : 0;
@@ -281,6 +476,13 @@ void permute_bwd(Context* c, const void* dxp, const int32_t* row_of, i64 T, i64 
                  bool accumulate, int out_dtype) {
     if (T <= 0 || hidden <= 0) return;
     if (out_dtype < 0) out_dtype = dtype;
+    if (dtype == CATNN_BF16 && out_dtype == CATNN_F32 && hidden % 8 == 0 && aligned_to(dxp, 16) && aligned_to(dx, 16)) {
+        const int grid = (int)std::min<i64>(T, (i64)c->sm_count * 16);
+        k_permute_bwd_v<bf16, float, 8><<<grid, 128, 0, c->stream>>>((const bf16*)dxp, row_of, T, (int)k, hidden,
+                                                                     (float*)dx, accumulate ? 1 : 0);
+        launched(c);
+        return;
+    }
     dim3 grid(cdiv(hidden, 256), (unsigned)T);
     if (dtype == CATNN_BF16 && out_dtype == CATNN_F32)
         k_permute_bwd<<<grid, 256, 0, c->stream>>>((const bf16*)dxp, row_of, T, (int)k, hidden, (float*)dx, accumulate);

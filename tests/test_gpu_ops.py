@@ -221,10 +221,12 @@ def test_router_topk_bit_exact():
     assert abs(float(host(w).sum()) - 1.0) < 1e-6
 
 
-@pytest.mark.parametrize("align", [1, 128])
-def test_permute_map_stable(align):
-    r = rng(13)
-    T, E, k = 1000, 8, 2
+@pytest.mark.parametrize("align,T,E", [(1, 1000, 8), (128, 1000, 8), (1, 16384, 8), (128, 16384, 8), (128, 7000, 32)])
+def test_permute_map_stable(align, T, E):
+    """Counting-sort permutation (single-CTA below 4096 pairs, multi-CTA
+    histogram / scan / stable place above) against numpy's stable sort."""
+    r = rng(13 + T)
+    k = 2
     logits = r.standard_normal((T, E)).astype(np.float32)
     idx, _ = ops.router_topk(dev(logits), k)
     counts, offsets, row_of, src_of = ops.moe_permute_map(idx, E, align)
