@@ -65,6 +65,20 @@ void softmax_bwd(Context* c, const void* y, const void* dy, void* dx, i64 rows, 
 // then dlogits = p / rows with 1/rows taken off at the target, and the row
 // loss -ln(max(p_t, 1e-30)) into a per-row buffer that a single CTA sums in
 // row order.
+// e^x for the row kernels: on bf16 logits 2^(x·log2 e) with the MUFU
+// ex2.approx instruction (relative error ~1e-7, far below bf16's 4e-3);
+// fp32 logits keep expf (the fp32 path is held to the reference at 1e-5).
+template <typename T>
+__device__ __forceinline__ float row_exp(float x) {
+    if constexpr (sizeof(T) == 2) {
+        float y;
+        asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x * 1.4426950408889634f));
+        return y;
+    } else {
+        return expf(x);
+    }
+}
+
 // V-wide accesses along the row (16 bytes when aligned); the running
 // (max, sum) pair is rescaled once per vector.
 template <typename T, int V>
@@ -84,14 +98,14 @@ __global__ void k_xent_rows(const T* __restrict__ logits, const uint32_t* __rest
 #pragma unroll
         for (int j = 1; j < V; ++j) lm = fmaxf(lm, x[j]);
         if (lm > m) {
-            s = s * expf(m - lm);
+            s = s * row_exp<T>(m - lm);
             m = lm;
         }
 #pragma unroll
-        for (int j = 0; j < V; ++j) s += expf(x[j] - m);
+        for (int j = 0; j < V; ++j) s += row_exp<T>(x[j] - m);
     }
     float gm = block_max(m, red);
-    float sc = (m == -INFINITY) ? 0.f : s * expf(m - gm);
+    float sc = (m == -INFINITY) ? 0.f : s * row_exp<T>(m - gm);
     float gs = block_sum(sc, red);
     if (threadIdx.x == 0) {
         sh_m = gm;
@@ -108,7 +122,7 @@ __global__ void k_xent_rows(const T* __restrict__ logits, const uint32_t* __rest
         ldv<T, V>(in + i, x);
 #pragma unroll
         for (int j = 0; j < V; ++j) {
-            float p = expf(x[j] - sh_m) * inv;
+            float p = row_exp<T>(x[j] - sh_m) * inv;
             float d = p * rinv;
             if (i + j == (i64)t) {
                 d = d - rinv;
@@ -473,9 +487,163 @@ void rmsnorm_fwd_mixed(Context* c, const void* x, int x_dtype, const float* w, v
     launched(c);
 }
 
+// Fused RMSNorm backward for widths that are multiples of 1024 (<= 4096):
+// a CTA of 256 threads owns a chunk of rows, each thread 4 columns per
+// 1024; rows go 4 at a time (their loads in flight together, one block
+// reduction for the 8 row sums). x and dy stay in registers between the row
+// statistics and dx, and the weight-gradient partial Σ dy·x·inv of the
+// chunk accumulates in registers: no second pass over x and dy.
+constexpr int RB_ROWS = 4;
+template <typename TG, typename TC, int NC>
+__global__ void __launch_bounds__(256) k_rms_bwd_fused(const float* __restrict__ x, const float* __restrict__ w,
+                                                       const TG* __restrict__ dy, const float* __restrict__ dres,
+                                                       float* __restrict__ dx, TC* __restrict__ copy, i64 rows,
+                                                       int crows, float* __restrict__ pw, float eps) {
+    constexpr int last = NC * 1024;
+    __shared__ float red[8][2 * RB_ROWS];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const float n = (float)last;
+    float wv[NC][4], sw[NC][4];
+#pragma unroll
+    for (int g = 0; g < NC; ++g) {
+        ldv<float, 4>(w + g * 1024 + threadIdx.x * 4, wv[g]);
+#pragma unroll
+        for (int u = 0; u < 4; ++u) sw[g][u] = 0.f;
+    }
+    const i64 r0 = (i64)blockIdx.x * crows, r1 = min(rows, r0 + crows);
+    for (i64 rb = r0; rb < r1; rb += RB_ROWS) {
+        float xv[RB_ROWS][NC][4], gv[RB_ROWS][NC][4], part[2 * RB_ROWS];
+#pragma unroll
+        for (int q = 0; q < RB_ROWS; ++q) {
+            part[2 * q] = part[2 * q + 1] = 0.f;
+            const i64 r = rb + q;
+            if (r < r1) {
+#pragma unroll
+                for (int g = 0; g < NC; ++g) {
+                    const i64 o = r * last + g * 1024 + threadIdx.x * 4;
+                    ldv<float, 4>(x + o, xv[q][g]);
+                    ldv<TG, 4>(dy + o, gv[q][g]);
+                }
+            } else {
+#pragma unroll
+                for (int g = 0; g < NC; ++g)
+#pragma unroll
+                    for (int u = 0; u < 4; ++u) xv[q][g][u] = gv[q][g][u] = 0.f;
+            }
+#pragma unroll
+            for (int g = 0; g < NC; ++g)
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                    part[2 * q] += xv[q][g][u] * xv[q][g][u];
+                    part[2 * q + 1] += gv[q][g][u] * xv[q][g][u] * wv[g][u];
+                }
+        }
+#pragma unroll
+        for (int i = 0; i < 2 * RB_ROWS; ++i) part[i] = warp_sum(part[i]);
+        __syncthreads();  // the previous rows' reads of red are done
+        if (lane == 0)
+#pragma unroll
+            for (int i = 0; i < 2 * RB_ROWS; ++i) red[warp][i] = part[i];
+        __syncthreads();
+#pragma unroll
+        for (int q = 0; q < RB_ROWS; ++q) {
+            const i64 r = rb + q;
+            if (r >= r1) break;
+            float ssum = 0.f, di = 0.f;
+#pragma unroll
+            for (int k = 0; k < 8; ++k) {
+                ssum += red[k][2 * q];
+                di += red[k][2 * q + 1];
+            }
+            const float ms = ssum / n;
+            const float inv = 1.0f / sqrtf(ms + eps);
+            const float dms = di * -0.5f * powf(ms + eps, -1.5f);
+#pragma unroll
+            for (int g = 0; g < NC; ++g) {
+                const i64 o = r * last + g * 1024 + threadIdx.x * 4;
+                float out[4], dr[4];
+                if (dres) ldv<float, 4>(dres + o, dr);
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                    const float v = xv[q][g][u];
+                    float rr = gv[q][g][u] * inv * wv[g][u] + dms * (2.0f * v / n);
+                    if (dres) rr += dr[u];
+                    out[u] = rr;
+                    sw[g][u] += gv[q][g][u] * v * inv;
+                }
+                stv<float, 4>(dx + o, out);
+                if (copy) stv<TC, 4>(copy + o, out);
+            }
+        }
+    }
+    if (pw) {
+#pragma unroll
+        for (int g = 0; g < NC; ++g) stv<float, 4>(pw + (i64)blockIdx.x * last + g * 1024 + threadIdx.x * 4, sw[g]);
+    }
+}
+
+// Sums the chunk partials of k_rms_bwd_fused: 32 columns x 8 slices per CTA,
+// slice j adds chunks j, j+8, ... in order, slices are added 0..7.
+__global__ void __launch_bounds__(256) k_cols_final8(const float* __restrict__ p, int chunks, i64 last,
+                                                     float* __restrict__ out, int acc) {
+    __shared__ float red[8][33];
+    const int col = threadIdx.x & 31, slice = threadIdx.x >> 5;
+    const i64 j = (i64)blockIdx.x * 32 + col;
+    float s = 0.f;
+    if (j < last) {
+#pragma unroll 4
+        for (int ch = slice; ch < chunks; ch += 8) s += p[(i64)ch * last + j];
+    }
+    red[slice][col] = s;
+    __syncthreads();
+    if (slice == 0 && j < last) {
+        float t = red[0][col];
+#pragma unroll
+        for (int k = 1; k < 8; ++k) t += red[k][col];
+        out[j] = acc ? out[j] + t : t;
+    }
+}
+
+template <typename TG, typename TC>
+static bool rms_bwd_fused(Context* c, const float* x, const float* w, const TG* dy, const float* dres, float* dx, TC* copy,
+                          float* dw, bool dw_acc, i64 rows, i64 last, float eps) {
+    const int nc = (int)(last / 1024);
+    if (last % 1024 != 0 || nc < 1 || nc > 4) return false;
+    if (!aligned_to(x, 16) || !aligned_to(w, 16) || !aligned_to(dy, 16) || !aligned_to(dres, 16) ||
+        !aligned_to(dx, 16) || !aligned_to(copy, 16))
+        return false;
+    // chunks: enough CTAs to fill the GPU, a multiple of RB_ROWS rows each
+    i64 crows = cdiv(rows, (i64)c->sm_count * 4);
+    crows = std::max<i64>(RB_ROWS, cdiv(crows, RB_ROWS) * RB_ROWS);
+    const int chunks = (int)cdiv(rows, crows);
+    float* pw = dw ? (float*)c->scratch_for((size_t)chunks * last * 4) : nullptr;
+#define RBF(NCV) \
+    k_rms_bwd_fused<TG, TC, NCV><<<chunks, 256, 0, c->stream>>>(x, w, dy, dres, dx, copy, rows, (int)crows, pw, eps)
+    if (nc == 1) RBF(1);
+    else if (nc == 2) RBF(2);
+    else if (nc == 3) RBF(3);
+    else RBF(4);
+#undef RBF
+    if (dw) k_cols_final8<<<(unsigned)cdiv(last, 32), 256, 0, c->stream>>>(pw, chunks, last, dw, dw_acc ? 1 : 0);
+    launched(c, dw ? 2 : 1);
+    return true;
+}
+
 void rmsnorm_bwd_mixed(Context* c, const float* x, const float* w, const void* dy, int g_dtype, const float* dres, float* dx,
                        void* copy, int copy_dtype, float* dw, bool dw_acc, i64 rows, i64 last, float eps) {
     if (rows <= 0 || last <= 0) return;
+    {
+        bool done;
+        if (g_dtype == CATNN_BF16)
+            done = (copy_dtype == CATNN_BF16 || !copy)
+                       ? rms_bwd_fused(c, x, w, (const bf16*)dy, dres, dx, (bf16*)copy, dw, dw_acc, rows, last, eps)
+                       : rms_bwd_fused(c, x, w, (const bf16*)dy, dres, dx, (float*)copy, dw, dw_acc, rows, last, eps);
+        else
+            done = (copy_dtype == CATNN_BF16 || !copy)
+                       ? rms_bwd_fused(c, x, w, (const float*)dy, dres, dx, (bf16*)copy, dw, dw_acc, rows, last, eps)
+                       : rms_bwd_fused(c, x, w, (const float*)dy, dres, dx, (float*)copy, dw, dw_acc, rows, last, eps);
+        if (done) return;
+    }
     const int crows = col_chunk_rows(c, rows, last);
     int chunks = cdiv(rows, crows);
     float* invs = (float*)c->scratch_for((size_t)rows * 4 + (size_t)chunks * last * 4);

@@ -117,8 +117,11 @@ def test_mixtral_tiny_shape_fp32():
                 exact=True)
 
 
-def test_moe_sweep_shape_bf16_adam():
-    """Reduced config 5 (bf16 compute, fp32 master, fp32 router, Adam) vs the fp32 oracle.
+@pytest.mark.parametrize("hidden,mid,layers,heads,batch,seq", [(256, 512, 2, 4, 2, 128), (1024, 1024, 1, 16, 1, 256)])
+def test_moe_sweep_shape_bf16_adam(hidden, mid, layers, heads, batch, seq):
+    """Reduced config 5 (bf16 compute, fp32 master, fp32 router, Adam) vs the fp32 oracle;
+    the second case has config 5's width (d 1024, 16 heads of 64), which takes the
+    width-specific kernels (fused RMSNorm backward, tcgen05 attention).
 
     Top-k routing is discontinuous: bf16 rounding of the attention branch
     (~0.2%) moves a few tokens across a near-tie, and those tokens then
@@ -127,8 +130,8 @@ def test_moe_sweep_shape_bf16_adam():
     comparison, and the fraction of decisions that differ from the free
     oracle is bounded separately. The oracle reads the weights the tensor
     cores consume (tc_inputs)."""
-    cfg = MoeConfig.make(2048, 256, 512, 2, 4, 4, 8, 2, batch=2, seq=128, rope_theta=1e6, dtype=torch.bfloat16,
-                         optimizer="adam", lr=1e-3)
+    cfg = MoeConfig.make(2048, hidden, mid, layers, heads, heads, 8, 2, batch=batch, seq=seq, rope_theta=1e6,
+                         dtype=torch.bfloat16, optimizer="adam", lr=1e-3)
     P = init_params(cfg, 4)
     tokens = np.random.default_rng(4).integers(0, 2048, cfg.batch * cfg.seq)
     tr = MoeTrainer(cfg)
