@@ -337,6 +337,9 @@ __global__ void __launch_bounds__(NT, 2)
 // layout (128-byte rows, 16-byte chunks XOR-swizzled by row).
 
 constexpr int BB = 64;                           // the looped block (queries in k_dkdv, keys in k_dq)
+// 8 compute warps: two per TMEM lane quadrant, each takes 32 of the 64
+// columns of its rows (the backward has no row reductions to combine)
+constexpr int NTB = 320, NCW = 8;
 constexpr uint32_t T64 = 64 * HD * 2;            // 8 KB: a 64-row tile
 constexpr uint32_t T128 = 128 * HD * 2;          // 16 KB: a 128-row tile
 constexpr uint32_t QD_STAGE = 2 * T64 + 1024;    // Q, dO and the block's L, D
@@ -386,7 +389,7 @@ __device__ __forceinline__ void ld_row64(uint32_t taddr, uint32_t (&v)[64]) {
     tc::tmem_ld32(taddr + 32, v1);
 }
 
-__global__ void __launch_bounds__(NT, 2)
+__global__ void __launch_bounds__(NTB, 2)
     k_dkdv(const __grid_constant__ CUtensorMap mk, const __grid_constant__ CUtensorMap mv,
            const __grid_constant__ CUtensorMap mq, const __grid_constant__ CUtensorMap mdo, BwdArgs a) {
     extern __shared__ uint8_t smem_raw[];
@@ -425,8 +428,8 @@ __global__ void __launch_bounds__(NT, 2)
             tc::mbar_init(&qd_empty[i], 1);
         }
         tc::mbar_init(st_full, 1);
-        tc::mbar_init(st_free, 4);
-        tc::mbar_init(pd_full, 4);
+        tc::mbar_init(st_free, NCW);
+        tc::mbar_init(pd_full, NCW);
         tc::mbar_init(pd_free, 1);
         tc::mbar_init(acc_full, 1);
         tc::mbar_init(drain, 1);
@@ -486,13 +489,13 @@ __global__ void __launch_bounds__(NT, 2)
             bool ok = tc::mbar_wait(kv_full, 0, a.status, 4);
             const uint32_t aK = tc::smem_u32(sK), aV = tc::smem_u32(sV);
             const uint32_t aP = tc::smem_u32(sP), aDS = tc::smem_u32(sDS);
-            for (int it = 0; it < n && ok; ++it) {
+            // Sᵀ, dPᵀ of block it: issued as soon as the compute warps hold the
+            // previous block's in registers, so they overlap that block's math
+            auto issue_st = [&](int it) -> bool {
                 const int st = it & 1;
                 if (!tc::mbar_wait(&qd_full[st], (it >> 1) & 1, a.status, 4) ||
-                    !tc::mbar_wait(st_free, (it & 1) ^ 1, a.status, 4)) {
-                    ok = false;
-                    break;
-                }
+                    !tc::mbar_wait(st_free, (it & 1) ^ 1, a.status, 4))
+                    return false;
                 tc::tc_fence_after();
                 const uint32_t bQ = tc::smem_u32(sQD + st * QD_STAGE), bO = bQ + T64;
 #pragma unroll
@@ -504,6 +507,16 @@ __global__ void __launch_bounds__(NT, 2)
                     tc::mma_bf16(tmem + C_DP, tc::sdesc(aV + kk * 32, 16, 1024), tc::sdesc(bO + kk * 32, 16, 1024), ID_T,
                                  kk != 0);
                 tc::mma_commit(st_full);
+                return true;
+            };
+            if (ok && n > 0) ok = issue_st(0);
+            for (int it = 0; it < n && ok; ++it) {
+                const int st = it & 1;
+                const uint32_t bQ = tc::smem_u32(sQD + st * QD_STAGE), bO = bQ + T64;
+                if (it + 1 < n && !issue_st(it + 1)) {
+                    ok = false;
+                    break;
+                }
                 if (!tc::mbar_wait(pd_full, it & 1, a.status, 4)) {
                     ok = false;
                     break;
@@ -525,8 +538,8 @@ __global__ void __launch_bounds__(NT, 2)
             tc::mbar_wait(drain, 0, a.status, 4, 400000000ll, false);
         }
     } else {
-        // ---------------- compute: thread = key row
-        const int qd = warp & 3;
+        // ---------------- compute: thread = key row, 32 of its 64 query columns
+        const int qd = warp & 3, c0 = ((warp - 2) >> 2) * 32;
         const int r = qd * 32 + lane;
         const int key = k0 + r;
         const uint32_t lane_off = (uint32_t)(qd * 32) << 16;
@@ -542,9 +555,9 @@ __global__ void __launch_bounds__(NT, 2)
                 break;
             }
             tc::tc_fence_after();
-            uint32_t s[64], dp[64];
-            ld_row64(tmem + lane_off + C_S, s);
-            ld_row64(tmem + lane_off + C_DP, dp);
+            uint32_t s[32], dp[32];
+            tc::tmem_ld32(tmem + lane_off + C_S + c0, s);
+            tc::tmem_ld32(tmem + lane_off + C_DP + c0, dp);
             tc::tmem_ld_wait();
             tc::tc_fence_before();
             __syncwarp();
@@ -560,18 +573,22 @@ __global__ void __launch_bounds__(NT, 2)
                 break;
             }
 #pragma unroll
-            for (int chunk = 0; chunk < 8; ++chunk) {
+            for (int ch = 0; ch < 4; ++ch) {
                 float p[8], ds[8];
+                const float4 l0 = *(const float4*)(sL + c0 + ch * 8), l1 = *(const float4*)(sL + c0 + ch * 8 + 4);
+                const float4 d0 = *(const float4*)(sD + c0 + ch * 8), d1 = *(const float4*)(sD + c0 + ch * 8 + 4);
+                const float lv[8] = {l0.x, l0.y, l0.z, l0.w, l1.x, l1.y, l1.z, l1.w};
+                const float dv8[8] = {d0.x, d0.y, d0.z, d0.w, d1.x, d1.y, d1.z, d1.w};
 #pragma unroll
                 for (int t = 0; t < 8; ++t) {
-                    const int c = chunk * 8 + t, q = q0 + c;
-                    float pv = ex2(fmaf(__uint_as_float(s[c]), sc, -sL[c]));
+                    const int c = ch * 8 + t, q = q0 + c0 + c;
+                    float pv = ex2(fmaf(__uint_as_float(s[c]), sc, -lv[t]));
                     if (!full && (q < qlo || q > qhi)) pv = 0.f;
                     p[t] = pv;
-                    ds[t] = pv * (__uint_as_float(dp[c]) - sD[c]);
+                    ds[t] = pv * (__uint_as_float(dp[c]) - dv8[t]);
                 }
-                st_chunk8(prow, r, chunk, p);
-                st_chunk8(dsrow, r, chunk, ds);
+                st_chunk8(prow, r, c0 / 8 + ch, p);
+                st_chunk8(dsrow, r, c0 / 8 + ch, ds);
             }
             tc::fence_proxy_async();
             __syncwarp();
@@ -579,14 +596,14 @@ __global__ void __launch_bounds__(NT, 2)
         }
         if (ok && n > 0 && tc::mbar_wait(acc_full, 0, a.status, 4)) {
             tc::tc_fence_after();
-            uint32_t dv[64], dk[64];
-            ld_row64(tmem + lane_off + C_DV, dv);
-            ld_row64(tmem + lane_off + C_DK, dk);
+            uint32_t dv[32], dk[32];
+            tc::tmem_ld32(tmem + lane_off + C_DV + c0, dv);
+            tc::tmem_ld32(tmem + lane_off + C_DK + c0, dk);
             tc::tmem_ld_wait();
             if (key < a.s) {
-                const long long off = (seq_row + key) * a.kv_stride + kvh * HD;
+                const long long off = (seq_row + key) * a.kv_stride + kvh * HD + c0;
 #pragma unroll
-                for (int c = 0; c < 8; ++c) {
+                for (int c = 0; c < 4; ++c) {
                     uint4 pv, pk;
                     __nv_bfloat162* a2 = (__nv_bfloat162*)&pv;
                     __nv_bfloat162* b2 = (__nv_bfloat162*)&pk;
@@ -610,7 +627,7 @@ __global__ void __launch_bounds__(NT, 2)
     }
 }
 
-__global__ void __launch_bounds__(NT, 2)
+__global__ void __launch_bounds__(NTB, 2)
     k_dq(const __grid_constant__ CUtensorMap mq, const __grid_constant__ CUtensorMap mdo,
          const __grid_constant__ CUtensorMap mk, const __grid_constant__ CUtensorMap mv, BwdArgs a) {
     extern __shared__ uint8_t smem_raw[];
@@ -648,8 +665,8 @@ __global__ void __launch_bounds__(NT, 2)
             tc::mbar_init(&kv_empty[i], 1);
         }
         tc::mbar_init(st_full, 1);
-        tc::mbar_init(st_free, 4);
-        tc::mbar_init(ds_full, 4);
+        tc::mbar_init(st_free, NCW);
+        tc::mbar_init(ds_full, NCW);
         tc::mbar_init(ds_free, 1);
         tc::mbar_init(acc_full, 1);
         tc::mbar_init(drain, 1);
@@ -694,13 +711,12 @@ __global__ void __launch_bounds__(NT, 2)
             constexpr uint32_t ID_Q = tc::idesc_bf16(128, HD, false, true);   // dQ (K MN-major)
             bool ok = tc::mbar_wait(q_full, 0, a.status, 4);
             const uint32_t aQ = tc::smem_u32(sQ), aO = tc::smem_u32(sO), aDS = tc::smem_u32(sDS);
-            for (int j = 0; j < n && ok; ++j) {
+            // S, dP of block j: issued once the compute warps hold block j-1's
+            auto issue_st = [&](int j) -> bool {
                 const int st = j % 3;
                 if (!tc::mbar_wait(&kv_full[st], (j / 3) & 1, a.status, 4) ||
-                    !tc::mbar_wait(st_free, (j & 1) ^ 1, a.status, 4)) {
-                    ok = false;
-                    break;
-                }
+                    !tc::mbar_wait(st_free, (j & 1) ^ 1, a.status, 4))
+                    return false;
                 tc::tc_fence_after();
                 const uint32_t bK = tc::smem_u32(sKV + st * 2 * T64), bV = bK + T64;
 #pragma unroll
@@ -712,6 +728,16 @@ __global__ void __launch_bounds__(NT, 2)
                     tc::mma_bf16(tmem + C_DP, tc::sdesc(aO + kk * 32, 16, 1024), tc::sdesc(bV + kk * 32, 16, 1024), ID_S,
                                  kk != 0);
                 tc::mma_commit(st_full);
+                return true;
+            };
+            if (ok && n > 0) ok = issue_st(0);
+            for (int j = 0; j < n && ok; ++j) {
+                const int st = j % 3;
+                const uint32_t bK = tc::smem_u32(sKV + st * 2 * T64);
+                if (j + 1 < n && !issue_st(j + 1)) {
+                    ok = false;
+                    break;
+                }
                 if (!tc::mbar_wait(ds_full, j & 1, a.status, 4)) {
                     ok = false;
                     break;
@@ -729,8 +755,8 @@ __global__ void __launch_bounds__(NT, 2)
             tc::mbar_wait(drain, 0, a.status, 4, 400000000ll, false);
         }
     } else {
-        // ---------------- compute: thread = query row
-        const int qd = warp & 3;
+        // ---------------- compute: thread = query row, 32 of its 64 key columns
+        const int qd = warp & 3, c0 = ((warp - 2) >> 2) * 32;
         const int r = qd * 32 + lane;
         const int row = q0 + r;
         const uint32_t lane_off = (uint32_t)(qd * 32) << 16;
@@ -748,9 +774,9 @@ __global__ void __launch_bounds__(NT, 2)
                 break;
             }
             tc::tc_fence_after();
-            uint32_t s[64], dp[64];
-            ld_row64(tmem + lane_off + C_S, s);
-            ld_row64(tmem + lane_off + C_DP, dp);
+            uint32_t s[32], dp[32];
+            tc::tmem_ld32(tmem + lane_off + C_S + c0, s);
+            tc::tmem_ld32(tmem + lane_off + C_DP + c0, dp);
             tc::tmem_ld_wait();
             tc::tc_fence_before();
             __syncwarp();
@@ -761,16 +787,16 @@ __global__ void __launch_bounds__(NT, 2)
                 break;
             }
 #pragma unroll
-            for (int chunk = 0; chunk < 8; ++chunk) {
+            for (int ch = 0; ch < 4; ++ch) {
                 float ds[8];
 #pragma unroll
                 for (int t = 0; t < 8; ++t) {
-                    const int c = chunk * 8 + t, key = kb0 + c;
+                    const int c = ch * 8 + t, key = kb0 + c0 + c;
                     float pv = ex2(fmaf(__uint_as_float(s[c]), sc, -L));
                     if (!full && (key < lo || key > hi)) pv = 0.f;
                     ds[t] = pv * (__uint_as_float(dp[c]) - D);
                 }
-                st_chunk8(dsrow, r, chunk, ds);
+                st_chunk8(dsrow, r, c0 / 8 + ch, ds);
             }
             tc::fence_proxy_async();
             __syncwarp();
@@ -778,13 +804,13 @@ __global__ void __launch_bounds__(NT, 2)
         }
         if (ok && n > 0 && tc::mbar_wait(acc_full, 0, a.status, 4)) {
             tc::tc_fence_after();
-            uint32_t dq[64];
-            ld_row64(tmem + lane_off + C_DQ, dq);
+            uint32_t dq[32];
+            tc::tmem_ld32(tmem + lane_off + C_DQ + c0, dq);
             tc::tmem_ld_wait();
             if (row < a.s) {
-                bf16* out = a.dq + (seq_row + row) * a.q_stride + h * HD;
+                bf16* out = a.dq + (seq_row + row) * a.q_stride + h * HD + c0;
 #pragma unroll
-                for (int c = 0; c < 8; ++c) {
+                for (int c = 0; c < 4; ++c) {
                     uint4 pk;
                     __nv_bfloat162* b2 = (__nv_bfloat162*)&pk;
 #pragma unroll
@@ -884,9 +910,9 @@ void attention_bwd_tc5(Context* c, const void* q, const void* k, const void* v, 
         CUDA_OK(cudaFuncSetAttribute(k_dq, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_DQ));
         attr[c->device] = true;
     }
-    k_dkdv<<<dim3((unsigned)cdiv(s, 128), (unsigned)hkv, (unsigned)b), NT, SMEM_DKDV, c->stream>>>(mk128, mv128, mq64,
+    k_dkdv<<<dim3((unsigned)cdiv(s, 128), (unsigned)hkv, (unsigned)b), NTB, SMEM_DKDV, c->stream>>>(mk128, mv128, mq64,
                                                                                                     mdo64, a);
-    k_dq<<<dim3((unsigned)cdiv(s, 128), (unsigned)h, (unsigned)b), NT, SMEM_DQ, c->stream>>>(mq128, mdo128, mk64, mv64,
+    k_dq<<<dim3((unsigned)cdiv(s, 128), (unsigned)h, (unsigned)b), NTB, SMEM_DQ, c->stream>>>(mq128, mdo128, mk64, mv64,
                                                                                               a);
     launched(c, 2);
 }
