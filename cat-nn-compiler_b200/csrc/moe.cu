@@ -519,22 +519,23 @@ __device__ __forceinline__ float silu_grad_f(float x) {
 // h = silu(a) ⊙ c. a, c: [rows, F] views with leading dimension lda
 // (a fused [a | c] buffer passes cc = a + F and lda = 2F). CTAs stride over
 // rows, threads over V-wide column vectors (16-byte accesses when aligned).
+// One flat index over (row, vector) so every thread has work; 32-bit index
+// math (the host guarantees rows * F / V < 2^31).
 template <typename TI, typename T, int V>
 __global__ void __launch_bounds__(256) k_swiglu(const TI* __restrict__ a, const TI* __restrict__ cc, T* __restrict__ h,
                                                 i64 rows, i64 F, i64 lda, i64 ldh, const int32_t* __restrict__ rows_dev) {
     if (rows_dev && *rows_dev < rows) rows = *rows_dev;
-    for (i64 r = blockIdx.x; r < rows; r += gridDim.x) {
-        const TI* ar = a + r * lda;
-        const TI* cr = cc + r * lda;
-        T* hr = h + r * ldh;
-        for (i64 f = (i64)threadIdx.x * V; f < F; f += (i64)blockDim.x * V) {
-            float av[V], cv[V], o[V];
-            ldv<TI, V>(ar + f, av);
-            ldv<TI, V>(cr + f, cv);
+    const uint32_t vpr = (uint32_t)(F / V);
+    const uint32_t total = (uint32_t)rows * vpr;
+    for (uint32_t idx = blockIdx.x * blockDim.x + threadIdx.x; idx < total; idx += gridDim.x * blockDim.x) {
+        const uint32_t r = idx / vpr;
+        const i64 f = (i64)(idx - r * vpr) * V;
+        float av[V], cv[V], o[V];
+        ldv<TI, V>(a + r * lda + f, av);
+        ldv<TI, V>(cc + r * lda + f, cv);
 #pragma unroll
-            for (int j = 0; j < V; ++j) o[j] = silu_f(av[j]) * cv[j];
-            stv<T, V>(hr + f, o);
-        }
+        for (int j = 0; j < V; ++j) o[j] = silu_f(av[j]) * cv[j];
+        stv<T, V>(h + r * ldh + f, o);
     }
 }
 
@@ -545,23 +546,22 @@ __global__ void __launch_bounds__(256) k_swiglu_bwd(const TI* __restrict__ a, co
                                                     i64 rows, i64 F, i64 lda, i64 ldd,
                                                     const int32_t* __restrict__ rows_dev) {
     if (rows_dev && *rows_dev < rows) rows = *rows_dev;
-    for (i64 r = blockIdx.x; r < rows; r += gridDim.x) {
-        const TI* ar = a + r * lda;
-        const TI* cr = cc + r * lda;
-        const TG* gr = dh + r * F;
-        for (i64 f = (i64)threadIdx.x * V; f < F; f += (i64)blockDim.x * V) {
-            float av[V], cv[V], g[V], oa[V], oc[V];
-            ldv<TI, V>(ar + f, av);
-            ldv<TI, V>(cr + f, cv);
-            ldv<TG, V>(gr + f, g);
+    const uint32_t vpr = (uint32_t)(F / V);
+    const uint32_t total = (uint32_t)rows * vpr;
+    for (uint32_t idx = blockIdx.x * blockDim.x + threadIdx.x; idx < total; idx += gridDim.x * blockDim.x) {
+        const uint32_t r = idx / vpr;
+        const i64 f = (i64)(idx - r * vpr) * V;
+        float av[V], cv[V], g[V], oa[V], oc[V];
+        ldv<TI, V>(a + r * lda + f, av);
+        ldv<TI, V>(cc + r * lda + f, cv);
+        ldv<TG, V>(dh + r * F + f, g);
 #pragma unroll
-            for (int j = 0; j < V; ++j) {
-                oa[j] = g[j] * cv[j] * silu_grad_f(av[j]);
-                oc[j] = g[j] * silu_f(av[j]);
-            }
-            stv<T, V>(da + r * ldd + f, oa);
-            stv<T, V>(dc + r * ldd + f, oc);
+        for (int j = 0; j < V; ++j) {
+            oa[j] = g[j] * cv[j] * silu_grad_f(av[j]);
+            oc[j] = g[j] * silu_f(av[j]);
         }
+        stv<T, V>(da + r * ldd + f, oa);
+        stv<T, V>(dc + r * ldd + f, oc);
     }
 }
 
@@ -578,12 +578,17 @@ static int swiglu_vec(bool all_bf16, i64 F, std::initializer_list<i64> pitches,
     return v;
 }
 
-static int row_grid(Context* c, i64 rows) { return (int)std::min<i64>(rows, (i64)c->sm_count * 16); }
+// Grid of the flat (row, vector) loops; the index space must fit 32 bits.
+static int row_grid(Context* c, i64 rows, i64 F = 0, int v = 1) {
+    const i64 total = F > 0 ? rows * (F / v) : rows * 256;
+    CATNN_CHECK(total < (1ll << 31), CATNN_ERR_SHAPE, "swiglu: too many elements for one launch");
+    return (int)std::max<i64>(1, std::min<i64>(cdiv(total, 256), (i64)c->sm_count * 16));
+}
 
 template <typename TI, typename T>
 static void launch_swiglu(Context* c, const void* a, const void* cc, void* h, i64 rows, i64 F, i64 lda, i64 ldh,
                           int v, const int32_t* rows_dev) {
-    int g = row_grid(c, rows);
+    int g = row_grid(c, rows, F, v);
     auto A = (const TI*)a;
     auto Cc = (const TI*)cc;
     auto H = (T*)h;
@@ -607,7 +612,7 @@ void swiglu_act(Context* c, const void* a, const void* cc, void* h, i64 rows, i6
 template <typename TI, typename TG, typename T>
 static void launch_swiglu_bwd(Context* c, const void* a, const void* cc, const void* dh, void* da, void* dc, i64 rows,
                               i64 F, i64 lda, i64 ldd, int v, const int32_t* rows_dev) {
-    int g = row_grid(c, rows);
+    int g = row_grid(c, rows, F, v);
     auto A = (const TI*)a;
     auto Cc = (const TI*)cc;
     auto G = (const TG*)dh;
