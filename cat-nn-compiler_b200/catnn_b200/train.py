@@ -154,6 +154,11 @@ class MoeTrainer:
         torch.cuda.synchronize(self.device)
         return out
 
+    def set_graphs(self, enable=True):
+        """Replay the step body as a CUDA graph (catnn_moe_trainer_set_graphs)."""
+        self._bind()
+        _lib.call("catnn_moe_trainer_set_graphs", self.handle, int(bool(enable)))
+
     def check(self):
         self._bind()
         _lib.call("catnn_moe_trainer_check", self.handle)

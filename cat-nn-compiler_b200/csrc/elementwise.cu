@@ -180,6 +180,9 @@ void sgd(Context* c, float* p, const float* g, i64 n, float lr, bf16* shadow) {
 // p = p - (lr*(m/max(b1t,1e-30))) / (sqrt(v/max(b2t,1e-30)) + eps).
 struct AdamK {
     float lr, b1, omb1, b2, omb2, d1, d2, eps;
+    // when set, the bias-correction divisors (d1, d2) are read from device
+    // memory at kernel start (a replayed CUDA graph keeps its launch arguments)
+    const float* d12;
     __device__ __forceinline__ float step(float& p, float gi, float& m, float& v) const {
         float mi = __fadd_rn(__fmul_rn(b1, m), __fmul_rn(omb1, gi));
         float vi = __fadd_rn(__fmul_rn(b2, v), __fmul_rn(__fmul_rn(omb2, gi), gi));
@@ -197,6 +200,10 @@ struct AdamK {
 template <typename G, int V>
 __global__ void __launch_bounds__(256) k_adam(float* __restrict__ p, const G* __restrict__ g, float* __restrict__ m,
                                               float* __restrict__ v, i64 n, AdamK k, bf16* __restrict__ sh) {
+    if (k.d12) {
+        k.d1 = k.d12[0];
+        k.d2 = k.d12[1];
+    }
     const i64 nv = n / V;
     for (i64 i = blockIdx.x * (i64)blockDim.x + threadIdx.x; i < nv; i += (i64)gridDim.x * blockDim.x) {
         const i64 o = i * V;
@@ -227,13 +234,21 @@ static float powi_f32(float a, uint64_t b) {
     return r;
 }
 
-void adam(Context* c, float* p, const void* g, float* m, float* v, i64 n, uint64_t t, float lr, float b1, float b2,
-          float eps, int g_dtype, bf16* shadow) {
-    if (n <= 0) return;
+void adam_divisors(uint64_t t, float b1, float b2, float* d12) {
     volatile float one = 1.0f;
     float b1t = one - powi_f32(b1, t), b2t = one - powi_f32(b2, t);
+    d12[0] = std::max(b1t, 1e-30f);
+    d12[1] = std::max(b2t, 1e-30f);
+}
+
+void adam(Context* c, float* p, const void* g, float* m, float* v, i64 n, uint64_t t, float lr, float b1, float b2,
+          float eps, int g_dtype, bf16* shadow, const float* d12_dev) {
+    if (n <= 0) return;
+    volatile float one = 1.0f;
+    float d12[2];
+    adam_divisors(t, b1, b2, d12);
     float omb1 = one - b1, omb2 = one - b2;
-    AdamK k{lr, b1, omb1, b2, omb2, std::max(b1t, 1e-30f), std::max(b2t, 1e-30f), eps};
+    AdamK k{lr, b1, omb1, b2, omb2, d12[0], d12[1], eps, d12_dev};
     const int gs = g_dtype == CATNN_BF16 ? 2 : 4;
     const bool vec = aligned_to(p, 16) && aligned_to(m, 16) && aligned_to(v, 16) && aligned_to(g, 4 * gs) &&
                      aligned_to(shadow, 8);

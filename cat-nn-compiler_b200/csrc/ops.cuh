@@ -71,7 +71,9 @@ void fill_f32(Context* c, float* p, float v, i64 n);
 void col_sum(Context* c, const void* x, i64 rows, i64 cols, float* out, int dtype, bool accumulate);
 void sgd(Context* c, float* p, const float* g, i64 n, float lr, bf16* shadow);
 void adam(Context* c, float* p, const void* g, float* m, float* v, i64 n, uint64_t t, float lr, float b1,
-          float b2, float eps, int g_dtype, bf16* shadow);
+          float b2, float eps, int g_dtype, bf16* shadow, const float* d12_dev = nullptr);
+// Adam bias-correction divisors max(1 - b^t, 1e-30) for step t (host).
+void adam_divisors(uint64_t t, float b1, float b2, float* d12);
 
 // ---- softmax / losses / norms (norms.cu)
 void softmax_fwd(Context* c, const void* x, void* y, i64 rows, i64 last, int dtype);

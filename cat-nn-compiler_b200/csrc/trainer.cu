@@ -197,6 +197,7 @@ void MoeTrainer::alloc() {
     dxf = ac.take<char>(T * d * e);
     CUDA_OK(cudaMallocHost(&h_tokens, Tg * 4));
     CUDA_OK(cudaMallocHost(&h_loss, 64));
+    CUDA_OK(cudaMalloc(&d12, 2 * sizeof(float)));
     act_bytes = tot;
     if (ep) {
         // every buffer a peer reads or writes lives in act_block: map it once
@@ -232,6 +233,16 @@ void MoeTrainer::release() {
         cudaStreamSynchronize(c->stream);
         map_id = -1;
     }
+    drop_graphs();
+    if (gs) {
+        cudaStreamSynchronize(gs);
+        cudaEventDestroy(ev_in);
+        cudaEventDestroy(ev_out);
+        cudaStreamDestroy(gs);
+        gs = nullptr;
+    }
+    if (d12) cudaFree(d12);
+    d12 = nullptr;
     if (us) {
         cudaStreamSynchronize(us);
         cudaEventDestroy(ev_u);
@@ -422,7 +433,7 @@ void MoeTrainer::update_range(i64 off, i64 n) {
     if (n <= 0) return;
     bf16* sh = dt == CATNN_BF16 ? (bf16*)Sh + off : nullptr;
     if (opt == 0) sgd(c, P + off, G + off, n, lr, sh);
-    else adam(c, P + off, G + off, Mo + off, Vo + off, n, t_step, lr, b1, b2, aeps, CATNN_F32, sh);
+    else adam(c, P + off, G + off, Mo + off, Vo + off, n, t_step, lr, b1, b2, aeps, CATNN_F32, sh, d12);
 }
 
 namespace {
@@ -468,20 +479,76 @@ void MoeTrainer::join_updates() {
     CUDA_OK(cudaStreamWaitEvent(c->stream, ev_u_done, 0));
 }
 
+void MoeTrainer::run_body() {
+    forward();
+    backward();  // enqueues the gradient allreduces and the updates bucket by bucket
+    if (!ep) join_updates();
+}
+
+void MoeTrainer::drop_graphs() {
+    for (int k = 0; k < 2; ++k) {
+        if (gexec[k]) cudaGraphExecDestroy(gexec[k]);
+        gexec[k] = nullptr;
+        warmed[k] = false;
+    }
+}
+
 void MoeTrainer::step(const uint32_t* tokens_dev, float* loss_dev, bool upd) {
     if (tokens_dev != tokens) CUDA_OK(cudaMemcpyAsync(tokens, tokens_dev, Tg * 4, cudaMemcpyDeviceToDevice, c->stream));
     upd_pending = upd;
-    if (upd && opt == 1) ++t_step;
-    forward();
-    backward();  // enqueues the gradient allreduces and the updates bucket by bucket
+    if (upd && opt == 1) {
+        ++t_step;
+        // the divisors travel through device memory, so a replayed graph sees this step's
+        float h12[2];
+        adam_divisors(t_step, b1, b2, h12);
+        CUDA_OK(cudaMemcpyAsync(d12, h12, sizeof(h12), cudaMemcpyHostToDevice, c->stream));
+    }
+    if (graphs && !ep) {
+        const int key = upd ? 1 : 0;
+        CUDA_OK(cudaEventRecord(ev_in, c->stream));
+        CUDA_OK(cudaStreamWaitEvent(gs, ev_in, 0));
+        {
+            OnStream on(c, gs);
+            if (gexec[key]) {
+                CUDA_OK(cudaGraphLaunch(gexec[key], gs));
+                c->launches += glaunch[key];
+            } else if (!warmed[key]) {
+                run_body();  // eager: every workspace reaches its size before a capture
+                warmed[key] = true;
+            } else {
+                const uint64_t l0 = c->launches;
+                CUDA_OK(cudaStreamBeginCapture(gs, cudaStreamCaptureModeThreadLocal));
+                cudaGraph_t g = nullptr;
+                try {
+                    run_body();
+                } catch (...) {
+                    cudaStreamEndCapture(gs, &g);
+                    if (g) cudaGraphDestroy(g);
+                    throw;
+                }
+                CUDA_OK(cudaStreamEndCapture(gs, &g));
+                glaunch[key] = c->launches - l0;
+                cudaGraphExec_t ex = nullptr;
+                cudaError_t e = cudaGraphInstantiate(&ex, g, 0);
+                cudaGraphDestroy(g);
+                CUDA_OK(e);
+                gexec[key] = ex;
+                CUDA_OK(cudaGraphLaunch(ex, gs));  // the captured step has not run yet
+            }
+        }
+        CUDA_OK(cudaEventRecord(ev_out, gs));
+        CUDA_OK(cudaStreamWaitEvent(c->stream, ev_out, 0));
+    } else {
+        run_body();
+    }
     if (ep) {
         // The last allreduce completes only once every rank has finished its
         // backward pass, so no rank's next dispatch can overwrite a buffer a
         // peer still reads.
         comm->join_overlapped();
         CUDA_OK(cudaMemcpyAsync(loss, G + o_loss, 4, cudaMemcpyDeviceToDevice, c->stream));
+        join_updates();
     }
-    join_updates();
     upd_pending = false;
     if (loss_dev && loss_dev != loss) CUDA_OK(cudaMemcpyAsync(loss_dev, loss, 4, cudaMemcpyDeviceToDevice, c->stream));
 }
@@ -599,6 +666,23 @@ int catnn_moe_trainer_create_ep(catnn_ctx* h, const catnn_moe_config* cf, catnn_
         throw;
     }
     *out = t;
+    ABI_END
+}
+
+int catnn_moe_trainer_set_graphs(catnn_moe_trainer* h, int enable) {
+    ABI_BEGIN
+    MoeTrainer& t = tr(h);
+    CATNN_CHECK(!t.ep || !enable, CATNN_ERR_UNSUPPORTED, "graph replay: single-GPU trainers only");
+    if (enable && !t.gs) {
+        CUDA_OK(cudaStreamCreateWithFlags(&t.gs, cudaStreamNonBlocking));
+        CUDA_OK(cudaEventCreateWithFlags(&t.ev_in, cudaEventDisableTiming));
+        CUDA_OK(cudaEventCreateWithFlags(&t.ev_out, cudaEventDisableTiming));
+    }
+    if (!enable) {
+        if (t.gs) CUDA_OK(cudaStreamSynchronize(t.gs));
+        t.drop_graphs();
+    }
+    t.graphs = enable != 0;
     ABI_END
 }
 

@@ -84,6 +84,19 @@ struct MoeTrainer {
     bool upd_pending = false;
     cudaStream_t us = nullptr;
     cudaEvent_t ev_u = nullptr, ev_u_done = nullptr;
+    // CUDA-graph replay of the single-GPU step (catnn_moe_trainer_set_graphs):
+    // the body (forward, backward, updates) runs on the trainer's own stream
+    // gs; the first step of each kind (with / without update) runs eagerly
+    // and sizes every workspace, the second is captured, later ones replay.
+    bool graphs = false;
+    cudaStream_t gs = nullptr;
+    cudaEvent_t ev_in = nullptr, ev_out = nullptr;
+    cudaGraphExec_t gexec[2] = {nullptr, nullptr};
+    bool warmed[2] = {false, false};
+    uint64_t glaunch[2] = {0, 0};
+    float* d12 = nullptr;  // device [2]: Adam bias-correction divisors of the running step
+    void run_body();
+    void drop_graphs();
     void update_range(i64 off, i64 n);          // on the context's current stream
     void update_after_main(i64 off, i64 n);     // on us, after the work enqueued so far
     void update_after_comm(i64 off, i64 n);     // on us, after the last allreduce enqueued

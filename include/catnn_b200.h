@@ -317,6 +317,14 @@ int catnn_moe_trainer_activation(catnn_moe_trainer* t, int which, int64_t layer,
 /* Synchronizes and reports device-side errors of earlier steps (token id or
  * target out of range, a bounded wait that ran out). */
 int catnn_moe_trainer_check(catnn_moe_trainer* t);
+/* enable != 0: later steps replay a CUDA graph of the step body (forward,
+ * backward, updates) on the trainer's own stream, ordered after the work
+ * already on the context stream; the first step with and without update runs
+ * eagerly and sizes every workspace, the second is captured. Same results as
+ * eager steps. Single-GPU trainers only (an expert-parallel trainer returns
+ * CATNN_ERR_UNSUPPORTED). Tensor shapes and buffers are fixed per trainer, so
+ * a graph never goes stale; disable to release the graphs. */
+int catnn_moe_trainer_set_graphs(catnn_moe_trainer* t, int enable);
 
 /* ------------------------------------------------------------ multi-GPU (one node) */
 /* One rank of a group of 1..8 processes, one GPU each. The reference runs

@@ -218,3 +218,31 @@ def test_bad_token_is_reported():
     with pytest.raises(ShapeMismatch):
         tr.check()
     tr.close()
+
+
+def test_graph_replay_matches_eager():
+    """The step replayed as a CUDA graph gives the eager step's results bit for
+    bit (loss every step, then parameters, gradients and Adam state through
+    updates), and its launches are still counted."""
+    cfg = MoeConfig.make(2048, 256, 512, 2, 4, 4, 8, 2, batch=2, seq=128, rope_theta=1e6, dtype=torch.bfloat16,
+                         optimizer="adam", lr=1e-3)
+    P = init_params(cfg, 5)
+    tok = torch.as_tensor(np.random.default_rng(5).integers(0, 2048, cfg.batch * cfg.seq).astype(np.int32)).cuda()
+    a, b = MoeTrainer(cfg), MoeTrainer(cfg)
+    a.set_params(P)
+    b.set_params(P)
+    b.set_graphs(True)
+    la, lb = torch.zeros(1, device="cuda"), torch.zeros(1, device="cuda")
+    n0 = b.ctx.launch_count()
+    for upd in (False, False, True, True, True, False, True):
+        a.step(tok, update=upd, loss_out=la)
+        b.step(tok, update=upd, loss_out=lb)
+        torch.cuda.synchronize()
+        assert torch.equal(la, lb), (upd, float(la), float(lb))
+    assert torch.equal(a.params(), b.params())
+    assert torch.equal(a.grads(), b.grads())
+    assert b.ctx.launch_count() - n0 > 7 * 100, "replayed launches are counted"
+    a.check()
+    b.check()
+    a.close()
+    b.close()
