@@ -41,7 +41,7 @@ struct TcArgs {
     int ksplit, kchunk;
     float* part;
     long long c_group_stride_part;  // elements between two slices of part
-    // tma_c: plain full 32-row blocks of C are staged in shared memory and
+    // tma_c: full 32-row blocks of C (no accumulate) are staged in shared memory and
     // written by TMA bulk stores of mapC
     int tma_c;
 };
@@ -153,8 +153,8 @@ __global__ void __launch_bounds__(192, 1)
 
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
-    // epilogue staging for TMA stores: per epilogue warp 8 KB (four 2 KB
-    // bf16 blocks or two 4 KB fp32 blocks of 32 x 32)
+    // epilogue staging for TMA stores: per epilogue warp four 2 KB blocks
+    // of 32 rows x 64 bytes
     uint8_t* stage_c = smem + STAGES * STAGE_BYTES;
     uint64_t* full = (uint64_t*)(stage_c + EPI_STAGE_BYTES);
     uint64_t* empty = full + STAGES;
@@ -323,21 +323,57 @@ __global__ void __launch_bounds__(192, 1)
                     continue;
                 }
                 bool full_chunk = a.vec_ok && (col0 + 32 <= a.N);
-                if (plain && use_tma) {
+                if (use_tma) {
                     // Stage the warp's 32 x 32 block with the store map's swizzle
                     // (16-byte chunk c of row l at chunk c ^ f(l): conflict-free
                     // st.shared), then one lane issues an async TMA store: whole
                     // 64/128-byte row segments, fewer L2 transactions than per-row
-                    // 16-byte stores, no stall of the warp.
+                    // 16-byte stores, no stall of the warp. Bias, residual (16-byte
+                    // loads) and activation are applied first, one uniform branch
+                    // per option.
                     const bool z = ti.klen <= 0;
-                    const int nbuf = a.c_bf16 ? 4 : 2;
-                    const uint32_t bbytes = a.c_bf16 ? 2048 : 4096;
-                    const int b = (int)(nst % (uint32_t)nbuf);
-                    const uint32_t sb = tc::smem_u32(stage_c + q * 8192 + b * bbytes);
-                    if (lane == 0) {
-                        if (a.c_bf16) tc::bulk_wait_read<3>();  // this buffer's previous store has read it
-                        else tc::bulk_wait_read<1>();
+                    if (!plain) {
+                        float v[32];
+#pragma unroll
+                        for (int i = 0; i < 32; ++i) v[i] = z ? 0.f : __uint_as_float(r[i]);
+                        if (a.bias) {
+#pragma unroll
+                            for (int i = 0; i < 32; ++i)
+                                if (col0 + i < a.N) v[i] += a.bias[col0 + i];
+                        }
+                        if (a.resid) {
+                            const float* rs = a.resid + crow + col0;
+                            if (col0 + 32 <= a.N) {
+#pragma unroll
+                                for (int i4 = 0; i4 < 8; ++i4) {
+                                    const float4 q4 = *(const float4*)(rs + i4 * 4);
+                                    v[i4 * 4] += q4.x;
+                                    v[i4 * 4 + 1] += q4.y;
+                                    v[i4 * 4 + 2] += q4.z;
+                                    v[i4 * 4 + 3] += q4.w;
+                                }
+                            } else {
+#pragma unroll
+                                for (int i = 0; i < 32; ++i)
+                                    if (col0 + i < a.N) v[i] += rs[i];
+                            }
+                        }
+                        if (a.act == CATNN_ACT_RELU) {
+#pragma unroll
+                            for (int i = 0; i < 32; ++i) v[i] = act_apply(v[i], CATNN_ACT_RELU);
+                        } else if (a.act == CATNN_ACT_GELU) {
+#pragma unroll
+                            for (int i = 0; i < 32; ++i) v[i] = act_apply(v[i], CATNN_ACT_GELU);
+                        }
+#pragma unroll
+                        for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(v[i]);
                     }
+                    const bool zz = plain && z;  // r now holds the final values unless plain
+                    // four 2 KB buffers per warp: a bf16 chunk is one 32 x 32 box,
+                    // an fp32 chunk two 32 x 16 boxes (64-byte rows either way)
+                    const int b = (int)(nst & 3u);
+                    const uint32_t sb = tc::smem_u32(stage_c + q * 8192 + b * 2048);
+                    if (lane == 0) tc::bulk_wait_read<3>();  // this buffer's previous store has read it
                     __syncwarp();
                     if (a.c_bf16) {
 #pragma unroll
@@ -346,26 +382,42 @@ __global__ void __launch_bounds__(192, 1)
                             __nv_bfloat162* pp = (__nv_bfloat162*)&pk;
 #pragma unroll
                             for (int j = 0; j < 4; ++j)
-                                pp[j] = z ? __floats2bfloat162_rn(0.f, 0.f)
-                                          : __floats2bfloat162_rn(__uint_as_float(r[c4 * 8 + 2 * j]),
-                                                                  __uint_as_float(r[c4 * 8 + 2 * j + 1]));
+                                pp[j] = zz ? __floats2bfloat162_rn(0.f, 0.f)
+                                           : __floats2bfloat162_rn(__uint_as_float(r[c4 * 8 + 2 * j]),
+                                                                   __uint_as_float(r[c4 * 8 + 2 * j + 1]));
                             tc::st_shared_v4(sb + lane * 64 + ((c4 ^ ((lane >> 1) & 3)) << 4), pk);
                         }
-                    } else {
-#pragma unroll
-                        for (int c8 = 0; c8 < 8; ++c8) {
-                            uint4 pk = z ? make_uint4(0, 0, 0, 0)
-                                         : make_uint4(r[c8 * 4], r[c8 * 4 + 1], r[c8 * 4 + 2], r[c8 * 4 + 3]);
-                            tc::st_shared_v4(sb + lane * 128 + ((c8 ^ (lane & 7)) << 4), pk);
+                        tc::fence_proxy_async();
+                        __syncwarp();
+                        if (lane == 0) {
+                            tc::tma_store_2d(&mapC, stage_c + q * 8192 + b * 2048, col0, (int)ybase);
+                            tc::bulk_commit();
                         }
+                        ++nst;
+                        continue;
                     }
-                    tc::fence_proxy_async();
-                    __syncwarp();
-                    if (lane == 0) {
-                        tc::tma_store_2d(&mapC, stage_c + q * 8192 + b * bbytes, col0, (int)ybase);
-                        tc::bulk_commit();
+#pragma unroll
+                    for (int hh = 0; hh < 2; ++hh) {
+                        const int bh = (int)(nst & 3u);
+                        const uint32_t sbh = tc::smem_u32(stage_c + q * 8192 + bh * 2048);
+                        if (hh == 1) {
+                            if (lane == 0) tc::bulk_wait_read<3>();
+                            __syncwarp();
+                        }
+#pragma unroll
+                        for (int c4 = 0; c4 < 4; ++c4) {
+                            const int e0 = hh * 16 + c4 * 4;
+                            uint4 pk = zz ? make_uint4(0, 0, 0, 0) : make_uint4(r[e0], r[e0 + 1], r[e0 + 2], r[e0 + 3]);
+                            tc::st_shared_v4(sbh + lane * 64 + ((c4 ^ ((lane >> 1) & 3)) << 4), pk);
+                        }
+                        tc::fence_proxy_async();
+                        __syncwarp();
+                        if (lane == 0) {
+                            tc::tma_store_2d(&mapC, stage_c + q * 8192 + bh * 2048, col0 + hh * 16, (int)ybase);
+                            tc::bulk_commit();
+                        }
+                        ++nst;
                     }
-                    ++nst;
                     continue;
                 }
                 if (plain && full_chunk) {
@@ -565,19 +617,19 @@ static CUtensorMap make_map(const void* base, i64 rows, i64 cols, i64 ld, int bo
     return m;
 }
 
-// Store map of the epilogue: [rows, cols] with leading dimension ld, box 32
-// x 32; bf16 rows of the box are 64 B (64-byte swizzle), fp32 rows 128 B
-// (128-byte swizzle) — the layouts the epilogue's staging writes follow.
+// Store map of the epilogue: [rows, cols] with leading dimension ld, boxes
+// of 32 rows x 64 bytes (32 bf16 or 16 fp32 columns), 64-byte swizzle — the
+// layout the epilogue's staging writes follow.
 static CUtensorMap make_store_map(const void* base, i64 rows, i64 cols, i64 ld, bool fp32) {
     CUtensorMap m;
     const int es = fp32 ? 4 : 2;
     cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
     cuuint64_t strides[1] = {(cuuint64_t)(ld * es)};
-    cuuint32_t box[2] = {32, 32};
+    cuuint32_t box[2] = {fp32 ? 16u : 32u, 32u};
     cuuint32_t estr[2] = {1, 1};
     CUresult r = encode_fn()(&m, fp32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
                              const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                             fp32 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
+                             CU_TENSOR_MAP_SWIZZLE_64B,
                              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     CATNN_CHECK(r == CUDA_SUCCESS, CATNN_ERR_CUDA, "cuTensorMapEncodeTiled (store) failed (" + std::to_string((int)r) + ")");
     return m;
@@ -675,8 +727,8 @@ static void run_tc(Context* c, TcArgs a, bool a_mn, bool b_mn, const bf16* A, i6
     {
         const int es = a.c_bf16 ? 2 : 4;
         const i64 crows = a.mode == 2 ? (i64)a.groups * a.M : (i64)a.M;
-        const bool plain = !a.bias && !a.resid && a.act == CATNN_ACT_NONE && !a.accumulate;
-        if (plain && a.ksplit <= 1 && aligned16(a.C) && (a.ldc * es) % 16 == 0 && a.N >= 32 &&
+        // residual rows are read with 16-byte loads in the staged epilogue
+        if (!a.accumulate && aligned16(a.resid) && a.ksplit <= 1 && aligned16(a.C) && (a.ldc * es) % 16 == 0 && a.N >= 32 &&
             (a.mode != 2 || a.c_group_stride == (long long)a.M * a.ldc) && crows < (1ll << 31)) {
             mc = make_store_map(a.C, crows, a.N, a.ldc, !a.c_bf16);
             a.tma_c = 1;
