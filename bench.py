@@ -209,8 +209,7 @@ def run_ours(args):
         from catnn_b200.dist import Comm
         comm = Comm.from_process_group(local)
     tr = MoeTrainer(mc, device=local, comm=comm)
-    if world == 1:
-        tr.set_graphs(True)  # the step body replays as one CUDA graph after its first two runs
+    tr.set_graphs(True)  # the step body replays as one CUDA graph after its first two runs (every rank)
     # weights N(0, 0.02), norms 1; identical on every rank (same seed)
     g = torch.Generator(device=f"cuda:{local}").manual_seed(cfg["seed"])
     P = torch.randn(tr.n_params, generator=g, device=f"cuda:{local}") * 0.02

@@ -114,8 +114,19 @@ __device__ void wait_flags(uint64_t* const* flag_ptrs, int rank, int world, uint
 // All ranks: flags[rank] of every rank := epoch (release, system scope),
 // then wait for this epoch from every rank. Writes of earlier kernels on
 // the stream are complete when this kernel starts, so the release publishes them.
-__global__ void k_comm_barrier(uint64_t* const* flag_ptrs, int rank, int world, uint64_t epoch, int64_t timeout_ns,
+// The epoch is this rank's barrier count, kept on the device (*ctr, touched
+// only by this rank's barriers, in stream order): every rank passes the same
+// barriers in the same order, so the counts agree, and a barrier replayed in
+// a CUDA graph takes the next epoch like an eager one.
+__global__ void k_comm_barrier(uint64_t* const* flag_ptrs, int rank, int world, uint64_t* ctr, int64_t timeout_ns,
                                int* status) {
+    __shared__ uint64_t e;
+    if (threadIdx.x == 0) {
+        e = *ctr + 1;
+        *ctr = e;
+    }
+    __syncthreads();
+    const uint64_t epoch = e;
     int p = threadIdx.x;
     if (p < world) {
         __threadfence_system();
@@ -185,8 +196,9 @@ Comm::Mapped Comm::map(void* local, size_t bytes) {
 }
 
 void Comm::barrier() {
-    ++epoch;
-    k_comm_barrier<<<1, 32, 0, c->stream>>>(flag_ptrs_dev, rank, world, epoch, timeout_ns, c->status);
+    ++epoch;  // host mirror of the device count (diagnostics)
+    k_comm_barrier<<<1, 32, 0, c->stream>>>(flag_ptrs_dev, rank, world, flag_block + EPOCH_SLOT, timeout_ns,
+                                             c->status);
     launched(c);
 }
 

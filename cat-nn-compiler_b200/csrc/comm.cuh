@@ -18,6 +18,8 @@ namespace catnn {
 // Status slot set by a device wait that ran out of time (and the epoch it waited for).
 constexpr int COMM_STATUS_SLOT = 12;
 constexpr int COMM_MAX_WORLD = 8;
+// word of the (256-byte, zeroed) flag block holding this rank's barrier count
+constexpr int EPOCH_SLOT = 31;
 
 struct NcclFns;
 

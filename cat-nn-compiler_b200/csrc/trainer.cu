@@ -460,6 +460,7 @@ void MoeTrainer::update_after_main(i64 off, i64 n) {
     make_update_stream(&us, &ev_u, &ev_u_done);
     CUDA_OK(cudaEventRecord(ev_u, c->stream));
     CUDA_OK(cudaStreamWaitEvent(us, ev_u, 0));
+    upd_forked = true;
     OnStream on(c, us);
     update_range(off, n);
 }
@@ -469,12 +470,16 @@ void MoeTrainer::update_after_comm(i64 off, i64 n) {
     make_update_stream(&us, &ev_u, &ev_u_done);
     CUDA_OK(cudaEventRecord(ev_u, comm->side));
     CUDA_OK(cudaStreamWaitEvent(us, ev_u, 0));
+    upd_forked = true;
     OnStream on(c, us);
     update_range(off, n);
 }
 
 void MoeTrainer::join_updates() {
-    if (!us) return;
+    // only a step that forked updates onto us joins it (inside a graph capture
+    // a wait on work the capture never forked is an error)
+    if (!us || !upd_forked) return;
+    upd_forked = false;
     CUDA_OK(cudaEventRecord(ev_u_done, us));
     CUDA_OK(cudaStreamWaitEvent(c->stream, ev_u_done, 0));
 }
@@ -482,7 +487,14 @@ void MoeTrainer::join_updates() {
 void MoeTrainer::run_body() {
     forward();
     backward();  // enqueues the gradient allreduces and the updates bucket by bucket
-    if (!ep) join_updates();
+    if (ep) {
+        // The last allreduce completes only once every rank has finished its
+        // backward pass, so no rank's next dispatch can overwrite a buffer a
+        // peer still reads.
+        comm->join_overlapped();
+        CUDA_OK(cudaMemcpyAsync(loss, G + o_loss, 4, cudaMemcpyDeviceToDevice, c->stream));
+    }
+    join_updates();
 }
 
 void MoeTrainer::drop_graphs() {
@@ -503,7 +515,7 @@ void MoeTrainer::step(const uint32_t* tokens_dev, float* loss_dev, bool upd) {
         adam_divisors(t_step, b1, b2, h12);
         CUDA_OK(cudaMemcpyAsync(d12, h12, sizeof(h12), cudaMemcpyHostToDevice, c->stream));
     }
-    if (graphs && !ep) {
+    if (graphs) {
         const int key = upd ? 1 : 0;
         CUDA_OK(cudaEventRecord(ev_in, c->stream));
         CUDA_OK(cudaStreamWaitEvent(gs, ev_in, 0));
@@ -540,14 +552,6 @@ void MoeTrainer::step(const uint32_t* tokens_dev, float* loss_dev, bool upd) {
         CUDA_OK(cudaStreamWaitEvent(c->stream, ev_out, 0));
     } else {
         run_body();
-    }
-    if (ep) {
-        // The last allreduce completes only once every rank has finished its
-        // backward pass, so no rank's next dispatch can overwrite a buffer a
-        // peer still reads.
-        comm->join_overlapped();
-        CUDA_OK(cudaMemcpyAsync(loss, G + o_loss, 4, cudaMemcpyDeviceToDevice, c->stream));
-        join_updates();
     }
     upd_pending = false;
     if (loss_dev && loss_dev != loss) CUDA_OK(cudaMemcpyAsync(loss_dev, loss, 4, cudaMemcpyDeviceToDevice, c->stream));
@@ -672,7 +676,6 @@ int catnn_moe_trainer_create_ep(catnn_ctx* h, const catnn_moe_config* cf, catnn_
 int catnn_moe_trainer_set_graphs(catnn_moe_trainer* h, int enable) {
     ABI_BEGIN
     MoeTrainer& t = tr(h);
-    CATNN_CHECK(!t.ep || !enable, CATNN_ERR_UNSUPPORTED, "graph replay: single-GPU trainers only");
     if (enable && !t.gs) {
         CUDA_OK(cudaStreamCreateWithFlags(&t.gs, cudaStreamNonBlocking));
         CUDA_OK(cudaEventCreateWithFlags(&t.ev_in, cudaEventDisableTiming));

@@ -82,6 +82,7 @@ struct MoeTrainer {
     // as soon as a bucket's gradients are final (summed over ranks when
     // replicated), overlapping the rest of the backward pass.
     bool upd_pending = false;
+    bool upd_forked = false;  // this step enqueued work on us
     cudaStream_t us = nullptr;
     cudaEvent_t ev_u = nullptr, ev_u_done = nullptr;
     // CUDA-graph replay of the single-GPU step (catnn_moe_trainer_set_graphs):

@@ -318,12 +318,13 @@ int catnn_moe_trainer_activation(catnn_moe_trainer* t, int which, int64_t layer,
  * target out of range, a bounded wait that ran out). */
 int catnn_moe_trainer_check(catnn_moe_trainer* t);
 /* enable != 0: later steps replay a CUDA graph of the step body (forward,
- * backward, updates) on the trainer's own stream, ordered after the work
- * already on the context stream; the first step with and without update runs
- * eagerly and sizes every workspace, the second is captured. Same results as
- * eager steps. Single-GPU trainers only (an expert-parallel trainer returns
- * CATNN_ERR_UNSUPPORTED). Tensor shapes and buffers are fixed per trainer, so
- * a graph never goes stale; disable to release the graphs. */
+ * backward, updates, and for an expert-parallel trainer its device barriers,
+ * peer-memory exchanges and NCCL allreduces) on the trainer's own stream,
+ * ordered after the work already on the context stream; the first step with
+ * and without update runs eagerly and sizes every workspace, the second is
+ * captured. Same results as eager steps. Tensor shapes and buffers are fixed
+ * per trainer, so a graph never goes stale; disable to release the graphs.
+ * On an expert-parallel trainer every rank must use the same setting. */
 int catnn_moe_trainer_set_graphs(catnn_moe_trainer* t, int enable);
 
 /* ------------------------------------------------------------ multi-GPU (one node) */

@@ -40,6 +40,7 @@ def main():
     ap.add_argument("--config", default="f32")
     ap.add_argument("--out", required=True)
     ap.add_argument("--steps", type=int, default=2)
+    ap.add_argument("--graphs", action="store_true", help="replay the step as a CUDA graph")
     a = ap.parse_args()
     rank, world, local = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"]), int(os.environ["LOCAL_RANK"])
     torch.cuda.set_device(local)
@@ -49,6 +50,9 @@ def main():
         cfg = config(a.config)
         tr = MoeTrainer(cfg, local, comm=comm)
         tr.set_params(init_params(cfg, seed=3))
+        if a.graphs:
+            # the first update step runs eagerly, the second is captured, later ones replay
+            tr.set_graphs(True)
         tok = torch.as_tensor(tokens(cfg).astype(np.int32)).to(f"cuda:{local}")
         loss = torch.zeros(1, device=f"cuda:{local}")
         tr.step(tok, update=False, loss_out=loss)
@@ -63,6 +67,12 @@ def main():
         out["params"] = tr.params().cpu().numpy()
         out["x_last"] = tr.activation("x_last").cpu().numpy()
         np.savez(os.path.join(a.out, f"rank{rank}.npz"), **out)
+        if a.graphs:
+            # replays of the captured steps: every device wait must still hold
+            for upd in (True, True, False, False, True):
+                tr.step(tok, update=upd, loss_out=loss)
+            tr.check()
+            assert np.isfinite(float(loss.item()))
         torch.cuda.synchronize()
         tr.close()
         comm.close()

@@ -119,16 +119,21 @@ def _expert_mask(cfg, world, rank):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-@pytest.mark.parametrize("name", ["f32", "bf16"])
-def test_ep_two_ranks_match_single_gpu(name, tmp_path):
+@pytest.mark.parametrize("name,graphs", [("f32", False), ("bf16", False), ("bf16", True)])
+def test_ep_two_ranks_match_single_gpu(name, graphs, tmp_path):
+    """graphs=True: the ranks run their update steps as CUDA graphs (device
+    barriers, peer-memory exchanges and NCCL allreduces inside): the second
+    update step is captured and launched; after the compared state is saved
+    the worker replays more steps and checks every bounded wait held."""
     world = 2
+    steps = 2
     env = dict(os.environ, NCCL_NVLS_ENABLE="0")
     cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", f"--nproc-per-node={world}",
            "--master-addr=127.0.0.1", "--master-port=29541", os.path.join(HERE, "ep_worker.py"), "--config", name,
-           "--out", str(tmp_path)]
+           "--out", str(tmp_path), "--steps", str(steps)] + (["--graphs"] if graphs else [])
     r = subprocess.run(cmd, env=env, capture_output=True, text=True, timeout=600)
     assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
-    cfg, ref = _single(name)
+    cfg, ref = _single(name, steps)
     ranks = [dict(np.load(tmp_path / f"rank{q}.npz")) for q in range(world)]
     masks = [_expert_mask(cfg, world, q) for q in range(world)]
     anyexp = np.any(masks, axis=0)

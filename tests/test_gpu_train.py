@@ -234,7 +234,7 @@ def test_graph_replay_matches_eager():
     b.set_graphs(True)
     la, lb = torch.zeros(1, device="cuda"), torch.zeros(1, device="cuda")
     n0 = b.ctx.launch_count()
-    for upd in (False, False, True, True, True, False, True):
+    for upd in (True, True, True, False, False, False, True):
         a.step(tok, update=upd, loss_out=la)
         b.step(tok, update=upd, loss_out=lb)
         torch.cuda.synchronize()
