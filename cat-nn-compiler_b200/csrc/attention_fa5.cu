@@ -343,7 +343,8 @@ constexpr int NTB = 320, NCW = 8;
 constexpr uint32_t T64 = 64 * HD * 2;            // 8 KB: a 64-row tile
 constexpr uint32_t T128 = 128 * HD * 2;          // 16 KB: a 128-row tile
 constexpr uint32_t QD_STAGE = 2 * T64 + 1024;    // Q, dO and the block's L, D
-constexpr size_t SMEM_DKDV = 2 * T128 + 2 * QD_STAGE + 2 * T128 + 1024 + 512;
+constexpr int QS = 4;  // Q/dO stages of k_dkdv
+constexpr size_t SMEM_DKDV = 2 * T128 + QS * QD_STAGE + 4 * T128 + 1024 + 512;
 constexpr size_t SMEM_DQ = 2 * T128 + 3 * 2 * T64 + T128 + 1024 + 512;
 
 struct BwdArgs {
@@ -389,28 +390,33 @@ __device__ __forceinline__ void ld_row64(uint32_t taddr, uint32_t (&v)[64]) {
     tc::tmem_ld32(taddr + 32, v1);
 }
 
-__global__ void __launch_bounds__(NTB, 2)
+// One CTA per SM: a 4-deep Q/dO ring keeps the loads about three blocks
+// ahead (the tiles come from L2 with ~2 K cycles of latency), and Sᵀ/dPᵀ
+// (TMEM) and P/dS (shared memory) are double-buffered so the MMAs of one
+// block overlap the next block's math.
+__global__ void __launch_bounds__(NTB, 1)
     k_dkdv(const __grid_constant__ CUtensorMap mk, const __grid_constant__ CUtensorMap mv,
            const __grid_constant__ CUtensorMap mq, const __grid_constant__ CUtensorMap mdo, BwdArgs a) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
     uint8_t* sK = smem;
     uint8_t* sV = sK + T128;
-    uint8_t* sQD = sV + T128;  // 2 stages: Q | dO | L[64] D[64]
-    uint8_t* sP = sQD + 2 * QD_STAGE;
-    uint8_t* sDS = sP + T128;
-    uint64_t* bars = (uint64_t*)(sDS + T128);
+    uint8_t* sQD = sV + T128;  // QS stages: Q | dO | L[64] D[64]
+    uint8_t* sP = sQD + QS * QD_STAGE;  // [2] Pᵀ tiles
+    uint8_t* sDS = sP + 2 * T128;       // [2] dSᵀ tiles
+    uint64_t* bars = (uint64_t*)(sDS + 2 * T128);
     uint64_t* kv_full = bars;
     uint64_t* qd_full = kv_full + 1;
-    uint64_t* qd_empty = qd_full + 2;
-    uint64_t* st_full = qd_empty + 2;
-    uint64_t* st_free = st_full + 1;
-    uint64_t* pd_full = st_free + 1;
-    uint64_t* pd_free = pd_full + 1;
-    uint64_t* acc_full = pd_free + 1;
+    uint64_t* qd_empty = qd_full + QS;
+    uint64_t* st_full = qd_empty + QS;
+    uint64_t* st_free = st_full + 2;
+    uint64_t* pd_full = st_free + 2;
+    uint64_t* pd_free = pd_full + 2;
+    uint64_t* acc_full = pd_free + 2;
     uint64_t* drain = acc_full + 1;
     uint32_t* tmem_slot = (uint32_t*)(drain + 1);
-    constexpr uint32_t C_S = 0, C_DP = 64, C_DV = 128, C_DK = 192;
+    // TMEM columns: Sᵀ[2] 0 / 64, dPᵀ[2] 128 / 192, dV 256, dK 320
+    constexpr uint32_t C_S = 0, C_DP = 128, C_DV = 256, C_DK = 320;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int kb = gridDim.x - 1 - blockIdx.x;  // early keys see the most queries: first
@@ -423,19 +429,21 @@ __global__ void __launch_bounds__(NTB, 2)
 
     if (threadIdx.x == 0) {
         tc::mbar_init(kv_full, 1);
-        for (int i = 0; i < 2; ++i) {
+        for (int i = 0; i < QS; ++i) {
             tc::mbar_init(&qd_full[i], 1);
             tc::mbar_init(&qd_empty[i], 1);
         }
-        tc::mbar_init(st_full, 1);
-        tc::mbar_init(st_free, NCW);
-        tc::mbar_init(pd_full, NCW);
-        tc::mbar_init(pd_free, 1);
+        for (int i = 0; i < 2; ++i) {
+            tc::mbar_init(&st_full[i], 1);
+            tc::mbar_init(&st_free[i], NCW);
+            tc::mbar_init(&pd_full[i], NCW);
+            tc::mbar_init(&pd_free[i], 1);
+        }
         tc::mbar_init(acc_full, 1);
         tc::mbar_init(drain, 1);
         tc::fence_mbar_init();
     }
-    if (warp == 1) tc::tmem_alloc(tmem_slot, 256);
+    if (warp == 1) tc::tmem_alloc(tmem_slot, 512);
     tc::tc_fence_before();
     __syncthreads();
     tc::tc_fence_after();
@@ -448,14 +456,16 @@ __global__ void __launch_bounds__(NTB, 2)
             tc::tma_load_2d(sK, &mk, kvh * HD, (int)(seq_row + k0), kv_full);
             tc::tma_load_2d(sV, &mv, kvh * HD, (int)(seq_row + k0), kv_full);
         }
-        int last_ph[2] = {-1, -1};
+        int last_ph[QS];
+        for (int i = 0; i < QS; ++i) last_ph[i] = -1;
         int ok = 1;
         for (int it = 0; it < n; ++it) {
-            const int st = it & 1;
-            if (lane == 0) ok = tc::mbar_wait(&qd_empty[st], ((it >> 1) & 1) ^ 1, a.status, 4);
+            const int st = it % QS;
+            const int ph = (it / QS) & 1;
+            if (lane == 0) ok = tc::mbar_wait(&qd_empty[st], ph ^ 1, a.status, 4);
             ok = __shfl_sync(0xffffffffu, ok, 0);
             if (!ok) break;
-            last_ph[st] = (it >> 1) & 1;
+            last_ph[st] = ph;
             const int h = kvh * grp + it / nq;
             const int q0 = (qb0 + it % nq) * BB;
             uint8_t* stg = sQD + st * QD_STAGE;
@@ -478,7 +488,7 @@ __global__ void __launch_bounds__(NTB, 2)
         if (!ok && lane == 0) {
             // let the copies in flight land before the CTA exits
             tc::mbar_wait(kv_full, 0, a.status, 4, 400000000ll, false);
-            for (int i = 0; i < 2; ++i)
+            for (int i = 0; i < QS; ++i)
                 if (last_ph[i] >= 0) tc::mbar_wait(&qd_full[i], (uint32_t)last_ph[i], a.status, 4, 400000000ll, false);
         }
     } else if (warp == 1) {
@@ -488,40 +498,40 @@ __global__ void __launch_bounds__(NTB, 2)
             constexpr uint32_t ID_A = tc::idesc_bf16(128, HD, false, true);   // dV, dK
             bool ok = tc::mbar_wait(kv_full, 0, a.status, 4);
             const uint32_t aK = tc::smem_u32(sK), aV = tc::smem_u32(sV);
-            const uint32_t aP = tc::smem_u32(sP), aDS = tc::smem_u32(sDS);
-            // Sᵀ, dPᵀ of block it: issued as soon as the compute warps hold the
-            // previous block's in registers, so they overlap that block's math
+            // Sᵀ, dPᵀ of block it into buffer it & 1, once that buffer's previous
+            // contents are in the compute warps' registers
             auto issue_st = [&](int it) -> bool {
-                const int st = it & 1;
-                if (!tc::mbar_wait(&qd_full[st], (it >> 1) & 1, a.status, 4) ||
-                    !tc::mbar_wait(st_free, (it & 1) ^ 1, a.status, 4))
+                const int st = it % QS, sb = it & 1;
+                if (!tc::mbar_wait(&qd_full[st], (it / QS) & 1, a.status, 4) ||
+                    !tc::mbar_wait(&st_free[sb], ((it >> 1) & 1) ^ 1, a.status, 4))
                     return false;
                 tc::tc_fence_after();
                 const uint32_t bQ = tc::smem_u32(sQD + st * QD_STAGE), bO = bQ + T64;
 #pragma unroll
                 for (int kk = 0; kk < HD / 16; ++kk)
-                    tc::mma_bf16(tmem + C_S, tc::sdesc(aK + kk * 32, 16, 1024), tc::sdesc(bQ + kk * 32, 16, 1024), ID_T,
-                                 kk != 0);
+                    tc::mma_bf16(tmem + C_S + sb * BB, tc::sdesc(aK + kk * 32, 16, 1024), tc::sdesc(bQ + kk * 32, 16, 1024),
+                                 ID_T, kk != 0);
 #pragma unroll
                 for (int kk = 0; kk < HD / 16; ++kk)
-                    tc::mma_bf16(tmem + C_DP, tc::sdesc(aV + kk * 32, 16, 1024), tc::sdesc(bO + kk * 32, 16, 1024), ID_T,
-                                 kk != 0);
-                tc::mma_commit(st_full);
+                    tc::mma_bf16(tmem + C_DP + sb * BB, tc::sdesc(aV + kk * 32, 16, 1024), tc::sdesc(bO + kk * 32, 16, 1024),
+                                 ID_T, kk != 0);
+                tc::mma_commit(&st_full[sb]);
                 return true;
             };
             if (ok && n > 0) ok = issue_st(0);
             for (int it = 0; it < n && ok; ++it) {
-                const int st = it & 1;
+                const int st = it % QS, pb = it & 1;
                 const uint32_t bQ = tc::smem_u32(sQD + st * QD_STAGE), bO = bQ + T64;
                 if (it + 1 < n && !issue_st(it + 1)) {
                     ok = false;
                     break;
                 }
-                if (!tc::mbar_wait(pd_full, it & 1, a.status, 4)) {
+                if (!tc::mbar_wait(&pd_full[pb], (it >> 1) & 1, a.status, 4)) {
                     ok = false;
                     break;
                 }
                 tc::tc_fence_after();
+                const uint32_t aP = tc::smem_u32(sP + pb * T128), aDS = tc::smem_u32(sDS + pb * T128);
 #pragma unroll
                 for (int kk = 0; kk < BB / 16; ++kk)
                     tc::mma_bf16(tmem + C_DV, tc::sdesc(aP + kk * 32, 16, 1024), tc::sdesc(bO + kk * 2048, 8192, 1024),
@@ -530,7 +540,7 @@ __global__ void __launch_bounds__(NTB, 2)
                 for (int kk = 0; kk < BB / 16; ++kk)
                     tc::mma_bf16(tmem + C_DK, tc::sdesc(aDS + kk * 32, 16, 1024), tc::sdesc(bQ + kk * 2048, 8192, 1024),
                                  ID_A, (it | kk) != 0);
-                tc::mma_commit(pd_free);
+                tc::mma_commit(&pd_free[pb]);
                 tc::mma_commit(&qd_empty[st]);
             }
             if (ok) tc::mma_commit(acc_full);
@@ -545,33 +555,32 @@ __global__ void __launch_bounds__(NTB, 2)
         const uint32_t lane_off = (uint32_t)(qd * 32) << 16;
         const float sc = a.scale * LOG2E;
         const int qlo = bqlo(a, key), qhi = bqhi(a, key);
-        const uint32_t prow = tc::smem_u32(sP) + r * 128, dsrow = tc::smem_u32(sDS) + r * 128;
         bool ok = true;
         for (int it = 0; it < n && ok; ++it) {
-            const int st = it & 1;
+            const int st = it % QS, sb = it & 1;
             const int q0 = (qb0 + it % nq) * BB;
-            if (!tc::mbar_wait(st_full, it & 1, a.status, 4)) {
+            if (!tc::mbar_wait(&st_full[sb], (it >> 1) & 1, a.status, 4)) {
                 ok = false;
                 break;
             }
             tc::tc_fence_after();
             uint32_t s[32], dp[32];
-            tc::tmem_ld32(tmem + lane_off + C_S + c0, s);
-            tc::tmem_ld32(tmem + lane_off + C_DP + c0, dp);
+            tc::tmem_ld32(tmem + lane_off + C_S + sb * BB + c0, s);
+            tc::tmem_ld32(tmem + lane_off + C_DP + sb * BB + c0, dp);
             tc::tmem_ld_wait();
             tc::tc_fence_before();
             __syncwarp();
-            if (lane == 0) tc::mbar_arrive(st_free);
+            if (lane == 0) tc::mbar_arrive(&st_free[sb]);
             // no masking when every (query, key) pair of the block is visible
             const bool full = q0 >= bqlo(a, klast) && q0 + BB - 1 <= bqhi(a, k0) && q0 + BB - 1 < a.s;
             const float* sL = (const float*)(sQD + st * QD_STAGE + 2 * T64);
             const float* sD = sL + 64;
-            // the MMAs of the previous block have read P and dS (their commit
-            // precedes the one that filled S and dP: no wait in practice)
-            if (!tc::mbar_wait(pd_free, (it & 1) ^ 1, a.status, 4)) {
+            // the MMAs of block it - 2 have read this P / dS buffer
+            if (!tc::mbar_wait(&pd_free[sb], ((it >> 1) & 1) ^ 1, a.status, 4)) {
                 ok = false;
                 break;
             }
+            const uint32_t prow = tc::smem_u32(sP + sb * T128) + r * 128, dsrow = tc::smem_u32(sDS + sb * T128) + r * 128;
 #pragma unroll
             for (int ch = 0; ch < 4; ++ch) {
                 float p[8], ds[8];
@@ -592,7 +601,7 @@ __global__ void __launch_bounds__(NTB, 2)
             }
             tc::fence_proxy_async();
             __syncwarp();
-            if (lane == 0) tc::mbar_arrive(pd_full);
+            if (lane == 0) tc::mbar_arrive(&pd_full[sb]);
         }
         if (ok && n > 0 && tc::mbar_wait(acc_full, 0, a.status, 4)) {
             tc::tc_fence_after();
@@ -623,7 +632,7 @@ __global__ void __launch_bounds__(NTB, 2)
     __syncthreads();
     if (warp == 1) {
         tc::tc_fence_after();
-        tc::tmem_dealloc(tmem, 256);
+        tc::tmem_dealloc(tmem, 512);
     }
 }
 
