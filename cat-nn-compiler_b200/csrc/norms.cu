@@ -473,6 +473,92 @@ __global__ void k_rms_cols_mx(const TX* __restrict__ x, const TG* __restrict__ d
     pw[(i64)blockIdx.y * last + j] = sw;
 }
 
+// MoE input of a layer in one pass over x (fp32 [rows, NC*1024]): the RMSNorm
+// y = x·inv·w (moe.rs:317; k_rms_fwd_mx's expression), stored as bf16 for the
+// expert GEMMs and as fp32 for the router, and the router logits y·gate
+// (gate fp32 [last, E], E <= 32) from registers: each of the 256 threads
+// holds 4·NC columns and their gate rows for every row the CTA visits.
+template <int NC, int EB>
+__global__ void __launch_bounds__(256) k_rms_router(const float* __restrict__ x, const float* __restrict__ w,
+                                                    const float* __restrict__ gate, int E, i64 rows, float eps,
+                                                    bf16* __restrict__ y16, float* __restrict__ y32,
+                                                    float* __restrict__ logits) {
+    constexpr int last = NC * 1024;
+    __shared__ float red[8];
+    __shared__ float lred[8][EB];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    float wv[NC][4], gv[NC][4][EB];
+#pragma unroll
+    for (int g = 0; g < NC; ++g) {
+        const int c = g * 1024 + threadIdx.x * 4;
+        ldv<float, 4>(w + c, wv[g]);
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+#pragma unroll
+            for (int e = 0; e < EB; ++e) gv[g][u][e] = e < E ? gate[(i64)(c + u) * E + e] : 0.f;
+    }
+    for (i64 r = blockIdx.x; r < rows; r += gridDim.x) {
+        float xv[NC][4];
+        float ss = 0.f;
+#pragma unroll
+        for (int g = 0; g < NC; ++g) {
+            ldv<float, 4>(x + r * last + g * 1024 + threadIdx.x * 4, xv[g]);
+#pragma unroll
+            for (int u = 0; u < 4; ++u) ss += xv[g][u] * xv[g][u];
+        }
+        ss = warp_sum(ss);
+        if (lane == 0) red[warp] = ss;
+        __syncthreads();
+        float tot = 0.f;
+#pragma unroll
+        for (int k = 0; k < 8; ++k) tot += red[k];
+        const float inv = 1.0f / sqrtf(tot / (float)last + eps);
+        float lg[EB];
+#pragma unroll
+        for (int e = 0; e < EB; ++e) lg[e] = 0.f;
+#pragma unroll
+        for (int g = 0; g < NC; ++g) {
+            float yv[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                yv[u] = xv[g][u] * inv * wv[g][u];
+#pragma unroll
+                for (int e = 0; e < EB; ++e) lg[e] = fmaf(yv[u], gv[g][u][e], lg[e]);
+            }
+            const i64 o = r * last + g * 1024 + threadIdx.x * 4;
+            stv<float, 4>(y32 + o, yv);
+            stv<bf16, 4>(y16 + o, yv);
+        }
+#pragma unroll
+        for (int e = 0; e < EB; ++e) lg[e] = warp_sum(lg[e]);
+        if (lane == 0)
+#pragma unroll
+            for (int e = 0; e < EB; ++e) lred[warp][e] = lg[e];
+        __syncthreads();
+        if (threadIdx.x < E) {
+            float t = 0.f;
+#pragma unroll
+            for (int k = 0; k < 8; ++k) t += lred[k][threadIdx.x];
+            logits[r * E + threadIdx.x] = t;
+        }
+        __syncthreads();  // red / lred are rewritten by the next row
+    }
+}
+
+bool rms_router_fused(Context* c, const float* x, const float* w, const float* gate, i64 E, i64 rows, i64 last,
+                      float eps, bf16* y16, float* y32, float* logits) {
+    const int nc = (int)(last / 1024);
+    if (rows <= 0 || last % 1024 != 0 || nc < 1 || nc > 2 || E < 1 || E > 16) return false;
+    if (!aligned_to(x, 16) || !aligned_to(w, 16) || !aligned_to(y16, 8) || !aligned_to(y32, 16)) return false;
+    const int grid = (int)std::min<i64>(rows, (i64)c->sm_count * 8);
+    if (nc == 1 && E <= 8) k_rms_router<1, 8><<<grid, 256, 0, c->stream>>>(x, w, gate, (int)E, rows, eps, y16, y32, logits);
+    else if (nc == 1) k_rms_router<1, 16><<<grid, 256, 0, c->stream>>>(x, w, gate, (int)E, rows, eps, y16, y32, logits);
+    else if (E <= 8) k_rms_router<2, 8><<<grid, 256, 0, c->stream>>>(x, w, gate, (int)E, rows, eps, y16, y32, logits);
+    else k_rms_router<2, 16><<<grid, 256, 0, c->stream>>>(x, w, gate, (int)E, rows, eps, y16, y32, logits);
+    launched(c);
+    return true;
+}
+
 void rmsnorm_fwd_mixed(Context* c, const void* x, int x_dtype, const float* w, void* y, int y_dtype, i64 rows, i64 last,
                        float eps) {
     if (rows <= 0 || last <= 0) return;

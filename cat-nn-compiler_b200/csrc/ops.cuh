@@ -95,6 +95,11 @@ void rmsnorm_bwd(Context* c, const void* x, const float* w, const void* dy, void
                  i64 last, float eps, int dtype, bool dw_accumulate, const void* dres = nullptr);
 
 // Mixed storage: fp32 residual stream in, bf16 (or fp32) normalized out.
+// The MoE input in one pass (width a multiple of 1024 up to 2048, E <= 16,
+// aligned rows): bf16 and fp32 RMSNorm outputs and the router logits
+// y32·gate. Returns false (nothing launched) when the shape does not fit.
+bool rms_router_fused(Context* c, const float* x, const float* w, const float* gate, i64 E, i64 rows, i64 last,
+                      float eps, bf16* y16, float* y32, float* logits);
 void rmsnorm_fwd_mixed(Context* c, const void* x, int x_dtype, const float* w, void* y, int y_dtype, i64 rows, i64 last,
                        float eps);
 // dx (fp32) = rmsnorm adjoint of dy (g_dtype) at x (fp32) + dres (fp32, optional);

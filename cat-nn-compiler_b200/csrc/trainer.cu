@@ -313,9 +313,13 @@ void MoeTrainer::forward() {
         // The router runs in fp32 on every path (fp32 normalized input, fp32
         // master gate): top-k decisions then match the reference's f32 logits
         // instead of flipping near ties on bf16-rounded inputs.
-        rmsnorm_fwd_mixed(c, a.x_mid, CATNN_F32, P + q.rms_moe, a.xm, dt, T, d, eps);
-        if (dt == CATNN_BF16) rmsnorm_fwd_mixed(c, a.x_mid, CATNN_F32, P + q.rms_moe, a.xm32, CATNN_F32, T, d, eps);
-        gemm(c, false, false, T, E, d, a.xm32, d, P + q.gate, E, a.logits, E, CATNN_F32, CATNN_F32, nullptr, 0, false);
+        if (dt != CATNN_BF16 || !rms_router_fused(c, a.x_mid, P + q.rms_moe, P + q.gate, E, T, d, eps, (bf16*)a.xm,
+                                                  a.xm32, a.logits)) {
+            rmsnorm_fwd_mixed(c, a.x_mid, CATNN_F32, P + q.rms_moe, a.xm, dt, T, d, eps);
+            if (dt == CATNN_BF16) rmsnorm_fwd_mixed(c, a.x_mid, CATNN_F32, P + q.rms_moe, a.xm32, CATNN_F32, T, d, eps);
+            gemm(c, false, false, T, E, d, a.xm32, d, P + q.gate, E, a.logits, E, CATNN_F32, CATNN_F32, nullptr, 0,
+                 false);
+        }
         router_topk(c, a.logits, T, E, K, a.idx, a.w);
         if (!ep) {
             permute_map(c, a.idx, T, E, K, align, cap, a.counts, a.off, a.row_of, a.src_of);
