@@ -51,7 +51,8 @@ def peaks():
 
 
 def step_flops(cfg, tokens):
-    """Algorithmic FLOPs of one training step (forward x3), per SURVEY §8(d)."""
+    """Algorithmic FLOPs of one training step: the GEMM and attention FLOPs of the forward, times 3
+    (forward + the two backward products)."""
     d, F, V, S, L, k = cfg["hidden"], cfg["mid"], cfg["vocab"], cfg["seq"], cfg["layers"], cfg["top_k"]
     E = cfg["experts"]
     per_tok = L * (8 * d * d + 2 * d * (S + 1) + k * 6 * d * F + 2 * d * E) + 2 * d * V

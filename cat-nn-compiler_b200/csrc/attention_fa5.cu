@@ -383,13 +383,6 @@ __device__ __forceinline__ void st_chunk8(uint32_t row_addr, int r, int chunk, c
                  : "memory");
 }
 
-__device__ __forceinline__ void ld_row64(uint32_t taddr, uint32_t (&v)[64]) {
-    uint32_t (&v0)[32] = *reinterpret_cast<uint32_t(*)[32]>(&v[0]);
-    uint32_t (&v1)[32] = *reinterpret_cast<uint32_t(*)[32]>(&v[32]);
-    tc::tmem_ld32(taddr, v0);
-    tc::tmem_ld32(taddr + 32, v1);
-}
-
 // One CTA per SM: a 4-deep Q/dO ring keeps the loads about three blocks
 // ahead (the tiles come from L2 with ~2 K cycles of latency), and Sᵀ/dPᵀ
 // (TMEM) and P/dS (shared memory) are double-buffered so the MMAs of one

@@ -96,6 +96,6 @@ def test_packed_layout_matches_oracle_and_abi(libpath):
         n = C.c_int64()
         _lib.call("catnn_moe_trainer_param_count", C.byref(cfg), C.byref(n))
         assert n.value == ref["total"]
-    # config 5: about 435 M parameters (SURVEY: ≈434.7 M with n_kv = 16)
+    # config 5: about 435 M parameters (n_kv = 16)
     big = O.MixCfg(32000, 1024, 3584, 4, 16, 16, 8, 2).layout()["total"]
     assert 4.3e8 < big < 4.4e8

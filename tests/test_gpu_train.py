@@ -59,7 +59,7 @@ def tc_inputs(cfg, P):
 def run_compare(cfg, P, tokens, close, steps=1, exact=False, report=None, oracle_params=None):
     """exact=True also runs the oracle's f64 instantiation and passes it to
     `close` so an element the fp32 oracle itself rounds worse than the band
-    allows is judged against the exact value."""
+    allows is checked against the exact value."""
     tr = MoeTrainer(cfg)
     tr.set_params(P)
     tok = torch.as_tensor(tokens.astype(np.int32)).cuda()
@@ -77,7 +77,7 @@ def run_compare(cfg, P, tokens, close, steps=1, exact=False, report=None, oracle
         ex = O.mixtral_step(oc, Pref.astype(np.float64), tokens, cfg.batch, cfg.seq, f64=True) if exact else None
         close(loss, np.float32(rl), what=f"loss step {s}", exact=None if ex is None else ex[0])
         g = tr.grads().cpu().numpy()
-        gscale = float(np.max(np.abs(rg)))  # a tensor whose gradient vanishes is judged on the model's scale
+        gscale = float(np.max(np.abs(rg)))  # a tensor whose gradient vanishes is measured on the model's scale
         for name, sl in groups(cfg):
             close(g[sl], rg[sl], what=f"grad {name} step {s}", exact=None if ex is None else ex[1][sl],
                   scale=max(gscale * 1e-2, float(np.max(np.abs(rg[sl])))))
