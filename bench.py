@@ -169,6 +169,47 @@ def dominant_kernel(local, pairs, E, warm, reps):
     return e0.elapsed_time(e1) / reps, 2.0 * int(counts.sum()) * 2 * F * d, rows, F, d
 
 
+def gemm_sweep(local, peak):
+    """Config 2: C = A·B with M = N = K in {1024, 4096, 8192}, A and B N(0,1)/sqrt(K)
+    and N(0,1), bf16 operands, fp32 accumulation; forward (2K³) and forward +
+    backward (dA = dC·Bᵀ, dB = Aᵀ·dC: 6K³), timed with CUDA events."""
+    import torch
+    from catnn_b200 import ops
+    g = torch.Generator(device=f"cuda:{local}").manual_seed(1)
+    out = {}
+    stream = torch.cuda.current_stream(local)
+    for K in (1024, 4096, 8192):
+        A = (torch.randn(K, K, generator=g, device=f"cuda:{local}") / K ** 0.5).to(torch.bfloat16)
+        B = torch.randn(K, K, generator=g, device=f"cuda:{local}").to(torch.bfloat16)
+        dC = torch.randn(K, K, generator=g, device=f"cuda:{local}").to(torch.bfloat16)
+        C, dA, dB = (torch.empty(K, K, device=f"cuda:{local}", dtype=torch.bfloat16) for _ in range(3))
+        reps = 20 if K < 8192 else 8
+
+        def fwd():
+            ops.gemm(A, B, out=C)
+
+        def fwdbwd():
+            ops.gemm(A, B, out=C)
+            ops.gemm(dC, B, trans_b=True, out=dA)
+            ops.gemm(A, dC, trans_a=True, out=dB)
+        res = {}
+        for name, f, flops in (("fwd", fwd, 2 * K ** 3), ("fwd_bwd", fwdbwd, 6 * K ** 3)):
+            for _ in range(3):
+                f()
+            torch.cuda.synchronize(local)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            for _ in range(reps):
+                f()
+            e1.record(stream)
+            torch.cuda.synchronize(local)
+            ms = e0.elapsed_time(e1) / reps
+            tf = flops / (ms * 1e-3) / 1e12
+            res[name] = {"ms": round(ms, 4), "tflops": round(tf, 1), "frac": round(tf / peak, 3)}
+        out[str(K)] = res
+    return out
+
+
 def run_kernel_only(args):
     import torch
     torch.cuda.set_device(0)
@@ -311,6 +352,9 @@ def run_ours(args):
                      "algorithmic_bytes": gemm_bytes(rows, cfg["experts"] // world, F, d), "launch_ms": kms},
         "clocks": clk,
     }
+    if world == 1:
+        # config 2 (dense GEMM fwd / fwd+bwd, bf16): the metric's "GEMM TFLOP/s and % of tensor peak"
+        out["gemm_sweep"] = {"peak_tflops": peak, "peak_source": f"{pk_kind} bf16_tflops", **gemm_sweep(local, peak)}
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         P_host = tr.params().cpu().numpy()
         out["cpu_baseline"] = cpu_baseline_port(P_host, cfg)

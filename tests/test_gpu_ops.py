@@ -445,3 +445,70 @@ def test_attention_core_bf16_tensor_core(b, s, h, kv, hd, causal, window):
     for name, a16, a32 in zip(("dq", "dk", "dv"), g16, g32):
         assert rel_l2(a16, host(a32)) < 1e-2, (name, rel_l2(a16, host(a32)))
         close_bf16(a16, host(a32), what=f"fa bwd {name}", atol=4e-3)
+
+
+# ------------------------------------------------------------------ BASELINE configs 1 and 3
+def test_mlp_twelve_sgd_steps_match_oracle():
+    """Config 1's run: the f32 MLP (784 -> 256 ReLU -> 10, softmax cross-entropy)
+    trained for 12 SGD steps (lr 0.05) on the GPU and in the oracle from the
+    same Xavier-uniform weights; all 12 losses and the final weights agree at
+    the fp32 band (train.rs:71 mlp_step, optim.rs:32 Sgd::put)."""
+    r = rng(0)
+    a1, a2 = np.sqrt(6.0 / (784 + 256)), np.sqrt(6.0 / (256 + 10))
+    w1 = r.uniform(-a1, a1, (784, 256)).astype(np.float32)
+    w2 = r.uniform(-a2, a2, (256, 10)).astype(np.float32)
+    b1, b2 = np.zeros(256, np.float32), np.zeros(10, np.float32)
+    x = r.standard_normal((64, 784)).astype(np.float32)
+    lab = r.integers(0, 10, 64)
+    gw = [dev(t) for t in (w1, b1, w2, b2)]
+    X, L = dev(x), dev(lab, torch.int32)
+    ow = [t.copy() for t in (w1, b1, w2, b2)]
+    for step in range(12):
+        loss, *grads = ops.mlp_step(*gw, X, labels=L)
+        for p, g in zip(gw, grads):
+            ops.sgd_(p, g, 0.05)
+        rl, *rg = O.mlp_step(*ow, x, labels=lab)
+        ow = [O.sgd_put(p, g, 0.05) for p, g in zip(ow, rg)]
+        close_f32(np.float32(float(loss)), np.float32(rl), what=f"loss at step {step}")
+    for name, g, o in zip(("w1", "b1", "w2", "b2"), gw, ow):
+        close_f32(g, o, floor=1e-4, what=f"{name} after 12 steps")
+
+
+def test_transformer_block_fwd_bwd_f32():
+    """Config 3's block (pre-LN, causal multi-head attention, GELU FFN, both
+    residuals; fp32 weights N(0, 0.02), LayerNorm gamma 1 / beta 0, injected dY)
+    composed from the GPU operators in the oracle's order, against the oracle's
+    block (a reduced shape: B2 S128 d256 h4 FFN 1024, so the sequential oracle
+    runs in seconds)."""
+    r = rng(2)
+    b, s, d, h, ff = 2, 128, 256, 4, 1024
+    W = {"g1": np.ones(d, np.float32), "be1": np.zeros(d, np.float32), "g2": np.ones(d, np.float32),
+         "be2": np.zeros(d, np.float32), "c1": np.zeros(ff, np.float32), "c2": np.zeros(d, np.float32)}
+    for k, shape in (("wq", (d, d)), ("wk", (d, d)), ("wv", (d, d)), ("wo", (d, d)), ("f1", (d, ff)), ("f2", (ff, d))):
+        W[k] = (r.standard_normal(shape) * 0.02).astype(np.float32)
+    x = r.standard_normal((b, s, d)).astype(np.float32)
+    dy = r.standard_normal((b, s, d)).astype(np.float32)
+    G = {k: dev(v) for k, v in W.items()}
+    X, DY = dev(x), dev(dy)
+    ln1 = ops.layer_norm(X, G["g1"], G["be1"])
+    att = ops.attention(ln1, G["wq"], G["wk"], G["wv"], G["wo"], h, causal=True)
+    hh = ops.add(X, att)
+    ln2 = ops.layer_norm(hh, G["g2"], G["be2"])
+    u = ops.linear(ln2, G["f1"], G["c1"])
+    gl = ops.gelu(u)
+    y = ops.add(hh, ops.linear(gl, G["f2"], G["c2"]))
+    dgl, df2, dc2 = ops.linear_backward(gl, G["f2"], DY)
+    du = ops.gelu_backward(u, dgl)
+    dln2, df1, dc1 = ops.linear_backward(ln2, G["f1"], du)
+    dh, dg2, dbe2 = ops.layer_norm_backward(hh, G["g2"], dln2)
+    dh = ops.add(dh, DY)
+    dln1, dwq, dwk, dwv, dwo = ops.attention_backward(ln1, G["wq"], G["wk"], G["wv"], G["wo"], dh, h, causal=True)
+    dxa, dg1, dbe1 = ops.layer_norm_backward(X, G["g1"], dln1)
+    dx = ops.add(dxa, dh)
+    ry, rdx, rg = O.block_fwd_bwd(W, x, dy, h)
+    close_f32(y, ry, rtol=1e-4, floor=1e-5, what="block y")
+    close_f32(dx, rdx, rtol=1e-4, floor=1e-4, what="block dx")
+    got = {"g1": dg1, "be1": dbe1, "wq": dwq, "wk": dwk, "wv": dwv, "wo": dwo, "g2": dg2, "be2": dbe2, "f1": df1,
+           "c1": dc1, "f2": df2, "c2": dc2}
+    for k, g in got.items():
+        close_f32(g, rg[k], rtol=1e-4, floor=1e-4, what=f"block d{k}")
