@@ -62,6 +62,8 @@ SIGNATURES = {
     "catnn_moe_permute": [VP, VP, VP, I64, I64, I64, VP, I32],
     "catnn_moe_unpermute": [VP, VP, VP, VP, I64, I64, I64, VP, I32],
     "catnn_grouped_gemm": [VP, I32, I64, I64, I64, I64, VP, VP, VP, VP, I32, I32],
+    "catnn_moe_expert_swiglu_fwd": [VP, VP, VP, VP, I64, I64, I64, I64, VP, VP],
+    "catnn_moe_expert_swiglu_bwd": [VP, VP, VP, VP, VP, I64, I64, I64, I64, VP],
     "catnn_swiglu_fwd": [VP, VP, VP, VP, VP, VP, I64, I64, I64, I32],
     "catnn_swiglu_bwd": [VP, VP, VP, VP, VP, VP, VP, VP, VP, VP, I64, I64, I64, I32],
     "catnn_moe_fwd": [VP, VP, VP, VP, VP, VP, VP, I64, I64, I64, I64, I64, I32],

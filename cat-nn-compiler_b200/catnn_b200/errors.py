@@ -54,6 +54,12 @@ class CommError(CatError):
     code = 10
 
 
+class Fibration(CatError):
+    """An activation that cannot be rebuilt on this device (raised on the host
+    only, as coord.rs:443-458 does)."""
+    code = 12
+
+
 _BY_CODE = {cls.code: cls for cls in (ShapeMismatch, DTypeMismatch, UnknownPort, Wiring, Unlawful, CudaError,
                                       InvalidArgument, DeviceTimeout, Unsupported, CommError)}
 

@@ -436,6 +436,38 @@ def grouped_gemm(a, b, offsets, trans_b=False, out=None, out_dtype=None):
     return out
 
 
+def interleave_w13(w1s, w3s):
+    """[E, hidden, 2·mid] with each expert's w1 and w3 columns interleaved in
+    blocks of 128 (the layout of the fused SwiGLU expert GEMMs)."""
+    E, h, F = w1s.shape
+    if F % 128:
+        raise ShapeMismatch("interleaved w13: mid must be a multiple of 128")
+    return torch.stack((w1s.reshape(E, h, F // 128, 128), w3s.reshape(E, h, F // 128, 128)), 3).reshape(E, h, 2 * F)
+
+
+def moe_expert_swiglu(x, w13, offsets):
+    """ac = x·w13 and h = silu(a)·c per expert group, the SwiGLU in the GEMM
+    epilogue (catnn_moe_expert_swiglu_fwd; bf16). Returns (ac, h)."""
+    _same(x, w13)
+    rows, hidden = x.shape
+    E, _, F2 = w13.shape
+    ac = torch.empty(rows, F2, dtype=x.dtype, device=x.device)
+    h = torch.empty(rows, F2 // 2, dtype=x.dtype, device=x.device)
+    _lib.call("catnn_moe_expert_swiglu_fwd", _h(x), _p(x), _p(w13), _p(offsets), rows, hidden, F2 // 2, E, _p(ac), _p(h))
+    return ac, h
+
+
+def moe_expert_swiglu_backward(dy, w2, ac, offsets):
+    """dac = [da | dc] from dh = dy·w2ᵀ per expert group and the saved ac
+    (catnn_moe_expert_swiglu_bwd; bf16)."""
+    _same(dy, w2, ac)
+    rows, hidden = dy.shape
+    E, F, _ = w2.shape
+    dac = torch.empty(rows, 2 * F, dtype=dy.dtype, device=dy.device)
+    _lib.call("catnn_moe_expert_swiglu_bwd", _h(dy), _p(dy), _p(w2), _p(ac), _p(offsets), rows, hidden, F, E, _p(dac))
+    return dac
+
+
 def swiglu(x, w1, w3, w2):
     """moe::swiglu (moe.rs:159)."""
     _same(x, w1, w3, w2)

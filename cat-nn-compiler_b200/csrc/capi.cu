@@ -11,14 +11,6 @@ namespace {
 void need(bool ok, const char* what) { CATNN_CHECK(ok, CATNN_ERR_INVALID, std::string("null argument: ") + what); }
 void shape(bool ok, const std::string& what) { CATNN_CHECK(ok, CATNN_ERR_SHAPE, what); }
 
-// Reads and clears a device status slot; synchronizes the stream.
-int take_status(Context* c, int slot) {
-    int v = 0;
-    CUDA_OK(cudaMemcpyAsync(&v, c->status + slot, 4, cudaMemcpyDeviceToHost, c->stream));
-    CUDA_OK(cudaStreamSynchronize(c->stream));
-    if (v) CUDA_OK(cudaMemsetAsync(c->status + slot, 0, 4, c->stream));
-    return v;
-}
 
 void linear_fwd_impl(Context* c, const void* x, const void* w, const float* b, void* y, i64 M, i64 K, i64 N, int act,
                      int dtype) {

@@ -10,13 +10,6 @@ namespace {
 void need(bool ok, const char* what) { CATNN_CHECK(ok, CATNN_ERR_INVALID, std::string("null argument: ") + what); }
 void shape(bool ok, const std::string& what) { CATNN_CHECK(ok, CATNN_ERR_SHAPE, what); }
 
-int take_status(Context* c, int slot) {
-    int v = 0;
-    CUDA_OK(cudaMemcpyAsync(&v, c->status + slot, 4, cudaMemcpyDeviceToHost, c->stream));
-    CUDA_OK(cudaStreamSynchronize(c->stream));
-    if (v) CUDA_OK(cudaMemsetAsync(c->status + slot, 0, 4, c->stream));
-    return v;
-}
 
 // Row alignment of the expert blocks: tensor-core tiles are 128 rows.
 int moe_align(int dtype) { return dtype == CATNN_BF16 ? 128 : 1; }
@@ -163,6 +156,30 @@ int catnn_grouped_gemm(catnn_ctx* h, int trans_b, int64_t rows, int64_t N, int64
     shape(rows >= 0 && N > 0 && K > 0 && groups >= 1 && groups <= 1024, "grouped_gemm: sizes");
     CATNN_CHECK(dtype == CATNN_BF16 || c_dtype == CATNN_F32, CATNN_ERR_DTYPE, "fp32 grouped gemm writes fp32");
     grouped(c, dtype, trans_b != 0, rows, N, K, (int)groups, offsets, A, B, C, false, c_dtype);
+    ABI_END
+}
+
+int catnn_moe_expert_swiglu_fwd(catnn_ctx* h, const void* x, const void* w13, const int32_t* offsets, int64_t rows,
+                                int64_t hidden, int64_t mid, int64_t groups, void* ac, void* hh) {
+    ABI_BEGIN
+    Context* c = unwrap(h);
+    need(x && w13 && offsets && ac && hh, "expert swiglu arguments");
+    shape(rows >= 0 && hidden >= 16 && mid > 0 && mid % 128 == 0 && groups >= 1 && groups <= 1024,
+          "expert swiglu: sizes (mid a multiple of 128)");
+    gemm_grouped_swiglu_fwd_tc(c, rows, mid, hidden, (int)groups, offsets, (const bf16*)x, hidden, (const bf16*)w13,
+                               (bf16*)ac, (bf16*)hh);
+    ABI_END
+}
+
+int catnn_moe_expert_swiglu_bwd(catnn_ctx* h, const void* dy, const void* w2, const void* ac, const int32_t* offsets,
+                                int64_t rows, int64_t hidden, int64_t mid, int64_t groups, void* dac) {
+    ABI_BEGIN
+    Context* c = unwrap(h);
+    need(dy && w2 && ac && offsets && dac, "expert swiglu backward arguments");
+    shape(rows >= 0 && hidden >= 16 && mid > 0 && mid % 128 == 0 && groups >= 1 && groups <= 1024,
+          "expert swiglu backward: sizes (mid a multiple of 128)");
+    gemm_grouped_swiglu_bwd_tc(c, rows, mid, hidden, (int)groups, offsets, (const bf16*)dy, hidden, (const bf16*)w2,
+                               (const bf16*)ac, (bf16*)dac);
     ABI_END
 }
 

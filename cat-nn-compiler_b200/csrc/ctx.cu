@@ -1,12 +1,27 @@
 // Context lifecycle, error text, memory helpers and the checksum — the
 // device-side state a catnn DeviceHandler (crates/catnn-rt/src/handler.rs)
 // needs once its kernels run on a GPU.
+#include <mutex>
+
 #include "ops.cuh"
 
 namespace catnn {
 
 static thread_local std::string g_last_error;
 void set_last_error(const std::string& msg) { g_last_error = msg; }
+
+int take_status(Context* c, int slot) {
+    int v = 0;
+    CUDA_OK(cudaMemcpyAsync(&v, c->status + slot, 4, cudaMemcpyDeviceToHost, c->stream));
+    CUDA_OK(cudaStreamSynchronize(c->stream));
+    if (v) CUDA_OK(cudaMemsetAsync(c->status + slot, 0, 4, c->stream));
+    return v;
+}
+
+// Live contexts per device (the allocation-free entry point's cached
+// address is dropped with the device's last context).
+static int g_live_ctx[64] = {0};
+static std::mutex g_live_ctx_mu;
 
 void* Context::scratch_for(size_t bytes) {
     if (bytes <= scratch_bytes) return scratch;
@@ -81,11 +96,19 @@ int catnn_ctx_create(int device, catnn_ctx** out) {
     CUDA_OK(cudaGetDeviceProperties(&prop, device));
     CATNN_CHECK(prop.major == 10 && prop.minor == 0, CATNN_ERR_UNSUPPORTED,
                 std::string("libcatnn_b200 is built for sm_100a (B200); device is ") + prop.name);
+    CATNN_CHECK(device < 64, CATNN_ERR_INVALID, "catnn_ctx_create: device index above 63");
+    // resolve the allocation-free entry point's array here, where loading the
+    // library's code on the device may allocate
+    xent_row_loss_buffer(device);
     catnn_ctx* h = new catnn_ctx();
     h->c.device = device;
     h->c.sm_count = prop.multiProcessorCount;
     CUDA_OK(cudaMalloc(&h->c.status, 64 * sizeof(int)));
     CUDA_OK(cudaMemset(h->c.status, 0, 64 * sizeof(int)));
+    {
+        std::lock_guard<std::mutex> lock(g_live_ctx_mu);
+        ++g_live_ctx[device];
+    }
     *out = h;
     ABI_END
 }
@@ -100,6 +123,10 @@ int catnn_ctx_destroy(catnn_ctx* h) {
     if (h->c.tc_sched) cudaFree(h->c.tc_sched);
     if (h->c.rope_tab) cudaFree(h->c.rope_tab);
     if (h->c.work) cudaFree(h->c.work);
+    {
+        std::lock_guard<std::mutex> lock(g_live_ctx_mu);
+        if (--g_live_ctx[h->c.device] == 0) xent_noalloc_forget(h->c.device);
+    }
     delete h;
     ABI_END
 }

@@ -44,6 +44,18 @@ struct TcArgs {
     // tma_c: full 32-row blocks of C (no accumulate) are staged in shared memory and
     // written by TMA bulk stores of mapC
     int tma_c;
+    // SwiGLU epilogues of the MoE expert GEMMs (mode 1, bf16). The [a | c]
+    // columns are interleaved in blocks of 128: block j holds a's columns
+    // [128j, 128j + 128) and then the same columns of c, so one 256-wide
+    // output tile holds both halves of 128 SwiGLU columns.
+    //  epi 1 (x·W13): C = [a | c] in that layout (bf16, what the backward reads)
+    //         and aux = h = silu(a)·c ([rows, F], ld ldaux) from the rounded a, c;
+    //  epi 2 (dyp·W2ᵀ = dh, never stored): reads a, c from aux ([rows, 2F],
+    //         ld ldaux), writes C = [da | dc] (same layout, ld ldc) with
+    //         da = dh·c·silu'(a), dc = dh·silu(a) from dh rounded to bf16.
+    int epi;
+    void* aux;
+    long long ldaux;
 };
 
 static constexpr int BM = 128, BK = 64;
@@ -132,6 +144,53 @@ __device__ __forceinline__ TileInfo tile_at_base(const TcArgs& a, int t) {
     return ti;
 }
 
+// moe.rs:12-14 / adjoint.rs:208-215 (the same expressions as k_swiglu / k_swiglu_bwd)
+__device__ __forceinline__ float tc_silu(float x) { return x / (1.0f + expf(-x)); }
+__device__ __forceinline__ float tc_silu_grad(float x) {
+    float s = 1.0f / (1.0f + expf(-x));
+    return s + x * s * (1.0f - s);
+}
+
+// 32 bf16 values (packed in pairs) of one row of a warp's 32-row block:
+// staged in the warp's shared-memory ring with the store map's 64-byte
+// swizzle and written by one TMA store at (x, y) when the block's 32 rows are
+// all valid (tma), else stored directly by the lanes with valid rows.
+struct Stage32 {
+    uint8_t* stage;  // this warp's four 2 KB buffers
+    uint32_t* nst;   // stores issued by the warp (picks the buffer)
+    int lane;
+    __device__ __forceinline__ void put(const uint32_t (&pk)[16], const CUtensorMap* map, bool tma, int x, int y,
+                                        bf16* direct, bool row_ok) {
+        if (tma) {
+            const int b = (int)(*nst & 3u);
+            const uint32_t sb = tc::smem_u32(stage + b * 2048);
+            if (lane == 0) tc::bulk_wait_read<3>();
+            __syncwarp();
+#pragma unroll
+            for (int c4 = 0; c4 < 4; ++c4)
+                tc::st_shared_v4(sb + lane * 64 + ((c4 ^ ((lane >> 1) & 3)) << 4),
+                                 make_uint4(pk[c4 * 4], pk[c4 * 4 + 1], pk[c4 * 4 + 2], pk[c4 * 4 + 3]));
+            tc::fence_proxy_async();
+            __syncwarp();
+            if (lane == 0) {
+                tc::tma_store_2d(map, stage + b * 2048, x, y);
+                tc::bulk_commit();
+            }
+            ++*nst;
+        } else if (row_ok) {
+#pragma unroll
+            for (int c4 = 0; c4 < 4; ++c4)
+                *(uint4*)(direct + c4 * 8) = make_uint4(pk[c4 * 4], pk[c4 * 4 + 1], pk[c4 * 4 + 2], pk[c4 * 4 + 3]);
+        }
+    }
+};
+
+__device__ __forceinline__ uint32_t pack_bf16x2(float x, float y) {
+    __nv_bfloat162 h = __floats2bfloat162_rn(x, y);
+    return *(uint32_t*)&h;
+}
+__device__ __forceinline__ float2 unpack_bf16x2(uint32_t v) { return __bfloat1622float2(*(__nv_bfloat162*)&v); }
+
 __device__ __forceinline__ float act_apply(float v, int act) {
     if (act == CATNN_ACT_RELU) return fmaxf(v, 0.f);
     if (act == CATNN_ACT_GELU) {
@@ -144,7 +203,7 @@ __device__ __forceinline__ float act_apply(float v, int act) {
 template <bool A_MN, bool B_MN, int BN, int STAGES>
 __global__ void __launch_bounds__(192, 1)
     k_gemm_tc(const __grid_constant__ CUtensorMap mapA, const __grid_constant__ CUtensorMap mapB,
-              const __grid_constant__ CUtensorMap mapC, TcArgs a) {
+              const __grid_constant__ CUtensorMap mapC, const __grid_constant__ CUtensorMap mapD, TcArgs a) {
     constexpr uint32_t A_BYTES = BM * BK * 2;
     constexpr uint32_t B_BYTES = BN * BK * 2;
     constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
@@ -291,6 +350,76 @@ __global__ void __launch_bounds__(192, 1)
             const bool use_tma = a.tma_c && a.ksplit <= 1 && row0 + 32 <= ti.mlimit;
             const long long ybase =
                 a.mode == 0 ? row0 : (a.mode == 1 ? (long long)ti.arow0 + row0 : (long long)ti.g * a.M + row0);
+            if (a.epi != 0) {
+                // SwiGLU epilogues (mode 1, bf16, no split-K; see TcArgs::epi)
+                Stage32 st{stage_c + q * 8192, &nst, lane};
+                const bool tma = a.tma_c && row0 + 32 <= ti.mlimit;
+                const long long grow = (long long)ti.arow0 + row;
+                if (a.epi == 1) {
+                    bf16* acp = (bf16*)a.C + grow * a.ldc;
+                    bf16* hp = (bf16*)a.aux + grow * a.ldaux;
+                    const int hcol0 = (ti.n0 >> 8) << 7;
+#pragma unroll 1
+                    for (int cc = 0; cc < 4; ++cc) {
+                        uint32_t ra[32], rc[32];
+                        tc::tmem_ld32(tmem_base + ((uint32_t)(q * 32) << 16) + acc * BN + cc * 32, ra);
+                        tc::tmem_ld32(tmem_base + ((uint32_t)(q * 32) << 16) + acc * BN + 128 + cc * 32, rc);
+                        tc::tmem_ld_wait();
+                        uint32_t pa[16], pc[16], ph[16];
+#pragma unroll
+                        for (int j = 0; j < 16; ++j) {
+                            pa[j] = pack_bf16x2(__uint_as_float(ra[2 * j]), __uint_as_float(ra[2 * j + 1]));
+                            pc[j] = pack_bf16x2(__uint_as_float(rc[2 * j]), __uint_as_float(rc[2 * j + 1]));
+                            const float2 av = unpack_bf16x2(pa[j]), cv = unpack_bf16x2(pc[j]);
+                            ph[j] = pack_bf16x2(tc_silu(av.x) * cv.x, tc_silu(av.y) * cv.y);
+                        }
+                        const int ca = ti.n0 + cc * 32, ch = hcol0 + cc * 32;
+                        st.put(pa, &mapC, tma, ca, (int)ybase, acp + ca, rv);
+                        st.put(pc, &mapC, tma, ca + 128, (int)ybase, acp + ca + 128, rv);
+                        st.put(ph, &mapD, tma, ch, (int)ybase, hp + ch, rv);
+                    }
+                } else {
+                    const bf16* acin = (const bf16*)a.aux + grow * a.ldaux;
+                    bf16* dacp = (bf16*)a.C + grow * a.ldc;
+#pragma unroll 1
+                    for (int cc = 0; cc < BN / 32; ++cc) {
+                        const int f0 = ti.n0 + cc * 32;
+                        if (f0 >= a.N) break;  // warp-uniform
+                        uint32_t r[32];
+                        tc::tmem_ld32(tmem_base + ((uint32_t)(q * 32) << 16) + acc * BN + cc * 32, r);
+                        // a and c of these 32 SwiGLU columns (interleaved layout)
+                        const int col = ((f0 >> 7) << 8) + (f0 & 127);
+                        uint4 va[4], vc[4];
+                        if (rv) {
+#pragma unroll
+                            for (int c4 = 0; c4 < 4; ++c4) {
+                                va[c4] = *(const uint4*)(acin + col + c4 * 8);
+                                vc[c4] = *(const uint4*)(acin + col + 128 + c4 * 8);
+                            }
+                        } else {
+#pragma unroll
+                            for (int c4 = 0; c4 < 4; ++c4) va[c4] = vc[c4] = make_uint4(0, 0, 0, 0);
+                        }
+                        tc::tmem_ld_wait();
+                        const uint32_t* ua = (const uint32_t*)va;
+                        const uint32_t* uc = (const uint32_t*)vc;
+                        uint32_t pda[16], pdc[16];
+#pragma unroll
+                        for (int j = 0; j < 16; ++j) {
+                            const float2 av = unpack_bf16x2(ua[j]), cv = unpack_bf16x2(uc[j]);
+                            const float2 g = unpack_bf16x2(pack_bf16x2(__uint_as_float(r[2 * j]), __uint_as_float(r[2 * j + 1])));
+                            pda[j] = pack_bf16x2(g.x * cv.x * tc_silu_grad(av.x), g.y * cv.y * tc_silu_grad(av.y));
+                            pdc[j] = pack_bf16x2(g.x * tc_silu(av.x), g.y * tc_silu(av.y));
+                        }
+                        st.put(pda, &mapC, tma, col, (int)ybase, dacp + col, rv);
+                        st.put(pdc, &mapC, tma, col + 128, (int)ybase, dacp + col + 128, rv);
+                    }
+                }
+                tc::tc_fence_before();
+                __syncwarp();
+                if (lane == 0) tc::mbar_arrive(&tempty[acc]);
+                continue;
+            }
 #pragma unroll 1
             for (int cc = 0; cc < BN / 32; ++cc) {
                 int col0 = ti.n0 + cc * 32;
@@ -642,8 +771,8 @@ CUtensorMap tma_map_bf16(const void* base, i64 rows, i64 cols, i64 ld, int box_c
 }
 
 template <bool A_MN, bool B_MN, int BN, int STAGES>
-static void launch_tc(Context* c, const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mc, const TcArgs& a,
-                      int grid) {
+static void launch_tc(Context* c, const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mc,
+                      const CUtensorMap& md, const TcArgs& a, int grid) {
     constexpr size_t smem = (size_t)STAGES * (BM * BK * 2 + BN * BK * 2) + EPI_STAGE_BYTES + 1024 + 256;
     static_assert(smem <= 232448, "shared memory per CTA");
     static bool attr_set[64] = {false};
@@ -653,17 +782,17 @@ static void launch_tc(Context* c, const CUtensorMap& ma, const CUtensorMap& mb, 
                                      (int)smem));
         attr_set[dev] = true;
     }
-    k_gemm_tc<A_MN, B_MN, BN, STAGES><<<grid, 192, smem, c->stream>>>(ma, mb, mc, a);
+    k_gemm_tc<A_MN, B_MN, BN, STAGES><<<grid, 192, smem, c->stream>>>(ma, mb, mc, md, a);
     launched(c);
 }
 
 template <int BN, int STAGES>
 static void dispatch_tc(Context* c, bool a_mn, bool b_mn, const CUtensorMap& ma, const CUtensorMap& mb,
-                        const CUtensorMap& mc, const TcArgs& a, int grid) {
-    if (!a_mn && !b_mn) launch_tc<false, false, BN, STAGES>(c, ma, mb, mc, a, grid);
-    else if (!a_mn && b_mn) launch_tc<false, true, BN, STAGES>(c, ma, mb, mc, a, grid);
-    else if (a_mn && !b_mn) launch_tc<true, false, BN, STAGES>(c, ma, mb, mc, a, grid);
-    else launch_tc<true, true, BN, STAGES>(c, ma, mb, mc, a, grid);
+                        const CUtensorMap& mc, const CUtensorMap& md, const TcArgs& a, int grid) {
+    if (!a_mn && !b_mn) launch_tc<false, false, BN, STAGES>(c, ma, mb, mc, md, a, grid);
+    else if (!a_mn && b_mn) launch_tc<false, true, BN, STAGES>(c, ma, mb, mc, md, a, grid);
+    else if (a_mn && !b_mn) launch_tc<true, false, BN, STAGES>(c, ma, mb, mc, md, a, grid);
+    else launch_tc<true, true, BN, STAGES>(c, ma, mb, mc, md, a, grid);
 }
 
 static bool aligned16(const void* p) { return ((uintptr_t)p & 15) == 0; }
@@ -721,10 +850,21 @@ static void run_tc(Context* c, TcArgs a, bool a_mn, bool b_mn, const bf16* A, i6
         }
     }
     // output map for the plain epilogue's TMA stores (C as one 2-D [rows, N] matrix)
-    CUtensorMap mc;
+    CUtensorMap mc, md;
     std::memset(&mc, 0, sizeof(mc));
+    std::memset(&md, 0, sizeof(md));
     a.tma_c = 0;
-    {
+    if (a.epi != 0) {
+        // SwiGLU epilogues: C is [rows, 2F] (epi 1: [a | c]; epi 2: [da | dc]),
+        // and epi 1 also stores h [rows, F] through md
+        const i64 F = a.epi == 1 ? a.N / 2 : a.N;
+        if (aligned16(a.C) && (a.ldc * 2) % 16 == 0 && a.M < (1 << 30) &&
+            (a.epi == 2 || (aligned16(a.aux) && (a.ldaux * 2) % 16 == 0))) {
+            mc = make_store_map(a.C, a.M, 2 * F, a.ldc, false);
+            if (a.epi == 1) md = make_store_map(a.aux, a.M, F, a.ldaux, false);
+            a.tma_c = 1;
+        }
+    } else {
         const int es = a.c_bf16 ? 2 : 4;
         const i64 crows = a.mode == 2 ? (i64)a.groups * a.M : (i64)a.M;
         // residual rows are read with 16-byte loads in the staged epilogue
@@ -736,8 +876,8 @@ static void run_tc(Context* c, TcArgs a, bool a_mn, bool b_mn, const bf16* A, i6
     }
     int grid = grid_bound < c->sm_count ? grid_bound : c->sm_count;
     if (grid < 1) grid = 1;
-    if (BN == 128) dispatch_tc<128, 6>(c, a_mn, b_mn, ma, mb, mc, a, grid);
-    else dispatch_tc<256, 4>(c, a_mn, b_mn, ma, mb, mc, a, grid);
+    if (BN == 128) dispatch_tc<128, 6>(c, a_mn, b_mn, ma, mb, mc, md, a, grid);
+    else dispatch_tc<256, 4>(c, a_mn, b_mn, ma, mb, mc, md, a, grid);
     if (a.ksplit > 1) {
         int g = (int)std::min<i64>(part_rows, (i64)c->sm_count * 16);
         k_splitk_reduce<<<g, 256, 0, c->stream>>>(a, part_rows);
@@ -838,6 +978,61 @@ void gemm_grouped_wgrad_bf16_tc(Context* c, i64 total_rows, i64 N, i64 K, int gr
     // Split-K slices each group's rows; the chunk is sized for the mean group.
     run_tc(c, a, true, true, A, total_rows, K, lda, D, total_rows, N, ldd, tiles, tiles, cdiv(total_rows, groups),
            (i64)groups * K);
+}
+
+// MoE expert forward with the SwiGLU fused into the epilogue: per expert g,
+// AC[rows_g] = X[rows_g]·W13_g with W13_g [K, 2F] in the 128-column
+// interleaved [a | c] layout (TcArgs::epi), and H[rows_g] = silu(a)·c.
+void gemm_grouped_swiglu_fwd_tc(Context* c, i64 total_rows, i64 F, i64 K, int groups, const int32_t* offsets,
+                                const bf16* X, i64 ldx, const bf16* W13, bf16* AC, bf16* H) {
+    if (total_rows <= 0 || groups <= 0) return;
+    CATNN_CHECK(F % 128 == 0 && K >= 16 && tc_ok(X, ldx, W13, 2 * F), CATNN_ERR_UNSUPPORTED,
+                "swiglu gemm: F must be a multiple of 128, K >= 16, operands 16-byte aligned");
+    TcArgs a{};
+    a.mode = 1;
+    a.groups = groups;
+    a.offsets = offsets;
+    a.M = (int)total_rows;
+    a.N = (int)(2 * F);
+    a.K = (int)K;
+    a.b_group_rows = (int)K;
+    a.C = AC;
+    a.ldc = 2 * F;
+    a.c_bf16 = 1;
+    a.vec_ok = 1;
+    a.epi = 1;
+    a.aux = H;
+    a.ldaux = F;
+    int bound = (cdiv(total_rows, BM) + groups) * cdiv(2 * F, 256);
+    run_tc(c, a, false, true, X, total_rows, K, ldx, W13, (i64)groups * K, 2 * F, 2 * F, bound);
+}
+
+// MoE expert backward through the SwiGLU: per expert g, dh = dY[rows_g]·W2_gᵀ
+// (W2_g [F, K] row-major, read K-major) is never stored; the epilogue reads a,
+// c from AC (interleaved layout) and writes DAC = [da | dc] in that layout.
+void gemm_grouped_swiglu_bwd_tc(Context* c, i64 total_rows, i64 F, i64 K, int groups, const int32_t* offsets,
+                                const bf16* DY, i64 lddy, const bf16* W2, const bf16* AC, bf16* DAC) {
+    if (total_rows <= 0 || groups <= 0) return;
+    CATNN_CHECK(F % 128 == 0 && K >= 16 && tc_ok(DY, lddy, W2, K) && aligned16(AC), CATNN_ERR_UNSUPPORTED,
+                "swiglu gemm: F must be a multiple of 128, K >= 16, operands 16-byte aligned");
+    TcArgs a{};
+    a.mode = 1;
+    a.groups = groups;
+    a.offsets = offsets;
+    a.M = (int)total_rows;
+    a.N = (int)F;
+    a.K = (int)K;
+    a.b_group_rows = (int)F;
+    a.C = DAC;
+    a.ldc = 2 * F;
+    a.c_bf16 = 1;
+    a.vec_ok = 1;
+    a.epi = 2;
+    a.aux = const_cast<bf16*>(AC);
+    a.ldaux = 2 * F;
+    const int BN = F <= 128 ? 128 : 256;
+    int bound = (cdiv(total_rows, BM) + groups) * cdiv(F, BN);
+    run_tc(c, a, false, false, DY, total_rows, K, lddy, W2, (i64)groups * F, K, K, bound);
 }
 
 }  // namespace catnn

@@ -771,15 +771,24 @@ static __device__ __align__(256) float g_xent_row_loss[CATNN_XENT_NOALLOC_MAX_RO
 static float* g_xent_row_loss_ptr[64] = {nullptr};
 static std::mutex g_xent_row_loss_mu;
 
-static float* xent_row_loss_buffer(int device) {
+float* xent_row_loss_buffer(int device) {
     CATNN_CHECK(device >= 0 && device < 64, CATNN_ERR_INVALID, "device index out of range");
     std::lock_guard<std::mutex> lock(g_xent_row_loss_mu);
     if (!g_xent_row_loss_ptr[device]) {
+        int cur = -1;
+        CUDA_OK(cudaGetDevice(&cur));
+        CATNN_CHECK(cur == device, CATNN_ERR_INVALID, "xent_row_loss_buffer: the device must be current");
         void* p = nullptr;
         CUDA_OK(cudaGetSymbolAddress(&p, g_xent_row_loss));
         g_xent_row_loss_ptr[device] = (float*)p;
     }
     return g_xent_row_loss_ptr[device];
+}
+
+void xent_noalloc_forget(int device) {
+    if (device < 0 || device >= 64) return;
+    std::lock_guard<std::mutex> lock(g_xent_row_loss_mu);
+    g_xent_row_loss_ptr[device] = nullptr;
 }
 
 }  // namespace catnn
@@ -802,14 +811,6 @@ extern "C" int catnn_xent_fwdbwd_noalloc(catnn_ctx* h, const void* logits, const
     launch_xent_rows(c, logits, targets, rows, vocab, dlogits, dtype, rl, err, rows);
     k_sum_rows_mean<<<1, 1024, 0, c->stream>>>(rl, rows, loss, rows);
     launched(c, 2);
-    if (check) {
-        int v = 0;
-        CUDA_OK(cudaMemcpyAsync(&v, err, 4, cudaMemcpyDeviceToHost, c->stream));
-        CUDA_OK(cudaStreamSynchronize(c->stream));
-        if (v) {
-            CUDA_OK(cudaMemsetAsync(err, 0, 4, c->stream));
-            throw Error(CATNN_ERR_SHAPE, "ce targets: a target is >= the number of classes");
-        }
-    }
+    if (check && take_status(c, 9)) throw Error(CATNN_ERR_SHAPE, "ce targets: a target is >= the number of classes");
     ABI_END
 }

@@ -25,6 +25,19 @@ namespace catnn {
 
 Context* unwrap(catnn_ctx* h);
 
+// Reads and clears device status slot `slot` of the context; synchronizes
+// the stream. Returns the value that was there.
+int take_status(Context* c, int slot);
+
+// The allocation-free cross-entropy's row-loss array (norms.cu): its device
+// address on `device`, resolved once per device with that device current.
+// catnn_ctx_create calls this, so that the lookup (which can load the
+// library's code on the device) happens where allocation is allowed;
+// xent_noalloc_forget drops the address when the device's last context is
+// destroyed (a later cudaDeviceReset invalidates it).
+float* xent_row_loss_buffer(int device);
+void xent_noalloc_forget(int device);
+
 inline size_t dsize(int dtype) { return dtype == CATNN_BF16 ? 2 : 4; }
 inline void check_dtype(int dtype) {
     CATNN_CHECK(dtype == CATNN_F32 || dtype == CATNN_BF16, CATNN_ERR_DTYPE,
@@ -56,6 +69,12 @@ void gemm_grouped_wgrad_bf16_tc(Context* c, i64 total_rows, i64 N, i64 K, int gr
                                 const int32_t* offsets, const bf16* A, i64 lda, const bf16* D, i64 ldd,
                                 void* dB, i64 strideB, int c_dtype, bool accumulate);
 // fp32 grouped GEMM for the parity path (same conventions).
+// The expert GEMMs with the SwiGLU fused into the epilogue (gemm_tc.cu):
+// W13 / AC / DAC use the 128-column interleaved [a | c] layout.
+void gemm_grouped_swiglu_fwd_tc(Context* c, i64 total_rows, i64 F, i64 K, int groups, const int32_t* offsets,
+                                const bf16* X, i64 ldx, const bf16* W13, bf16* AC, bf16* H);
+void gemm_grouped_swiglu_bwd_tc(Context* c, i64 total_rows, i64 F, i64 K, int groups, const int32_t* offsets,
+                                const bf16* DY, i64 lddy, const bf16* W2, const bf16* AC, bf16* DAC);
 void gemm_grouped_f32(Context* c, bool ta_rows, bool tb, i64 total_rows, i64 N, i64 K, int groups,
                       const int32_t* offsets, const float* A, i64 lda, const float* B, i64 strideB,
                       i64 ldb, float* C, i64 ldc, i64 strideC, bool accumulate);

@@ -72,8 +72,16 @@ void MoeTrainer::import_packed(const float* pk, float* dst) {
         cp(dst + q.rms_moe, p, d); p += d;
         cp(dst + q.gate, p, d * E); p += d * E;
         // this rank's experts [e0, e0 + El) of w1[E], w3[E], w2[E]
-        cp2(dst + q.w13, 2 * F, p + e0 * d * F, F, F, El * d); p += E * d * F;
-        cp2(dst + q.w13 + F, 2 * F, p + e0 * d * F, F, F, El * d); p += E * d * F;
+        if (ilv) {
+            for (i64 j = 0; j < F / 128; ++j) {
+                cp2(dst + q.w13 + 256 * j, 2 * F, p + e0 * d * F + 128 * j, F, 128, El * d);
+                cp2(dst + q.w13 + 256 * j + 128, 2 * F, p + E * d * F + e0 * d * F + 128 * j, F, 128, El * d);
+            }
+            p += 2 * E * d * F;
+        } else {
+            cp2(dst + q.w13, 2 * F, p + e0 * d * F, F, F, El * d); p += E * d * F;
+            cp2(dst + q.w13 + F, 2 * F, p + e0 * d * F, F, F, El * d); p += E * d * F;
+        }
         cp(dst + q.w2, p + e0 * F * d, El * F * d); p += E * F * d;
     }
     cp(dst + o_final, p, d); p += d;
@@ -100,8 +108,16 @@ void MoeTrainer::export_packed(const float* src, float* pk) {
         cp(p, src + q.wo, qd * d); p += qd * d;
         cp(p, src + q.rms_moe, d); p += d;
         cp(p, src + q.gate, d * E); p += d * E;
-        cp2(p + e0 * d * F, F, src + q.w13, 2 * F, F, El * d); p += E * d * F;
-        cp2(p + e0 * d * F, F, src + q.w13 + F, 2 * F, F, El * d); p += E * d * F;
+        if (ilv) {
+            for (i64 j = 0; j < F / 128; ++j) {
+                cp2(p + e0 * d * F + 128 * j, F, src + q.w13 + 256 * j, 2 * F, 128, El * d);
+                cp2(p + E * d * F + e0 * d * F + 128 * j, F, src + q.w13 + 256 * j + 128, 2 * F, 128, El * d);
+            }
+            p += 2 * E * d * F;
+        } else {
+            cp2(p + e0 * d * F, F, src + q.w13, 2 * F, F, El * d); p += E * d * F;
+            cp2(p + e0 * d * F, F, src + q.w13 + F, 2 * F, F, El * d); p += E * d * F;
+        }
         cp(p + e0 * F * d, src + q.w2, El * F * d); p += E * F * d;
     }
     cp(p, src + o_final, d); p += d;
@@ -324,8 +340,13 @@ void MoeTrainer::forward() {
         if (!ep) {
             permute_map(c, a.idx, T, E, K, align, cap, a.counts, a.off, a.row_of, a.src_of);
             permute_rows(c, a.xm, a.src_of, cap, d, K, a.xp, dt);
-            expert_gemm(c, dt, false, cap, 2 * F, d, (int)E, a.off, a.xp, d, W(q.w13), a.ac, 2 * F, dt);
-            swiglu_act(c, a.ac, (char*)a.ac + F * e, a.h, cap, F, 2 * F, F, dt);
+            if (ilv) {
+                gemm_grouped_swiglu_fwd_tc(c, cap, F, d, (int)E, a.off, (const bf16*)a.xp, d, (const bf16*)W(q.w13),
+                                           (bf16*)a.ac, (bf16*)a.h);
+            } else {
+                expert_gemm(c, dt, false, cap, 2 * F, d, (int)E, a.off, a.xp, d, W(q.w13), a.ac, 2 * F, dt);
+                swiglu_act(c, a.ac, (char*)a.ac + F * e, a.h, cap, F, 2 * F, F, dt);
+            }
             expert_gemm(c, dt, false, cap, d, F, (int)E, a.off, a.h, F, W(q.w2), a.yp, d, dt);
             unpermute_rows(c, a.yp, a.row_of, a.w, T, K, d, x_out, CATNN_F32, false, dt, a.x_mid);
         } else {
@@ -338,8 +359,13 @@ void MoeTrainer::forward() {
             ep_dispatch(c, a.xm, a.idx, a.row_of, a.off, a.plan, tab(a.xp), tab(a.src_of), a.dest, T, (int)K, d,
                         (int)El, align, rank, world, cap, dt);
             comm->barrier();
-            expert_gemm(c, dt, false, cap, 2 * F, d, (int)El, a.plan, a.xp, d, W(q.w13), a.ac, 2 * F, dt);
-            swiglu_act(c, a.ac, (char*)a.ac + F * e, a.h, cap, F, 2 * F, F, dt, -1, a.plan + El);
+            if (ilv) {
+                gemm_grouped_swiglu_fwd_tc(c, cap, F, d, (int)El, a.plan, (const bf16*)a.xp, d, (const bf16*)W(q.w13),
+                                           (bf16*)a.ac, (bf16*)a.h);
+            } else {
+                expert_gemm(c, dt, false, cap, 2 * F, d, (int)El, a.plan, a.xp, d, W(q.w13), a.ac, 2 * F, dt);
+                swiglu_act(c, a.ac, (char*)a.ac + F * e, a.h, cap, F, 2 * F, F, dt, -1, a.plan + El);
+            }
             expert_gemm(c, dt, false, cap, d, F, (int)El, a.plan, a.h, F, W(q.w2), a.yp, d, dt);
             comm->barrier();
             // weighted sum read from the owners' expert outputs
@@ -384,10 +410,16 @@ void MoeTrainer::backward() {
             ep_unpermute_bwd(c, a.yp, a.src_of, a.plan, tab(a.w), tab(dx), tab(dwts), cap, T * K, (int)K, d, (int)El,
                              world, dyp, dt);
         }
-        expert_gemm(c, dt, true, cap, F, d, ng, goff, dyp, d, W(q.w2), dh, F, dt);
-        expert_wgrad(c, dt, cap, d, F, ng, goff, a.h, F, dyp, d, G + q.w2);
-        swiglu_act_bwd(c, a.ac, (char*)a.ac + F * e, dh, dac, (char*)dac + F * e, cap, F, 2 * F, 2 * F, dt, -1,
-                       ep ? a.plan + El : nullptr);
+        if (ilv) {
+            gemm_grouped_swiglu_bwd_tc(c, cap, F, d, ng, goff, (const bf16*)dyp, d, (const bf16*)W(q.w2),
+                                       (const bf16*)a.ac, (bf16*)dac);
+            expert_wgrad(c, dt, cap, d, F, ng, goff, a.h, F, dyp, d, G + q.w2);
+        } else {
+            expert_gemm(c, dt, true, cap, F, d, ng, goff, dyp, d, W(q.w2), dh, F, dt);
+            expert_wgrad(c, dt, cap, d, F, ng, goff, a.h, F, dyp, d, G + q.w2);
+            swiglu_act_bwd(c, a.ac, (char*)a.ac + F * e, dh, dac, (char*)dac + F * e, cap, F, 2 * F, 2 * F, dt, -1,
+                           ep ? a.plan + El : nullptr);
+        }
         expert_gemm(c, dt, true, cap, d, 2 * F, ng, goff, dac, 2 * F, W(q.w13), dxp, d, dt);
         expert_wgrad(c, dt, cap, 2 * F, d, ng, goff, a.xp, d, dac, 2 * F, G + q.w13);
         if (!ep) {
@@ -630,6 +662,7 @@ void configure(MoeTrainer& t, const catnn_moe_config* cf, int rank = 0, int worl
     CATNN_CHECK(t.Tg * t.K < (1ll << 31), CATNN_ERR_SHAPE, "too many (token, slot) pairs");
     if (t.dt == CATNN_BF16)
         CATNN_CHECK(t.d % 64 == 0 && t.F % 64 == 0, CATNN_ERR_SHAPE, "bf16 path: hidden and mid must be multiples of 64");
+    t.ilv = t.dt == CATNN_BF16 && t.F % 128 == 0;
 }
 
 }  // namespace

@@ -27,6 +27,10 @@ struct MoeTrainer {
     float eps;
     double theta;
     int dt;  // activation / weight-shadow storage (CATNN_F32 or CATNN_BF16)
+    // bf16 path with F a multiple of 128: the expert GEMMs carry the SwiGLU in
+    // their epilogues, and w13 / its gradient / the saved [a | c] rows use the
+    // 128-column interleaved layout (blocks [w1 cols 128j.. | w3 cols 128j..])
+    bool ilv = false;
     int opt;  // 0 SGD, 1 Adam
     float lr, b1, b2, aeps;
     uint64_t t_step = 0;

@@ -130,11 +130,13 @@ int catnn_xent_fwdbwd(catnn_ctx* ctx, const void* logits, const uint32_t* target
  * block on the allocator). Same arguments, same results; its per-row scratch
  * is a fixed array inside the library (CATNN_XENT_NOALLOC_MAX_ROWS floats per
  * device, held until exit), so rows above that limit are rejected with
- * CATNN_ERR_SHAPE. It calls no allocator. The first call on a device looks
- * up that array's device address; make it before any stream capture.
- * Calls share the array: two calls whose kernels overlap on the GPU (other
- * streams, other contexts of the device) race. No counterpart in the
- * reference: its CPU kernels allocate on the host per call. */
+ * CATNN_ERR_SHAPE. It calls no allocator: catnn_ctx_create already looked up
+ * the array's device address on that device (the lookup can load the
+ * library's device code, which allocates), and the address is dropped when
+ * the device's last context is destroyed. Calls share the array: two calls
+ * whose kernels overlap on the GPU (other streams, other contexts of the
+ * device) race. No counterpart in the reference: its CPU kernels allocate on
+ * the host per call. */
 #define CATNN_XENT_NOALLOC_MAX_ROWS 65536
 int catnn_xent_fwdbwd_noalloc(catnn_ctx* ctx, const void* logits, const uint32_t* targets, int64_t rows,
                               int64_t vocab, float* loss, void* dlogits, int dtype, int check);
@@ -232,6 +234,24 @@ int catnn_moe_unpermute(catnn_ctx* ctx, const void* yp, const int32_t* row_of, c
  * The per-expert products moe::moe computes token by token (moe.rs:207-221). */
 int catnn_grouped_gemm(catnn_ctx* ctx, int trans_b, int64_t rows, int64_t N, int64_t K, int64_t groups,
                        const int32_t* offsets, const void* A, const void* B, void* C, int dtype, int c_dtype);
+/* The SwiGLU expert GEMMs with the activation in the tensor-core GEMM's
+ * epilogue (bf16 only; mid a multiple of 128; each group's rows a multiple
+ * of 128 as catnn_moe_permute_map with align 128 gives them). w13 [groups,
+ * hidden, 2·mid] holds each expert's w1 and w3 columns interleaved in blocks
+ * of 128 (block j: w1 columns 128j..128j+127, then the same w3 columns), and
+ * ac / dac use that column layout too.
+ * _fwd: per group g, ac = x_g·w13_g ([a | c] rounded to bf16) and
+ *       h = silu(a)·c [rows, mid] from the rounded a, c — the first half of
+ *       moe::swiglu (moe.rs:159-174).
+ * _bwd: per group g, dh = dy_g·w2_gᵀ (w2 [groups, mid, hidden]) rounded to
+ *       bf16 and, from the saved ac, dac = [da | dc] with da = dh·c·silu'(a),
+ *       dc = dh·silu(a) — swiglu_backward's activation adjoint
+ *       (adjoint.rs:239-242); dh itself is never stored. */
+int catnn_moe_expert_swiglu_fwd(catnn_ctx* ctx, const void* x, const void* w13, const int32_t* offsets,
+                                int64_t rows, int64_t hidden, int64_t mid, int64_t groups, void* ac, void* h);
+int catnn_moe_expert_swiglu_bwd(catnn_ctx* ctx, const void* dy, const void* w2, const void* ac,
+                                const int32_t* offsets, int64_t rows, int64_t hidden, int64_t mid,
+                                int64_t groups, void* dac);
 /* SwiGLU expert w2(silu(x·w1) ⊙ (x·w3)) on x [T,hidden]. moe::swiglu (moe.rs:159). */
 int catnn_swiglu_fwd(catnn_ctx* ctx, const void* x, const void* w1, const void* w3, const void* w2,
                      void* y, int64_t T, int64_t hidden, int64_t mid, int dtype);

@@ -10,22 +10,34 @@ namespace orc {
 // adjoint.rs:35-61 — one sequential i-j-p nest:
 // db[j] += g; dw[p][j] += x[i][p]*g; dx[i][p] += g*w[p][j].
 // Outputs are overwritten (zeroed first). db may be null.
+// Every element's accumulation order is the nest's: dx[i][p] sums over j
+// ascending, dw[p][j] and db[j] over i ascending. The three outputs are
+// written by separate loops (dx split by rows i, dw by rows p over threads),
+// which keeps each of those sums, and so every value, as the single nest
+// produces it.
 template <typename T>
 void linear_backward(const T* x, const T* w, const T* dy, T* dx, T* dw, T* db, i64 m, i64 k, i64 n) {
     std::fill(dx, dx + m * k, (T)0);
     std::fill(dw, dw + k * n, (T)0);
-    if (db) std::fill(db, db + n, (T)0);
-    for (i64 i = 0; i < m; ++i)
+    if (db) {
+        std::fill(db, db + n, (T)0);
+        for (i64 i = 0; i < m; ++i)
+            for (i64 j = 0; j < n; ++j) db[j] += dy[i * n + j];
+    }
+    split_rows(m, [=](i64 i) {
+        T* dxi = dx + i * k;
         for (i64 j = 0; j < n; ++j) {
             T g = dy[i * n + j];
-            if (db) db[j] += g;
-            const T* xi = x + i * k;
-            T* dxi = dx + i * k;
-            for (i64 p = 0; p < k; ++p) {
-                dw[p * n + j] += xi[p] * g;
-                dxi[p] += g * w[p * n + j];
-            }
+            for (i64 p = 0; p < k; ++p) dxi[p] += g * w[p * n + j];
         }
+    });
+    split_rows(k, [=](i64 p) {
+        T* dwp = dw + p * n;
+        for (i64 i = 0; i < m; ++i) {
+            T xp = x[i * k + p];
+            for (i64 j = 0; j < n; ++j) dwp[j] += xp * dy[i * n + j];
+        }
+    });
 }
 
 // adjoint.rs:63-74
@@ -174,6 +186,16 @@ void router_backward_ste(const T* x, const T* gate, const T* d_weights, T* dx, T
 // expert output, d_w = <y_e, dy_t>, backprop w*dy through the SwiGLU, and
 // add the single-token expert gradients into the expert's accumulators.
 // Then the router STE adjoint adds into dx.
+//
+// Two phases with the reference's arithmetic per element:
+//  1. per (t, k) pair (tokens split over threads; each pair writes only its
+//     own rows): the forward recompute, d_w, dh = w2·(w·dy), da, dc and the
+//     token's dx contribution — the single-token swiglu_backward, whose weight
+//     gradients are the outer products x_t[p]·da[j], x_t[p]·dc[j] and
+//     h[p]·(w·dy)[j] (one rounding each: 0 + a·b);
+//  2. each expert's gradient rows (split over threads) add those products
+//     over the expert's pairs in (t, k) order — the order the sequential loop
+//     adds the per-token gradients in.
 template <typename T>
 void moe_backward(const T* x, const T* gate, const T* w1s, const T* w3s, const T* w2s, const T* dy,
                   T* dx, T* dgate, T* dw1s, T* dw3s, T* dw2s, i64 tokens, i64 hidden, i64 mid,
@@ -185,35 +207,82 @@ void moe_backward(const T* x, const T* gate, const T* w1s, const T* w3s, const T
     std::fill(dw1s, dw1s + n_exp * hidden * mid, (T)0);
     std::fill(dw3s, dw3s + n_exp * hidden * mid, (T)0);
     std::fill(dw2s, dw2s + n_exp * mid * hidden, (T)0);
-    std::vector<T> ye(hidden), dye(hidden), dxe(hidden);
-    std::vector<T> g1(hidden * mid), g3(hidden * mid), g2(mid * hidden);
-    for (i64 t = 0; t < tokens; ++t) {
+    const i64 pairs = tokens * k;
+    std::vector<T> H(pairs * mid), DA(pairs * mid), DC(pairs * mid), DYE(pairs * hidden);
+    split_rows(tokens, [&](i64 t) {
         const T* xt = x + t * hidden;
         const T* dyt = dy + t * hidden;
+        std::vector<T> a(mid), c(mid), ye(hidden), dh(mid), dxe(hidden), dx3(hidden);
         for (i64 kk = 0; kk < k; ++kk) {
-            i64 e = idx[t * k + kk];
-            T wt = wts[t * k + kk];
+            const i64 pr = t * k + kk;
+            i64 e = idx[pr];
+            T wt = wts[pr];
             const T* w1 = w1s + e * hidden * mid;
             const T* w3 = w3s + e * hidden * mid;
             const T* w2 = w2s + e * mid * hidden;
-            swiglu(xt, w1, w3, w2, ye.data(), 1, hidden, mid);
+            T* h = H.data() + pr * mid;
+            T* da = DA.data() + pr * mid;
+            T* dc = DC.data() + pr * mid;
+            T* dye = DYE.data() + pr * hidden;
+            // swiglu (moe.rs:159-174) for one token
+            matmul_seq(xt, w1, a.data(), 1, hidden, mid);
+            matmul_seq(xt, w3, c.data(), 1, hidden, mid);
+            for (i64 i = 0; i < mid; ++i) h[i] = silu(a[i]) * c[i];
+            matmul_seq(h, w2, ye.data(), 1, mid, hidden);
             T s = 0;
             for (i64 i = 0; i < hidden; ++i) s += ye[i] * dyt[i];
-            dwts[t * k + kk] = s;
+            dwts[pr] = s;
             for (i64 i = 0; i < hidden; ++i) dye[i] = dyt[i] * wt;
-            swiglu_backward(xt, w1, w3, w2, dye.data(), dxe.data(), g1.data(), g3.data(), g2.data(),
-                            1, hidden, mid);
+            // swiglu_backward (adjoint.rs:217-251) for one token: dh, da, dc, dx
+            std::fill(dh.begin(), dh.end(), (T)0);
+            for (i64 j = 0; j < hidden; ++j) {
+                T g = dye[j];
+                for (i64 q = 0; q < mid; ++q) dh[q] += g * w2[q * hidden + j];
+            }
+            for (i64 i = 0; i < mid; ++i) {
+                da[i] = dh[i] * c[i] * silu_grad(a[i]);
+                dc[i] = dh[i] * silu(a[i]);
+            }
+            std::fill(dxe.begin(), dxe.end(), (T)0);
+            std::fill(dx3.begin(), dx3.end(), (T)0);
+            for (i64 j = 0; j < mid; ++j) {
+                T g1 = da[j], g3 = dc[j];
+                for (i64 q = 0; q < hidden; ++q) {
+                    dxe[q] += g1 * w1[q * mid + j];
+                    dx3[q] += g3 * w3[q * mid + j];
+                }
+            }
+            for (i64 i = 0; i < hidden; ++i) dxe[i] += dx3[i];
             for (i64 i = 0; i < hidden; ++i) dx[t * hidden + i] += dxe[i];
-            T* a1 = dw1s + e * hidden * mid;
-            T* a3 = dw3s + e * hidden * mid;
-            T* a2 = dw2s + e * mid * hidden;
-            for (i64 i = 0; i < hidden * mid; ++i) {
-                a1[i] += g1[i];
-                a3[i] += g3[i];
-                a2[i] += g2[i];
+        }
+    });
+    std::vector<std::vector<i64>> of_expert(n_exp);
+    for (i64 pr = 0; pr < pairs; ++pr) of_expert[idx[pr]].push_back(pr);
+    const i64 rows_e = hidden + mid;  // w1/w3 rows, then w2 rows, per expert
+    split_rows(n_exp * rows_e, [&](i64 task) {
+        const i64 e = task / rows_e, r = task % rows_e;
+        if (r < hidden) {
+            T* a1 = dw1s + e * hidden * mid + r * mid;
+            T* a3 = dw3s + e * hidden * mid + r * mid;
+            for (i64 pr : of_expert[e]) {
+                const T xp = x[(pr / k) * hidden + r];
+                const T* da = DA.data() + pr * mid;
+                const T* dc = DC.data() + pr * mid;
+                for (i64 j = 0; j < mid; ++j) {
+                    a1[j] += xp * da[j];
+                    a3[j] += xp * dc[j];
+                }
+            }
+        } else {
+            const i64 q = r - hidden;
+            T* a2 = dw2s + e * mid * hidden + q * hidden;
+            for (i64 pr : of_expert[e]) {
+                const T hq = H[pr * mid + q];
+                const T* dye = DYE.data() + pr * hidden;
+                for (i64 j = 0; j < hidden; ++j) a2[j] += hq * dye[j];
             }
         }
-    }
+    });
     std::vector<T> dxg(tokens * hidden);
     router_backward_ste(x, gate, dwts.data(), dxg.data(), dgate, tokens, hidden, n_exp, k, forced);
     for (i64 i = 0; i < tokens * hidden; ++i) dx[i] += dxg[i];
@@ -275,10 +344,15 @@ void gqa_backward(const T* x, const T* wq, const T* wk, const T* wv, const T* wo
     i64 repeats = n_heads / (n_kv > 1 ? n_kv : 1);
     if (repeats < 1) repeats = 1;
     const T scale = (T)1.0 / std::sqrt((T)hd);
-    std::vector<T> dq(bs * qd, (T)0), dk(bs * kd, (T)0), dv(bs * kd, (T)0), dsc(s);
-    for (i64 bi = 0; bi < b; ++bi)
-        for (i64 h = 0; h < n_heads; ++h) {
-            i64 kv_h = h / repeats;
+    std::vector<T> dq(bs * qd, (T)0), dk(bs * kd, (T)0), dv(bs * kd, (T)0);
+    // One thread per (batch, kv head): it runs the query heads that share the
+    // kv head in ascending order, so every dk/dv element accumulates over
+    // (h, i, j) in the sequential nest's order and dq rows are disjoint.
+    const i64 n_groups = n_heads / repeats;
+    split_rows(b * n_groups, [&](i64 bg) {
+        const i64 bi = bg / n_groups, kv_h = bg % n_groups;
+        std::vector<T> dsc(s);
+        for (i64 h = kv_h * repeats; h < (kv_h + 1) * repeats; ++h) {
             for (i64 i = 0; i < s; ++i) {
                 i64 start = win_start(i, window);
                 i64 o_off = ((bi * s + i) * n_heads + h) * hd;
@@ -303,6 +377,7 @@ void gqa_backward(const T* x, const T* wq, const T* wk, const T* wv, const T* wo
                 }
             }
         }
+    });
     rope_all(dq.data(), b, s, n_heads, hd, -theta);
     rope_all(dk.data(), b, s, n_kv, hd, -theta);
     std::vector<T> dxk(bs * d), dxv(bs * d);
@@ -326,8 +401,11 @@ void attention_backward(const T* x, const T* wq, const T* wk, const T* wv, const
     linear<T>(x, wk, nullptr, k.data(), bs, d, d, 1);
     linear<T>(x, wv, nullptr, v.data(), bs, d, d, 1);
     const T scale = (T)1.0 / std::sqrt((T)d_head);
-    for (i64 bi = 0; bi < b; ++bi)
-        for (i64 h = 0; h < n_heads; ++h) {
+    // The (batch, head) pairs below touch disjoint slices of every buffer:
+    // one pair per thread, each element accumulated in the nest's order.
+    split_rows(b * n_heads, [&](i64 bh) {
+        const i64 bi = bh / n_heads, h = bh % n_heads;
+        {
             T* sc = attn.data() + (bi * n_heads + h) * s * s;
             for (i64 i = 0; i < s; ++i)
                 for (i64 j = 0; j < s; ++j) {
@@ -348,11 +426,13 @@ void attention_backward(const T* x, const T* wq, const T* wk, const T* wv, const
                     ctx[bi * s * d + i * d + h * d_head + t] = acc;
                 }
         }
+    });
     std::vector<T> dctx(bs * d);
     linear_backward(ctx.data(), wo, dy, dctx.data(), dwo, (T*)nullptr, bs, d, d);
     std::vector<T> dattn(attn.size()), dv(bs * d, (T)0);
-    for (i64 bi = 0; bi < b; ++bi)
-        for (i64 h = 0; h < n_heads; ++h) {
+    split_rows(b * n_heads, [&](i64 bh) {
+        const i64 bi = bh / n_heads, h = bh % n_heads;
+        {
             i64 base = (bi * n_heads + h) * s * s;
             for (i64 i = 0; i < s; ++i)
                 for (i64 j = 0; j < s; ++j) {
@@ -366,17 +446,19 @@ void attention_backward(const T* x, const T* wq, const T* wk, const T* wv, const
                     dattn[base + i * s + j] = g;
                 }
         }
+    });
     std::vector<T> dsc(attn.size());
-    for (i64 r = 0; r < b * n_heads * s; ++r) {
+    split_rows(b * n_heads * s, [&](i64 r) {
         const T* a = attn.data() + r * s;
         const T* g = dattn.data() + r * s;
         T dot = 0;
         for (i64 j = 0; j < s; ++j) dot += a[j] * g[j];
         for (i64 j = 0; j < s; ++j) dsc[r * s + j] = a[j] * (g[j] - dot);
-    }
+    });
     std::vector<T> dq(bs * d, (T)0), dk(bs * d, (T)0);
-    for (i64 bi = 0; bi < b; ++bi)
-        for (i64 h = 0; h < n_heads; ++h) {
+    split_rows(b * n_heads, [&](i64 bh) {
+        const i64 bi = bh / n_heads, h = bh % n_heads;
+        {
             i64 base = (bi * n_heads + h) * s * s;
             for (i64 i = 0; i < s; ++i)
                 for (i64 j = 0; j < s; ++j) {
@@ -389,6 +471,7 @@ void attention_backward(const T* x, const T* wq, const T* wk, const T* wv, const
                     }
                 }
         }
+    });
     std::vector<T> dxk(bs * d), dxv(bs * d);
     linear_backward(x, wq, dq.data(), dx, dwq, (T*)nullptr, bs, d, d);
     linear_backward(x, wk, dk.data(), dxk.data(), dwk, (T*)nullptr, bs, d, d);

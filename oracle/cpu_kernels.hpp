@@ -31,14 +31,26 @@ template <typename T> inline T tmax(T a, T b) { return std::fmax(a, b); }
 // in the reference (cpu.rs:39,61,188). Each output row is produced by one
 // thread, so the partition never changes a value. ORACLE_THREADS caps the
 // count (default: all hardware threads).
+//
+// The same helper also splits loops the reference runs sequentially, but
+// only loops whose iterations write disjoint outputs and where each output
+// element is still accumulated by one thread in the reference's order (rows
+// of a GEMM, heads of attention, tokens of the MoE forward, rows of a
+// weight gradient). Values are then bit-identical to the sequential loop;
+// only the wall time changes. A call made from inside a parallel region
+// runs sequentially (no nested thread spawning).
 inline int oracle_threads() {
     const char* e = std::getenv("ORACLE_THREADS");
     int n = e ? std::atoi(e) : (int)std::thread::hardware_concurrency();
     return n < 1 ? 1 : n;
 }
+inline bool& in_parallel_region() {
+    static thread_local bool flag = false;
+    return flag;
+}
 template <typename F> void parallel_rows(i64 rows, F f) {
     int nt = oracle_threads();
-    if (nt <= 1 || rows < 2) {
+    if (nt <= 1 || rows < 2 || in_parallel_region()) {
         for (i64 r = 0; r < rows; ++r) f(r);
         return;
     }
@@ -46,9 +58,24 @@ template <typename F> void parallel_rows(i64 rows, F f) {
     std::vector<std::thread> pool;
     for (int t = 0; t < nt; ++t)
         pool.emplace_back([=]() {
+            in_parallel_region() = true;
             for (i64 r = t; r < rows; r += nt) f(r);
         });
     for (auto& th : pool) th.join();
+}
+// The oracle-only splits (loops the reference runs on one thread). With
+// ORACLE_SPLIT=0 they run sequentially, so a timing run reproduces the
+// reference's own threading: threads only where Rayon splits rows.
+inline bool oracle_split() {
+    const char* e = std::getenv("ORACLE_SPLIT");
+    return !e || std::atoi(e) != 0;
+}
+template <typename F> void split_rows(i64 rows, F f) {
+    if (!oracle_split()) {
+        for (i64 r = 0; r < rows; ++r) f(r);
+        return;
+    }
+    parallel_rows(rows, f);
 }
 
 // tensor.rs:259-268 — Tensor::lcg. state = max(seed,1); per element
@@ -101,7 +128,7 @@ template <typename T> void gelu(const T* x, T* y, i64 n) {
 // NaN-ignoring fold from -inf, e = exp(x - max) summed left to right,
 // then multiplied by inv = 1 / max(sum, 1e-30).
 template <typename T> void softmax_last(const T* x, T* y, i64 rows, i64 last) {
-    for (i64 r = 0; r < rows; ++r) {
+    parallel_rows(rows, [=](i64 r) {
         const T* in = x + r * last;
         T* out = y + r * last;
         T mx = -INFINITY;
@@ -113,14 +140,14 @@ template <typename T> void softmax_last(const T* x, T* y, i64 rows, i64 last) {
         }
         T inv = (T)1.0 / tmax(sum, (T)1e-30);
         for (i64 i = 0; i < last; ++i) out[i] *= inv;
-    }
+    });
 }
 
 // cpu.rs:54-78 — two-pass population variance.
 template <typename T>
 void layer_norm(const T* x, const T* gamma, const T* beta, T* y, i64 rows, i64 last, T eps) {
     const T n = (T)last;
-    for (i64 r = 0; r < rows; ++r) {
+    parallel_rows(rows, [=](i64 r) {
         const T* in = x + r * last;
         T* out = y + r * last;
         T s = 0;
@@ -134,7 +161,7 @@ void layer_norm(const T* x, const T* gamma, const T* beta, T* y, i64 rows, i64 l
         T var = v / n;
         T inv = (T)1.0 / std::sqrt(var + eps);
         for (i64 i = 0; i < last; ++i) out[i] = (in[i] - mean) * inv * gamma[i] + beta[i];
-    }
+    });
 }
 
 // cpu.rs:80-98 — same-length add, or b broadcast over the last dim.
@@ -150,16 +177,17 @@ template <typename T> void mul(const T* a, const T* b, T* y, i64 n) {
     for (i64 i = 0; i < n; ++i) y[i] = a[i] * b[i];
 }
 
-// cpu.rs:115-126 — sequential GEMM, s += a*b in p order.
+// cpu.rs:115-126 — sequential GEMM, s += a*b in p order (rows split over
+// threads; each element's sum is unchanged).
 template <typename T> void matmul_seq(const T* a, const T* b, T* c, i64 m, i64 k, i64 n) {
-    for (i64 i = 0; i < m; ++i) {
+    split_rows(m, [=](i64 i) {
         const T* ai = a + i * k;
         for (i64 j = 0; j < n; ++j) {
             T s = 0;
             for (i64 p = 0; p < k; ++p) s += ai[p] * b[p * n + j];
             c[i * n + j] = s;
         }
-    }
+    });
 }
 
 // cpu.rs:186-232 — the row-parallel GEMM with 8-lane accumulators.
@@ -230,9 +258,11 @@ void attention(const T* x, const T* wq, const T* wk, const T* wv, const T* wo, T
     linear<T>(x, wk, nullptr, k.data(), b * s, d, d, 1);
     linear<T>(x, wv, nullptr, v.data(), b * s, d, d, 1);
     const T scale = (T)1.0 / std::sqrt((T)d_head);
-    std::vector<T> scores(s * s);
-    for (i64 bi = 0; bi < b; ++bi)
-        for (i64 h = 0; h < n_heads; ++h) {
+    // (batch, head) pairs are independent: one per thread, own score buffer
+    split_rows(b * n_heads, [&](i64 bh) {
+        const i64 bi = bh / n_heads, h = bh % n_heads;
+        std::vector<T> scores(s * s);
+        {
             for (i64 i = 0; i < s; ++i)
                 for (i64 j = 0; j < s; ++j) {
                     if (causal && j > i) {
@@ -254,6 +284,7 @@ void attention(const T* x, const T* wq, const T* wk, const T* wv, const T* wo, T
                     ctx[bi * s * d + i * d + h * d_head + t] = acc;
                 }
         }
+    });
     linear<T>(ctx.data(), wo, nullptr, y, b * s, d, d, 1);
 }
 

@@ -77,10 +77,12 @@ void gqa_core(const T* q, const T* k, const T* v, T* ctx, T* probs, i64 b, i64 s
     i64 repeats = n_heads / (n_kv > 1 ? n_kv : 1);
     if (repeats < 1) repeats = 1;
     const T scale = (T)1.0 / std::sqrt((T)hd);
-    std::vector<T> scores(s);
     std::fill(ctx, ctx + b * s * n_heads * hd, (T)0);
-    for (i64 bi = 0; bi < b; ++bi)
-        for (i64 h = 0; h < n_heads; ++h) {
+    // (batch, head) pairs write disjoint ctx / probs slices: one per thread
+    split_rows(b * n_heads, [&](i64 bh) {
+        const i64 bi = bh / n_heads, h = bh % n_heads;
+        std::vector<T> scores(s);
+        {
             i64 kv_h = h / repeats;
             for (i64 i = 0; i < s; ++i) {
                 i64 start = win_start(i, window);
@@ -107,6 +109,7 @@ void gqa_core(const T* q, const T* k, const T* v, T* ctx, T* probs, i64 b, i64 s
                 }
             }
         }
+    });
 }
 
 // moe.rs:64-136 — GQA + RoPE + optional window on x [B,S,d] (RMS-normed).
@@ -197,10 +200,12 @@ template <typename T>
 void moe(const T* x, const T* gate, const T* w1s, const T* w3s, const T* w2s, T* y, i64 tokens,
          i64 hidden, i64 mid, i64 n_exp, i64 k, const int64_t* forced = nullptr) {
     std::vector<int64_t> idx(tokens * k);
-    std::vector<T> wts(tokens * k), logits(tokens * n_exp), ye(hidden);
+    std::vector<T> wts(tokens * k), logits(tokens * n_exp);
     route(x, gate, tokens, hidden, n_exp, k, idx.data(), wts.data(), logits.data(), forced);
     std::fill(y, y + tokens * hidden, (T)0);
-    for (i64 t = 0; t < tokens; ++t)
+    // tokens are independent (each writes its own output row): one per thread
+    split_rows(tokens, [&](i64 t) {
+        std::vector<T> ye(hidden);
         for (i64 kk = 0; kk < k; ++kk) {
             i64 e = idx[t * k + kk];
             T wt = wts[t * k + kk];
@@ -208,17 +213,19 @@ void moe(const T* x, const T* gate, const T* w1s, const T* w3s, const T* w2s, T*
                    w2s + e * mid * hidden, ye.data(), 1, hidden, mid);
             for (i64 i = 0; i < hidden; ++i) y[t * hidden + i] += wt * ye[i];
         }
+    });
 }
 
 // moe.rs:325-333 — logits = x · w^T with w stored [vocab, hidden]; the
 // reference transposes then runs linear_seq, i.e. a sequential p-order dot.
 template <typename T> void lm_head(const T* x, const T* w, T* y, i64 rows, i64 hidden, i64 vocab) {
-    for (i64 i = 0; i < rows; ++i)
+    split_rows(rows, [=](i64 i) {
         for (i64 j = 0; j < vocab; ++j) {
             T s = 0;
             for (i64 p = 0; p < hidden; ++p) s += x[i * hidden + p] * w[j * hidden + p];
             y[i * vocab + j] = s;
         }
+    });
 }
 
 }  // namespace orc

@@ -480,11 +480,13 @@ def mixtral_forward(cfg, P, tokens, batch, seq):
     return logits
 
 
-def mixtral_step(cfg, P, tokens, batch, seq, f64=False):
-    """train.rs:261 mixtral_step -> (loss, packed grads)."""
+def mixtral_step(cfg, P, tokens, batch, seq, f64=False, out=None):
+    """train.rs:261 mixtral_step -> (loss, packed grads). `out` (optional, same
+    shape and dtype as P) receives the gradients instead of a new array."""
     a, P = cfg.arr(), _arr(P, f64)
     tok = np.ascontiguousarray(tokens, np.uint32)
-    G = np.empty_like(P)
+    G = np.empty_like(P) if out is None else out
+    assert G.shape == P.shape and G.dtype == P.dtype and G.flags["C_CONTIGUOUS"]
     loss = (C.c_double if f64 else C.c_float)()
     rc = _fn("mixtral_step", f64)(_p(a), C.c_float(cfg.eps), C.c_double(cfg.theta), _p(P), _p(tok), I64(batch), I64(seq),
                                   C.byref(loss), _p(G))
@@ -530,19 +532,22 @@ def mlp_step(w1, b1, w2, b2, x, labels=None, y_mse=None):
 BLOCK_KEYS = ["g1", "be1", "wq", "wk", "wv", "wo", "g2", "be2", "f1", "c1", "f2", "c2"]
 
 
-def block_fwd_bwd(W, x, dy, n_heads, eps=1e-5):
+def block_fwd_bwd(W, x, dy, n_heads, eps=1e-5, f64=False):
     """Causal pre-LN transformer block fwd (+bwd when dy is given).
 
-    W: dict of BLOCK_KEYS arrays. Returns (y, dx, grads dict)."""
-    x = _arr(x)
+    W: dict of BLOCK_KEYS arrays. Returns (y, dx, grads dict). f64=True runs
+    the same loop nests in double precision (the exact reference of the
+    parity tests' fallback)."""
+    x = _arr(x, f64)
     b, s, d = x.shape
     ff = W["f1"].shape[1]
-    Wc = [_arr(W[k]) for k in BLOCK_KEYS]
+    Wc = [_arr(W[k], f64) for k in BLOCK_KEYS]
     Gs = [np.empty_like(w) for w in Wc]
     Wp = (VP * 12)(*[w.ctypes.data for w in Wc])
     Gp = (VP * 12)(*[g.ctypes.data for g in Gs])
     y = np.empty_like(x)
     dx = np.empty_like(x)
-    dyc = _arr(dy) if dy is not None else None
-    lib().orc_block_fwd_bwd(Wp, Gp, _p(x), _p(dyc), _p(y), _p(dx), I64(b), I64(s), I64(d), I64(n_heads), I64(ff), C.c_float(eps))
+    dyc = _arr(dy, f64) if dy is not None else None
+    _fn("block_fwd_bwd", f64)(Wp, Gp, _p(x), _p(dyc), _p(y), _p(dx), I64(b), I64(s), I64(d), I64(n_heads), I64(ff),
+                              _scalar(eps, f64))
     return y, (dx if dy is not None else None), dict(zip(BLOCK_KEYS, Gs))

@@ -164,8 +164,14 @@ int orc_mlp_step(const float* w1, const float* b1, const float* w2, const float*
 // W and G: 12 pointers each in the order g1, be1, wq, wk, wv, wo, g2, be2, f1, c1, f2, c2.
 void orc_block_fwd_bwd(const float* const* W, float* const* G, const float* x, const float* dy, float* y, float* dx,
                        i64 b, i64 s, i64 d, i64 heads, i64 ff, float eps) {
-    orc::BlockW w{W[0], W[1], W[2], W[3], W[4], W[5], W[6], W[7], W[8], W[9], W[10], W[11]};
-    orc::BlockG g{G[0], G[1], G[2], G[3], G[4], G[5], G[6], G[7], G[8], G[9], G[10], G[11]};
+    orc::BlockW<float> w{W[0], W[1], W[2], W[3], W[4], W[5], W[6], W[7], W[8], W[9], W[10], W[11]};
+    orc::BlockG<float> g{G[0], G[1], G[2], G[3], G[4], G[5], G[6], G[7], G[8], G[9], G[10], G[11]};
+    orc::block_fwd_bwd(w, x, dy, y, dx, g, b, s, d, heads, ff, eps);
+}
+void orc64_block_fwd_bwd(const double* const* W, double* const* G, const double* x, const double* dy, double* y,
+                         double* dx, i64 b, i64 s, i64 d, i64 heads, i64 ff, double eps) {
+    orc::BlockW<double> w{W[0], W[1], W[2], W[3], W[4], W[5], W[6], W[7], W[8], W[9], W[10], W[11]};
+    orc::BlockG<double> g{G[0], G[1], G[2], G[3], G[4], G[5], G[6], G[7], G[8], G[9], G[10], G[11]};
     orc::block_fwd_bwd(w, x, dy, y, dx, g, b, s, d, heads, ff, eps);
 }
 

@@ -234,17 +234,18 @@ int mlp_step(const T* w1, const T* b1, const T* w2, const T* b2, const T* x, con
 //   y = h + linear(gelu(linear(layer_norm(h; g2, be2), f1, c1)), f2, c2)
 // with cpu::linear (8-lane order) for every projection and the adjoints of
 // adjoint.rs for the backward, given an injected dy.
-struct BlockW {
-    const float *g1, *be1, *wq, *wk, *wv, *wo, *g2, *be2, *f1, *c1, *f2, *c2;
+template <typename T> struct BlockW {
+    const T *g1, *be1, *wq, *wk, *wv, *wo, *g2, *be2, *f1, *c1, *f2, *c2;
 };
-struct BlockG {
-    float *g1, *be1, *wq, *wk, *wv, *wo, *g2, *be2, *f1, *c1, *f2, *c2;
+template <typename T> struct BlockG {
+    T *g1, *be1, *wq, *wk, *wv, *wo, *g2, *be2, *f1, *c1, *f2, *c2;
 };
 
-inline void block_fwd_bwd(const BlockW& W, const float* x, const float* dy, float* y, float* dx,
-                          const BlockG& G, i64 b, i64 s, i64 d, i64 heads, i64 ff, float eps) {
+template <typename T>
+void block_fwd_bwd(const BlockW<T>& W, const T* x, const T* dy, T* y, T* dx, const BlockG<T>& G, i64 b, i64 s,
+                   i64 d, i64 heads, i64 ff, T eps) {
     i64 n = b * s, hdim = d / heads;
-    std::vector<float> ln1(n * d), att(n * d), hh(n * d), ln2(n * d), u(n * ff), gl(n * ff), f(n * d);
+    std::vector<T> ln1(n * d), att(n * d), hh(n * d), ln2(n * d), u(n * ff), gl(n * ff), f(n * d);
     layer_norm(x, W.g1, W.be1, ln1.data(), n, d, eps);
     attention(ln1.data(), W.wq, W.wk, W.wv, W.wo, att.data(), b, s, d, heads, hdim, 1);
     add(x, att.data(), hh.data(), n * d);
@@ -254,7 +255,7 @@ inline void block_fwd_bwd(const BlockW& W, const float* x, const float* dy, floa
     linear(gl.data(), W.f2, W.c2, f.data(), n, ff, d, 1);
     add(hh.data(), f.data(), y, n * d);
     if (!dy) return;
-    std::vector<float> dgl(n * ff), du(n * ff), dln2(n * d), dh(n * d), dln1(n * d), dxa(n * d);
+    std::vector<T> dgl(n * ff), du(n * ff), dln2(n * d), dh(n * d), dln1(n * d), dxa(n * d);
     linear_backward(gl.data(), W.f2, dy, dgl.data(), G.f2, G.c2, n, ff, d);
     gelu_backward(u.data(), dgl.data(), du.data(), n * ff);
     linear_backward(ln2.data(), W.f1, du.data(), dln2.data(), G.f1, G.c1, n, d, ff);

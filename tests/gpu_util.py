@@ -59,6 +59,29 @@ def close_bf16(got, ref, what="", atol=ATOL_BF16):
                            f"{scale:.3e}, worst got {got.reshape(-1)[i]:.5e} ref {ref.reshape(-1)[i]:.5e}")
 
 
+U_BF16 = 2.0 ** -8  # unit roundoff of bf16 (8 significant bits, round to nearest)
+
+
+def close_bf16_derived(got, ref, rounding_bound, what=""):
+    """The bf16 band plus a derived bound: |got - ref| <= 2e-2·|ref| +
+    1e-3·max(1, max|ref|) + rounding_bound, where rounding_bound is the
+    first-order effect, per element, of the bf16 roundings of intermediates
+    that the tensor-core path stores and the fp32 reference keeps in fp32
+    (each test derives it from the exact intermediates and states which
+    roundings it covers)."""
+    got = host(got) if torch.is_tensor(got) else np.asarray(got, np.float32)
+    ref = np.asarray(ref, np.float64).reshape(got.shape)
+    rb = np.asarray(rounding_bound, np.float64).reshape(got.shape)
+    scale = max(1.0, float(np.max(np.abs(ref)))) if ref.size else 1.0
+    err = np.abs(got.astype(np.float64) - ref)
+    bound = RTOL_BF16 * np.abs(ref) + ATOL_BF16 * scale + rb
+    bad = err > bound
+    i = int(np.argmax(err - bound)) if ref.size else 0
+    assert not bad.any(), (f"{what}: {int(bad.sum())}/{ref.size} out of tolerance; max excess "
+                           f"{float(np.max(err - bound)):.3e}, worst got {got.reshape(-1)[i]:.5e} ref "
+                           f"{ref.reshape(-1)[i]:.5e} rounding bound {rb.reshape(-1)[i]:.3e}")
+
+
 def rel_l2(got, ref):
     got = host(got) if torch.is_tensor(got) else np.asarray(got, np.float32)
     ref = np.asarray(ref, np.float64).reshape(got.shape)
