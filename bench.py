@@ -42,7 +42,12 @@ def parse():
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-workloads", action="store_true", help="N=1: skip the config 1/3/4 measurements")
     p.add_argument("--kernel-only", action="store_true",
-                   help="run only the dominant kernel (grouped expert GEMM, W13 forward shape) for profiling")
+                   help="run only one kernel at its config-5 shape for profiling (--kernel)")
+    p.add_argument("--kernel", default="w13",
+                   choices=["w13", "swiglu_fwd", "swiglu_bwd", "attn", "step_small"],
+                   help="w13: grouped expert GEMM (W13 forward shape); swiglu_fwd / swiglu_bwd: the expert GEMMs "
+                        "with the SwiGLU epilogues; attn: tcgen05 flash attention fwd + bwd (B8 S2048 H16 hd64); "
+                        "step_small: trainer steps at config-5 widths on 2 sequences (its HBM-bound kernels)")
     p.add_argument("--reps", type=int, default=20)
     return p.parse_args()
 
@@ -460,12 +465,68 @@ def workload_tiny(local, steps, cpu):
 
 
 def run_kernel_only(args):
+    """One kernel at its config-5 per-launch shape, `args.reps` launches, for
+    ncu captures (the printed timing is informational)."""
+    import numpy as np
     import torch
+    from catnn_b200 import ops
     torch.cuda.set_device(0)
     T = CFG["global_batch"] * CFG["seq"]
-    ms, flops, rows, F, d = dominant_kernel(0, T * CFG["top_k"], CFG["experts"], 1, args.reps)
-    print(json.dumps({"kernel": "k_gemm_tc grouped W13 forward", "rows": rows, "N": 2 * F, "K": d, "ms": ms,
-                      "tflops": flops / (ms * 1e-3) / 1e12}), flush=True)
+    F, d, E = CFG["mid"], CFG["hidden"], CFG["experts"]
+    if args.kernel == "w13":
+        ms, flops, rows, F, d = dominant_kernel(0, T * CFG["top_k"], E, 1, args.reps)
+        print(json.dumps({"kernel": "k_gemm_tc grouped W13 forward", "rows": rows, "N": 2 * F, "K": d, "ms": ms,
+                          "tflops": flops / (ms * 1e-3) / 1e12}), flush=True)
+        return
+    dev = "cuda:0"
+    stream = torch.cuda.current_stream(0)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+
+    def timed(fn, flops, name, **kw):
+        fn()
+        torch.cuda.synchronize()
+        e0.record(stream)
+        for _ in range(args.reps):
+            fn()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / args.reps
+        print(json.dumps({"kernel": name, "ms": ms, "tflops": flops / (ms * 1e-3) / 1e12, **kw}), flush=True)
+    if args.kernel in ("swiglu_fwd", "swiglu_bwd"):
+        rng = np.random.default_rng(CFG["seed"])
+        counts = np.bincount(rng.integers(0, E, T * CFG["top_k"]), minlength=E)
+        offs = np.concatenate([[0], np.cumsum(-(-counts // 128) * 128)]).astype(np.int32)
+        rows = int(offs[-1])
+        off = torch.as_tensor(offs).to(dev)
+        X = (torch.randn(rows, d, device=dev) * 0.5).to(torch.bfloat16)
+        W13 = (torch.randn(E, d, 2 * F, device=dev) / d ** 0.5).to(torch.bfloat16)
+        ac, h = ops.moe_expert_swiglu(X, W13, off)
+        if args.kernel == "swiglu_fwd":
+            timed(lambda: ops.moe_expert_swiglu(X, W13, off), 2.0 * int(counts.sum()) * 2 * F * d,
+                  "k_gemm_tc grouped W13 + SwiGLU epilogue", rows=rows)
+        else:
+            W2 = (torch.randn(E, F, d, device=dev) / F ** 0.5).to(torch.bfloat16)
+            DY = torch.randn(rows, d, device=dev).to(torch.bfloat16)
+            timed(lambda: ops.moe_expert_swiglu_backward(DY, W2, ac, off), 2.0 * int(counts.sum()) * F * d,
+                  "k_gemm_tc grouped W2 dgrad + SwiGLU adjoint epilogue", rows=rows)
+    elif args.kernel == "attn":
+        B, S, H, hd = CFG["global_batch"], CFG["seq"], CFG["heads"], CFG["hidden"] // CFG["heads"]
+        q, k, v, do = (torch.randn(B, S, H, hd, device=dev).to(torch.bfloat16) for _ in range(4))
+        do = do.reshape(B, S, H * hd)
+        o, lse = ops.attention_core(q, k, v, True)
+        fwd = 2.0 * B * H * S * S * hd  # causal half of 4·B·H·S²·hd
+        timed(lambda: ops.attention_core(q, k, v, True), fwd, "fa5 forward (causal)")
+        timed(lambda: ops.attention_core_backward(q, k, v, o, lse, do, True), 2.5 * fwd, "fa5 backward (causal)")
+    elif args.kernel == "step_small":
+        from catnn_b200.train import MoeConfig, MoeTrainer, init_params
+        mc = MoeConfig.make(CFG["vocab"], d, F, 1, CFG["heads"], CFG["kv_heads"], E, CFG["top_k"], batch=2, seq=CFG["seq"],
+                            rope_theta=CFG["rope_theta"], dtype=torch.bfloat16, optimizer="adam", lr=CFG["lr"])
+        tr = MoeTrainer(mc)
+        tr.set_params(init_params(mc, CFG["seed"]))
+        tok = torch.randint(0, CFG["vocab"], (2 * CFG["seq"],), device=dev, dtype=torch.int32)
+        loss = torch.zeros(1, device=dev)
+        timed(lambda: tr.step(tok, update=True, loss_out=loss), 0.0, "trainer step, 1 layer, 4096 tokens")
+        tr.close()
 
 
 def run_ours(args):

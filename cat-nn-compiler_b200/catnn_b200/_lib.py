@@ -64,6 +64,7 @@ SIGNATURES = {
     "catnn_grouped_gemm": [VP, I32, I64, I64, I64, I64, VP, VP, VP, VP, I32, I32],
     "catnn_moe_expert_swiglu_fwd": [VP, VP, VP, VP, I64, I64, I64, I64, VP, VP],
     "catnn_moe_expert_swiglu_bwd": [VP, VP, VP, VP, VP, I64, I64, I64, I64, VP],
+    "catnn_kernel_describe": [VP, C.c_char_p, I32, VP, VP],
     "catnn_swiglu_fwd": [VP, VP, VP, VP, VP, VP, I64, I64, I64, I32],
     "catnn_swiglu_bwd": [VP, VP, VP, VP, VP, VP, VP, VP, VP, VP, I64, I64, I64, I32],
     "catnn_moe_fwd": [VP, VP, VP, VP, VP, VP, VP, I64, I64, I64, I64, I64, I32],

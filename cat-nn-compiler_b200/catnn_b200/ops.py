@@ -552,3 +552,34 @@ def checksum(x):
     v = C.c_uint64()
     _lib.call("catnn_checksum_f32", _h(x), _p(x), x.numel(), C.byref(v))
     return int(v.value)
+
+
+# ------------------------------------------------------------------ kernel resources
+class KernelShape(C.Structure):
+    """catnn_kernel_shape (include/catnn_b200.h)."""
+    _fields_ = [(n, C.c_int64) for n in ("rows", "width", "inner", "batch", "seq", "heads", "head_dim")]
+
+
+class KernelResource(C.Structure):
+    """catnn_kernel_resource (include/catnn_b200.h): KernelResource of
+    crates/catnn-compile/src/kernel/resource.rs:28-44, measured."""
+    _fields_ = [("kernel", C.c_char * 192), ("file", C.c_char * 32), ("registers_per_thread", C.c_int32),
+                ("max_threads_per_block", C.c_int32), ("static_smem_bytes", C.c_int64),
+                ("dynamic_smem_bytes", C.c_int64), ("local_bytes_per_thread", C.c_int64), ("grid", C.c_uint32 * 3),
+                ("block", C.c_uint32 * 3), ("launch_arg_bytes", C.c_int64), ("code_bytes", C.c_int64),
+                ("code_estimated", C.c_int32), ("binary_version", C.c_int32)]
+
+
+def kernel_describe(op, dtype=torch.bfloat16, device=None, rows=0, width=0, inner=0, batch=0, seq=0, heads=0,
+                    head_dim=0):
+    """The resource record of the kernel that runs IR op `op` (resource::describe,
+    resource.rs:159), as a dict."""
+    shape = KernelShape(rows, width, inner, batch, seq, heads, head_dim)
+    out = KernelResource()
+    h = context(device).bind()
+    _lib.call("catnn_kernel_describe", h, op.encode(), BF16 if dtype == torch.bfloat16 else F32, C.byref(shape),
+              C.byref(out))
+    d = {f: getattr(out, f) for f, _ in KernelResource._fields_}
+    d["kernel"], d["file"] = out.kernel.decode(), out.file.decode()
+    d["grid"], d["block"] = list(out.grid), list(out.block)
+    return d

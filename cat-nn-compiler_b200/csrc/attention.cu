@@ -637,4 +637,25 @@ void attention_bwd(Context* c, const void* q, const void* k, const void* v, cons
     launched(c, 3);
 }
 
+// attention / gqa_attention on the fp32 path (k_attn_fwd, 16 queries per
+// CTA) and the embedding gather (one CTA per token).
+KernelInfo attention_info(Context* c, const std::string& op, int dtype, const KShape& s) {
+    KernelInfo k;
+    if (op == "attention" || op == "gqa_attention") {
+        k.fn = dtype == CATNN_BF16 ? (const void*)k_attn_fwd<bf16> : (const void*)k_attn_fwd<float>;
+        k.file = "attention.cu";
+        k.grid[0] = (unsigned)cdiv(s.seq, AQ);
+        k.grid[1] = (unsigned)s.heads;
+        k.grid[2] = (unsigned)s.batch;
+        k.block[0] = 128;
+        k.dyn_smem = attn_smem_bytes(0, s.head_dim);
+    } else if (op == "embedding") {
+        k.fn = dtype == CATNN_BF16 ? (const void*)k_embed<bf16> : (const void*)k_embed<float>;
+        k.file = "attention.cu";
+        k.grid[0] = (unsigned)std::max<i64>(1, s.rows);
+        k.block[0] = s.width >= 256 ? 256 : 64;
+    }
+    return k;
+}
+
 }  // namespace catnn

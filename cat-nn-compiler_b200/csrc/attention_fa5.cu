@@ -919,4 +919,19 @@ void attention_bwd_tc5(Context* c, const void* q, const void* k, const void* v, 
     launched(c, 2);
 }
 
+// attention / gqa_attention on the bf16 path (head_dim 64): the forward
+// kernel, one CTA per 128 queries of a (batch, head).
+KernelInfo fa5_info(Context* c, const std::string& op, const KShape& s) {
+    KernelInfo k;
+    if (!(op == "attention" || op == "gqa_attention") || s.head_dim != fa5::HD) return k;
+    k.fn = (const void*)fa5::k_fwd;
+    k.file = "attention_fa5.cu";
+    k.grid[0] = (unsigned)cdiv(s.seq, fa5::BQ);
+    k.grid[1] = (unsigned)s.heads;
+    k.grid[2] = (unsigned)s.batch;
+    k.block[0] = fa5::NT;
+    k.dyn_smem = fa5::SMEM;
+    return k;
+}
+
 }  // namespace catnn

@@ -265,4 +265,21 @@ void adam(Context* c, float* p, const void* g, float* m, float* v, i64 n, uint64
     launched(c, (head > 0) + (n > head));
 }
 
+// Elementwise ops and the optimizers: grid-stride, at most 8 CTAs per SM.
+KernelInfo elementwise_info(Context* c, const std::string& op, int dtype, const KShape& s) {
+    KernelInfo k;
+    const bool b = dtype == CATNN_BF16;
+    const i64 n = s.rows * s.width;
+    if (op == "relu" || op == "gelu") k.fn = b ? (const void*)k_act_fwd<bf16> : (const void*)k_act_fwd<float>;
+    else if (op == "add" || op == "residual_add") k.fn = b ? (const void*)k_add<bf16> : (const void*)k_add<float>;
+    else if (op == "mul") k.fn = b ? (const void*)k_mul<bf16> : (const void*)k_mul<float>;
+    else if (op == "sgd") k.fn = (const void*)k_sgd;
+    else if (op == "adam") k.fn = (const void*)k_adam<float, 4>;
+    else return k;
+    k.file = "elementwise.cu";
+    k.grid[0] = (unsigned)ew_grid(c, op == "adam" ? (n + 3) / 4 : n);
+    k.block[0] = 256;
+    return k;
+}
+
 }  // namespace catnn

@@ -499,4 +499,17 @@ void gemm(Context* c, bool ta, bool tb, i64 M, i64 N, i64 K, const void* A, i64 
                      resid);
 }
 
+// fp32 GEMMs of linear / matmul / lm_head / the MoE experts: 128 x 128
+// output tiles, 256 threads.
+KernelInfo sgemm_info(Context* c, const std::string& op, const KShape& s) {
+    KernelInfo k;
+    if (!(op == "linear" || op == "matmul" || op == "lm_head" || op == "moe")) return k;
+    k.fn = op == "lm_head" ? (const void*)k_sgemm<float, false, true> : (const void*)k_sgemm<float, false, false>;
+    k.file = "gemm.cu";
+    k.grid[0] = (unsigned)cdiv(s.width, 128);
+    k.grid[1] = (unsigned)cdiv(s.rows, 128);
+    k.block[0] = 256;
+    return k;
+}
+
 }  // namespace catnn

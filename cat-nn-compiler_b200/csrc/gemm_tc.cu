@@ -2,7 +2,10 @@
 // accumulators, fed by TMA. Persistent, warp-specialized:
 //   warp 0      TMA producer (one elected thread) over a STAGES-deep ring
 //   warp 1      TMEM owner + MMA issuer (one thread), 128 x BN x 16 MMAs
-//   warps 2..5  epilogue: TMEM -> registers -> bias/activation -> HBM
+//   warps 2..9  epilogue: TMEM -> registers -> bias/activation -> HBM; two
+//               warps per TMEM lane quadrant (warp % 4), each taking half of
+//               the tile's columns, so one warp's latency hides behind the
+//               other's work on the same sub-partition
 // Two TMEM accumulators (2*BN columns) let the epilogue of tile i overlap
 // the MMAs of tile i+1. Every mbarrier wait is bounded (see tc::mbar_wait).
 //
@@ -59,7 +62,9 @@ struct TcArgs {
 };
 
 static constexpr int BM = 128, BK = 64;
-static constexpr uint32_t EPI_STAGE_BYTES = 4 * 8192;
+static constexpr int EPI_WARPS = 8;
+static constexpr int GEMM_THREADS = 32 * (2 + EPI_WARPS);
+static constexpr uint32_t EPI_STAGE_BYTES = EPI_WARPS * 2 * 2048;  // two 2 KB buffers per epilogue warp
 
 struct TileInfo {
     int g, m0, n0, kstart, klen, mlimit, arow0, ks;
@@ -144,10 +149,16 @@ __device__ __forceinline__ TileInfo tile_at_base(const TcArgs& a, int t) {
     return ti;
 }
 
-// moe.rs:12-14 / adjoint.rs:208-215 (the same expressions as k_swiglu / k_swiglu_bwd)
-__device__ __forceinline__ float tc_silu(float x) { return x / (1.0f + expf(-x)); }
+// moe.rs:12-14 / adjoint.rs:208-215 for the bf16 epilogues: σ(x) = 1/(1+e^-x)
+// with the hardware exponential and reciprocal (a few ulp of fp32; the
+// results are rounded to bf16, whose unit is 2^-8). One epilogue warp per
+// sub-partition runs these serially, so short dependency chains matter more
+// than the last fp32 bit: the IEEE exp and division cost ~35 instructions
+// with branches, these ~6.
+__device__ __forceinline__ float tc_sigmoid(float x) { return __frcp_rn(1.0f + __expf(-x)); }
+__device__ __forceinline__ float tc_silu(float x) { return x * tc_sigmoid(x); }
 __device__ __forceinline__ float tc_silu_grad(float x) {
-    float s = 1.0f / (1.0f + expf(-x));
+    const float s = tc_sigmoid(x);
     return s + x * s * (1.0f - s);
 }
 
@@ -162,9 +173,9 @@ struct Stage32 {
     __device__ __forceinline__ void put(const uint32_t (&pk)[16], const CUtensorMap* map, bool tma, int x, int y,
                                         bf16* direct, bool row_ok) {
         if (tma) {
-            const int b = (int)(*nst & 3u);
+            const int b = (int)(*nst & 1u);
             const uint32_t sb = tc::smem_u32(stage + b * 2048);
-            if (lane == 0) tc::bulk_wait_read<3>();
+            if (lane == 0) tc::bulk_wait_read<1>();
             __syncwarp();
 #pragma unroll
             for (int c4 = 0; c4 < 4; ++c4)
@@ -201,7 +212,7 @@ __device__ __forceinline__ float act_apply(float v, int act) {
 }
 
 template <bool A_MN, bool B_MN, int BN, int STAGES>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(GEMM_THREADS, 1)
     k_gemm_tc(const __grid_constant__ CUtensorMap mapA, const __grid_constant__ CUtensorMap mapB,
               const __grid_constant__ CUtensorMap mapC, const __grid_constant__ CUtensorMap mapD, TcArgs a) {
     constexpr uint32_t A_BYTES = BM * BK * 2;
@@ -230,7 +241,7 @@ __global__ void __launch_bounds__(192, 1)
         }
         for (int i = 0; i < 2; ++i) {
             tc::mbar_init(&tfull[i], 1);
-            tc::mbar_init(&tempty[i], 4);
+            tc::mbar_init(&tempty[i], EPI_WARPS);
         }
         tc::mbar_init(drain, 1);
         tc::fence_mbar_init();
@@ -329,7 +340,9 @@ __global__ void __launch_bounds__(192, 1)
         tc::mbar_wait(drain, 0, a.status, 2, 400000000ll, false);
     } else if (warp >= 2) {
         // ---------------- epilogue
-        const int q = warp & 3;
+        const int ew = warp - 2;     // epilogue warp 0..7
+        const int q = warp & 3;      // TMEM lane quadrant this warp may read
+        const int half = ew >> 2;    // which half of the tile's columns
         const bool plain = !a.bias && !a.resid && a.act == CATNN_ACT_NONE && !a.accumulate;
         int it = 0;
         uint32_t nst = 0;  // TMA stores issued by this warp (picks the staging buffer)
@@ -352,7 +365,7 @@ __global__ void __launch_bounds__(192, 1)
                 a.mode == 0 ? row0 : (a.mode == 1 ? (long long)ti.arow0 + row0 : (long long)ti.g * a.M + row0);
             if (a.epi != 0) {
                 // SwiGLU epilogues (mode 1, bf16, no split-K; see TcArgs::epi)
-                Stage32 st{stage_c + q * 8192, &nst, lane};
+                Stage32 st{stage_c + ew * 4096, &nst, lane};
                 const bool tma = a.tma_c && row0 + 32 <= ti.mlimit;
                 const long long grow = (long long)ti.arow0 + row;
                 if (a.epi == 1) {
@@ -360,7 +373,7 @@ __global__ void __launch_bounds__(192, 1)
                     bf16* hp = (bf16*)a.aux + grow * a.ldaux;
                     const int hcol0 = (ti.n0 >> 8) << 7;
 #pragma unroll 1
-                    for (int cc = 0; cc < 4; ++cc) {
+                    for (int cc = half * 2; cc < half * 2 + 2; ++cc) {
                         uint32_t ra[32], rc[32];
                         tc::tmem_ld32(tmem_base + ((uint32_t)(q * 32) << 16) + acc * BN + cc * 32, ra);
                         tc::tmem_ld32(tmem_base + ((uint32_t)(q * 32) << 16) + acc * BN + 128 + cc * 32, rc);
@@ -381,16 +394,12 @@ __global__ void __launch_bounds__(192, 1)
                 } else {
                     const bf16* acin = (const bf16*)a.aux + grow * a.ldaux;
                     bf16* dacp = (bf16*)a.C + grow * a.ldc;
-#pragma unroll 1
-                    for (int cc = 0; cc < BN / 32; ++cc) {
+                    // a and c of 32 SwiGLU columns (interleaved layout) for chunk cc,
+                    // loaded one chunk ahead so their latency overlaps the math
+                    auto load_ac = [&](int cc, uint4 (&va)[4], uint4 (&vc)[4]) {
                         const int f0 = ti.n0 + cc * 32;
-                        if (f0 >= a.N) break;  // warp-uniform
-                        uint32_t r[32];
-                        tc::tmem_ld32(tmem_base + ((uint32_t)(q * 32) << 16) + acc * BN + cc * 32, r);
-                        // a and c of these 32 SwiGLU columns (interleaved layout)
                         const int col = ((f0 >> 7) << 8) + (f0 & 127);
-                        uint4 va[4], vc[4];
-                        if (rv) {
+                        if (rv && f0 < a.N) {
 #pragma unroll
                             for (int c4 = 0; c4 < 4; ++c4) {
                                 va[c4] = *(const uint4*)(acin + col + c4 * 8);
@@ -400,6 +409,24 @@ __global__ void __launch_bounds__(192, 1)
 #pragma unroll
                             for (int c4 = 0; c4 < 4; ++c4) va[c4] = vc[c4] = make_uint4(0, 0, 0, 0);
                         }
+                    };
+                    uint4 na[4], nc[4];
+                    const int c_beg = half * (BN / 64), c_end = c_beg + BN / 64;
+                    load_ac(c_beg, na, nc);
+#pragma unroll 1
+                    for (int cc = c_beg; cc < c_end; ++cc) {
+                        const int f0 = ti.n0 + cc * 32;
+                        if (f0 >= a.N) break;  // warp-uniform
+                        uint32_t r[32];
+                        tc::tmem_ld32(tmem_base + ((uint32_t)(q * 32) << 16) + acc * BN + cc * 32, r);
+                        const int col = ((f0 >> 7) << 8) + (f0 & 127);
+                        uint4 va[4], vc[4];
+#pragma unroll
+                        for (int c4 = 0; c4 < 4; ++c4) {
+                            va[c4] = na[c4];
+                            vc[c4] = nc[c4];
+                        }
+                        if (cc + 1 < c_end) load_ac(cc + 1, na, nc);
                         tc::tmem_ld_wait();
                         const uint32_t* ua = (const uint32_t*)va;
                         const uint32_t* uc = (const uint32_t*)vc;
@@ -421,7 +448,7 @@ __global__ void __launch_bounds__(192, 1)
                 continue;
             }
 #pragma unroll 1
-            for (int cc = 0; cc < BN / 32; ++cc) {
+            for (int cc = half * (BN / 64); cc < (half + 1) * (BN / 64); ++cc) {
                 int col0 = ti.n0 + cc * 32;
                 if (col0 >= a.N) break;  // warp-uniform
                 uint32_t r[32];
@@ -500,9 +527,9 @@ __global__ void __launch_bounds__(192, 1)
                     const bool zz = plain && z;  // r now holds the final values unless plain
                     // four 2 KB buffers per warp: a bf16 chunk is one 32 x 32 box,
                     // an fp32 chunk two 32 x 16 boxes (64-byte rows either way)
-                    const int b = (int)(nst & 3u);
-                    const uint32_t sb = tc::smem_u32(stage_c + q * 8192 + b * 2048);
-                    if (lane == 0) tc::bulk_wait_read<3>();  // this buffer's previous store has read it
+                    const int b = (int)(nst & 1u);
+                    const uint32_t sb = tc::smem_u32(stage_c + ew * 4096 + b * 2048);
+                    if (lane == 0) tc::bulk_wait_read<1>();  // this buffer's previous store has read it
                     __syncwarp();
                     if (a.c_bf16) {
 #pragma unroll
@@ -519,7 +546,7 @@ __global__ void __launch_bounds__(192, 1)
                         tc::fence_proxy_async();
                         __syncwarp();
                         if (lane == 0) {
-                            tc::tma_store_2d(&mapC, stage_c + q * 8192 + b * 2048, col0, (int)ybase);
+                            tc::tma_store_2d(&mapC, stage_c + ew * 4096 + b * 2048, col0, (int)ybase);
                             tc::bulk_commit();
                         }
                         ++nst;
@@ -527,10 +554,10 @@ __global__ void __launch_bounds__(192, 1)
                     }
 #pragma unroll
                     for (int hh = 0; hh < 2; ++hh) {
-                        const int bh = (int)(nst & 3u);
-                        const uint32_t sbh = tc::smem_u32(stage_c + q * 8192 + bh * 2048);
+                        const int bh = (int)(nst & 1u);
+                        const uint32_t sbh = tc::smem_u32(stage_c + ew * 4096 + bh * 2048);
                         if (hh == 1) {
-                            if (lane == 0) tc::bulk_wait_read<3>();
+                            if (lane == 0) tc::bulk_wait_read<1>();
                             __syncwarp();
                         }
 #pragma unroll
@@ -542,7 +569,7 @@ __global__ void __launch_bounds__(192, 1)
                         tc::fence_proxy_async();
                         __syncwarp();
                         if (lane == 0) {
-                            tc::tma_store_2d(&mapC, stage_c + q * 8192 + bh * 2048, col0 + hh * 16, (int)ybase);
+                            tc::tma_store_2d(&mapC, stage_c + ew * 4096 + bh * 2048, col0 + hh * 16, (int)ybase);
                             tc::bulk_commit();
                         }
                         ++nst;
@@ -782,7 +809,7 @@ static void launch_tc(Context* c, const CUtensorMap& ma, const CUtensorMap& mb, 
                                      (int)smem));
         attr_set[dev] = true;
     }
-    k_gemm_tc<A_MN, B_MN, BN, STAGES><<<grid, 192, smem, c->stream>>>(ma, mb, mc, md, a);
+    k_gemm_tc<A_MN, B_MN, BN, STAGES><<<grid, GEMM_THREADS, smem, c->stream>>>(ma, mb, mc, md, a);
     launched(c);
 }
 
@@ -1033,6 +1060,24 @@ void gemm_grouped_swiglu_bwd_tc(Context* c, i64 total_rows, i64 F, i64 K, int gr
     const int BN = F <= 128 ? 128 : 256;
     int bound = (cdiv(total_rows, BM) + groups) * cdiv(F, BN);
     run_tc(c, a, false, false, DY, total_rows, K, lddy, W2, (i64)groups * F, K, K, bound);
+}
+
+// linear / matmul / moe: A K-major, weights [in, out] (MN-major); lm_head:
+// table [vocab, hidden] (K-major). Persistent grid: one CTA per SM at most.
+KernelInfo gemm_tc_info(Context* c, const std::string& op, const KShape& s) {
+    KernelInfo k;
+    const bool lm = op == "lm_head";
+    if (!(lm || op == "linear" || op == "matmul" || op == "moe")) return k;
+    const bool big = s.width > 128;
+    if (big) k.fn = lm ? (const void*)k_gemm_tc<false, false, 256, 4> : (const void*)k_gemm_tc<false, true, 256, 4>;
+    else k.fn = lm ? (const void*)k_gemm_tc<false, false, 128, 6> : (const void*)k_gemm_tc<false, true, 128, 6>;
+    const int BN = big ? 256 : 128, ST = big ? 4 : 6;
+    k.file = "gemm_tc.cu";
+    const i64 tiles = (i64)cdiv(s.rows, BM) * cdiv(s.width, BN);
+    k.grid[0] = (unsigned)std::max<i64>(1, std::min<i64>(tiles, c->sm_count));
+    k.block[0] = GEMM_THREADS;
+    k.dyn_smem = (size_t)ST * (BM * BK * 2 + BN * BK * 2) + EPI_STAGE_BYTES + 1024 + 256;
+    return k;
 }
 
 }  // namespace catnn

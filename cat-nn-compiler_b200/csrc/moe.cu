@@ -637,4 +637,23 @@ void swiglu_act_bwd(Context* c, const void* a, const void* cc, const void* dh, v
     launched(c);
 }
 
+// The router's top-k (128 tokens per CTA) and the SwiGLU activation
+// (grid-stride, 256 threads).
+KernelInfo moe_info(Context* c, const std::string& op, int dtype, const KShape& s) {
+    KernelInfo k;
+    const bool b = dtype == CATNN_BF16;
+    if (op == "router") {
+        k.fn = (const void*)k_router_topk;
+        k.file = "moe.cu";
+        k.grid[0] = (unsigned)cdiv(s.rows, 128);
+        k.block[0] = 128;
+    } else if (op == "swiglu") {
+        k.fn = b ? (const void*)k_swiglu<bf16, bf16, 8> : (const void*)k_swiglu<float, float, 4>;
+        k.file = "moe.cu";
+        k.grid[0] = (unsigned)row_grid(c, std::max<i64>(1, s.rows), s.width, b ? 8 : 4);
+        k.block[0] = 256;
+    }
+    return k;
+}
+
 }  // namespace catnn

@@ -791,6 +791,24 @@ void xent_noalloc_forget(int device) {
     g_xent_row_loss_ptr[device] = nullptr;
 }
 
+// rms_norm, layer_norm, softmax and the cross-entropy loss: one CTA per row.
+KernelInfo norms_info(Context* c, const std::string& op, int dtype, const KShape& s) {
+    KernelInfo k;
+    const bool b = dtype == CATNN_BF16;
+    if (op == "rms_norm") k.fn = b ? (const void*)k_rms_fwd<bf16> : (const void*)k_rms_fwd<float>;
+    else if (op == "layer_norm") k.fn = b ? (const void*)k_ln_fwd<bf16> : (const void*)k_ln_fwd<float>;
+    else if (op == "softmax") k.fn = b ? (const void*)k_softmax<bf16> : (const void*)k_softmax<float>;
+    else if (op == "cross_entropy") {
+        const int v = b ? 8 : 4;
+        if (s.width % v == 0) k.fn = b ? (const void*)k_xent_rows<bf16, 8> : (const void*)k_xent_rows<float, 4>;
+        else k.fn = b ? (const void*)k_xent_rows<bf16, 1> : (const void*)k_xent_rows<float, 1>;
+    } else return k;
+    k.file = "norms.cu";
+    k.grid[0] = (unsigned)std::max<i64>(1, s.rows);
+    k.block[0] = row_threads(s.width);
+    return k;
+}
+
 }  // namespace catnn
 
 extern "C" int catnn_xent_fwdbwd_noalloc(catnn_ctx* h, const void* logits, const uint32_t* targets, int64_t rows,

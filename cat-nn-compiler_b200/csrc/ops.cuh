@@ -25,6 +25,31 @@ namespace catnn {
 
 Context* unwrap(catnn_ctx* h);
 
+// One kernel of this library as catnn_kernel_describe reports it: the host
+// stub of the __global__ function, the translation unit it is compiled in
+// (whose cubin size is the code size), and the launch geometry its launcher
+// uses for a problem of the given shape. fn is null when a file has no
+// kernel for the op.
+struct KShape {
+    i64 rows, width, inner;    // GEMM: M, N, K; row kernels: rows x width
+    i64 batch, seq, heads, head_dim;
+};
+struct KernelInfo {
+    const void* fn = nullptr;
+    const char* file = "";
+    unsigned grid[3] = {1, 1, 1};
+    unsigned block[3] = {1, 1, 1};
+    size_t dyn_smem = 0;
+};
+// per-file lookups of the kernel that carries an IR op (resource.cu)
+KernelInfo gemm_tc_info(Context* c, const std::string& op, const KShape& s);
+KernelInfo sgemm_info(Context* c, const std::string& op, const KShape& s);
+KernelInfo fa5_info(Context* c, const std::string& op, const KShape& s);
+KernelInfo attention_info(Context* c, const std::string& op, int dtype, const KShape& s);
+KernelInfo norms_info(Context* c, const std::string& op, int dtype, const KShape& s);
+KernelInfo elementwise_info(Context* c, const std::string& op, int dtype, const KShape& s);
+KernelInfo moe_info(Context* c, const std::string& op, int dtype, const KShape& s);
+
 // Reads and clears device status slot `slot` of the context; synchronizes
 // the stream. Returns the value that was there.
 int take_status(Context* c, int slot);

@@ -397,6 +397,41 @@ int catnn_comm_check(catnn_comm* comm);
 int catnn_moe_trainer_create_ep(catnn_ctx* ctx, const catnn_moe_config* cfg, catnn_comm* comm,
                                 catnn_moe_trainer** out);
 
+/* ------------------------------------------------------------ kernel resources */
+/* The measured KernelResource of an IR op on this backend — what
+ * resource::describe (crates/catnn-compile/src/kernel/resource.rs:159-193)
+ * returns for the CudaSm121 backend as estimates, here for the sm_100a
+ * kernel the op's launcher actually runs: registers per thread, static and
+ * local memory and the kernel-argument bytes from the CUDA runtime; the
+ * launch geometry and dynamic shared memory the launcher uses for `shape`;
+ * the code size as the cubin of the kernel's source file, measured at build
+ * time (code_estimated = 0). op: linear, matmul, lm_head, moe, attention,
+ * gqa_attention, embedding, rms_norm, layer_norm, softmax, cross_entropy,
+ * relu, gelu, add, residual_add, mul, router, swiglu, sgd, adam; other ops
+ * are CATNN_ERR_UNSUPPORTED. shape: GEMMs M = rows, N = width, K = inner;
+ * row kernels rows x width; attention batch, seq, heads, head_dim. */
+typedef struct catnn_kernel_shape {
+    int64_t rows, width, inner;
+    int64_t batch, seq, heads, head_dim;
+} catnn_kernel_shape;
+typedef struct catnn_kernel_resource {
+    char kernel[192];  /* the __global__ function (mangled name) */
+    char file[32];     /* the source file it is compiled from */
+    int32_t registers_per_thread;
+    int32_t max_threads_per_block;
+    int64_t static_smem_bytes;
+    int64_t dynamic_smem_bytes;
+    int64_t local_bytes_per_thread;
+    uint32_t grid[3];
+    uint32_t block[3];
+    int64_t launch_arg_bytes;
+    int64_t code_bytes;
+    int32_t code_estimated;
+    int32_t binary_version;
+} catnn_kernel_resource;
+int catnn_kernel_describe(catnn_ctx* ctx, const char* op, int dtype, const catnn_kernel_shape* shape,
+                          catnn_kernel_resource* out);
+
 #ifdef __cplusplus
 }
 #endif

@@ -60,15 +60,20 @@ def close_bf16(got, ref, what="", atol=ATOL_BF16):
 
 
 U_BF16 = 2.0 ** -8  # unit roundoff of bf16 (8 significant bits, round to nearest)
+U2_3 = U_BF16 ** 2 / 3  # variance of one bf16 rounding's relative error (uniform on [-u, u])
+LAMBDA = 6.0  # standard deviations of a probabilistic rounding-error bound
 
 
 def close_bf16_derived(got, ref, rounding_bound, what=""):
     """The bf16 band plus a derived bound: |got - ref| <= 2e-2·|ref| +
     1e-3·max(1, max|ref|) + rounding_bound, where rounding_bound is the
-    first-order effect, per element, of the bf16 roundings of intermediates
-    that the tensor-core path stores and the fp32 reference keeps in fp32
-    (each test derives it from the exact intermediates and states which
-    roundings it covers)."""
+    effect, per element, of the bf16 roundings of intermediates that the
+    tensor-core path stores and the fp32 reference keeps in fp32 (each test
+    derives it from the exact intermediates and states which roundings it
+    covers): LAMBDA standard deviations of the propagated first-order error,
+    each rounding an independent relative error of variance u²/3 (the
+    probabilistic rounding-error model; the worst-case sum of |terms| over a
+    few hundred products is an order of magnitude looser)."""
     got = host(got) if torch.is_tensor(got) else np.asarray(got, np.float32)
     ref = np.asarray(ref, np.float64).reshape(got.shape)
     rb = np.asarray(rounding_bound, np.float64).reshape(got.shape)

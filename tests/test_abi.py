@@ -99,3 +99,27 @@ def test_packed_layout_matches_oracle_and_abi(libpath):
     # config 5: about 435 M parameters (n_kv = 16)
     big = O.MixCfg(32000, 1024, 3584, 4, 16, 16, 8, 2).layout()["total"]
     assert 4.3e8 < big < 4.4e8
+
+
+def test_build_records_kernel_resources():
+    """The build's record behind catnn_kernel_describe: every source file has a
+    measured cubin size, every kernel its -Xptxas -v registers, and the
+    tensor-core GEMM and attention kernels spill nothing."""
+    import json
+    import os
+    import catnn_b200.build as b
+    b.build()
+    info = json.load(open(b.INFO))
+    srcs = {os.path.basename(s) for s in b.sources()} - {b.LAST}
+    assert srcs <= set(info["cubin_bytes"]), srcs - set(info["cubin_bytes"])
+    assert all(n > 0 for n in info["cubin_bytes"].values())
+    ks = info["kernels"]
+    assert len(ks) > 50
+    gemm = [k for k in ks if "k_gemm_tc" in k]
+    fa5 = [k for k in ks if "fa5" in k]
+    assert gemm and fa5
+    for name in gemm + fa5:
+        assert ks[name]["registers"] > 0 and ks[name]["spill_stores"] == 0, (name, ks[name])
+    inc = open(os.path.join(b.BUILD, "code_sizes.inc")).read()
+    for f, n in info["cubin_bytes"].items():
+        assert f'"{f}", {n}' in inc

@@ -7,7 +7,7 @@ import numpy as np
 import pytest
 import torch
 
-from gpu_util import U_BF16, bf16_round, close_bf16, close_bf16_derived, close_f32, dev, host, rng
+from gpu_util import LAMBDA, U2_3, bf16_round, close_bf16, close_bf16_derived, close_f32, dev, host, rng
 from oracle import oracle as O
 
 pytestmark = pytest.mark.gpu
@@ -477,11 +477,13 @@ def test_moe_bf16_grouped_tensor_core():
     dy = bf16_round(r.standard_normal((T, H)).astype(np.float32))
     args = [dev(a, torch.bfloat16) for a in (x, gate, w1s, w3s, w2s)]
     # The bf16 path stores h = silu(a)·c and the output y in bf16 (a, c and the
-    # expert outputs stay fp32); first-order bound of those two roundings from
-    # the exact values: δyp = Σ_p u·|h_p|·|w2[p, :]|, δy = Σ_k w_k·δyp_k + u·|y|.
+    # expert outputs stay fp32). Probabilistic bound of those roundings (each an
+    # independent relative error of variance u²/3, propagated through the
+    # linear maps, LAMBDA standard deviations): var(yp) = u²/3·Σ_p h_p²·w2[p,:]²,
+    # var(y) = Σ_k w_k²·var(yp_k) + u²/3·y².
     idx, wts, _ = O.route(x, gate, k)
     X64 = x.astype(np.float64)
-    dyp = np.zeros((T, k, H))
+    var_yp = np.zeros((T, k, H))
     y64 = np.zeros((T, H))
     for j in range(k):
         for e in range(E):
@@ -489,29 +491,85 @@ def test_moe_bf16_grouped_tensor_core():
             a = X64[rows] @ w1s[e].astype(np.float64)
             c = X64[rows] @ w3s[e].astype(np.float64)
             hh = a / (1.0 + np.exp(-a)) * c
-            dyp[rows, j] = U_BF16 * np.abs(hh) @ np.abs(w2s[e].astype(np.float64))
+            var_yp[rows, j] = U2_3 * hh ** 2 @ w2s[e].astype(np.float64) ** 2
             y64[rows] += wts[rows, j, None] * (hh @ w2s[e].astype(np.float64))
-    bound = (np.abs(wts)[:, :, None] * dyp).sum(1) + U_BF16 * np.abs(y64)
+    bound = LAMBDA * np.sqrt((wts[:, :, None] ** 2 * var_yp).sum(1) + U2_3 * y64 ** 2)
     close_bf16_derived(ops.moe(*args, k), O.moe(x, gate, w1s, w3s, w2s, k), bound, what="moe bf16")
     got = ops.moe_backward(*args, dev(dy, torch.bfloat16), k)
     ref = O.moe_backward(x, gate, w1s, w3s, w2s, dy, k)
-    for name, g, rr in zip(("dx", "dgate", "dw1", "dw3", "dw2"), got, ref):
-        close_bf16(g, rr, what=f"moe bf16 {name}")
+    bounds = moe_backward_rounding_bounds(x, gate, w1s, w3s, w2s, dy, idx, wts)
+    for name, g, rr, bnd in zip(("dx", "dgate", "dw1", "dw3", "dw2"), got, ref, bounds):
+        close_bf16_derived(g, rr, bnd, what=f"moe bf16 {name}")
 
 
-@pytest.mark.parametrize("b,s,h,kv,hd,causal,window", [(2, 200, 4, 4, 64, True, None), (1, 130, 4, 2, 64, True, 48),
-                                                        (2, 96, 2, 2, 128, True, None), (1, 64, 2, 2, 64, False, None),
-                                                        (1, 257, 2, 1, 128, True, 100), (1, 1024, 2, 1, 64, True, None),
-                                                        (2, 384, 2, 2, 64, False, None), (1, 600, 4, 2, 64, True, 200)])
+def moe_backward_rounding_bounds(x, gate, w1s, w3s, w2s, dy, idx, wts):
+    """Probabilistic bounds (LAMBDA standard deviations) of the bf16 roundings
+    in the MoE adjoint's bf16 path (catnn_moe_bwd), from the exact values:
+    dyp = w·dy stored bf16; dh = dyp·w2ᵀ (fp32) then da, dc stored bf16;
+    dxp = da·w1ᵀ stored bf16, then + dc·w3ᵀ stored bf16 again; the token sum
+    dx stored bf16; the router's dlogits rounded to bf16 before dlog·gateᵀ
+    (added into dx, rounded again) and xᵀ·dlog; h stored bf16 for the w2
+    gradient; every output stored bf16. Each rounding is an independent
+    relative error of variance u²/3; errors that reach an output through two
+    paths (dh into both da and dc) are combined before squaring."""
+    T, H = x.shape
+    E, _, F = w1s.shape
+    k = idx.shape[1]
+    X = x.astype(np.float64)
+    DY = dy.astype(np.float64)
+    v_dx = np.zeros((T, H))
+    dx_sum = np.zeros((T, H))
+    v_dw1, v_dw3, v_dw2 = np.zeros((E, H, F)), np.zeros((E, H, F)), np.zeros((E, F, H))
+    dw1, dw3, dw2 = np.zeros((E, H, F)), np.zeros((E, H, F)), np.zeros((E, F, H))
+    dwt = np.zeros((T, k))
+    for j in range(k):
+        for e in range(E):
+            rows = np.nonzero(idx[:, j] == e)[0]
+            W1, W3, W2 = (w.astype(np.float64) for w in (w1s[e], w3s[e], w2s[e]))
+            xe, wt = X[rows], wts[rows, j, None]
+            a, c = xe @ W1, xe @ W3
+            sig = 1.0 / (1.0 + np.exp(-a))
+            ga, gc = c * (sig + a * sig * (1 - sig)), a * sig  # da = dh·ga, dc = dh·gc
+            hh = a * sig * c
+            dwt[rows, j] = ((hh @ W2) * DY[rows]).sum(1)
+            dyp = wt * DY[rows]
+            dh = dyp @ W2.T
+            v_dh = U2_3 * dyp ** 2 @ (W2 ** 2).T
+            da, dc = dh * ga, dh * gc
+            dxp1 = da @ W1.T
+            dxp = dxp1 + dc @ W3.T
+            # dh's error reaches dxp through both da and dc: combined coefficients
+            v_dx[rows] += (v_dh[:, None, :] * (ga[:, None, :] * W1[None] + gc[:, None, :] * W3[None]) ** 2).sum(2)
+            v_dx[rows] += U2_3 * ((da ** 2) @ (W1 ** 2).T + (dc ** 2) @ (W3 ** 2).T + dxp1 ** 2 + dxp ** 2)
+            dx_sum[rows] += dxp
+            dw1[e] += xe.T @ da
+            dw3[e] += xe.T @ dc
+            dw2[e] += hh.T @ dyp
+            v_dw1[e] += (xe ** 2).T @ (ga ** 2 * v_dh + U2_3 * da ** 2)
+            v_dw3[e] += (xe ** 2).T @ (gc ** 2 * v_dh + U2_3 * dc ** 2)
+            v_dw2[e] += 2 * U2_3 * (hh ** 2).T @ (dyp ** 2)
+    dlog = np.zeros((T, E))
+    dot = (wts * dwt).sum(1, keepdims=True)
+    np.put_along_axis(dlog, idx, wts * (dwt - dot), axis=1)
+    G = gate.astype(np.float64)
+    dx = dx_sum + dlog @ G.T
+    v_dx += U2_3 * (dx_sum ** 2 + (dlog ** 2) @ (G ** 2).T + dx ** 2)
+    dgate = X.T @ dlog
+    v_dgate = (X ** 2).T @ (U2_3 * dlog ** 2) + U2_3 * dgate ** 2
+    out = (v_dx, v_dgate, v_dw1 + U2_3 * dw1 ** 2, v_dw3 + U2_3 * dw3 ** 2, v_dw2 + U2_3 * dw2 ** 2)
+    return tuple(LAMBDA * np.sqrt(v) for v in out)
+
+
 def attention_rounding_bounds(q, k, v, do, causal, window):
-    """First-order bounds, per element, of the bf16 roundings the tensor-core
-    flash attention makes and the fp32 attention core does not: P rounded for
-    P·V (forward) and Pᵀ·dO (dV), the output O rounded (it feeds
-    D = rowsum(dO∘O)), dS = P∘(dP - D) rounded for dS·K (dQ) and dSᵀ·Q (dK),
-    and the outputs rounded; from the exact (f64) attention of the same
-    inputs. Returns (bound_o, bound_dq, bound_dk, bound_dv) in the inputs'
-    layouts."""
-    u = U_BF16
+    """Probabilistic bounds (LAMBDA standard deviations), per element, of the
+    bf16 roundings the tensor-core flash attention makes and the fp32
+    attention core does not: P rounded for P·V (forward) and Pᵀ·dO (dV), the
+    output O rounded (it feeds D = rowsum(dO∘O), whose error enters every dS
+    of the row, so that term is propagated as one correlated error per row),
+    dS = P∘(dP - D) rounded for dS·K (dQ) and dSᵀ·Q (dK), and the outputs
+    rounded; from the exact (f64) attention of the same inputs. Each
+    rounding is an independent relative error of variance u²/3. Returns
+    (bound_o, bound_dq, bound_dk, bound_dv) in the inputs' layouts."""
     b, s, h, hd = q.shape
     kv = k.shape[2]
     rep = h // kv
@@ -536,19 +594,24 @@ def attention_rounding_bounds(q, k, v, do, causal, window):
     dq = np.einsum("bhij,bjhd->bihd", dS, Kr) * scale
     dk = np.einsum("bhij,bihd->bjhd", dS, Q) * scale
     dv = np.einsum("bhij,bihd->bjhd", P, dO)
-    dO_abs = np.abs(dO)
-    bO = u * np.einsum("bhij,bjhd->bihd", P, np.abs(Vr)) + u * np.abs(Ov)
-    dD = np.einsum("bihd,bihd->bhi", dO_abs, bO)
-    bdS = P * dD[..., None] + u * np.abs(dS)
-    bdq = scale * np.einsum("bhij,bjhd->bihd", bdS, np.abs(Kr)) + u * np.abs(dq)
-    bdk = scale * np.einsum("bhij,bihd->bjhd", bdS, np.abs(Q)) + u * np.abs(dk)
-    bdv = u * np.einsum("bhij,bihd->bjhd", P, dO_abs) + u * np.abs(dv)
-    # kv heads shared by `rep` query heads sum their bounds
-    bdk = bdk.reshape(b, s, kv, rep, hd).sum(3)
-    bdv = bdv.reshape(b, s, kv, rep, hd).sum(3)
-    return bO.reshape(b, s, h * hd), bdq, bdk, bdv
+    v_O = U2_3 * (np.einsum("bhij,bjhd->bihd", P ** 2, Vr ** 2) + Ov ** 2)
+    v_D = np.einsum("bihd,bihd->bhi", dO ** 2, v_O)
+    PK = np.einsum("bhij,bjhd->bihd", P, Kr)  # Σ_j P_ij K_j: how D's error reaches dq
+    v_dq = scale ** 2 * (U2_3 * np.einsum("bhij,bjhd->bihd", dS ** 2, Kr ** 2)
+                         + PK ** 2 * v_D.transpose(0, 2, 1)[..., None]) + U2_3 * dq ** 2
+    v_dk = scale ** 2 * (U2_3 * np.einsum("bhij,bihd->bjhd", dS ** 2, Q ** 2)
+                         + np.einsum("bhij,bihd,bhi->bjhd", P ** 2, Q ** 2, v_D))
+    v_dv = U2_3 * np.einsum("bhij,bihd->bjhd", P ** 2, dO ** 2)
+    # kv heads shared by `rep` query heads sum their variances; outputs rounded
+    v_dk = v_dk.reshape(b, s, kv, rep, hd).sum(3) + U2_3 * dk.reshape(b, s, kv, rep, hd).sum(3) ** 2
+    v_dv = v_dv.reshape(b, s, kv, rep, hd).sum(3) + U2_3 * dv.reshape(b, s, kv, rep, hd).sum(3) ** 2
+    return tuple(LAMBDA * np.sqrt(v) for v in (v_O.reshape(b, s, h * hd), v_dq, v_dk, v_dv))
 
 
+@pytest.mark.parametrize("b,s,h,kv,hd,causal,window", [(2, 200, 4, 4, 64, True, None), (1, 130, 4, 2, 64, True, 48),
+                                                        (2, 96, 2, 2, 128, True, None), (1, 64, 2, 2, 64, False, None),
+                                                        (1, 257, 2, 1, 128, True, 100), (1, 1024, 2, 1, 64, True, None),
+                                                        (2, 384, 2, 2, 64, False, None), (1, 600, 4, 2, 64, True, 200)])
 def test_attention_core_bf16_tensor_core(b, s, h, kv, hd, causal, window):
     """Flash attention on the tensor cores (tcgen05 + TMEM for head_dim 64,
     mma.sync for 128; forward and backward) vs the fp32 attention
