@@ -49,6 +49,7 @@ def parse():
                         "with the SwiGLU epilogues; attn: tcgen05 flash attention fwd + bwd (B8 S2048 H16 hd64); "
                         "step_small: trainer steps at config-5 widths on 2 sequences (its HBM-bound kernels)")
     p.add_argument("--reps", type=int, default=20)
+    p.add_argument("--batch", type=int, default=2, help="--kernel step_small: sequences per step (1 layer)")
     return p.parse_args()
 
 
@@ -519,13 +520,15 @@ def run_kernel_only(args):
         timed(lambda: ops.attention_core_backward(q, k, v, o, lse, do, True), 2.5 * fwd, "fa5 backward (causal)")
     elif args.kernel == "step_small":
         from catnn_b200.train import MoeConfig, MoeTrainer, init_params
-        mc = MoeConfig.make(CFG["vocab"], d, F, 1, CFG["heads"], CFG["kv_heads"], E, CFG["top_k"], batch=2, seq=CFG["seq"],
-                            rope_theta=CFG["rope_theta"], dtype=torch.bfloat16, optimizer="adam", lr=CFG["lr"])
+        mc = MoeConfig.make(CFG["vocab"], d, F, 1, CFG["heads"], CFG["kv_heads"], E, CFG["top_k"], batch=args.batch,
+                            seq=CFG["seq"], rope_theta=CFG["rope_theta"], dtype=torch.bfloat16, optimizer="adam",
+                            lr=CFG["lr"])
         tr = MoeTrainer(mc)
         tr.set_params(init_params(mc, CFG["seed"]))
-        tok = torch.randint(0, CFG["vocab"], (2 * CFG["seq"],), device=dev, dtype=torch.int32)
+        tok = torch.randint(0, CFG["vocab"], (args.batch * CFG["seq"],), device=dev, dtype=torch.int32)
         loss = torch.zeros(1, device=dev)
-        timed(lambda: tr.step(tok, update=True, loss_out=loss), 0.0, "trainer step, 1 layer, 4096 tokens")
+        timed(lambda: tr.step(tok, update=True, loss_out=loss), 0.0,
+              f"trainer step, 1 layer, {args.batch * CFG['seq']} tokens")
         tr.close()
 
 
