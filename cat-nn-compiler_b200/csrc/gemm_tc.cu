@@ -212,7 +212,7 @@ __device__ __forceinline__ float act_apply(float v, int act) {
 }
 
 template <bool A_MN, bool B_MN, int BN, int STAGES>
-__global__ void __launch_bounds__(GEMM_THREADS, 1)
+__global__ void __maxnreg__(200)  // 320 threads x 200 registers fit the 64 K register file
     k_gemm_tc(const __grid_constant__ CUtensorMap mapA, const __grid_constant__ CUtensorMap mapB,
               const __grid_constant__ CUtensorMap mapC, const __grid_constant__ CUtensorMap mapD, TcArgs a) {
     constexpr uint32_t A_BYTES = BM * BK * 2;
@@ -259,8 +259,8 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         // ---------------- TMA producer
         int s = 0;
         uint32_t ph = 0;
-        int last_ph[STAGES];
-        for (int i = 0; i < STAGES; ++i) last_ph[i] = -1;
+        // per stage: was it ever filled (bit in used), and the parity of its last fill
+        uint32_t used = 0, last_par = 0;
         bool ok = true;
         for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
             TileInfo ti = tile_at<BN>(a, t);
@@ -288,7 +288,8 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
 #pragma unroll
                     for (int j = 0; j < BN / 64; ++j) tc::tma_load_2d(sB + j * 8192, &mapB, ti.n0 + 64 * j, brow, &full[s]);
                 }
-                last_ph[s] = (int)ph;
+                used |= 1u << s;
+                last_par = (last_par & ~(1u << s)) | (ph << s);
                 if (++s == STAGES) {
                     s = 0;
                     ph ^= 1;
@@ -298,7 +299,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         if (!ok) {
             // Abort: let the copies already in flight land before the CTA exits.
             for (int i = 0; i < STAGES; ++i)
-                if (last_ph[i] >= 0) tc::mbar_wait(&full[i], (uint32_t)last_ph[i], a.status, 1, 400000000ll, false);
+                if ((used >> i) & 1u) tc::mbar_wait(&full[i], (last_par >> i) & 1u, a.status, 1, 400000000ll, false);
         }
     } else if (warp == 1 && lane == 0) {
         // ---------------- MMA issuer
