@@ -44,10 +44,11 @@ def parse():
     p.add_argument("--kernel-only", action="store_true",
                    help="run only one kernel at its config-5 shape for profiling (--kernel)")
     p.add_argument("--kernel", default="w13",
-                   choices=["w13", "swiglu_fwd", "swiglu_bwd", "attn", "step_small"],
+                   choices=["w13", "swiglu_fwd", "swiglu_bwd", "attn", "step_small", "gemm_tf32"],
                    help="w13: grouped expert GEMM (W13 forward shape); swiglu_fwd / swiglu_bwd: the expert GEMMs "
                         "with the SwiGLU epilogues; attn: tcgen05 flash attention fwd + bwd (B8 S2048 H16 hd64); "
-                        "step_small: trainer steps at config-5 widths on 2 sequences (its HBM-bound kernels)")
+                        "step_small: trainer steps at config-5 widths on 2 sequences (its HBM-bound kernels); "
+                        "gemm_tf32: the TF32 tensor-core GEMM at 4096^3")
     p.add_argument("--reps", type=int, default=20)
     p.add_argument("--batch", type=int, default=2, help="--kernel step_small: sequences per step (1 layer)")
     return p.parse_args()
@@ -278,12 +279,20 @@ def gemm_sweep(local, peak):
             ops.gemm(A, B, out=C)
             ops.gemm(dC, B, trans_b=True, out=dA)
             ops.gemm(A, dC, trans_a=True, out=dB)
+        A32, B32 = A.float(), B.float()
+        C32 = torch.empty(K, K, device=f"cuda:{local}")
+
+        def fwd_tf32():
+            ops.gemm(A32, B32, out=C32, tf32=True)
         res = {}
-        for name, f, flops in (("fwd", fwd, 2 * K ** 3), ("fwd_bwd", fwdbwd, 6 * K ** 3)):
+        # kind::tf32 runs at half the kind::f16 rate: its roofline is half the measured bf16 peak
+        for name, f, flops, pk in (("fwd", fwd, 2 * K ** 3, peak), ("fwd_bwd", fwdbwd, 6 * K ** 3, peak),
+                                   ("fwd_tf32", fwd_tf32, 2 * K ** 3, peak / 2)):
             ms, _ = graph_time_ms(f, local, reps)
             tf = flops / (ms * 1e-3) / 1e12
-            res[name] = {"ms": round(ms, 4), "tflops": round(tf, 1), "frac": round(tf / peak, 3)}
+            res[name] = {"ms": round(ms, 4), "tflops": round(tf, 1), "frac": round(tf / pk, 3)}
         out[str(K)] = res
+        del A32, B32, C32
     return out
 
 
@@ -518,6 +527,12 @@ def run_kernel_only(args):
         fwd = 2.0 * B * H * S * S * hd  # causal half of 4·B·H·S²·hd
         timed(lambda: ops.attention_core(q, k, v, True), fwd, "fa5 forward (causal)")
         timed(lambda: ops.attention_core_backward(q, k, v, o, lse, do, True), 2.5 * fwd, "fa5 backward (causal)")
+    elif args.kernel == "gemm_tf32":
+        K = 4096
+        A = torch.randn(K, K, device=dev) / K ** 0.5
+        B = torch.randn(K, K, device=dev)
+        C = torch.empty(K, K, device=dev)
+        timed(lambda: ops.gemm(A, B, trans_b=True, out=C, tf32=True), 2.0 * K ** 3, "k_gemm_tc tf32 (K-major A, B)", K=K)
     elif args.kernel == "step_small":
         from catnn_b200.train import MoeConfig, MoeTrainer, init_params
         mc = MoeConfig.make(CFG["vocab"], d, F, 1, CFG["heads"], CFG["kv_heads"], E, CFG["top_k"], batch=args.batch,
@@ -635,6 +650,34 @@ def run_ours(args):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     e2e_ms = float(t)
 
+    # where a rank's step goes: device-clock stamps at the step's phase
+    # boundaries (one extra profiled step, replayed as a graph like the timed
+    # ones), per phase the max over ranks
+    tr.set_profile(True)
+    for _ in range(3):
+        tr.step(tokens, update=True, loss_out=loss)
+    phases = tr.timeline()
+    tr.set_profile(False)
+    barrier()
+    if world > 1:
+        every = [None] * world
+        dist.all_gather_object(every, phases)
+    else:
+        every = [phases]
+    agg = {}
+    for name, ms_ in every[0]:
+        agg.setdefault(name, 0.0)
+    for rk in every:
+        seen = {}
+        for name, ms_ in rk:
+            seen[name] = seen.get(name, 0.0) + ms_
+        for name, v in seen.items():
+            agg[name] = max(agg.get(name, 0.0), v)
+    phase_breakdown = {"ms_max_over_ranks": {k: round(v, 4) for k, v in agg.items()},
+                       "step_ms_per_rank": [round(sum(v for _, v in rk), 4) for rk in every],
+                       "how": "device clock (%globaltimer) stamped on the step's stream at phase boundaries; the time of "
+                              "a phase includes the waits (barriers, peer flags) inside it; summed over layers"}
+
     # dominant kernel: the grouped expert GEMM (W13 forward shape), timed live
     pk, pk_kind = peaks()
     kms, kflops, rows, F, d = dominant_kernel(local, T_global * cfg["top_k"] // world, cfg["experts"] // world, 3,
@@ -668,6 +711,7 @@ def run_ours(args):
         "tflops_per_step": step_flops(cfg, T_global) / 1e12,
         "model_tflops_achieved": step_flops(cfg, T_global) / (ms * 1e-3) / 1e12,
         "loss_step0": loss_step0,
+        "phases": phase_breakdown,
         "loss_last": last_loss,
         "roofline": {"bound": "tensor", "kernel": "k_gemm_tc grouped (expert W13 forward, rows=%d, N=%d, K=%d)"
                      % (rows, 2 * F, d), "achieved": achieved, "peak": peak, "unit": "TFLOP/s",

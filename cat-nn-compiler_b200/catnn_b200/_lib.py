@@ -83,6 +83,8 @@ SIGNATURES = {
     "catnn_moe_trainer_check": [VP],
     "catnn_moe_trainer_activation": [VP, I32, I64, VP],
     "catnn_moe_trainer_set_graphs": [VP, I32],
+    "catnn_moe_trainer_set_profile": [VP, I32],
+    "catnn_moe_trainer_timeline": [VP, C.POINTER(I64), I32, C.c_char_p, I64, C.POINTER(I32)],
     "catnn_moe_trainer_create_ep": [VP, VP, VP, PP],
     "catnn_comm_unique_id": [VP],
     "catnn_comm_create": [VP, I32, I32, VP, PP],

@@ -14,7 +14,7 @@ import torch
 from . import _lib
 from .errors import DTypeMismatch, InvalidArgument, ShapeMismatch
 
-F32, BF16 = 0, 1
+F32, BF16, TF32 = 0, 1, 2
 ACT = {"none": 0, None: 0, "relu": 1, "gelu": 2}
 
 
@@ -89,9 +89,13 @@ def _f32(t, what):
 
 
 # ------------------------------------------------------------------ dense
-def gemm(a, b, trans_a=False, trans_b=False, out=None, out_dtype=None, bias=None, act="none", accumulate=False):
-    """C = act(op(a)·op(b) + bias) (+C)."""
+def gemm(a, b, trans_a=False, trans_b=False, out=None, out_dtype=None, bias=None, act="none", accumulate=False,
+         tf32=False):
+    """C = act(op(a)·op(b) + bias) (+C). tf32=True multiplies fp32 a, b on
+    the tensor cores as TF32 (fp32 accumulation) instead of the fp32 path."""
     _same(a, b)
+    if tf32 and a.dtype != torch.float32:
+        raise DTypeMismatch("tf32 gemm takes fp32 operands")
     M, K = (a.shape[1], a.shape[0]) if trans_a else (a.shape[0], a.shape[1])
     Kb, N = (b.shape[1], b.shape[0]) if trans_b else (b.shape[0], b.shape[1])
     if K != Kb:
@@ -100,7 +104,7 @@ def gemm(a, b, trans_a=False, trans_b=False, out=None, out_dtype=None, bias=None
         out = torch.empty(M, N, dtype=out_dtype or a.dtype, device=a.device)
     _f32(bias, "bias")
     _lib.call("catnn_gemm", _h(a), int(trans_a), int(trans_b), M, N, K, _p(a), a.shape[1], _p(b), b.shape[1], _p(out),
-              N, _dt(a), _dt(out), _p(bias), ACT[act], int(accumulate))
+              N, TF32 if tf32 else _dt(a), _dt(out), _p(bias), ACT[act], int(accumulate))
     return out
 
 

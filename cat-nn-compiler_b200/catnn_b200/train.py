@@ -70,7 +70,8 @@ class MoeTrainer:
     the data-parallel + expert-parallel trainer (catnn_moe_trainer_create_ep):
     ``cfg.batch`` is then the global batch, steps take the global token
     array, and ``params()`` / ``grads()`` fill the replicated entries and this
-    rank's experts of the packed vector (other experts' entries are zero)."""
+    rank's experts of the packed vector (other experts' entries are zero);
+    with a communicator they are collective (every rank calls them)."""
 
     def __init__(self, cfg, device=0, comm=None):
         self.cfg = cfg
@@ -158,6 +159,23 @@ class MoeTrainer:
         """Replay the step body as a CUDA graph (catnn_moe_trainer_set_graphs)."""
         self._bind()
         _lib.call("catnn_moe_trainer_set_graphs", self.handle, int(bool(enable)))
+
+    def set_profile(self, enable=True):
+        """Record device-clock stamps at the step's phase boundaries
+        (catnn_moe_trainer_set_profile)."""
+        self._bind()
+        _lib.call("catnn_moe_trainer_set_profile", self.handle, int(bool(enable)))
+
+    def timeline(self):
+        """Phases of the last profiled step: [(name, milliseconds since the
+        previous stamp)], from the device clock."""
+        ns = (C.c_int64 * 64)()
+        names = C.create_string_buffer(4096)
+        count = C.c_int()
+        self._bind()
+        _lib.call("catnn_moe_trainer_timeline", self.handle, ns, 64, names, 4096, C.byref(count))
+        labels = names.value.decode().split("\n")[:count.value]
+        return [(labels[i], (ns[i] - ns[i - 1]) / 1e6) for i in range(1, count.value)]
 
     def check(self):
         self._bind()

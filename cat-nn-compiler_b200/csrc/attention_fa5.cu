@@ -336,16 +336,17 @@ __global__ void __launch_bounds__(NT, 2)
 // changes. P and dS are written by the compute threads in the A-operand
 // layout (128-byte rows, 16-byte chunks XOR-swizzled by row).
 
-constexpr int BB = 64;                           // the looped block (queries in k_dkdv, keys in k_dq)
-// 8 compute warps: two per TMEM lane quadrant, each takes 32 of the 64
-// columns of its rows (the backward has no row reductions to combine)
-constexpr int NTB = 320, NCW = 8;
-constexpr uint32_t T64 = 64 * HD * 2;            // 8 KB: a 64-row tile
-constexpr uint32_t T128 = 128 * HD * 2;          // 16 KB: a 128-row tile
-constexpr uint32_t QD_STAGE = 2 * T64 + 1024;    // Q, dO and the block's L, D
-constexpr int QS = 4;  // Q/dO stages of k_dkdv
-constexpr size_t SMEM_DKDV = 2 * T128 + QS * QD_STAGE + 4 * T128 + 1024 + 512;
-constexpr size_t SMEM_DQ = 2 * T128 + 3 * 2 * T64 + T128 + 1024 + 512;
+constexpr int BB = 128;                          // the looped block (queries in k_dkdv, keys in k_dq)
+// 8 compute warps: two per TMEM lane quadrant, each takes 64 of the block's
+// 128 columns of its rows (the backward has no row reductions to combine)
+constexpr int NTB = 320, NCW = 8, HALF = BB / 2;
+constexpr uint32_t T128 = 128 * HD * 2;          // 16 KB: a 128-row tile of 64 bf16 (one 128-byte swizzle atom)
+constexpr uint32_t TPD = 2 * T128;               // 32 KB: a 128 x 128 bf16 P / dS tile, two atoms of 64 columns
+constexpr uint32_t QD_STAGE = 2 * T128 + 1024;   // Q, dO and the block's L[128], D[128]
+constexpr int QS = 3;                            // Q/dO stages of k_dkdv
+constexpr int KS = 3;                            // K/V stages of k_dq
+constexpr size_t SMEM_DKDV = 2 * T128 + QS * QD_STAGE + 2 * TPD + 1024 + 512;
+constexpr size_t SMEM_DQ = 2 * T128 + KS * 2 * T128 + 2 * TPD + 1024 + 512;
 
 struct BwdArgs {
     int b, s, h, hkv;
@@ -372,21 +373,29 @@ __device__ __forceinline__ int bqhi(const BwdArgs& a, int k) {
     return min(a.s - 1, k + a.window - 1);
 }
 
-// 16-byte chunk `chunk` (8 bf16) of row r of a 128-byte-row swizzled tile
-__device__ __forceinline__ void st_chunk8(uint32_t row_addr, int r, int chunk, const float (&x)[8]) {
+// 16-byte chunk `chunk` (8 bf16, columns 8·chunk..) of row r of a 128 x 128
+// tile stored as two 128-byte-row swizzled atoms (columns 0-63, 64-127)
+__device__ __forceinline__ void st_chunk8(uint32_t tile, int r, int chunk, const float (&x)[8]) {
     uint4 pk;
     __nv_bfloat162* pp = (__nv_bfloat162*)&pk;
 #pragma unroll
     for (int t = 0; t < 4; ++t) pp[t] = __floats2bfloat162_rn(x[2 * t], x[2 * t + 1]);
-    asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(row_addr + ((chunk ^ (r & 7)) << 4)), "r"(pk.x),
-                 "r"(pk.y), "r"(pk.z), "r"(pk.w)
+    const uint32_t addr = tile + (chunk >> 3) * T128 + r * 128 + (((chunk & 7) ^ (r & 7)) << 4);
+    asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(pk.x), "r"(pk.y), "r"(pk.z), "r"(pk.w)
                  : "memory");
 }
 
-// One CTA per SM: a 4-deep Q/dO ring keeps the loads about three blocks
-// ahead (the tiles come from L2 with ~2 K cycles of latency), and Sᵀ/dPᵀ
-// (TMEM) and P/dS (shared memory) are double-buffered so the MMAs of one
-// block overlap the next block's math.
+// A operand descriptor for K-step kk of a 128 x 128 two-atom tile
+__device__ __forceinline__ uint64_t a2desc(uint32_t tile, int kk) {
+    return tc::sdesc(tile + (kk >> 2) * T128 + (kk & 3) * 32, 16, 1024);
+}
+
+// dK/dV: one CTA per 128 keys of a kv head; loops over the 128-query blocks
+// of every head of its group. Per block: Sᵀ = K·Qᵀ and dPᵀ = V·dOᵀ (M 128
+// keys, N 128 queries) into TMEM; the compute warps turn them into Pᵀ and
+// dSᵀ (bf16, shared memory); dV += Pᵀ·dO and dK += dSᵀ·Q (K = 128 queries)
+// accumulate in TMEM. Sᵀ/dPᵀ are single-buffered: the next block's products
+// are issued as soon as the compute warps hold the current ones in registers.
 __global__ void __launch_bounds__(NTB, 1)
     k_dkdv(const __grid_constant__ CUtensorMap mk, const __grid_constant__ CUtensorMap mv,
            const __grid_constant__ CUtensorMap mq, const __grid_constant__ CUtensorMap mdo, BwdArgs a) {
@@ -394,21 +403,21 @@ __global__ void __launch_bounds__(NTB, 1)
     uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
     uint8_t* sK = smem;
     uint8_t* sV = sK + T128;
-    uint8_t* sQD = sV + T128;  // QS stages: Q | dO | L[64] D[64]
-    uint8_t* sP = sQD + QS * QD_STAGE;  // [2] Pᵀ tiles
-    uint8_t* sDS = sP + 2 * T128;       // [2] dSᵀ tiles
-    uint64_t* bars = (uint64_t*)(sDS + 2 * T128);
+    uint8_t* sQD = sV + T128;           // QS stages: Q | dO | L[128] D[128]
+    uint8_t* sP = sQD + QS * QD_STAGE;  // Pᵀ tile
+    uint8_t* sDS = sP + TPD;            // dSᵀ tile
+    uint64_t* bars = (uint64_t*)(sDS + TPD);
     uint64_t* kv_full = bars;
     uint64_t* qd_full = kv_full + 1;
     uint64_t* qd_empty = qd_full + QS;
     uint64_t* st_full = qd_empty + QS;
-    uint64_t* st_free = st_full + 2;
-    uint64_t* pd_full = st_free + 2;
-    uint64_t* pd_free = pd_full + 2;
-    uint64_t* acc_full = pd_free + 2;
+    uint64_t* st_free = st_full + 1;
+    uint64_t* pd_full = st_free + 1;
+    uint64_t* pd_free = pd_full + 1;
+    uint64_t* acc_full = pd_free + 1;
     uint64_t* drain = acc_full + 1;
     uint32_t* tmem_slot = (uint32_t*)(drain + 1);
-    // TMEM columns: Sᵀ[2] 0 / 64, dPᵀ[2] 128 / 192, dV 256, dK 320
+    // TMEM columns: Sᵀ 0..127, dPᵀ 128..255, dV 256..319, dK 320..383
     constexpr uint32_t C_S = 0, C_DP = 128, C_DV = 256, C_DK = 320;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -426,12 +435,10 @@ __global__ void __launch_bounds__(NTB, 1)
             tc::mbar_init(&qd_full[i], 1);
             tc::mbar_init(&qd_empty[i], 1);
         }
-        for (int i = 0; i < 2; ++i) {
-            tc::mbar_init(&st_full[i], 1);
-            tc::mbar_init(&st_free[i], NCW);
-            tc::mbar_init(&pd_full[i], NCW);
-            tc::mbar_init(&pd_free[i], 1);
-        }
+        tc::mbar_init(st_full, 1);
+        tc::mbar_init(st_free, NCW);
+        tc::mbar_init(pd_full, NCW);
+        tc::mbar_init(pd_free, 1);
         tc::mbar_init(acc_full, 1);
         tc::mbar_init(drain, 1);
         tc::fence_mbar_init();
@@ -449,40 +456,40 @@ __global__ void __launch_bounds__(NTB, 1)
             tc::tma_load_2d(sK, &mk, kvh * HD, (int)(seq_row + k0), kv_full);
             tc::tma_load_2d(sV, &mv, kvh * HD, (int)(seq_row + k0), kv_full);
         }
-        int last_ph[QS];
-        for (int i = 0; i < QS; ++i) last_ph[i] = -1;
+        uint32_t used = 0, last_par = 0;
         int ok = 1;
         for (int it = 0; it < n; ++it) {
             const int st = it % QS;
-            const int ph = (it / QS) & 1;
+            const uint32_t ph = (it / QS) & 1;
             if (lane == 0) ok = tc::mbar_wait(&qd_empty[st], ph ^ 1, a.status, 4);
             ok = __shfl_sync(0xffffffffu, ok, 0);
             if (!ok) break;
-            last_ph[st] = ph;
             const int h = kvh * grp + it / nq;
             const int q0 = (qb0 + it % nq) * BB;
             uint8_t* stg = sQD + st * QD_STAGE;
-            float* sL = (float*)(stg + 2 * T64);
-            float* sD = sL + 64;
+            float* sL = (float*)(stg + 2 * T128);
+            float* sD = sL + 128;
             const long long lrow = ((long long)bi * a.h + h) * a.s;
 #pragma unroll
-            for (int u = 0; u < 2; ++u) {
-                const int c = lane * 2 + u, q = q0 + c;
+            for (int u = 0; u < 4; ++u) {
+                const int c = lane * 4 + u, q = q0 + c;
                 sL[c] = q < a.s ? a.lse[lrow + q] * LOG2E : INFINITY;
                 sD[c] = q < a.s ? a.dsum[lrow + q] : 0.f;
             }
             __syncwarp();
             if (lane == 0) {
-                tc::mbar_arrive_expect_tx(&qd_full[st], 2 * T64);
+                used |= 1u << st;
+                last_par = (last_par & ~(1u << st)) | (ph << st);
+                tc::mbar_arrive_expect_tx(&qd_full[st], 2 * T128);
                 tc::tma_load_2d(stg, &mq, h * HD, (int)(seq_row + q0), &qd_full[st]);
-                tc::tma_load_2d(stg + T64, &mdo, h * HD, (int)(seq_row + q0), &qd_full[st]);
+                tc::tma_load_2d(stg + T128, &mdo, h * HD, (int)(seq_row + q0), &qd_full[st]);
             }
         }
         if (!ok && lane == 0) {
             // let the copies in flight land before the CTA exits
             tc::mbar_wait(kv_full, 0, a.status, 4, 400000000ll, false);
             for (int i = 0; i < QS; ++i)
-                if (last_ph[i] >= 0) tc::mbar_wait(&qd_full[i], (uint32_t)last_ph[i], a.status, 4, 400000000ll, false);
+                if ((used >> i) & 1u) tc::mbar_wait(&qd_full[i], (last_par >> i) & 1u, a.status, 4, 400000000ll, false);
         }
     } else if (warp == 1) {
         if (lane == 0) {
@@ -491,49 +498,48 @@ __global__ void __launch_bounds__(NTB, 1)
             constexpr uint32_t ID_A = tc::idesc_bf16(128, HD, false, true);   // dV, dK
             bool ok = tc::mbar_wait(kv_full, 0, a.status, 4);
             const uint32_t aK = tc::smem_u32(sK), aV = tc::smem_u32(sV);
-            // Sᵀ, dPᵀ of block it into buffer it & 1, once that buffer's previous
-            // contents are in the compute warps' registers
+            const uint32_t aP = tc::smem_u32(sP), aDS = tc::smem_u32(sDS);
+            // Sᵀ, dPᵀ of block it, once the compute warps hold block it-1's in registers
             auto issue_st = [&](int it) -> bool {
-                const int st = it % QS, sb = it & 1;
+                const int st = it % QS;
                 if (!tc::mbar_wait(&qd_full[st], (it / QS) & 1, a.status, 4) ||
-                    !tc::mbar_wait(&st_free[sb], ((it >> 1) & 1) ^ 1, a.status, 4))
+                    !tc::mbar_wait(st_free, (it & 1) ^ 1, a.status, 4))
                     return false;
                 tc::tc_fence_after();
-                const uint32_t bQ = tc::smem_u32(sQD + st * QD_STAGE), bO = bQ + T64;
+                const uint32_t bQ = tc::smem_u32(sQD + st * QD_STAGE), bO = bQ + T128;
 #pragma unroll
                 for (int kk = 0; kk < HD / 16; ++kk)
-                    tc::mma_bf16(tmem + C_S + sb * BB, tc::sdesc(aK + kk * 32, 16, 1024), tc::sdesc(bQ + kk * 32, 16, 1024),
-                                 ID_T, kk != 0);
+                    tc::mma_bf16(tmem + C_S, tc::sdesc(aK + kk * 32, 16, 1024), tc::sdesc(bQ + kk * 32, 16, 1024), ID_T,
+                                 kk != 0);
 #pragma unroll
                 for (int kk = 0; kk < HD / 16; ++kk)
-                    tc::mma_bf16(tmem + C_DP + sb * BB, tc::sdesc(aV + kk * 32, 16, 1024), tc::sdesc(bO + kk * 32, 16, 1024),
-                                 ID_T, kk != 0);
-                tc::mma_commit(&st_full[sb]);
+                    tc::mma_bf16(tmem + C_DP, tc::sdesc(aV + kk * 32, 16, 1024), tc::sdesc(bO + kk * 32, 16, 1024), ID_T,
+                                 kk != 0);
+                tc::mma_commit(st_full);
                 return true;
             };
             if (ok && n > 0) ok = issue_st(0);
             for (int it = 0; it < n && ok; ++it) {
-                const int st = it % QS, pb = it & 1;
-                const uint32_t bQ = tc::smem_u32(sQD + st * QD_STAGE), bO = bQ + T64;
+                const int st = it % QS;
+                const uint32_t bQ = tc::smem_u32(sQD + st * QD_STAGE), bO = bQ + T128;
                 if (it + 1 < n && !issue_st(it + 1)) {
                     ok = false;
                     break;
                 }
-                if (!tc::mbar_wait(&pd_full[pb], (it >> 1) & 1, a.status, 4)) {
+                if (!tc::mbar_wait(pd_full, it & 1, a.status, 4)) {
                     ok = false;
                     break;
                 }
                 tc::tc_fence_after();
-                const uint32_t aP = tc::smem_u32(sP + pb * T128), aDS = tc::smem_u32(sDS + pb * T128);
 #pragma unroll
                 for (int kk = 0; kk < BB / 16; ++kk)
-                    tc::mma_bf16(tmem + C_DV, tc::sdesc(aP + kk * 32, 16, 1024), tc::sdesc(bO + kk * 2048, 8192, 1024),
-                                 ID_A, (it | kk) != 0);
+                    tc::mma_bf16(tmem + C_DV, a2desc(aP, kk), tc::sdesc(bO + kk * 2048, 8192, 1024), ID_A,
+                                 (it | kk) != 0);
 #pragma unroll
                 for (int kk = 0; kk < BB / 16; ++kk)
-                    tc::mma_bf16(tmem + C_DK, tc::sdesc(aDS + kk * 32, 16, 1024), tc::sdesc(bQ + kk * 2048, 8192, 1024),
-                                 ID_A, (it | kk) != 0);
-                tc::mma_commit(&pd_free[pb]);
+                    tc::mma_bf16(tmem + C_DK, a2desc(aDS, kk), tc::sdesc(bQ + kk * 2048, 8192, 1024), ID_A,
+                                 (it | kk) != 0);
+                tc::mma_commit(pd_free);
                 tc::mma_commit(&qd_empty[st]);
             }
             if (ok) tc::mma_commit(acc_full);
@@ -541,41 +547,49 @@ __global__ void __launch_bounds__(NTB, 1)
             tc::mbar_wait(drain, 0, a.status, 4, 400000000ll, false);
         }
     } else {
-        // ---------------- compute: thread = key row, 32 of its 64 query columns
-        const int qd = warp & 3, c0 = ((warp - 2) >> 2) * 32;
+        // ---------------- compute: thread = key row, 64 of the block's 128 query columns
+        const int qd = warp & 3, half = (warp - 2) >> 2, c0 = half * HALF;
         const int r = qd * 32 + lane;
         const int key = k0 + r;
         const uint32_t lane_off = (uint32_t)(qd * 32) << 16;
         const float sc = a.scale * LOG2E;
         const int qlo = bqlo(a, key), qhi = bqhi(a, key);
+        const uint32_t prow = tc::smem_u32(sP), dsrow = tc::smem_u32(sDS);
         bool ok = true;
         for (int it = 0; it < n && ok; ++it) {
-            const int st = it % QS, sb = it & 1;
+            const int st = it % QS;
             const int q0 = (qb0 + it % nq) * BB;
-            if (!tc::mbar_wait(&st_full[sb], (it >> 1) & 1, a.status, 4)) {
+            if (!tc::mbar_wait(st_full, it & 1, a.status, 4)) {
                 ok = false;
                 break;
             }
             tc::tc_fence_after();
-            uint32_t s[32], dp[32];
-            tc::tmem_ld32(tmem + lane_off + C_S + sb * BB + c0, s);
-            tc::tmem_ld32(tmem + lane_off + C_DP + sb * BB + c0, dp);
-            tc::tmem_ld_wait();
+            uint32_t s[HALF], dp[HALF];
+            {
+                uint32_t (&s0)[32] = *reinterpret_cast<uint32_t(*)[32]>(&s[0]);
+                uint32_t (&s1)[32] = *reinterpret_cast<uint32_t(*)[32]>(&s[32]);
+                uint32_t (&d0)[32] = *reinterpret_cast<uint32_t(*)[32]>(&dp[0]);
+                uint32_t (&d1)[32] = *reinterpret_cast<uint32_t(*)[32]>(&dp[32]);
+                tc::tmem_ld32(tmem + lane_off + C_S + c0, s0);
+                tc::tmem_ld32(tmem + lane_off + C_S + c0 + 32, s1);
+                tc::tmem_ld32(tmem + lane_off + C_DP + c0, d0);
+                tc::tmem_ld32(tmem + lane_off + C_DP + c0 + 32, d1);
+                tc::tmem_ld_wait();
+            }
             tc::tc_fence_before();
             __syncwarp();
-            if (lane == 0) tc::mbar_arrive(&st_free[sb]);
+            if (lane == 0) tc::mbar_arrive(st_free);
             // no masking when every (query, key) pair of the block is visible
             const bool full = q0 >= bqlo(a, klast) && q0 + BB - 1 <= bqhi(a, k0) && q0 + BB - 1 < a.s;
-            const float* sL = (const float*)(sQD + st * QD_STAGE + 2 * T64);
-            const float* sD = sL + 64;
-            // the MMAs of block it - 2 have read this P / dS buffer
-            if (!tc::mbar_wait(&pd_free[sb], ((it >> 1) & 1) ^ 1, a.status, 4)) {
+            const float* sL = (const float*)(sQD + st * QD_STAGE + 2 * T128);
+            const float* sD = sL + 128;
+            // the MMAs of the previous block have read the Pᵀ / dSᵀ tiles
+            if (!tc::mbar_wait(pd_free, (it & 1) ^ 1, a.status, 4)) {
                 ok = false;
                 break;
             }
-            const uint32_t prow = tc::smem_u32(sP + sb * T128) + r * 128, dsrow = tc::smem_u32(sDS + sb * T128) + r * 128;
 #pragma unroll
-            for (int ch = 0; ch < 4; ++ch) {
+            for (int ch = 0; ch < HALF / 8; ++ch) {
                 float p[8], ds[8];
                 const float4 l0 = *(const float4*)(sL + c0 + ch * 8), l1 = *(const float4*)(sL + c0 + ch * 8 + 4);
                 const float4 d0 = *(const float4*)(sD + c0 + ch * 8), d1 = *(const float4*)(sD + c0 + ch * 8 + 4);
@@ -594,16 +608,18 @@ __global__ void __launch_bounds__(NTB, 1)
             }
             tc::fence_proxy_async();
             __syncwarp();
-            if (lane == 0) tc::mbar_arrive(&pd_full[sb]);
+            if (lane == 0) tc::mbar_arrive(pd_full);
         }
         if (ok && n > 0 && tc::mbar_wait(acc_full, 0, a.status, 4)) {
             tc::tc_fence_after();
+            // each warp of a quadrant writes 32 of the 64 head columns
+            const int hc = half * 32;
             uint32_t dv[32], dk[32];
-            tc::tmem_ld32(tmem + lane_off + C_DV + c0, dv);
-            tc::tmem_ld32(tmem + lane_off + C_DK + c0, dk);
+            tc::tmem_ld32(tmem + lane_off + C_DV + hc, dv);
+            tc::tmem_ld32(tmem + lane_off + C_DK + hc, dk);
             tc::tmem_ld_wait();
             if (key < a.s) {
-                const long long off = (seq_row + key) * a.kv_stride + kvh * HD + c0;
+                const long long off = (seq_row + key) * a.kv_stride + kvh * HD + hc;
 #pragma unroll
                 for (int c = 0; c < 4; ++c) {
                     uint4 pv, pk;
@@ -629,27 +645,31 @@ __global__ void __launch_bounds__(NTB, 1)
     }
 }
 
-__global__ void __launch_bounds__(NTB, 2)
+// dQ: one CTA per 128 queries of a head; loops over its 128-key blocks:
+// S = Q·Kᵀ and dP = dO·Vᵀ (N = 128 keys) into TMEM, dS (bf16) to shared
+// memory (double-buffered), dQ += dS·K (K = 128 keys) in TMEM.
+__global__ void __launch_bounds__(NTB, 1)
     k_dq(const __grid_constant__ CUtensorMap mq, const __grid_constant__ CUtensorMap mdo,
          const __grid_constant__ CUtensorMap mk, const __grid_constant__ CUtensorMap mv, BwdArgs a) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
     uint8_t* sQ = smem;
     uint8_t* sO = sQ + T128;
-    uint8_t* sKV = sO + T128;  // 3 stages: K | V (64 keys each)
-    uint8_t* sDS = sKV + 3 * 2 * T64;
-    uint64_t* bars = (uint64_t*)(sDS + T128);
+    uint8_t* sKV = sO + T128;  // KS stages: K | V (128 keys each)
+    uint8_t* sDS = sKV + KS * 2 * T128;  // [2] dS tiles
+    uint64_t* bars = (uint64_t*)(sDS + 2 * TPD);
     uint64_t* q_full = bars;
     uint64_t* kv_full = q_full + 1;
-    uint64_t* kv_empty = kv_full + 3;
-    uint64_t* st_full = kv_empty + 3;
+    uint64_t* kv_empty = kv_full + KS;
+    uint64_t* st_full = kv_empty + KS;
     uint64_t* st_free = st_full + 1;
     uint64_t* ds_full = st_free + 1;
-    uint64_t* ds_free = ds_full + 1;
-    uint64_t* acc_full = ds_free + 1;
+    uint64_t* ds_free = ds_full + 2;
+    uint64_t* acc_full = ds_free + 2;
     uint64_t* drain = acc_full + 1;
     uint32_t* tmem_slot = (uint32_t*)(drain + 1);
-    constexpr uint32_t C_S = 0, C_DP = 64, C_DQ = 128;
+    // TMEM columns: S 0..127, dP 128..255, dQ 256..319
+    constexpr uint32_t C_S = 0, C_DP = 128, C_DQ = 256;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int qt = gridDim.x - 1 - blockIdx.x;
@@ -662,19 +682,21 @@ __global__ void __launch_bounds__(NTB, 2)
 
     if (threadIdx.x == 0) {
         tc::mbar_init(q_full, 1);
-        for (int i = 0; i < 3; ++i) {
+        for (int i = 0; i < KS; ++i) {
             tc::mbar_init(&kv_full[i], 1);
             tc::mbar_init(&kv_empty[i], 1);
         }
         tc::mbar_init(st_full, 1);
         tc::mbar_init(st_free, NCW);
-        tc::mbar_init(ds_full, NCW);
-        tc::mbar_init(ds_free, 1);
+        for (int i = 0; i < 2; ++i) {
+            tc::mbar_init(&ds_full[i], NCW);
+            tc::mbar_init(&ds_free[i], 1);
+        }
         tc::mbar_init(acc_full, 1);
         tc::mbar_init(drain, 1);
         tc::fence_mbar_init();
     }
-    if (warp == 1) tc::tmem_alloc(tmem_slot, 256);
+    if (warp == 1) tc::tmem_alloc(tmem_slot, 512);
     tc::tc_fence_before();
     __syncthreads();
     tc::tc_fence_after();
@@ -685,26 +707,27 @@ __global__ void __launch_bounds__(NTB, 2)
             tc::mbar_arrive_expect_tx(q_full, 2 * T128);
             tc::tma_load_2d(sQ, &mq, h * HD, (int)(seq_row + q0), q_full);
             tc::tma_load_2d(sO, &mdo, h * HD, (int)(seq_row + q0), q_full);
-            int last_ph[3] = {-1, -1, -1};
+            uint32_t used = 0, last_par = 0;
             bool ok = true;
             for (int j = 0; j < n; ++j) {
-                const int st = j % 3;
-                const uint32_t ph = (j / 3) & 1;
+                const int st = j % KS;
+                const uint32_t ph = (j / KS) & 1;
                 if (!tc::mbar_wait(&kv_empty[st], ph ^ 1, a.status, 4)) {
                     ok = false;
                     break;
                 }
-                uint8_t* stg = sKV + st * 2 * T64;
-                tc::mbar_arrive_expect_tx(&kv_full[st], 2 * T64);
+                uint8_t* stg = sKV + st * 2 * T128;
+                tc::mbar_arrive_expect_tx(&kv_full[st], 2 * T128);
                 const int krow = (int)(seq_row + (long long)(j0 + j) * BB);
                 tc::tma_load_2d(stg, &mk, kvh * HD, krow, &kv_full[st]);
-                tc::tma_load_2d(stg + T64, &mv, kvh * HD, krow, &kv_full[st]);
-                last_ph[st] = (int)ph;
+                tc::tma_load_2d(stg + T128, &mv, kvh * HD, krow, &kv_full[st]);
+                used |= 1u << st;
+                last_par = (last_par & ~(1u << st)) | (ph << st);
             }
             if (!ok) {
                 tc::mbar_wait(q_full, 0, a.status, 4, 400000000ll, false);
-                for (int i = 0; i < 3; ++i)
-                    if (last_ph[i] >= 0) tc::mbar_wait(&kv_full[i], (uint32_t)last_ph[i], a.status, 4, 400000000ll, false);
+                for (int i = 0; i < KS; ++i)
+                    if ((used >> i) & 1u) tc::mbar_wait(&kv_full[i], (last_par >> i) & 1u, a.status, 4, 400000000ll, false);
             }
         }
     } else if (warp == 1) {
@@ -715,12 +738,12 @@ __global__ void __launch_bounds__(NTB, 2)
             const uint32_t aQ = tc::smem_u32(sQ), aO = tc::smem_u32(sO), aDS = tc::smem_u32(sDS);
             // S, dP of block j: issued once the compute warps hold block j-1's
             auto issue_st = [&](int j) -> bool {
-                const int st = j % 3;
-                if (!tc::mbar_wait(&kv_full[st], (j / 3) & 1, a.status, 4) ||
+                const int st = j % KS;
+                if (!tc::mbar_wait(&kv_full[st], (j / KS) & 1, a.status, 4) ||
                     !tc::mbar_wait(st_free, (j & 1) ^ 1, a.status, 4))
                     return false;
                 tc::tc_fence_after();
-                const uint32_t bK = tc::smem_u32(sKV + st * 2 * T64), bV = bK + T64;
+                const uint32_t bK = tc::smem_u32(sKV + st * 2 * T128), bV = bK + T128;
 #pragma unroll
                 for (int kk = 0; kk < HD / 16; ++kk)
                     tc::mma_bf16(tmem + C_S, tc::sdesc(aQ + kk * 32, 16, 1024), tc::sdesc(bK + kk * 32, 16, 1024), ID_S,
@@ -734,22 +757,22 @@ __global__ void __launch_bounds__(NTB, 2)
             };
             if (ok && n > 0) ok = issue_st(0);
             for (int j = 0; j < n && ok; ++j) {
-                const int st = j % 3;
-                const uint32_t bK = tc::smem_u32(sKV + st * 2 * T64);
+                const int st = j % KS, db = j & 1;
+                const uint32_t bK = tc::smem_u32(sKV + st * 2 * T128);
                 if (j + 1 < n && !issue_st(j + 1)) {
                     ok = false;
                     break;
                 }
-                if (!tc::mbar_wait(ds_full, j & 1, a.status, 4)) {
+                if (!tc::mbar_wait(&ds_full[db], (j >> 1) & 1, a.status, 4)) {
                     ok = false;
                     break;
                 }
                 tc::tc_fence_after();
 #pragma unroll
                 for (int kk = 0; kk < BB / 16; ++kk)
-                    tc::mma_bf16(tmem + C_DQ, tc::sdesc(aDS + kk * 32, 16, 1024), tc::sdesc(bK + kk * 2048, 8192, 1024),
-                                 ID_Q, (j | kk) != 0);
-                tc::mma_commit(ds_free);
+                    tc::mma_bf16(tmem + C_DQ, a2desc(aDS + db * TPD, kk), tc::sdesc(bK + kk * 2048, 8192, 1024), ID_Q,
+                                 (j | kk) != 0);
+                tc::mma_commit(&ds_free[db]);
                 tc::mma_commit(&kv_empty[st]);
             }
             if (ok) tc::mma_commit(acc_full);
@@ -757,8 +780,8 @@ __global__ void __launch_bounds__(NTB, 2)
             tc::mbar_wait(drain, 0, a.status, 4, 400000000ll, false);
         }
     } else {
-        // ---------------- compute: thread = query row, 32 of its 64 key columns
-        const int qd = warp & 3, c0 = ((warp - 2) >> 2) * 32;
+        // ---------------- compute: thread = query row, 64 of the block's 128 key columns
+        const int qd = warp & 3, half = (warp - 2) >> 2, c0 = half * HALF;
         const int r = qd * 32 + lane;
         const int row = q0 + r;
         const uint32_t lane_off = (uint32_t)(qd * 32) << 16;
@@ -767,29 +790,38 @@ __global__ void __launch_bounds__(NTB, 2)
         const float L = row < a.s ? a.lse[lrow + row] * LOG2E : INFINITY;
         const float D = row < a.s ? a.dsum[lrow + row] : 0.f;
         const int lo = bklo(a, row), hi = min(bkhi(a, row), a.s - 1);
-        const uint32_t dsrow = tc::smem_u32(sDS) + r * 128;
         bool ok = true;
         for (int j = 0; j < n && ok; ++j) {
-            const int kb0 = (j0 + j) * BB;
+            const int kb0 = (j0 + j) * BB, db = j & 1;
             if (!tc::mbar_wait(st_full, j & 1, a.status, 4)) {
                 ok = false;
                 break;
             }
             tc::tc_fence_after();
-            uint32_t s[32], dp[32];
-            tc::tmem_ld32(tmem + lane_off + C_S + c0, s);
-            tc::tmem_ld32(tmem + lane_off + C_DP + c0, dp);
-            tc::tmem_ld_wait();
+            uint32_t s[HALF], dp[HALF];
+            {
+                uint32_t (&s0)[32] = *reinterpret_cast<uint32_t(*)[32]>(&s[0]);
+                uint32_t (&s1)[32] = *reinterpret_cast<uint32_t(*)[32]>(&s[32]);
+                uint32_t (&d0)[32] = *reinterpret_cast<uint32_t(*)[32]>(&dp[0]);
+                uint32_t (&d1)[32] = *reinterpret_cast<uint32_t(*)[32]>(&dp[32]);
+                tc::tmem_ld32(tmem + lane_off + C_S + c0, s0);
+                tc::tmem_ld32(tmem + lane_off + C_S + c0 + 32, s1);
+                tc::tmem_ld32(tmem + lane_off + C_DP + c0, d0);
+                tc::tmem_ld32(tmem + lane_off + C_DP + c0 + 32, d1);
+                tc::tmem_ld_wait();
+            }
             tc::tc_fence_before();
             __syncwarp();
             if (lane == 0) tc::mbar_arrive(st_free);
             const bool full = kb0 >= bklo(a, qlast) && kb0 + BB - 1 <= min(bkhi(a, q0), a.s - 1);
-            if (!tc::mbar_wait(ds_free, (j & 1) ^ 1, a.status, 4)) {
+            // the dQ MMA of block j - 2 has read this dS buffer
+            if (!tc::mbar_wait(&ds_free[db], ((j >> 1) & 1) ^ 1, a.status, 4)) {
                 ok = false;
                 break;
             }
+            const uint32_t dsrow = tc::smem_u32(sDS + db * TPD);
 #pragma unroll
-            for (int ch = 0; ch < 4; ++ch) {
+            for (int ch = 0; ch < HALF / 8; ++ch) {
                 float ds[8];
 #pragma unroll
                 for (int t = 0; t < 8; ++t) {
@@ -802,15 +834,16 @@ __global__ void __launch_bounds__(NTB, 2)
             }
             tc::fence_proxy_async();
             __syncwarp();
-            if (lane == 0) tc::mbar_arrive(ds_full);
+            if (lane == 0) tc::mbar_arrive(&ds_full[db]);
         }
         if (ok && n > 0 && tc::mbar_wait(acc_full, 0, a.status, 4)) {
             tc::tc_fence_after();
+            const int hc = half * 32;
             uint32_t dq[32];
-            tc::tmem_ld32(tmem + lane_off + C_DQ + c0, dq);
+            tc::tmem_ld32(tmem + lane_off + C_DQ + hc, dq);
             tc::tmem_ld_wait();
             if (row < a.s) {
-                bf16* out = a.dq + (seq_row + row) * a.q_stride + h * HD + c0;
+                bf16* out = a.dq + (seq_row + row) * a.q_stride + h * HD + hc;
 #pragma unroll
                 for (int c = 0; c < 4; ++c) {
                     uint4 pk;
@@ -828,7 +861,7 @@ __global__ void __launch_bounds__(NTB, 2)
     __syncthreads();
     if (warp == 1) {
         tc::tc_fence_after();
-        tc::tmem_dealloc(tmem, 256);
+        tc::tmem_dealloc(tmem, 512);
     }
 }
 
@@ -882,14 +915,10 @@ void attention_bwd_tc5(Context* c, const void* q, const void* k, const void* v, 
     using namespace fa5;
     if (b <= 0 || s <= 0 || h <= 0) return;
     CATNN_CHECK(b * s < (1ll << 31) && h % hkv == 0, CATNN_ERR_SHAPE, "attention: sizes");
-    CUtensorMap mq64 = tma_map_bf16(q, b * s, h * HD, q_stride, HD, 64);
     CUtensorMap mq128 = tma_map_bf16(q, b * s, h * HD, q_stride, HD, 128);
-    CUtensorMap mdo64 = tma_map_bf16(dout, b * s, h * HD, h * HD, HD, 64);
     CUtensorMap mdo128 = tma_map_bf16(dout, b * s, h * HD, h * HD, HD, 128);
     CUtensorMap mk128 = tma_map_bf16(k, b * s, hkv * HD, kv_stride, HD, 128);
     CUtensorMap mv128 = tma_map_bf16(v, b * s, hkv * HD, kv_stride, HD, 128);
-    CUtensorMap mk64 = tma_map_bf16(k, b * s, hkv * HD, kv_stride, HD, 64);
-    CUtensorMap mv64 = tma_map_bf16(v, b * s, hkv * HD, kv_stride, HD, 64);
     BwdArgs a{};
     a.b = (int)b;
     a.s = (int)s;
@@ -912,10 +941,10 @@ void attention_bwd_tc5(Context* c, const void* q, const void* k, const void* v, 
         CUDA_OK(cudaFuncSetAttribute(k_dq, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_DQ));
         attr[c->device] = true;
     }
-    k_dkdv<<<dim3((unsigned)cdiv(s, 128), (unsigned)hkv, (unsigned)b), NTB, SMEM_DKDV, c->stream>>>(mk128, mv128, mq64,
-                                                                                                    mdo64, a);
-    k_dq<<<dim3((unsigned)cdiv(s, 128), (unsigned)h, (unsigned)b), NTB, SMEM_DQ, c->stream>>>(mq128, mdo128, mk64, mv64,
-                                                                                              a);
+    k_dkdv<<<dim3((unsigned)cdiv(s, 128), (unsigned)hkv, (unsigned)b), NTB, SMEM_DKDV, c->stream>>>(mk128, mv128, mq128,
+                                                                                                    mdo128, a);
+    k_dq<<<dim3((unsigned)cdiv(s, 128), (unsigned)h, (unsigned)b), NTB, SMEM_DQ, c->stream>>>(mq128, mdo128, mk128,
+                                                                                              mv128, a);
     launched(c, 2);
 }
 

@@ -24,6 +24,7 @@ struct NcclFns {
     ncclResult_t (*commDestroy)(ncclComm_t);
     ncclResult_t (*allReduce)(const void*, void*, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t, cudaStream_t);
     ncclResult_t (*allGather)(const void*, void*, size_t, ncclDataType_t, ncclComm_t, cudaStream_t);
+    ncclResult_t (*reduceScatter)(const void*, void*, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t, cudaStream_t);
     ncclResult_t (*send)(const void*, size_t, ncclDataType_t, int, ncclComm_t, cudaStream_t);
     ncclResult_t (*recv)(void*, size_t, ncclDataType_t, int, ncclComm_t, cudaStream_t);
     ncclResult_t (*groupStart)();
@@ -56,6 +57,7 @@ static const NcclFns* nccl_fns() {
             fns.commDestroy = (decltype(fns.commDestroy))sym("ncclCommDestroy");
             fns.allReduce = (decltype(fns.allReduce))sym("ncclAllReduce");
             fns.allGather = (decltype(fns.allGather))sym("ncclAllGather");
+            fns.reduceScatter = (decltype(fns.reduceScatter))sym("ncclReduceScatter");
             fns.send = (decltype(fns.send))sym("ncclSend");
             fns.recv = (decltype(fns.recv))sym("ncclRecv");
             fns.groupStart = (decltype(fns.groupStart))sym("ncclGroupStart");
@@ -211,16 +213,48 @@ void Comm::allreduce_sum(void* buf, i64 n, int dtype) {
 
 void Comm::allreduce_overlapped(float* buf, i64 n) {
     if (world == 1 || n <= 0) return;
-    if (!side) {
-        int lo = 0, hi = 0;
-        CUDA_OK(cudaDeviceGetStreamPriorityRange(&lo, &hi));
-        CUDA_OK(cudaStreamCreateWithPriority(&side, cudaStreamNonBlocking, hi));
-        CUDA_OK(cudaEventCreateWithFlags(&ev_ready, cudaEventDisableTiming));
-        CUDA_OK(cudaEventCreateWithFlags(&ev_done, cudaEventDisableTiming));
-    }
+    make_side();
     CUDA_OK(cudaEventRecord(ev_ready, c->stream));
     CUDA_OK(cudaStreamWaitEvent(side, ev_ready, 0));
     NCCL_OK(fn, fn->allReduce(buf, buf, (size_t)n, ncclFloat32, ncclSum, nc(*this), side));
+}
+
+void Comm::make_side() {
+    if (side) return;
+    int lo = 0, hi = 0;
+    CUDA_OK(cudaDeviceGetStreamPriorityRange(&lo, &hi));
+    CUDA_OK(cudaStreamCreateWithPriority(&side, cudaStreamNonBlocking, hi));
+    CUDA_OK(cudaEventCreateWithFlags(&ev_ready, cudaEventDisableTiming));
+    CUDA_OK(cudaEventCreateWithFlags(&ev_done, cudaEventDisableTiming));
+}
+
+void Comm::reduce_scatter_overlapped(float* buf, i64 n) {
+    if (world == 1 || n <= 0) return;
+    CATNN_CHECK(n % world == 0, CATNN_ERR_SHAPE, "reduce-scatter: length not divisible by the ranks");
+    make_side();
+    CUDA_OK(cudaEventRecord(ev_ready, c->stream));
+    CUDA_OK(cudaStreamWaitEvent(side, ev_ready, 0));
+    const i64 chunk = n / world;
+    NCCL_OK(fn, fn->reduceScatter(buf, buf + rank * chunk, (size_t)chunk, ncclFloat32, ncclSum, nc(*this), side));
+}
+
+void Comm::allgather_after(void* buf, i64 n, int dtype, cudaEvent_t after) {
+    if (world == 1 || n <= 0) return;
+    CATNN_CHECK(n % world == 0, CATNN_ERR_SHAPE, "all-gather: length not divisible by the ranks");
+    make_side();
+    CUDA_OK(cudaStreamWaitEvent(side, after, 0));
+    const i64 chunk = n / world;
+    const size_t es = dtype == CATNN_BF16 ? 2 : 4;
+    NCCL_OK(fn, fn->allGather((char*)buf + rank * chunk * es, buf, (size_t)chunk, nccl_type(dtype), nc(*this), side));
+}
+
+void Comm::allgather(void* buf, i64 n, int dtype) {
+    if (world == 1 || n <= 0) return;
+    CATNN_CHECK(n % world == 0, CATNN_ERR_SHAPE, "all-gather: length not divisible by the ranks");
+    const i64 chunk = n / world;
+    const size_t es = dtype == CATNN_BF16 ? 2 : 4;
+    NCCL_OK(fn, fn->allGather((char*)buf + rank * chunk * es, buf, (size_t)chunk, nccl_type(dtype), nc(*this),
+                              c->stream));
 }
 
 void Comm::join_overlapped() {

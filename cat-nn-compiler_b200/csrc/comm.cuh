@@ -57,7 +57,17 @@ struct Comm {
     // enqueued so far on the context stream; join_overlapped makes the
     // context stream wait for every such allreduce.
     void allreduce_overlapped(float* buf, i64 n);
+    // Sharded counterparts on the communication stream (n divisible by the
+    // ranks, chunk = n / world): reduce_scatter_overlapped leaves the fp32 sum
+    // of chunk `rank` of buf in place (after the work enqueued so far on the
+    // context stream); allgather_after fills every chunk of buf from its
+    // owner's copy once `after` has completed (dtype CATNN_F32 or CATNN_BF16).
+    void reduce_scatter_overlapped(float* buf, i64 n);
+    void allgather_after(void* buf, i64 n, int dtype, cudaEvent_t after);
+    // In-place all-gather on the context stream.
+    void allgather(void* buf, i64 n, int dtype);
     void join_overlapped();
+    void make_side();
     cudaStream_t side = nullptr;
     cudaEvent_t ev_ready = nullptr, ev_done = nullptr;
     void release();

@@ -485,6 +485,16 @@ void gemm_grouped_f32(Context* c, bool ta_rows, bool tb, i64 total_rows, i64 N, 
 
 void gemm(Context* c, bool ta, bool tb, i64 M, i64 N, i64 K, const void* A, i64 lda, const void* B, i64 ldb,
           void* C, i64 ldc, int dtype, int c_dtype, const float* bias, int act, bool accumulate, const float* resid) {
+    if (dtype == CATNN_TF32) {
+        // fp32 operands, multiplied on the tensor cores as TF32
+        check_dtype(c_dtype);
+        CATNN_CHECK(M >= 0 && N >= 0 && K >= 0, CATNN_ERR_SHAPE, "gemm: negative size");
+        CATNN_CHECK(!(accumulate && act != CATNN_ACT_NONE), CATNN_ERR_INVALID, "gemm: accumulate with an activation");
+        CATNN_CHECK(!resid, CATNN_ERR_UNSUPPORTED, "tf32 gemm: no residual input");
+        gemm_tf32_tc(c, ta, tb, M, N, K, (const float*)A, lda, (const float*)B, ldb, C, ldc, c_dtype, bias, act,
+                     accumulate);
+        return;
+    }
     check_dtype(dtype);
     check_dtype(c_dtype);
     CATNN_CHECK(M >= 0 && N >= 0 && K >= 0, CATNN_ERR_SHAPE, "gemm: negative size");

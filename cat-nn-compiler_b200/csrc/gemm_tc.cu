@@ -211,14 +211,17 @@ __device__ __forceinline__ float act_apply(float v, int act) {
     return v;
 }
 
-template <bool A_MN, bool B_MN, int BN, int STAGES>
+template <bool A_MN, bool B_MN, int BN, int STAGES, bool TF32 = false>
 __global__ void __maxnreg__(200)  // 320 threads x 200 registers fit the 64 K register file
     k_gemm_tc(const __grid_constant__ CUtensorMap mapA, const __grid_constant__ CUtensorMap mapB,
               const __grid_constant__ CUtensorMap mapC, const __grid_constant__ CUtensorMap mapD, TcArgs a) {
     constexpr uint32_t A_BYTES = BM * BK * 2;
     constexpr uint32_t B_BYTES = BN * BK * 2;
     constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
-    constexpr uint32_t IDESC = tc::idesc_bf16(BM, BN, A_MN, B_MN);
+    static_assert(!TF32 || (!A_MN && !B_MN), "TF32 operands are K-major");
+    constexpr uint32_t IDESC = TF32 ? tc::idesc_tf32(BM, BN) : tc::idesc_bf16(BM, BN, A_MN, B_MN);
+    // K elements per stage: one 128-byte swizzle row (64 bf16 or 32 fp32)
+    constexpr int KB = TF32 ? BK / 2 : BK;
     constexpr uint32_t TMEM_COLS = 2 * BN;
 
     extern __shared__ uint8_t smem_raw[];
@@ -264,7 +267,7 @@ __global__ void __maxnreg__(200)  // 320 threads x 200 registers fit the 64 K re
         bool ok = true;
         for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
             TileInfo ti = tile_at<BN>(a, t);
-            int nkb = (ti.klen + BK - 1) / BK;
+            int nkb = (ti.klen + KB - 1) / KB;
             for (int kb = 0; kb < nkb; ++kb) {
                 if (!tc::mbar_wait(&empty[s], ph ^ 1, a.status, 1)) {
                     ok = false;
@@ -273,7 +276,7 @@ __global__ void __maxnreg__(200)  // 320 threads x 200 registers fit the 64 K re
                 uint8_t* sA = smem + s * STAGE_BYTES;
                 uint8_t* sB = sA + A_BYTES;
                 tc::mbar_arrive_expect_tx(&full[s], STAGE_BYTES);
-                int k = ti.kstart + kb * BK;
+                int k = ti.kstart + kb * KB;
                 if (!A_MN) {
                     tc::tma_load_2d(sA, &mapA, k, ti.arow0 + ti.m0, &full[s]);
                 } else {
@@ -313,7 +316,7 @@ __global__ void __maxnreg__(200)  // 320 threads x 200 registers fit the 64 K re
             if (!tc::mbar_wait(&tempty[acc], ((it >> 1) & 1) ^ 1, a.status, 2)) break;
             tc::tc_fence_after();
             uint32_t d = tmem_base + acc * BN;
-            int nkb = (ti.klen + BK - 1) / BK;
+            int nkb = (ti.klen + KB - 1) / KB;
             for (int kb = 0; kb < nkb; ++kb) {
                 if (!tc::mbar_wait(&full[s], ph, a.status, 2)) {
                     ok = false;
@@ -326,7 +329,8 @@ __global__ void __maxnreg__(200)  // 320 threads x 200 registers fit the 64 K re
                 for (int kk = 0; kk < BK / 16; ++kk) {
                     uint64_t ad = A_MN ? tc::sdesc(sA + kk * 2048, 8192, 1024) : tc::sdesc(sA + kk * 32, 16, 1024);
                     uint64_t bd = B_MN ? tc::sdesc(sB + kk * 2048, 8192, 1024) : tc::sdesc(sB + kk * 32, 16, 1024);
-                    tc::mma_bf16(d, ad, bd, IDESC, (kb | kk) != 0);
+                    if constexpr (TF32) tc::mma_tf32(d, ad, bd, IDESC, (kb | kk) != 0);
+                    else tc::mma_bf16(d, ad, bd, IDESC, (kb | kk) != 0);
                 }
                 tc::mma_commit(&empty[s]);
                 if (++s == STAGES) {
@@ -761,13 +765,14 @@ static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 
 // 2-D bf16 map over a row-major [rows, cols] matrix with leading dimension
 // ld (elements), box [box_cols (inner, 64 = 128 B), box_rows], 128B swizzle.
-static CUtensorMap make_map(const void* base, i64 rows, i64 cols, i64 ld, int box_cols, int box_rows) {
+static CUtensorMap make_map(const void* base, i64 rows, i64 cols, i64 ld, int box_cols, int box_rows, bool f32 = false) {
     CUtensorMap m;
     cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
-    cuuint64_t strides[1] = {(cuuint64_t)(ld * 2)};
+    cuuint64_t strides[1] = {(cuuint64_t)(ld * (f32 ? 4 : 2))};
     cuuint32_t box[2] = {(cuuint32_t)box_cols, (cuuint32_t)box_rows};
     cuuint32_t estr[2] = {1, 1};
-    CUresult r = encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+    CUresult r = encode_fn()(&m, f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
+                             const_cast<void*>(base), dims, strides, box, estr,
                              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     CATNN_CHECK(r == CUDA_SUCCESS, CATNN_ERR_CUDA, "cuTensorMapEncodeTiled failed (" + std::to_string((int)r) + ")");
@@ -798,7 +803,7 @@ CUtensorMap tma_map_bf16(const void* base, i64 rows, i64 cols, i64 ld, int box_c
     return make_map(base, rows, cols, ld, box_cols, box_rows);
 }
 
-template <bool A_MN, bool B_MN, int BN, int STAGES>
+template <bool A_MN, bool B_MN, int BN, int STAGES, bool TF32 = false>
 static void launch_tc(Context* c, const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mc,
                       const CUtensorMap& md, const TcArgs& a, int grid) {
     constexpr size_t smem = (size_t)STAGES * (BM * BK * 2 + BN * BK * 2) + EPI_STAGE_BYTES + 1024 + 256;
@@ -806,11 +811,11 @@ static void launch_tc(Context* c, const CUtensorMap& ma, const CUtensorMap& mb, 
     static bool attr_set[64] = {false};
     int dev = c->device;
     if (!attr_set[dev]) {
-        CUDA_OK(cudaFuncSetAttribute(k_gemm_tc<A_MN, B_MN, BN, STAGES>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        CUDA_OK(cudaFuncSetAttribute(k_gemm_tc<A_MN, B_MN, BN, STAGES, TF32>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      (int)smem));
         attr_set[dev] = true;
     }
-    k_gemm_tc<A_MN, B_MN, BN, STAGES><<<grid, GEMM_THREADS, smem, c->stream>>>(ma, mb, mc, md, a);
+    k_gemm_tc<A_MN, B_MN, BN, STAGES, TF32><<<grid, GEMM_THREADS, smem, c->stream>>>(ma, mb, mc, md, a);
     launched(c);
 }
 
@@ -858,12 +863,14 @@ static int pick_ksplit(Context* c, i64 tiles, i64 klen, i64 part_elems, int BN, 
 
 // Builds both maps for op(A) [M(or rows), K] and op(B) [K, N] and launches.
 // part_rows: rows of one split-K partial slice (0: no split-K).
-static void run_tc(Context* c, TcArgs a, bool a_mn, bool b_mn, const bf16* A, i64 a_rows, i64 a_cols, i64 lda,
-                   const bf16* B, i64 b_rows, i64 b_cols, i64 ldb, int grid_bound, i64 base_tiles = 0,
-                   i64 klen = 0, i64 part_rows = 0) {
+static void run_tc(Context* c, TcArgs a, bool a_mn, bool b_mn, const void* A, i64 a_rows, i64 a_cols, i64 lda,
+                   const void* B, i64 b_rows, i64 b_cols, i64 ldb, int grid_bound, i64 base_tiles = 0,
+                   i64 klen = 0, i64 part_rows = 0, bool tf32 = false) {
     const int BN = a.N <= 128 ? 128 : 256;
-    CUtensorMap ma = make_map(A, a_rows, a_cols, lda, 64, a_mn ? 64 : BM);
-    CUtensorMap mb = make_map(B, b_rows, b_cols, ldb, 64, b_mn ? 64 : BN);
+    // a box row is one 128-byte swizzle row: 64 bf16 or 32 fp32 elements of K
+    const int kbox = tf32 ? 32 : 64;
+    CUtensorMap ma = make_map(A, a_rows, a_cols, lda, kbox, a_mn ? 64 : BM, tf32);
+    CUtensorMap mb = make_map(B, b_rows, b_cols, ldb, kbox, b_mn ? 64 : BN, tf32);
     a.status = c->status;
     a.ksplit = 1;
     if (part_rows > 0) {
@@ -904,8 +911,15 @@ static void run_tc(Context* c, TcArgs a, bool a_mn, bool b_mn, const bf16* A, i6
     }
     int grid = grid_bound < c->sm_count ? grid_bound : c->sm_count;
     if (grid < 1) grid = 1;
-    if (BN == 128) dispatch_tc<128, 6>(c, a_mn, b_mn, ma, mb, mc, md, a, grid);
-    else dispatch_tc<256, 4>(c, a_mn, b_mn, ma, mb, mc, md, a, grid);
+    if (tf32) {
+        CATNN_CHECK(!a_mn && !b_mn, CATNN_ERR_UNSUPPORTED, "tf32 gemm: operands must be K-major");
+        if (BN == 128) launch_tc<false, false, 128, 6, true>(c, ma, mb, mc, md, a, grid);
+        else launch_tc<false, false, 256, 4, true>(c, ma, mb, mc, md, a, grid);
+    } else if (BN == 128) {
+        dispatch_tc<128, 6>(c, a_mn, b_mn, ma, mb, mc, md, a, grid);
+    } else {
+        dispatch_tc<256, 4>(c, a_mn, b_mn, ma, mb, mc, md, a, grid);
+    }
     if (a.ksplit > 1) {
         int g = (int)std::min<i64>(part_rows, (i64)c->sm_count * 16);
         k_splitk_reduce<<<g, 256, 0, c->stream>>>(a, part_rows);
@@ -920,6 +934,83 @@ static bool tc_ok(const void* A, i64 lda, const void* B, i64 ldb) {
 
 void gemm_bf16_simt(Context* c, bool ta, bool tb, i64 M, i64 N, i64 K, const bf16* A, i64 lda, const bf16* B, i64 ldb,
                     void* C, i64 ldc, int c_dtype, const float* bias, int act, bool accumulate, const float* resid);
+
+// out[c][r] = in[r][c] for an fp32 [rows, cols] matrix with leading dimension
+// ld (out is [cols, rows], dense): 32 x 32 tiles through shared memory.
+__global__ void __launch_bounds__(256) k_transpose_f32(const float* __restrict__ in, i64 rows, i64 cols, i64 ld,
+                                                       float* __restrict__ out) {
+    __shared__ float t[32][33];
+    const i64 r0 = (i64)blockIdx.y * 32, c0 = (i64)blockIdx.x * 32;
+    for (int i = threadIdx.y; i < 32; i += 8) {
+        const i64 r = r0 + i, cc = c0 + threadIdx.x;
+        t[i][threadIdx.x] = r < rows && cc < cols ? in[r * ld + cc] : 0.f;
+    }
+    __syncthreads();
+    for (int i = threadIdx.y; i < 32; i += 8) {
+        const i64 cc = c0 + i, r = r0 + threadIdx.x;
+        if (cc < cols && r < rows) out[cc * rows + r] = t[threadIdx.x][i];
+    }
+}
+
+static void transpose_f32(Context* c, const float* in, i64 rows, i64 cols, i64 ld, float* out) {
+    CATNN_CHECK(cdiv(rows, 32) <= 65535, CATNN_ERR_SHAPE, "transpose: too many rows");
+    k_transpose_f32<<<dim3((unsigned)cdiv(cols, 32), (unsigned)cdiv(rows, 32)), dim3(32, 8), 0, c->stream>>>(in, rows, cols,
+                                                                                                          ld, out);
+    launched(c);
+}
+
+// C = op(A)·op(B) with fp32 operands multiplied on the tensor cores as TF32
+// (kind::tf32: 10-bit mantissas, fp32 accumulation). The MMA reads both
+// operands K-major, so a transposed-layout operand (A stored [K, M] or B
+// stored [K, N]) is first copied K-major into the context's work arena.
+// Shapes the TMA path cannot take (pitches not a multiple of 4 elements,
+// N or K under 16, tiny products) run the fp32 CUDA-core GEMM instead.
+void gemm_tf32_tc(Context* c, bool ta, bool tb, i64 M, i64 N, i64 K, const float* A, i64 lda, const float* B, i64 ldb,
+                  void* C, i64 ldc, int c_dtype, const float* bias, int act, bool accumulate) {
+    if (M <= 0 || N <= 0) return;
+    CATNN_CHECK(M < (1ll << 31) && N < (1ll << 31) && K < (1ll << 31), CATNN_ERR_SHAPE, "gemm: dimension too large");
+    const bool copy = ta || !tb;  // an operand stored MN-major is first copied K-major (pitch K)
+    if (N < 16 || K < 16 || M * N < 128 * 64 || (lda % 4) || (ldb % 4) || (copy && K % 4) || !aligned16(A) ||
+        !aligned16(B)) {
+        gemm_f32(c, ta, tb, M, N, K, A, lda, B, ldb, C, ldc, c_dtype, bias, act, accumulate);
+        return;
+    }
+    const float* Ak = A;
+    const float* Bk = B;
+    i64 lak = lda, lbk = ldb;
+    if (copy) {
+        const size_t na = ta ? (size_t)M * K : 0, nb = !tb ? (size_t)N * K : 0;
+        Carver cv(c->work_for(Carver::need({na * 4, nb * 4})));
+        if (ta) {
+            float* t = cv.take<float>(na);
+            transpose_f32(c, A, K, M, lda, t);  // A [K, M] -> [M, K]
+            Ak = t;
+            lak = K;
+        }
+        if (!tb) {
+            float* t = cv.take<float>(nb);
+            transpose_f32(c, B, K, N, ldb, t);  // B [K, N] -> [N, K]
+            Bk = t;
+            lbk = K;
+        }
+    }
+    TcArgs a{};
+    a.mode = 0;
+    a.groups = 1;
+    a.M = (int)M;
+    a.N = (int)N;
+    a.K = (int)K;
+    a.C = C;
+    a.ldc = ldc;
+    a.c_bf16 = c_dtype == CATNN_BF16;
+    a.vec_ok = aligned16(C) && ((ldc * (a.c_bf16 ? 2 : 4)) % 16 == 0);
+    a.bias = bias;
+    a.act = act;
+    a.accumulate = accumulate ? 1 : 0;
+    const int BN = N <= 128 ? 128 : 256;
+    int tiles = cdiv(M, BM) * cdiv(N, BN);
+    run_tc(c, a, false, false, Ak, M, K, lak, Bk, N, K, lbk, tiles, tiles, K, M, true);
+}
 
 void gemm_bf16_tc(Context* c, bool ta, bool tb, i64 M, i64 N, i64 K, const bf16* A, i64 lda, const bf16* B, i64 ldb,
                   void* C, i64 ldc, int c_dtype, const float* bias, int act, bool accumulate, const float* resid) {

@@ -287,4 +287,135 @@ void ep_permute_bwd(Context* c, const PeerTab& dxp, const int32_t* idx, const in
     launched(c);
 }
 
+// ------------------------------------------------------------ vocab-sharded embedding
+// One CTA per token: the row comes from its owner's table over NVLink, 16 bytes per thread.
+__global__ void __launch_bounds__(256) k_ep_embed(const uint32_t* __restrict__ ids, PeerTab table, i64 vocab, i64 vs,
+                                                  i64 hidden, float* __restrict__ y, int* err) {
+    const i64 t = blockIdx.x;
+    const uint32_t id = ids[t];
+    const bool bad = (i64)id >= vocab;
+    if (bad && threadIdx.x == 0 && err) atomicExch(err, 1);
+    float* yr = y + t * hidden;
+    const float* row = bad ? nullptr : (const float*)table.p[id / vs] + (i64)id * hidden;
+    if ((hidden & 3) == 0) {
+        for (i64 i = threadIdx.x; i < hidden / 4; i += blockDim.x)
+            ((float4*)yr)[i] = bad ? make_float4(0.f, 0.f, 0.f, 0.f) : ((const float4*)row)[i];
+    } else {
+        for (i64 i = threadIdx.x; i < hidden; i += blockDim.x) yr[i] = bad ? 0.f : row[i];
+    }
+}
+
+// Keys (id - v0) * n + t of the global tokens t whose id lies in [v0, v1),
+// sorted ascending (by id, then token): one CTA compacts them in token
+// order (block scan) and bitonic-sorts the compacted list in shared memory.
+// Keys are unique, so the order is total. *m = number of keys.
+__global__ void __launch_bounds__(1024) k_ep_embed_keys(const uint32_t* __restrict__ ids, i64 n, i64 v0, i64 v1,
+                                                        uint32_t* __restrict__ keys, int* __restrict__ m) {
+    extern __shared__ uint32_t sk[];
+    __shared__ int wsum[32];
+    const int tid = threadIdx.x, nt = blockDim.x, lane = tid & 31, w = tid >> 5;
+    const i64 per = (n + nt - 1) / nt;
+    const i64 t0 = (i64)tid * per, t1 = t0 + per < n ? t0 + per : n;
+    int cnt = 0;
+    for (i64 t = t0; t < t1; ++t) cnt += (i64)ids[t] >= v0 && (i64)ids[t] < v1;
+    int x = cnt;
+    for (int o = 1; o < 32; o <<= 1) {
+        int y = __shfl_up_sync(0xffffffffu, x, o);
+        if (lane >= o) x += y;
+    }
+    if (lane == 31) wsum[w] = x;
+    __syncthreads();
+    if (w == 0) {
+        int sum = lane < (nt >> 5) ? wsum[lane] : 0;
+        for (int o = 1; o < 32; o <<= 1) {
+            int y = __shfl_up_sync(0xffffffffu, sum, o);
+            if (lane >= o) sum += y;
+        }
+        wsum[lane] = sum;  // inclusive prefix over warps
+    }
+    __syncthreads();
+    const int total = wsum[31];
+    int pos = x - cnt + (w > 0 ? wsum[w - 1] : 0);
+    for (i64 t = t0; t < t1; ++t) {
+        const i64 id = ids[t];
+        if (id >= v0 && id < v1) sk[pos++] = (uint32_t)((id - v0) * n + t);
+    }
+    int npow = 1;
+    while (npow < total) npow <<= 1;
+    __syncthreads();
+    for (int i = total + tid; i < npow; i += nt) sk[i] = 0xFFFFFFFFu;
+    __syncthreads();
+    for (int k = 2; k <= npow; k <<= 1)
+        for (int j = k >> 1; j > 0; j >>= 1) {
+            for (int i = tid; i < npow; i += nt) {
+                int p = i ^ j;
+                if (p > i) {
+                    uint32_t a = sk[i], b = sk[p];
+                    if ((a > b) == ((i & k) == 0)) {
+                        sk[i] = b;
+                        sk[p] = a;
+                    }
+                }
+            }
+            __syncthreads();
+        }
+    for (int i = tid; i < total; i += nt) keys[i] = sk[i];
+    if (tid == 0) *m = total;
+}
+
+// A CTA that starts a run of equal ids sums that run's dy rows in token
+// order onto zero (the one-GPU k_embed_bwd_runs arithmetic); token t's row
+// is row t % tpr of rank t / tpr's dy.
+__global__ void __launch_bounds__(256) k_ep_embed_bwd_runs(const uint32_t* __restrict__ keys, const int* __restrict__ m,
+                                                           i64 n, i64 tpr, PeerTab dy, float* __restrict__ dw_own,
+                                                           i64 hidden) {
+    const i64 cnt = *m;
+    for (i64 i = blockIdx.x; i < cnt; i += gridDim.x) {
+        const uint32_t id = keys[i] / (uint32_t)n;
+        if (i > 0 && keys[i - 1] / (uint32_t)n == id) continue;
+        i64 end = i + 1;
+        while (end < cnt && keys[end] / (uint32_t)n == id) ++end;
+        for (i64 col = threadIdx.x; col < hidden; col += blockDim.x) {
+            float s = 0.f;
+            for (i64 r = i; r < end; ++r) {
+                const i64 t = keys[r] % (uint32_t)n;
+                s = __fadd_rn(s, ((const float*)dy.p[t / tpr])[(t % tpr) * hidden + col]);
+            }
+            dw_own[(i64)id * hidden + col] = s;
+        }
+    }
+}
+
+void ep_embedding_fwd(Context* c, const uint32_t* ids, i64 n, const PeerTab& table, i64 vocab, i64 rows_per_rank,
+                      i64 hidden, float* y, int* err) {
+    if (n <= 0 || hidden <= 0) return;
+    k_ep_embed<<<(unsigned)n, 256, 0, c->stream>>>(ids, table, vocab, rows_per_rank, hidden, y, err);
+    launched(c);
+}
+
+void ep_embedding_bwd(Context* c, const uint32_t* ids_global, i64 n_global, i64 tokens_per_rank, const PeerTab& dy,
+                      i64 v0, i64 v1, i64 hidden, float* dw) {
+    if (v1 <= v0 || hidden <= 0) return;
+    float* own = dw + v0 * hidden;
+    CUDA_OK(cudaMemsetAsync(own, 0, (size_t)(v1 - v0) * hidden * 4, c->stream));
+    if (n_global <= 0) return;
+    CATNN_CHECK(n_global <= 32768, CATNN_ERR_UNSUPPORTED, "embedding backward: at most 32768 tokens per step");
+    CATNN_CHECK((unsigned long long)(v1 - v0) * (unsigned long long)n_global < 0xFFFFFFFFull, CATNN_ERR_UNSUPPORTED,
+                "embedding backward: rows * tokens must fit in 32 bits");
+    char* scr = (char*)c->scratch_for((size_t)n_global * 4 + 256);
+    uint32_t* keys = (uint32_t*)scr;
+    int* m = (int*)(scr + (size_t)n_global * 4);
+    static bool attr[64] = {false};
+    if (!attr[c->device]) {
+        CUDA_OK(cudaFuncSetAttribute(k_ep_embed_keys, cudaFuncAttributeMaxDynamicSharedMemorySize, 32768 * 4));
+        attr[c->device] = true;
+    }
+    i64 npow = 1;
+    while (npow < n_global) npow <<= 1;
+    k_ep_embed_keys<<<1, 1024, (size_t)npow * 4, c->stream>>>(ids_global, n_global, v0, v1, keys, m);
+    const int grid = (int)std::min<i64>(n_global, (i64)c->sm_count * 8);
+    k_ep_embed_bwd_runs<<<grid, 256, 0, c->stream>>>(keys, m, n_global, tokens_per_rank, dy, own, hidden);
+    launched(c, 2);
+}
+
 }  // namespace catnn

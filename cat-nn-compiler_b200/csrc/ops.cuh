@@ -94,6 +94,9 @@ void gemm_grouped_wgrad_bf16_tc(Context* c, i64 total_rows, i64 N, i64 K, int gr
                                 const int32_t* offsets, const bf16* A, i64 lda, const bf16* D, i64 ldd,
                                 void* dB, i64 strideB, int c_dtype, bool accumulate);
 // fp32 grouped GEMM for the parity path (same conventions).
+// fp32 operands on the tensor cores as TF32 (gemm_tc.cu).
+void gemm_tf32_tc(Context* c, bool ta, bool tb, i64 M, i64 N, i64 K, const float* A, i64 lda, const float* B, i64 ldb,
+                  void* C, i64 ldc, int c_dtype, const float* bias, int act, bool accumulate);
 // The expert GEMMs with the SwiGLU fused into the epilogue (gemm_tc.cu):
 // W13 / AC / DAC use the 128-column interleaved [a | c] layout.
 void gemm_grouped_swiglu_fwd_tc(Context* c, i64 total_rows, i64 F, i64 K, int groups, const int32_t* offsets,

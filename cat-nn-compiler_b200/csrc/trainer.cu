@@ -9,6 +9,7 @@
 //  - expert rows padded to 128 so every expert GEMM tile is single-expert;
 //  - weight gradients land in fp32 directly from the GEMM epilogue.
 #include <cstring>
+#include <string>
 
 #include "moe_ep.cuh"
 #include "trainer.cuh"
@@ -24,18 +25,38 @@ void MoeTrainer::plan_params() {
         o += al128(n);
         return r;
     };
-    o_embed = take(V * d);
+    // a sharded range starts and ends on a multiple of world*128 elements:
+    // its chunks are equal and 512-byte aligned
+    const i64 W = world;
+    auto pad = [&]() { o = (o + W * 128 - 1) / (W * 128) * (W * 128); };
+    Vs = (V + W - 1) / W;
+    v0 = std::min<i64>(V, rank * Vs);
+    v1 = std::min<i64>(V, v0 + Vs);
+    o_embed = take(W * Vs * d);
     lo.resize(L);
+    lb.resize(L);
     for (i64 l = 0; l < L; ++l) {
+        lb[l].s_off = o;
         lo[l].rms_attn = take(d);
-        lo[l].wqkv = take(d * qkvd);
-        lo[l].wo = take(qd * d);
         lo[l].rms_moe = take(d);
         lo[l].gate = take(d * E);
+        lb[l].s_len = o - lb[l].s_off;
+        pad();
+        lb[l].b_off = o;
+        lo[l].wqkv = take(d * qkvd);
+        lo[l].wo = take(qd * d);
+        pad();
+        lb[l].b_len = o - lb[l].b_off;
     }
+    fin.s_off = o;
     o_final = take(d);
-    o_lm = take(V * d);
     o_loss = take(1);
+    fin.s_len = o - fin.s_off;
+    pad();
+    fin.b_off = o;
+    o_lm = take(V * d);
+    pad();
+    fin.b_len = o - fin.b_off;
     n_rep = o;
     for (i64 l = 0; l < L; ++l) {
         lo[l].w13 = take(El * d * 2 * F);
@@ -216,7 +237,13 @@ void MoeTrainer::alloc() {
     CUDA_OK(cudaMalloc(&d12, 2 * sizeof(float)));
     act_bytes = tot;
     if (ep) {
-        // every buffer a peer reads or writes lives in act_block: map it once
+        // peers read the embedding rows this rank owns: map the parameter block
+        CUDA_OK(cudaStreamSynchronize(c->stream));
+        comm->map(param_block, ptot);
+        map_pid = (int)comm->maps.size() - 1;
+        ev_g.assign(L + 1, nullptr);
+        for (auto& ev : ev_g) CUDA_OK(cudaEventCreateWithFlags(&ev, cudaEventDisableTiming));
+        // every activation buffer a peer reads or writes lives in act_block: map it once
         CUDA_OK(cudaMemsetAsync(act_block, 0, tot, c->stream));
         CUDA_OK(cudaStreamSynchronize(c->stream));
         comm->map(act_block, tot);
@@ -231,24 +258,37 @@ PeerTab MoeTrainer::tab(Q* local) const {
     return t;
 }
 
+template <typename Q>
+PeerTab MoeTrainer::ptab(Q* local) const {
+    PeerTab t{};
+    for (int p = 0; p < world; ++p) t.p[p] = (void*)comm->at(comm->maps[map_pid], p, (char*)local);
+    return t;
+}
+
 void MoeTrainer::release() {
-    if (ep && map_id >= 0 && comm) {
+    if (ep && (map_id >= 0 || map_pid >= 0) && comm) {
         // close this rank's mappings of the peers' arenas; only when every
         // rank has done so may any rank free its own (collective)
         cudaStreamSynchronize(c->stream);
-        Comm::Mapped& m = comm->maps[map_id];
-        for (int p = 0; p < world; ++p)
-            if (p != rank && m.base[p]) {
-                cudaIpcCloseMemHandle(m.base[p]);
-                m.base[p] = nullptr;
-            }
+        for (int id : {map_id, map_pid}) {
+            if (id < 0) continue;
+            Comm::Mapped& m = comm->maps[id];
+            for (int p = 0; p < world; ++p)
+                if (p != rank && m.base[p]) {
+                    cudaIpcCloseMemHandle(m.base[p]);
+                    m.base[p] = nullptr;
+                }
+        }
         try {
             comm->barrier();
         } catch (...) {
         }
         cudaStreamSynchronize(c->stream);
-        map_id = -1;
+        map_id = map_pid = -1;
     }
+    for (auto& ev : ev_g)
+        if (ev) cudaEventDestroy(ev);
+    ev_g.clear();
     drop_graphs();
     if (gs) {
         cudaStreamSynchronize(gs);
@@ -259,6 +299,8 @@ void MoeTrainer::release() {
     }
     if (d12) cudaFree(d12);
     d12 = nullptr;
+    if (stamps) cudaFree(stamps);
+    stamps = nullptr;
     if (us) {
         cudaStreamSynchronize(us);
         cudaEventDestroy(ev_u);
@@ -281,6 +323,20 @@ __global__ void k_next_token(const uint32_t* __restrict__ tok, uint32_t* __restr
                              i64 vocab) {
     i64 i = blockIdx.x * (i64)blockDim.x + threadIdx.x;
     if (i < m) tg[i] = tok[(off + i + 1) % n] % (uint32_t)vocab;
+}
+
+// The device clock (ns) at this point of the stream.
+__global__ void k_stamp(unsigned long long* out) {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    *out = t;
+}
+
+void MoeTrainer::stamp(const char* name) {
+    if (!prof || (int)stamp_names.size() >= MAX_STAMPS) return;
+    k_stamp<<<1, 1, 0, c->stream>>>(stamps + stamp_names.size());
+    launched(c);
+    stamp_names.push_back(name);
 }
 
 // Expert GEMM over the sorted rows (bf16: tcgen05 grouped; fp32: CUDA cores).
@@ -309,7 +365,9 @@ void MoeTrainer::forward() {
     int* err = c->status + 10;
     k_next_token<<<cdiv(T, 256), 256, 0, c->stream>>>(tokens, targets, tok_off, T, Tg, V);
     launched(c);
-    embedding_fwd(c, tokens + tok_off, T, P + o_embed, V, d, acts[0].x_in, CATNN_F32, err);
+    if (ep) ep_embedding_fwd(c, tokens + tok_off, T, ptab(P + o_embed), V, Vs, d, acts[0].x_in, err);
+    else embedding_fwd(c, tokens + tok_off, T, P + o_embed, V, d, acts[0].x_in, CATNN_F32, err);
+    stamp("embedding");
     const int align = dt == CATNN_BF16 ? 128 : 1;
     for (i64 l = 0; l < L; ++l) {
         Act& a = acts[l];
@@ -325,6 +383,7 @@ void MoeTrainer::forward() {
         attention_fwd(c, qkv, qkv + qd * e, qkv + (qd + kd) * e, a.ctx, a.lse, B, S, H, Hkv, hd, true, window, dt, qkvd,
                       qkvd);
         gemm(c, false, false, T, d, qd, a.ctx, qd, W(q.wo), d, a.x_mid, d, dt, CATNN_F32, nullptr, 0, false, a.x_in);
+        stamp("fwd attention");
         // MoE half: x_out = x_mid + moe(rmsnorm(x_mid))   (moe.rs:317-319)
         // The router runs in fp32 on every path (fp32 normalized input, fp32
         // master gate): top-k decisions then match the reference's f32 logits
@@ -371,6 +430,7 @@ void MoeTrainer::forward() {
             // weighted sum read from the owners' expert outputs
             ep_combine(c, tab(a.yp), a.idx, a.dest, a.w, T, (int)K, d, (int)El, world, cap, x_out, a.x_mid, dt);
         }
+        stamp("fwd moe");
     }
     // final norm, LM head, fused cross-entropy (dlogits overwrite logits)
     rmsnorm_fwd_mixed(c, x_last, CATNN_F32, P + o_final, xf, dt, T, d, eps);
@@ -378,6 +438,7 @@ void MoeTrainer::forward() {
     // mean over the GLOBAL token count: the ranks' gradients then sum to the
     // one-GPU gradient, and so do their losses
     xent_fwdbwd(c, lg, targets, T, V, loss, lg, dt, c->status + 9, Tg);
+    stamp("lm head + loss");
 }
 
 void MoeTrainer::backward() {
@@ -386,15 +447,11 @@ void MoeTrainer::backward() {
     gemm(c, false, false, T, d, V, lg, V, W(o_lm), d, dxf, d, dt, dt, nullptr, 0, false);
     gemm(c, true, false, V, d, T, lg, V, xf, d, G + o_lm, d, dt, CATNN_F32, nullptr, 0, false);
     rmsnorm_bwd_mixed(c, x_last, P + o_final, dxf, dt, nullptr, dx, nullptr, dt, G + o_final, false, T, d, eps);
-    if (ep) {
-        // the loss rides in the gradient slot o_loss; final norm, LM head and
-        // loss are summed over ranks while the layers' adjoints run
-        CUDA_OK(cudaMemcpyAsync(G + o_loss, loss, 4, cudaMemcpyDeviceToDevice, c->stream));
-        comm->allreduce_overlapped(G + o_final, n_rep - o_final);
-        update_after_comm(o_final, n_rep - o_final);
-    } else {
-        update_after_main(o_final, n_rep - o_final);
-    }
+    stamp("bwd lm head");
+    // the loss rides in the gradient slot o_loss (summed over ranks with the
+    // final norm's gradient while the layers' adjoints run)
+    if (ep) CUDA_OK(cudaMemcpyAsync(G + o_loss, loss, 4, cudaMemcpyDeviceToDevice, c->stream));
+    post_bucket(fin, (int)L);
     for (i64 l = L - 1; l >= 0; --l) {
         Act& a = acts[l];
         const LayerOff& q = lo[l];
@@ -435,6 +492,7 @@ void MoeTrainer::backward() {
         // residual around the MoE: dx_mid = dx + rmsnorm'(dxm)   (train.rs:327-330)
         rmsnorm_bwd_mixed(c, a.x_mid, P + q.rms_moe, dxm, CATNN_F32, dx, dxmid, dxmid_lp, dt, G + q.rms_moe, false, T, d,
                           eps);
+        stamp("bwd moe");
         // attention adjoint (adjoint.rs:287-439)
         gemm(c, false, true, T, qd, d, dxmid_lp, d, W(q.wo), d, dctx, qd, dt, dt, nullptr, 0, false);
         gemm(c, true, false, qd, d, T, a.ctx, qd, dxmid_lp, d, G + q.wo, d, dt, CATNN_F32, nullptr, 0, false);
@@ -445,23 +503,60 @@ void MoeTrainer::backward() {
         gemm(c, true, false, d, qkvd, T, a.xn, d, dqkv, qkvd, G + q.wqkv, qkvd, dt, CATNN_F32, nullptr, 0, false);
         // residual around attention: dx_in = dx_mid + rmsnorm'(dxn)   (train.rs:348-351)
         rmsnorm_bwd_mixed(c, a.x_in, P + q.rms_attn, dxn, dt, dxmid, dx, nullptr, dt, G + q.rms_attn, false, T, d, eps);
-        // this layer's replicated gradients [rms_attn .. gate] and its experts are final
-        const i64 rep = q.gate + d * E - q.rms_attn;
-        if (ep) {
-            comm->allreduce_overlapped(G + q.rms_attn, rep);
-            update_after_comm(q.rms_attn, rep);
-        } else {
-            update_after_main(q.rms_attn, rep);
-        }
+        stamp("bwd attention");
+        // this layer's replicated gradients and its experts are final
+        post_bucket(lb[l], (int)l);
         update_after_main(q.w13, q.w2 + El * F * d - q.w13);
     }
-    embedding_bwd(c, tokens + tok_off, T, dx, G + o_embed, V, d, CATNN_F32);
     if (ep) {
-        comm->allreduce_overlapped(G + o_embed, V * d);
-        update_after_comm(o_embed, V * d);
+        comm->barrier();  // every rank's token rows of dx are final
+        ep_embedding_bwd(c, tokens, Tg, T, tab(dx), v0, v1, d, G + o_embed);
+        stamp("bwd embedding");
+        update_after_main(o_embed + v0 * d, (v1 - v0) * d);
+        // the last all-gather also waits for the embedding update: once it
+        // completes on any rank, every owner's rows are final for the next
+        // step's gather
+        if (upd_pending && !pend.empty()) CUDA_OK(cudaEventRecord(ev_g[pend.back()], us));
+        flush_gathers();
     } else {
+        embedding_bwd(c, tokens + tok_off, T, dx, G + o_embed, V, d, CATNN_F32);
+        stamp("bwd embedding");
         update_after_main(o_embed, V * d);
     }
+}
+
+void MoeTrainer::post_bucket(const Bucket& b, int id) {
+    if (!ep) {
+        update_after_main(b.s_off, b.b_off + b.b_len - b.s_off);
+        return;
+    }
+    comm->allreduce_overlapped(G + b.s_off, b.s_len);
+    update_after_comm(b.s_off, b.s_len);
+    comm->reduce_scatter_overlapped(G + b.b_off, b.b_len);
+    const i64 chunk = b.b_len / world;
+    update_after_comm(b.b_off + rank * chunk, chunk);
+    // the previous bucket's all-gather queues behind this reduce-scatter:
+    // its chunk's update has had the time in between
+    flush_gathers();
+    if (upd_pending) {
+        CUDA_OK(cudaEventRecord(ev_g[id], us));
+        pend.push_back(id);
+    }
+}
+
+void MoeTrainer::flush_gathers() {
+    for (int id : pend) {
+        const Bucket& b = id == (int)L ? fin : lb[id];
+        comm->allgather_after((char*)Sh + b.b_off * dsize(dt), b.b_len, dt, ev_g[id]);
+    }
+    pend.clear();
+}
+
+void MoeTrainer::gather_shards(float* base) {
+    if (!ep) return;
+    comm->allgather(base + o_embed, world * Vs * d, CATNN_F32);
+    for (i64 l = 0; l < L; ++l) comm->allgather(base + lb[l].b_off, lb[l].b_len, CATNN_F32);
+    comm->allgather(base + fin.b_off, fin.b_len, CATNN_F32);
 }
 
 // optim.rs:32-43 (SGD) / :95-119 (Adam) on parameters [off, off + n).
@@ -521,6 +616,8 @@ void MoeTrainer::join_updates() {
 }
 
 void MoeTrainer::run_body() {
+    stamp_names.clear();
+    stamp("start");
     forward();
     backward();  // enqueues the gradient allreduces and the updates bucket by bucket
     if (ep) {
@@ -529,8 +626,10 @@ void MoeTrainer::run_body() {
         // peer still reads.
         comm->join_overlapped();
         CUDA_OK(cudaMemcpyAsync(loss, G + o_loss, 4, cudaMemcpyDeviceToDevice, c->stream));
+        stamp("gradient all-reduce joined");
     }
     join_updates();
+    stamp("updates joined");
 }
 
 void MoeTrainer::drop_graphs() {
@@ -726,6 +825,45 @@ int catnn_moe_trainer_set_graphs(catnn_moe_trainer* h, int enable) {
     ABI_END
 }
 
+int catnn_moe_trainer_set_profile(catnn_moe_trainer* h, int enable) {
+    ABI_BEGIN
+    MoeTrainer& t = tr(h);
+    if (enable && !t.stamps) {
+        CUDA_OK(cudaMalloc(&t.stamps, MoeTrainer::MAX_STAMPS * sizeof(unsigned long long)));
+        CUDA_OK(cudaMemsetAsync(t.stamps, 0, MoeTrainer::MAX_STAMPS * sizeof(unsigned long long), t.c->stream));
+    }
+    if ((enable != 0) != t.prof) {
+        // the step body changes: captured graphs no longer match it
+        if (t.gs) CUDA_OK(cudaStreamSynchronize(t.gs));
+        t.drop_graphs();
+    }
+    t.prof = enable != 0;
+    ABI_END
+}
+
+int catnn_moe_trainer_timeline(catnn_moe_trainer* h, int64_t* ns, int max, char* names, int64_t names_len, int* count) {
+    ABI_BEGIN
+    MoeTrainer& t = tr(h);
+    CATNN_CHECK(ns && names && count && max >= 0 && names_len > 0, CATNN_ERR_INVALID, "null argument");
+    CATNN_CHECK(t.stamps != nullptr, CATNN_ERR_INVALID, "profiling was never enabled on this trainer");
+    const int n = std::min<int>((int)t.stamp_names.size(), max);
+    std::vector<unsigned long long> host(MoeTrainer::MAX_STAMPS);
+    if (t.gs) CUDA_OK(cudaStreamSynchronize(t.gs));
+    CUDA_OK(cudaStreamSynchronize(t.c->stream));
+    CUDA_OK(cudaMemcpy(host.data(), t.stamps, MoeTrainer::MAX_STAMPS * sizeof(unsigned long long),
+                       cudaMemcpyDeviceToHost));
+    std::string all;
+    for (int i = 0; i < n; ++i) {
+        ns[i] = (int64_t)host[i];
+        all += t.stamp_names[i];
+        all += '\n';
+    }
+    CATNN_CHECK((int64_t)all.size() < names_len, CATNN_ERR_INVALID, "names buffer too small");
+    std::memcpy(names, all.c_str(), all.size() + 1);
+    *count = n;
+    ABI_END
+}
+
 int catnn_moe_trainer_destroy(catnn_moe_trainer* h) {
     ABI_BEGIN
     if (!h) return CATNN_OK;
@@ -756,6 +894,8 @@ int catnn_moe_trainer_set_params(catnn_moe_trainer* h, const float* packed) {
         CUDA_OK(cudaMemsetAsync(t.Vo, 0, t.n_params * 4, t.c->stream));
         t.t_step = 0;
     }
+    // peers read the embedding rows this rank owns from the next step on
+    if (t.ep) t.comm->barrier();
     ABI_END
 }
 
@@ -763,6 +903,7 @@ int catnn_moe_trainer_get_params(catnn_moe_trainer* h, float* packed) {
     ABI_BEGIN
     MoeTrainer& t = tr(h);
     CATNN_CHECK(packed != nullptr, CATNN_ERR_INVALID, "null out");
+    t.gather_shards(t.P);
     t.export_packed(t.P, packed);
     ABI_END
 }
@@ -771,6 +912,7 @@ int catnn_moe_trainer_get_grads(catnn_moe_trainer* h, float* packed) {
     ABI_BEGIN
     MoeTrainer& t = tr(h);
     CATNN_CHECK(packed != nullptr, CATNN_ERR_INVALID, "null out");
+    t.gather_shards(t.G);
     t.export_packed(t.G, packed);
     ABI_END
 }

@@ -41,8 +41,24 @@ struct MoeTrainer {
         i64 rms_attn, wqkv, wo, rms_moe, gate, w13, w2;
     };
     std::vector<LayerOff> lo;
-    // replicated parameters (and the loss slot) come first: [0, n_rep) is
-    // what the gradient allreduce sums; this rank's experts follow
+    // replicated parameters (and the loss slot) come first, [0, n_rep); this
+    // rank's experts follow. Under expert parallelism (world ranks):
+    //  - the embedding table is vocab-sharded: rank r owns rows [r*Vs, r*Vs + Vs)
+    //    (its gradient, optimizer update and authoritative copy); the forward
+    //    gathers token rows from the owners over NVLink;
+    //  - every other replicated tensor sits in a bucket (the final norm + loss
+    //    slot + LM head, and one per layer). A bucket's small part (norm and
+    //    router weights, read in fp32) is allreduced and updated on every rank;
+    //    its big part (the GEMM weights, length a multiple of world*128) is
+    //    reduce-scattered, each rank updates its chunk, and the updated
+    //    storage-dtype copy is all-gathered. The fp32 master of another rank's
+    //    chunk is then stale until get_params gathers it.
+    struct Bucket {
+        i64 s_off, s_len, b_off, b_len;
+    };
+    Bucket fin{};
+    std::vector<Bucket> lb;
+    i64 Vs = 0, v0 = 0, v1 = 0;
     i64 o_embed, o_final, o_lm, o_loss, n_rep, n_params;
     float *P = nullptr, *G = nullptr, *Mo = nullptr, *Vo = nullptr;
     void* Sh = nullptr;
@@ -70,8 +86,13 @@ struct MoeTrainer {
     size_t act_bytes = 0;
     int32_t* src1 = nullptr;  // local align-1 map's row sources (expert parallel)
     int map_id = -1;          // act_block's entry in comm->maps
+    int map_pid = -1;         // param_block's entry in comm->maps
+    std::vector<cudaEvent_t> ev_g;  // per bucket (layers, then the final one): its chunk's update is done
+    std::vector<int> pend;          // buckets whose all-gather is not yet enqueued
     template <typename Q>
-    PeerTab tab(Q* local) const;
+    PeerTab tab(Q* local) const;   // a buffer of act_block on every rank
+    template <typename Q>
+    PeerTab ptab(Q* local) const;  // a buffer of param_block on every rank
     // host staging for the host-buffer step
     uint32_t* h_tokens = nullptr;
     float* h_loss = nullptr;
@@ -100,12 +121,25 @@ struct MoeTrainer {
     bool warmed[2] = {false, false};
     uint64_t glaunch[2] = {0, 0};
     float* d12 = nullptr;  // device [2]: Adam bias-correction divisors of the running step
+    // phase timeline (catnn_moe_trainer_set_profile): device clock stamps taken
+    // on the step's stream at phase boundaries
+    static constexpr int MAX_STAMPS = 64;
+    bool prof = false;
+    unsigned long long* stamps = nullptr;  // device [MAX_STAMPS]
+    std::vector<const char*> stamp_names;
+    void stamp(const char* name);
     void run_body();
     void drop_graphs();
     void update_range(i64 off, i64 n);          // on the context's current stream
     void update_after_main(i64 off, i64 n);     // on us, after the work enqueued so far
     void update_after_comm(i64 off, i64 n);     // on us, after the last allreduce enqueued
     void join_updates();
+    // a bucket's gradients are final: sum and update them (see Bucket)
+    void post_bucket(const Bucket& b, int id);
+    void flush_gathers();
+    // expert parallel: make the fp32 master (or the gradients) whole on every
+    // rank before an export. Collective.
+    void gather_shards(float* base);
     void step(const uint32_t* tokens_dev, float* loss_dev, bool upd);
     void import_packed(const float* packed, float* dst);
     void export_packed(const float* src, float* packed);

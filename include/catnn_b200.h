@@ -50,6 +50,10 @@ extern "C" {
 
 #define CATNN_F32 0
 #define CATNN_BF16 1
+/* catnn_gemm's `dtype` only: fp32 A/B multiplied on the tensor cores as TF32
+ * (10-bit mantissas, fp32 accumulation), for callers that keep fp32
+ * storage and accept the bf16 tolerance band. */
+#define CATNN_TF32 2
 
 #define CATNN_ACT_NONE 0
 #define CATNN_ACT_RELU 1 /* cpu.rs:14 */
@@ -346,6 +350,20 @@ int catnn_moe_trainer_check(catnn_moe_trainer* t);
  * per trainer, so a graph never goes stale; disable to release the graphs.
  * On an expert-parallel trainer every rank must use the same setting. */
 int catnn_moe_trainer_set_graphs(catnn_moe_trainer* t, int enable);
+/* Phase timeline of a step, for finding where a rank's step time goes
+ * (the reference's simulated per-layer timeline, train.rs
+ * mixtral_layer_timeline_excerpt, measured instead). With profiling on, the
+ * step records the device clock (%globaltimer, ns) on its stream at each
+ * phase boundary (the start, after the embedding, after each layer's
+ * attention and MoE halves, after the loss, after each layer's MoE and
+ * attention adjoints, after the embedding gradient, after the last gradient
+ * all-reduce, after the updates). Turning it on or off drops captured step
+ * graphs. catnn_moe_trainer_timeline copies the last step's stamps (up to
+ * max) into ns and their names, separated by '\n', into names (names_len
+ * bytes); *count receives the number of stamps. Synchronizes. */
+int catnn_moe_trainer_set_profile(catnn_moe_trainer* t, int enable);
+int catnn_moe_trainer_timeline(catnn_moe_trainer* t, int64_t* ns, int max, char* names, int64_t names_len,
+                               int* count);
 
 /* ------------------------------------------------------------ multi-GPU (one node) */
 /* One rank of a group of 1..8 processes, one GPU each. The reference runs
@@ -386,14 +404,20 @@ int catnn_comm_check(catnn_comm* comm);
 /* Data-parallel + expert-parallel trainer over the ranks of comm.
  * cfg->batch is the GLOBAL batch: rank r trains sequences
  * [r*batch/world, (r+1)*batch/world) and owns experts
- * [r*experts/world, (r+1)*experts/world) of every layer; all other
- * parameters are replicated and their gradients summed over ranks (NCCL).
- * Needs batch % world == 0 and experts % world == 0. Steps take the GLOBAL
- * token array [batch*seq] on every rank and report the global mean loss;
- * set_params reads the full packed vector; get_params / get_grads write the
- * replicated parameters and this rank's experts into a full packed vector
- * and leave the other experts' entries untouched. activation() returns this
- * rank's rows. With world == 1 it is the single-GPU trainer. */
+ * [r*experts/world, (r+1)*experts/world) of every layer. The embedding
+ * table is vocab-sharded (rank r owns rows [r*ceil(vocab/world), ...): their
+ * gradient, from every rank's token rows read over NVLink, and their update);
+ * the other parameters are replicated: norm and router weights are
+ * allreduced and updated on every rank, the attention and LM-head weights
+ * are reduce-scattered, updated in chunks and their storage-dtype copy
+ * all-gathered (NCCL). Needs batch % world == 0 and experts % world == 0.
+ * Steps take the GLOBAL token array [batch*seq] on every rank and report the
+ * global mean loss; set_params reads the full packed vector; get_params /
+ * get_grads are collective (every rank calls them: they first all-gather the
+ * sharded fp32 values) and write the replicated parameters and this rank's
+ * experts into a full packed vector, leaving the other experts' entries
+ * untouched. activation() returns this rank's rows. With world == 1 it is
+ * the single-GPU trainer. */
 int catnn_moe_trainer_create_ep(catnn_ctx* ctx, const catnn_moe_config* cfg, catnn_comm* comm,
                                 catnn_moe_trainer** out);
 

@@ -411,6 +411,63 @@ def test_gemm_config2_fwd_bwd_bf16(K):
         assert float((got - ref).abs().max()) <= 2e-2 * float(ref.abs().max()), what
 
 
+U_TF32 = 2.0 ** -10  # the tensor cores read the top 19 bits of an fp32 operand
+
+
+def tf32_bound(a, b, ta, tb):
+    """Rigorous error bound of a TF32 product against the exact one: each
+    operand loses at most a relative 2^-10 to the 10-bit mantissa and the
+    fp32 accumulation of K terms at most K·2^-24, all of Σ_k |a_ik||b_kj|."""
+    A = np.abs(a.T if ta else a).astype(np.float64)
+    B = np.abs(b.T if tb else b).astype(np.float64)
+    K = A.shape[1]
+    return (2 * U_TF32 + U_TF32 ** 2 + K * 2.0 ** -24) * (A @ B)
+
+
+@pytest.mark.parametrize("ta,tb", [(False, False), (True, False), (False, True), (True, True)])
+@pytest.mark.parametrize("M,N,K", [(512, 384, 1024), (200, 136, 100), (128, 256, 4096)])
+def test_gemm_tf32_tensor_core(ta, tb, M, N, K):
+    """fp32 operands multiplied as TF32 (kind::tf32) with fp32 accumulation:
+    inside the rigorous TF32 bound and the bf16 contract band, and closer to
+    the exact product than bf16 operands would be."""
+    r = rng(7 * M + N + K + 2 * ta + tb)
+    a = (r.standard_normal((K, M) if ta else (M, K)) / np.sqrt(K)).astype(np.float32)
+    b = r.standard_normal((N, K) if tb else (K, N)).astype(np.float32)
+    ref = (a.T if ta else a).astype(np.float64) @ (b.T if tb else b).astype(np.float64)
+    got = host(ops.gemm(dev(a), dev(b), ta, tb, tf32=True))
+    err = np.abs(got - ref)
+    bound = tf32_bound(a, b, ta, tb)
+    assert (err <= bound).all(), f"tf32 ta={ta} tb={tb}: worst excess {float((err - bound).max()):.3g}"
+    close_bf16(got, ref.astype(np.float32), what=f"tf32 ta={ta} tb={tb}")
+    bf = host(ops.gemm(dev(a, torch.bfloat16), dev(b, torch.bfloat16), ta, tb, out_dtype=torch.float32))
+    assert np.sqrt(np.mean(err ** 2)) < 0.5 * np.sqrt(np.mean((bf - ref) ** 2))
+
+
+def test_gemm_tf32_bias_act_accumulate_and_small_shapes():
+    r = rng(77)
+    M, N, K = 384, 256, 192
+    a = r.standard_normal((M, K)).astype(np.float32) / 8
+    b = r.standard_normal((K, N)).astype(np.float32)
+    bias = r.standard_normal(N).astype(np.float32)
+    ref = a.astype(np.float64) @ b + bias
+    bound = tf32_bound(a, b, False, False)
+    c = host(ops.gemm(dev(a), dev(b), bias=dev(bias), act="relu", tf32=True))
+    assert (np.abs(c - np.maximum(ref, 0)) <= bound).all()
+    c0 = dev(r.standard_normal((M, N)).astype(np.float32))
+    ref2 = host(c0) + (ref - bias)
+    ops.gemm(dev(a), dev(b), out=c0, accumulate=True, tf32=True)
+    assert (np.abs(host(c0) - ref2) <= bound + 1e-6 * np.abs(ref2)).all()
+    cb = ops.gemm(dev(a), dev(b), out_dtype=torch.bfloat16, tf32=True)
+    close_bf16(cb, (ref - bias).astype(np.float32), what="tf32 bf16 out")
+    # N < 16 and an unaligned leading dimension take the fp32 CUDA-core GEMM
+    for m, k, n in ((64, 256, 10), (7, 13, 5)):
+        x = r.standard_normal((m, k)).astype(np.float32)
+        w = r.standard_normal((k, n)).astype(np.float32)
+        close_f32(ops.gemm(dev(x), dev(w), tf32=True), O.matmul_seq(x, w), what=f"tf32 small {m}x{k}x{n}")
+    with pytest.raises(Exception):
+        ops.gemm(dev(a, torch.bfloat16), dev(b, torch.bfloat16), tf32=True)
+
+
 @pytest.mark.parametrize("tb", [False, True])
 def test_grouped_gemm_bf16_split_k(tb):
     """Two experts of 256 rows against K = 4096: M-grouped tiles cut in K."""

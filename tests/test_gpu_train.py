@@ -246,3 +246,39 @@ def test_graph_replay_matches_eager():
     b.check()
     a.close()
     b.close()
+
+
+def test_step_timeline_phases():
+    """catnn_moe_trainer_set_profile / _timeline: the device-clock stamps of a
+    profiled step name every phase (per layer), are non-decreasing, and their
+    sum is the step's device time; with graph replay the stamps are replayed
+    too; profiling off leaves the step's results unchanged."""
+    cfg = MoeConfig.make(1024, 256, 512, 2, 4, 4, 8, 2, batch=2, seq=128, rope_theta=1e4, dtype=torch.bfloat16,
+                         optimizer="adam", lr=1e-3)
+    P = init_params(cfg, 8)
+    tok = torch.as_tensor(np.random.default_rng(8).integers(0, 1024, 256).astype(np.int32)).cuda()
+    a, b = MoeTrainer(cfg), MoeTrainer(cfg)
+    a.set_params(P)
+    b.set_params(P)
+    b.set_graphs(True)
+    b.set_profile(True)
+    la, lb = torch.zeros(1, device="cuda"), torch.zeros(1, device="cuda")
+    for _ in range(4):  # eager, eager warm-up, capture, replay
+        a.step(tok, update=True, loss_out=la)
+        b.step(tok, update=True, loss_out=lb)
+        torch.cuda.synchronize()
+        assert torch.equal(la, lb)
+    phases = b.timeline()
+    names = [n for n, _ in phases]
+    assert names[0] == "embedding" and names[-1] == "updates joined"
+    assert names.count("fwd attention") == 2 and names.count("bwd moe") == 2
+    assert all(ms >= 0 for _, ms in phases)
+    total = sum(ms for _, ms in phases)
+    assert 0 < total < 1000
+    b.set_profile(False)
+    b.step(tok, update=True, loss_out=lb)
+    a.step(tok, update=True, loss_out=la)
+    torch.cuda.synchronize()
+    assert torch.equal(la, lb) and torch.equal(a.params(), b.params())
+    a.close()
+    b.close()
