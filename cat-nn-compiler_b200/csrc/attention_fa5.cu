@@ -29,7 +29,7 @@ constexpr uint32_t Q_BYTES = BQ * HD * 2;        // 16 KB
 constexpr uint32_t KV_BYTES = BKV * HD * 2;      // 8 KB each for K and V
 constexpr uint32_t STAGE_BYTES = 2 * KV_BYTES;   // K then V
 constexpr uint32_t P_BYTES = BQ * BKV * 2;       // 16 KB (one 64-key atom)
-constexpr uint32_t TMEM_COLS = 256;              // S: 2 x 64, O: 2 x 64 (two CTAs per SM)
+constexpr uint32_t TMEM_COLS = 256;              // S: 2 x 64, O: 64 (two CTAs per SM)
 constexpr uint32_t S_COL = 0, O_COL = 128;
 constexpr size_t SMEM = Q_BYTES + ST * STAGE_BYTES + 2 * P_BYTES + 1024 + 512;
 
@@ -57,6 +57,51 @@ __device__ __forceinline__ int klo(const Args& a, int i) {
 }
 __device__ __forceinline__ int khi(const Args& a, int i) { return a.causal ? i : a.s - 1; }
 
+// Packed fp32 pairs (sm_100 f32x2 instructions: two lanes of work per issue slot).
+__device__ __forceinline__ unsigned long long pk2(float a, float b) {
+    return ((unsigned long long)__float_as_uint(b) << 32) | __float_as_uint(a);
+}
+__device__ __forceinline__ unsigned long long fma2(unsigned long long a, unsigned long long b, unsigned long long c) {
+    unsigned long long d;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+    return d;
+}
+__device__ __forceinline__ unsigned long long add2(unsigned long long a, unsigned long long b) {
+    unsigned long long d;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+__device__ __forceinline__ float lo2(unsigned long long v) { return __uint_as_float((uint32_t)v); }
+__device__ __forceinline__ float hi2(unsigned long long v) { return __uint_as_float((uint32_t)(v >> 32)); }
+__device__ __forceinline__ float max3(float a, float b, float c) {
+    float d;
+    asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+    return d;
+}
+
+// 2^x on the FMA pipe, for a share of the exponentials so that the MUFU unit
+// (16 results per clock per SM, the forward's bound at head_dim 64) does
+// not carry all of them. Round-to-nearest split x = n + f (adding 1.5·2^23
+// leaves n in the low mantissa bits), f in [-0.5, 0.5], 2^f by a degree-3
+// polynomial fitted here to minimise the relative error on that interval
+// (at most 7.5e-5, against bf16's 2^-9 rounding of P), and 2^n added into
+// the exponent field. x is clamped at -126 (the result is then at most
+// 2^-126: subnormal or the least normal, i.e. zero to every later use).
+__device__ __forceinline__ float ex2_fma(float x) {
+    constexpr float C0 = 0.99992806f, C1 = 0.69326097f, C2 = 0.24261113f, C3 = 0.055171665f;
+    x = fmaxf(x, -126.f);
+    const float t = x + 12582912.f;
+    const float f = x - (t - 12582912.f);
+    const float p = fmaf(fmaf(fmaf(C3, f, C2), f, C1), f, C0);
+    return __int_as_float(__float_as_int(p) + ((__float_as_int(t) - 0x4B400000) << 23));
+}
+
+// The running max a row's exponentials are taken against is only moved up
+// (and O, l rescaled) when a block's max exceeds it by more than this (log2
+// units): P then stays below 2^8, and the rescale — a TMEM read-modify-write
+// of the row's O — is rare after the first blocks.
+constexpr float RESCALE_LOG2 = 8.f;
+
 __global__ void __launch_bounds__(NT, 2)
     k_fwd(const __grid_constant__ CUtensorMap mq, const __grid_constant__ CUtensorMap mk,
           const __grid_constant__ CUtensorMap mv, Args a) {
@@ -72,9 +117,8 @@ __global__ void __launch_bounds__(NT, 2)
     uint64_t* s_full = kv_empty + ST;
     uint64_t* s_free = s_full + 2;
     uint64_t* p_full = s_free + 2;
-    uint64_t* o_full = p_full + 2;
-    uint64_t* o_free = o_full + 2;
-    uint64_t* drain = o_free + 2;
+    uint64_t* o_done = p_full + 2;  // P_j·V_j accumulated into O (and P buffer j&1 read)
+    uint64_t* drain = o_done + 2;
     uint32_t* tmem_slot = (uint32_t*)(drain + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -96,8 +140,7 @@ __global__ void __launch_bounds__(NT, 2)
             tc::mbar_init(&s_full[i], 1);
             tc::mbar_init(&s_free[i], 4);
             tc::mbar_init(&p_full[i], 4);
-            tc::mbar_init(&o_full[i], 1);
-            tc::mbar_init(&o_free[i], 4);
+            tc::mbar_init(&o_done[i], 1);
         }
         tc::mbar_init(drain, 1);
         tc::fence_mbar_init();
@@ -145,7 +188,7 @@ __global__ void __launch_bounds__(NT, 2)
         if (lane == 0) {
             // ---------------- MMA issuer
             constexpr uint32_t IDS = tc::idesc_bf16(BQ, BKV, false, false);  // S = Q·Kᵀ (K-major both)
-            constexpr uint32_t IDO = tc::idesc_bf16(BQ, HD, false, true);    // O = P·V (V MN-major)
+            constexpr uint32_t IDO = tc::idesc_bf16(BQ, HD, false, true);    // O += P·V (V MN-major)
             bool ok = tc::mbar_wait(q_full, 0, a.status, 4);
             const uint32_t aq = tc::smem_u32(sQ);
             auto issue_s = [&](int j) -> bool {
@@ -168,11 +211,8 @@ __global__ void __launch_bounds__(NT, 2)
                     break;
                 }
                 const int st = j % ST, pb = j & 1;
+                // P_j is in shared memory and O holds the (rescaled) blocks before j
                 if (!tc::mbar_wait(&p_full[pb], (j >> 1) & 1, a.status, 4)) {
-                    ok = false;
-                    break;
-                }
-                if (!tc::mbar_wait(&o_free[pb], ((j >> 1) & 1) ^ 1, a.status, 4)) {
                     ok = false;
                     break;
                 }
@@ -181,9 +221,9 @@ __global__ void __launch_bounds__(NT, 2)
                 const uint32_t bv = tc::smem_u32(sKV + st * STAGE_BYTES + KV_BYTES);
 #pragma unroll
                 for (int kk = 0; kk < BKV / 16; ++kk)
-                    tc::mma_bf16(tmem + O_COL + pb * HD, tc::sdesc(ap + kk * 32, 16, 1024),
-                                 tc::sdesc(bv + kk * 2048, 8192, 1024), IDO, kk != 0);
-                tc::mma_commit(&o_full[pb]);
+                    tc::mma_bf16(tmem + O_COL, tc::sdesc(ap + kk * 32, 16, 1024), tc::sdesc(bv + kk * 2048, 8192, 1024),
+                                 IDO, (j | kk) != 0);
+                tc::mma_commit(&o_done[pb]);
                 tc::mma_commit(&kv_empty[st]);
             }
             tc::mma_commit(drain);
@@ -195,123 +235,141 @@ __global__ void __launch_bounds__(NT, 2)
         const int r = qd * 32 + lane;
         const int row = q0 + r;
         const uint32_t lane_off = (uint32_t)(qd * 32) << 16;
+        const uint32_t oa = tmem + lane_off + O_COL;
         const float sc = a.scale * LOG2E;
+        const unsigned long long sc2 = pk2(sc, sc);
         const int lo = klo(a, row), hi = min(khi(a, row), a.s - 1);
-        float o[HD];
-#pragma unroll
-        for (int i = 0; i < HD; ++i) o[i] = 0.f;
-        float m = -INFINITY, l = 0.f, alpha_prev = 1.f;
-        bool ok = true;
-        for (int j = 0; j <= nblk && ok; ++j) {
-            float alpha = 1.f;
-            if (j < nblk) {
-                const int sb = j & 1;
-                if (!tc::mbar_wait(&s_full[sb], (j >> 1) & 1, a.status, 4)) {
-                    ok = false;
-                    break;
-                }
-                tc::tc_fence_after();
-                const int k0 = (j0 + j) * BKV;
-                // masking only where some key of the block is outside [lo, hi] for some row
-                const bool full = k0 >= klo(a, min(q0 + BQ - 1, a.s - 1)) && k0 + BKV - 1 <= min(khi(a, q0), a.s - 1);
-                const uint32_t sa = tmem + lane_off + S_COL + sb * BKV;
-                // One TMEM read of the block's 64 scores per row (two loads in
-                // flight), kept in registers for both passes. Pass 1: block
-                // max in eight independent chains.
-                uint32_t v[64];
-                {
-                    uint32_t (&v0)[32] = *reinterpret_cast<uint32_t(*)[32]>(&v[0]);
-                    uint32_t (&v1)[32] = *reinterpret_cast<uint32_t(*)[32]>(&v[32]);
-                    tc::tmem_ld32(sa, v0);
-                    tc::tmem_ld32(sa + 32, v1);
-                    tc::tmem_ld_wait();
-                }
-                // S_j is in registers: the MMA may overwrite its buffer
-                tc::tc_fence_before();
-                __syncwarp();
-                if (lane == 0) tc::mbar_arrive(&s_free[sb]);
-                if (!full) {
-#pragma unroll
-                    for (int i = 0; i < 64; ++i)
-                        if (k0 + i < lo || k0 + i > hi) v[i] = __float_as_uint(-INFINITY);
-                }
-                float mxa[8];
-#pragma unroll
-                for (int u = 0; u < 8; ++u) mxa[u] = -INFINITY;
-#pragma unroll
-                for (int i = 0; i < 64; ++i) mxa[i & 7] = fmaxf(mxa[i & 7], __uint_as_float(v[i]));
-                float mx = fmaxf(fmaxf(fmaxf(mxa[0], mxa[1]), fmaxf(mxa[2], mxa[3])),
-                                 fmaxf(fmaxf(mxa[4], mxa[5]), fmaxf(mxa[6], mxa[7])));
-                // scale > 0: the max of the scaled scores is the scaled max
-                const float mn = fmaxf(m, mx * sc);
-                const float base = mn == -INFINITY ? 0.f : mn;
-                alpha = ex2(m - base);
-                m = mn;
-                float lsa[8];
-#pragma unroll
-                for (int u = 0; u < 8; ++u) lsa[u] = 0.f;
-                const uint32_t prow = tc::smem_u32(sP + sb * P_BYTES + r * 128);
-                // Pass 2: P = 2^(s·scale - max) (masked scores are -inf: P = 0),
-                // row sums, bf16 P to shared memory in 16-byte chunks
-#pragma unroll
-                for (int chunk = 0; chunk < BKV / 8; ++chunk) {
-                    float p[8];
-#pragma unroll
-                    for (int t = 0; t < 8; ++t) {
-                        p[t] = ex2(fmaf(__uint_as_float(v[chunk * 8 + t]), sc, -base));
-                        lsa[t] += p[t];
-                    }
-                    uint4 pk;
-                    __nv_bfloat162* pp = (__nv_bfloat162*)&pk;
-#pragma unroll
-                    for (int t = 0; t < 4; ++t) pp[t] = __floats2bfloat162_rn(p[2 * t], p[2 * t + 1]);
-                    asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(prow + ((chunk ^ (r & 7)) << 4)),
-                                 "r"(pk.x), "r"(pk.y), "r"(pk.z), "r"(pk.w)
-                                 : "memory");
-                }
-                const float ls = ((lsa[0] + lsa[1]) + (lsa[2] + lsa[3])) + ((lsa[4] + lsa[5]) + (lsa[6] + lsa[7]));
-                l = l * alpha + ls;
-                // P_j is in shared memory: hand it to the async proxy (the MMA)
-                tc::fence_proxy_async();
-                __syncwarp();
-                if (lane == 0) tc::mbar_arrive(&p_full[sb]);
+        // m: the max the exponentials use (log2 units, scale folded in), l: Σ P
+        float m = -INFINITY, l = 0.f;
+        bool ok = nblk > 0;
+        for (int j = 0; j < nblk && ok; ++j) {
+            const int sb = j & 1;
+            if (!tc::mbar_wait(&s_full[sb], (j >> 1) & 1, a.status, 4)) {
+                ok = false;
+                break;
             }
-            // fold in O_{j-1} = P_{j-1}·V_{j-1} (it used max m_{j-1}, so the
-            // accumulator is rescaled by alpha_{j-1} first)
-            if (j > 0) {
-                const int ob = (j - 1) & 1;
-                if (!tc::mbar_wait(&o_full[ob], ((j - 1) >> 1) & 1, a.status, 4)) {
+            tc::tc_fence_after();
+            const int k0 = (j0 + j) * BKV;
+            // masking only where some key of the block is outside [lo, hi] for some row
+            const bool full = k0 >= klo(a, min(q0 + BQ - 1, a.s - 1)) && k0 + BKV - 1 <= min(khi(a, q0), a.s - 1);
+            const uint32_t sa = tmem + lane_off + S_COL + sb * BKV;
+            uint32_t v[64];
+            {
+                uint32_t (&v0)[32] = *reinterpret_cast<uint32_t(*)[32]>(&v[0]);
+                uint32_t (&v1)[32] = *reinterpret_cast<uint32_t(*)[32]>(&v[32]);
+                tc::tmem_ld32(sa, v0);
+                tc::tmem_ld32(sa + 32, v1);
+                tc::tmem_ld_wait();
+            }
+            // S_j is in registers: the MMA may overwrite its buffer
+            tc::tc_fence_before();
+            __syncwarp();
+            if (lane == 0) tc::mbar_arrive(&s_free[sb]);
+            if (!full) {
+#pragma unroll
+                for (int i = 0; i < 64; ++i)
+                    if (k0 + i < lo || k0 + i > hi) v[i] = __float_as_uint(-INFINITY);
+            }
+            // block max: four chains of three-input maxima
+            float mxa[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+            for (int i = 0; i < 64; i += 8)
+#pragma unroll
+                for (int u = 0; u < 4; ++u) mxa[u] = max3(mxa[u], __uint_as_float(v[i + 2 * u]), __uint_as_float(v[i + 2 * u + 1]));
+            // scale > 0: the max of the scaled scores is the scaled max
+            const float mx = fmaxf(fmaxf(mxa[0], mxa[1]), fmaxf(mxa[2], mxa[3])) * sc;
+            const bool grow = m != -INFINITY && mx > m + RESCALE_LOG2;
+            if (m == -INFINITY) m = mx;  // nothing accumulated yet (O's rows, l are zero)
+            if (__any_sync(0xffffffffu, grow)) {
+                // O holds blocks < j (m != -inf implies j > 0): wait for P_{j-1}·V_{j-1}
+                // to land, then scale the row by 2^(m_old - m_new)
+                if (!tc::mbar_wait(&o_done[(j - 1) & 1], ((j - 1) >> 1) & 1, a.status, 4)) {
                     ok = false;
                     break;
                 }
                 tc::tc_fence_after();
-                const uint32_t oa = tmem + lane_off + O_COL + ob * HD;
+                const float alpha = grow ? ex2(m - mx) : 1.f;
+                if (grow) {
+                    l *= alpha;
+                    m = mx;
+                }
 #pragma unroll
                 for (int c = 0; c < HD / 32; ++c) {
-                    uint32_t v[32];
-                    tc::tmem_ld32(oa + c * 32, v);
+                    uint32_t o[32];
+                    tc::tmem_ld32(oa + c * 32, o);
                     tc::tmem_ld_wait();
 #pragma unroll
-                    for (int i = 0; i < 32; ++i) o[c * 32 + i] = o[c * 32 + i] * alpha_prev + __uint_as_float(v[i]);
+                    for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+                    tc::tmem_st32(oa + c * 32, o);
                 }
-                tc::tc_fence_before();
-                __syncwarp();
-                if (lane == 0) tc::mbar_arrive(&o_free[ob]);
+                tc::tmem_st_wait();
             }
-            alpha_prev = alpha;
-        }
-        if (ok && row < a.s) {
-            const float inv = l > 0.f ? 1.f / l : 0.f;
-            bf16* op = a.out + (seq_row + row) * (long long)(a.h * HD) + h * HD;
+            // P buffer sb was last read by P_{j-2}·V_{j-2}
+            if (j >= 2 && !tc::mbar_wait(&o_done[sb], ((j - 2) >> 1) & 1, a.status, 4)) {
+                ok = false;
+                break;
+            }
+            const float base = m == -INFINITY ? 0.f : m;
+            const unsigned long long nb2 = pk2(-base, -base);
+            unsigned long long ls2[4] = {0ull, 0ull, 0ull, 0ull};
+            const uint32_t prow = tc::smem_u32(sP + sb * P_BYTES + r * 128);
+            // P = 2^(s·scale - m) (masked scores are -inf: P = 0), row sums,
+            // bf16 P to shared memory in 16-byte chunks
 #pragma unroll
-            for (int c = 0; c < HD / 8; ++c) {
+            for (int chunk = 0; chunk < BKV / 8; ++chunk) {
+                float p[8];
+#pragma unroll
+                for (int t = 0; t < 4; ++t) {
+                    const unsigned long long x =
+                        fma2(pk2(__uint_as_float(v[chunk * 8 + 2 * t]), __uint_as_float(v[chunk * 8 + 2 * t + 1])), sc2, nb2);
+                    p[2 * t] = ex2(lo2(x));
+                    // one exponential in four on the FMA pipe
+                    p[2 * t + 1] = (t & 1) ? ex2_fma(hi2(x)) : ex2(hi2(x));
+                    ls2[t] = add2(ls2[t], pk2(p[2 * t], p[2 * t + 1]));
+                }
                 uint4 pk;
                 __nv_bfloat162* pp = (__nv_bfloat162*)&pk;
 #pragma unroll
-                for (int t = 0; t < 4; ++t) pp[t] = __floats2bfloat162_rn(o[c * 8 + 2 * t] * inv, o[c * 8 + 2 * t + 1] * inv);
-                *(uint4*)(op + c * 8) = pk;
+                for (int t = 0; t < 4; ++t) pp[t] = __floats2bfloat162_rn(p[2 * t], p[2 * t + 1]);
+                asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(prow + ((chunk ^ (r & 7)) << 4)), "r"(pk.x),
+                             "r"(pk.y), "r"(pk.z), "r"(pk.w)
+                             : "memory");
             }
-            a.lse[((long long)bi * a.h + h) * a.s + row] = l > 0.f ? (m + log2f(l)) / LOG2E : -INFINITY;
+            const unsigned long long s01 = add2(ls2[0], ls2[1]), s23 = add2(ls2[2], ls2[3]), s4 = add2(s01, s23);
+            l += lo2(s4) + hi2(s4);
+            // P_j in shared memory (generic proxy) and any O rescale (tcgen05.st) before the MMA reads them
+            tc::fence_proxy_async();
+            tc::tc_fence_before();
+            __syncwarp();
+            if (lane == 0) tc::mbar_arrive(&p_full[sb]);
+        }
+        // the last P·V has landed: O / l to global, and the natural-log lse
+        if (ok && !tc::mbar_wait(&o_done[(nblk - 1) & 1], ((nblk - 1) >> 1) & 1, a.status, 4)) ok = false;
+        if (ok) {
+            tc::tc_fence_after();
+            uint32_t o[64];
+            {
+                uint32_t (&o0)[32] = *reinterpret_cast<uint32_t(*)[32]>(&o[0]);
+                uint32_t (&o1)[32] = *reinterpret_cast<uint32_t(*)[32]>(&o[32]);
+                tc::tmem_ld32(oa, o0);
+                tc::tmem_ld32(oa + 32, o1);
+                tc::tmem_ld_wait();
+            }
+            if (row < a.s) {
+                const float inv = l > 0.f ? 1.f / l : 0.f;
+                bf16* op = a.out + (seq_row + row) * (long long)(a.h * HD) + h * HD;
+#pragma unroll
+                for (int c = 0; c < HD / 8; ++c) {
+                    uint4 pk;
+                    __nv_bfloat162* pp = (__nv_bfloat162*)&pk;
+#pragma unroll
+                    for (int t = 0; t < 4; ++t)
+                        pp[t] = __floats2bfloat162_rn(__uint_as_float(o[c * 8 + 2 * t]) * inv,
+                                                      __uint_as_float(o[c * 8 + 2 * t + 1]) * inv);
+                    *(uint4*)(op + c * 8) = pk;
+                }
+                a.lse[((long long)bi * a.h + h) * a.s + row] = l > 0.f ? (m + log2f(l)) / LOG2E : -INFINITY;
+            }
         }
     }
     tc::tc_fence_before();
