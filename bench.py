@@ -49,6 +49,8 @@ def parse():
                         "with the SwiGLU epilogues; attn: tcgen05 flash attention fwd + bwd (B8 S2048 H16 hd64); "
                         "step_small: trainer steps at config-5 widths on 2 sequences (its HBM-bound kernels); "
                         "gemm_tf32: the TF32 tensor-core GEMM at 4096^3")
+    p.add_argument("--batches", type=int, default=1,
+                   help="distinct resident token batches the steps cycle through (1: every step trains the same batch)")
     p.add_argument("--reps", type=int, default=20)
     p.add_argument("--batch", type=int, default=2, help="--kernel step_small: sequences per step (1 layer)")
     return p.parse_args()
@@ -593,7 +595,9 @@ def run_ours(args):
     P[L["final_norm"]:L["final_norm"] + h] = 1.0
     tr.set_params(P)
     gt = torch.Generator(device=f"cuda:{local}").manual_seed(cfg["seed"] + 1000)
-    tokens = torch.randint(0, cfg["vocab"], (T_global,), generator=gt, device=f"cuda:{local}", dtype=torch.int32)
+    pool = [torch.randint(0, cfg["vocab"], (T_global,), generator=gt, device=f"cuda:{local}", dtype=torch.int32)
+            for _ in range(max(args.batches, 1))]
+    tokens = pool[0]
     loss = torch.zeros(1, device=f"cuda:{local}")
     ctx = ops.context(local)
     stream = torch.cuda.current_stream(local)
@@ -609,8 +613,8 @@ def run_ours(args):
     barrier()
     tr.check()
     loss_step0 = float(loss)
-    for _ in range(args.warmup):
-        tr.step(tokens, update=True, loss_out=loss)
+    for i in range(args.warmup):
+        tr.step(pool[i % len(pool)], update=True, loss_out=loss)
     barrier()
     tr.check()
     clocks = Clocks(local)
@@ -618,8 +622,8 @@ def run_ours(args):
     barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
-    for _ in range(args.steps):
-        tr.step(tokens, update=True, loss_out=loss)
+    for i in range(args.steps):
+        tr.step(pool[i % len(pool)], update=True, loss_out=loss)
     e1.record(stream)
     barrier()
     ms = e0.elapsed_time(e1) / args.steps
@@ -635,12 +639,12 @@ def run_ours(args):
 
     # end to end through the public host-buffer call: host tokens -> device,
     # step, loss -> host, every step
-    host_tok = tokens.cpu().numpy().astype(np.uint32)
+    host_pool = [t.cpu().numpy().astype(np.uint32) for t in pool]
     barrier()
     clocks_e2e = Clocks(local)
     e0.record(stream)
-    for _ in range(args.steps):
-        tr.step_host(host_tok, update=True)
+    for i in range(args.steps):
+        tr.step_host(host_pool[i % len(host_pool)], update=True)
     e1.record(stream)
     barrier()
     e2e_ms = e0.elapsed_time(e1) / args.steps
@@ -654,11 +658,24 @@ def run_ours(args):
     # boundaries (one extra profiled step, replayed as a graph like the timed
     # ones), per phase the max over ranks
     tr.set_profile(True)
-    for _ in range(3):
-        tr.step(tokens, update=True, loss_out=loss)
+    for i in range(3):
+        tr.step(pool[i % len(pool)], update=True, loss_out=loss)
     phases = tr.timeline()
     tr.set_profile(False)
     barrier()
+    # routing balance of that last step: (token, slot) pairs per expert, summed
+    # over ranks, and the load of each rank's experts (what expert parallelism
+    # waits on at its barriers), as max / mean
+    E, K = cfg["experts"], cfg["top_k"]
+    cnt = torch.zeros(cfg["layers"], E, device=f"cuda:{local}", dtype=torch.float64)
+    for l in range(cfg["layers"]):
+        idx = torch.topk(tr.activation("router_logits", l), K, dim=1).indices
+        cnt[l] = torch.bincount(idx.flatten(), minlength=E).double()
+    if world > 1:
+        dist.all_reduce(cnt)
+    per_rank = cnt.view(cfg["layers"], world, E // world).sum(2)
+    routing = {"expert_max_over_mean": [round(float(x), 3) for x in (cnt.max(1).values / cnt.mean(1))],
+               "rank_max_over_mean": [round(float(x), 3) for x in (per_rank.max(1).values / per_rank.mean(1))]}
     if world > 1:
         every = [None] * world
         dist.all_gather_object(every, phases)
@@ -697,7 +714,8 @@ def run_ours(args):
         "scaling": "strong",
         "vs_baseline": None,
         "dtype": "bf16",
-        "data": "synthetic (token ids uniform [0,32000), weights N(0,0.02), seed 4)",
+        "data": "synthetic (token ids uniform [0,32000), weights N(0,0.02), seed 4)"
+                + (f"; {len(pool)} resident batches cycled" if len(pool) > 1 else ""),
         "config": {"workload": "config5_moe_train_step", "global_batch": cfg["global_batch"], "seq_len": cfg["seq"],
                    "tokens_per_step": T_global, "layers": 4, "d_model": 1024, "heads": 16, "experts": 8, "top_k": 2,
                    "ffn": 3584, "vocab": 32000, "optimizer": "adam (fp32 master)",
@@ -712,6 +730,7 @@ def run_ours(args):
         "model_tflops_achieved": step_flops(cfg, T_global) / (ms * 1e-3) / 1e12,
         "loss_step0": loss_step0,
         "phases": phase_breakdown,
+        "routing": routing,
         "loss_last": last_loss,
         "roofline": {"bound": "tensor", "kernel": "k_gemm_tc grouped (expert W13 forward, rows=%d, N=%d, K=%d)"
                      % (rows, 2 * F, d), "achieved": achieved, "peak": peak, "unit": "TFLOP/s",

@@ -75,27 +75,43 @@ __global__ void k_embed_bwd_runs(const uint32_t* __restrict__ keys, i64 n, const
     }
 }
 
-void embedding_bwd(Context* c, const uint32_t* ids, i64 n, const void* dy, float* dw, i64 vocab, i64 hidden, int dtype) {
-    if (vocab <= 0 || hidden <= 0) return;
-    CUDA_OK(cudaMemsetAsync(dw, 0, (size_t)vocab * hidden * 4, c->stream));
-    if (n <= 0) return;
+static void embed_bwd_check(i64 n, i64 vocab) {
     CATNN_CHECK(n <= 32768, CATNN_ERR_UNSUPPORTED, "embedding_bwd: at most 32768 tokens per call");
     CATNN_CHECK((unsigned long long)vocab * (unsigned long long)n < 0xFFFFFFFFull, CATNN_ERR_UNSUPPORTED,
                 "embedding_bwd: vocab * tokens must fit in 32 bits");
+}
+
+void embedding_bwd_keys(Context* c, const uint32_t* ids, i64 n, i64 vocab, uint32_t* keys) {
+    if (n <= 0) return;
+    embed_bwd_check(n, vocab);
     int npow = 1;
     while (npow < n) npow <<= 1;
-    uint32_t* keys = (uint32_t*)c->scratch_for((size_t)n * 4);
-    size_t smem = (size_t)npow * 4;
     static bool attr[64] = {false};
     if (!attr[c->device]) {
         CUDA_OK(cudaFuncSetAttribute(k_bitonic_keys, cudaFuncAttributeMaxDynamicSharedMemorySize, 32768 * 4));
         attr[c->device] = true;
     }
-    k_bitonic_keys<<<1, 1024, smem, c->stream>>>(ids, n, keys, npow);
+    k_bitonic_keys<<<1, 1024, (size_t)npow * 4, c->stream>>>(ids, n, keys, npow);
+    launched(c);
+}
+
+void embedding_bwd_runs(Context* c, const uint32_t* keys, i64 n, const void* dy, float* dw, i64 vocab, i64 hidden,
+                        int dtype) {
+    if (vocab <= 0 || hidden <= 0) return;
+    CUDA_OK(cudaMemsetAsync(dw, 0, (size_t)vocab * hidden * 4, c->stream));
+    if (n <= 0) return;
     int th = hidden >= 256 ? 256 : 64;
     if (dtype == CATNN_BF16) k_embed_bwd_runs<<<n, th, 0, c->stream>>>(keys, n, (const bf16*)dy, dw, hidden);
     else k_embed_bwd_runs<<<n, th, 0, c->stream>>>(keys, n, (const float*)dy, dw, hidden);
-    launched(c, 2);
+    launched(c);
+}
+
+void embedding_bwd(Context* c, const uint32_t* ids, i64 n, const void* dy, float* dw, i64 vocab, i64 hidden, int dtype) {
+    if (vocab <= 0 || hidden <= 0) return;
+    if (n > 0) embed_bwd_check(n, vocab);
+    uint32_t* keys = n > 0 ? (uint32_t*)c->scratch_for((size_t)n * 4) : nullptr;
+    embedding_bwd_keys(c, ids, n, vocab, keys);
+    embedding_bwd_runs(c, keys, n, dy, dw, vocab, hidden, dtype);
 }
 
 // ------------------------------------------------------------ RoPE

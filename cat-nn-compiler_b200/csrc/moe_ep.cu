@@ -393,18 +393,11 @@ void ep_embedding_fwd(Context* c, const uint32_t* ids, i64 n, const PeerTab& tab
     launched(c);
 }
 
-void ep_embedding_bwd(Context* c, const uint32_t* ids_global, i64 n_global, i64 tokens_per_rank, const PeerTab& dy,
-                      i64 v0, i64 v1, i64 hidden, float* dw) {
-    if (v1 <= v0 || hidden <= 0) return;
-    float* own = dw + v0 * hidden;
-    CUDA_OK(cudaMemsetAsync(own, 0, (size_t)(v1 - v0) * hidden * 4, c->stream));
+void ep_embedding_keys(Context* c, const uint32_t* ids_global, i64 n_global, i64 v0, i64 v1, uint32_t* keys, int* m) {
     if (n_global <= 0) return;
     CATNN_CHECK(n_global <= 32768, CATNN_ERR_UNSUPPORTED, "embedding backward: at most 32768 tokens per step");
-    CATNN_CHECK((unsigned long long)(v1 - v0) * (unsigned long long)n_global < 0xFFFFFFFFull, CATNN_ERR_UNSUPPORTED,
+    CATNN_CHECK((unsigned long long)(v1 - v0 + 1) * (unsigned long long)n_global < 0xFFFFFFFFull, CATNN_ERR_UNSUPPORTED,
                 "embedding backward: rows * tokens must fit in 32 bits");
-    char* scr = (char*)c->scratch_for((size_t)n_global * 4 + 256);
-    uint32_t* keys = (uint32_t*)scr;
-    int* m = (int*)(scr + (size_t)n_global * 4);
     static bool attr[64] = {false};
     if (!attr[c->device]) {
         CUDA_OK(cudaFuncSetAttribute(k_ep_embed_keys, cudaFuncAttributeMaxDynamicSharedMemorySize, 32768 * 4));
@@ -413,9 +406,18 @@ void ep_embedding_bwd(Context* c, const uint32_t* ids_global, i64 n_global, i64 
     i64 npow = 1;
     while (npow < n_global) npow <<= 1;
     k_ep_embed_keys<<<1, 1024, (size_t)npow * 4, c->stream>>>(ids_global, n_global, v0, v1, keys, m);
+    launched(c);
+}
+
+void ep_embedding_runs(Context* c, const uint32_t* keys, const int* m, i64 n_global, i64 tokens_per_rank,
+                       const PeerTab& dy, i64 v0, i64 v1, i64 hidden, float* dw) {
+    if (v1 <= v0 || hidden <= 0) return;
+    float* own = dw + v0 * hidden;
+    CUDA_OK(cudaMemsetAsync(own, 0, (size_t)(v1 - v0) * hidden * 4, c->stream));
+    if (n_global <= 0) return;
     const int grid = (int)std::min<i64>(n_global, (i64)c->sm_count * 8);
     k_ep_embed_bwd_runs<<<grid, 256, 0, c->stream>>>(keys, m, n_global, tokens_per_rank, dy, own, hidden);
-    launched(c, 2);
+    launched(c);
 }
 
 }  // namespace catnn

@@ -34,13 +34,16 @@ void ep_permute_bwd(Context* c, const PeerTab& dxp, const int32_t* idx, const in
 // copy of the whole table's address range).
 //  ep_embedding_fwd: y[t] = table.p[owner(id)][id] for this rank's n tokens,
 //    read over NVLink (ids >= vocab set *err and give zeros, as embedding_fwd);
-//  ep_embedding_bwd: for this rank's rows [v0, v1), dw[v] = the sum in global
+//  ep_embedding_keys + ep_embedding_runs: for this rank's rows [v0, v1), dw[v] = the sum in global
 //    token order of dy rows of every token with id v, dy of global token t
 //    read from rank t / tokens_per_rank (the order embedding_bwd sums in on
 //    one GPU). dw is the whole table's gradient; only rows [v0, v1) are written.
 void ep_embedding_fwd(Context* c, const uint32_t* ids, i64 n, const PeerTab& table, i64 vocab, i64 rows_per_rank,
                       i64 hidden, float* y, int* err);
-void ep_embedding_bwd(Context* c, const uint32_t* ids_global, i64 n_global, i64 tokens_per_rank, const PeerTab& dy,
-                      i64 v0, i64 v1, i64 hidden, float* dw);
+// in two launches: the keys (they depend on the ids only: keys n_global
+// uint32, *m their count) and the run sums
+void ep_embedding_keys(Context* c, const uint32_t* ids_global, i64 n_global, i64 v0, i64 v1, uint32_t* keys, int* m);
+void ep_embedding_runs(Context* c, const uint32_t* keys, const int* m, i64 n_global, i64 tokens_per_rank,
+                       const PeerTab& dy, i64 v0, i64 v1, i64 hidden, float* dw);
 
 }  // namespace catnn

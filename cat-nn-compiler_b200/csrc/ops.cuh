@@ -159,6 +159,11 @@ void embedding_fwd(Context* c, const uint32_t* ids, i64 n, const void* table, i6
                    int dtype, int* err);
 void embedding_bwd(Context* c, const uint32_t* ids, i64 n, const void* dy, float* dw, i64 vocab, i64 hidden,
                    int dtype);
+// The two halves of embedding_bwd: the sorted (id, token) keys, which depend
+// on the ids only (keys: n uint32), and the run sums from them.
+void embedding_bwd_keys(Context* c, const uint32_t* ids, i64 n, i64 vocab, uint32_t* keys);
+void embedding_bwd_runs(Context* c, const uint32_t* keys, i64 n, const void* dy, float* dw, i64 vocab, i64 hidden,
+                        int dtype);
 void rope(Context* c, void* x, i64 b, i64 s, i64 heads, i64 hd, double theta, bool inverse, int dtype,
           i64 row_stride = 0, i64 col_off = 0);
 void attention_fwd(Context* c, const void* q, const void* k, const void* v, void* o, float* lse, i64 b, i64 s,

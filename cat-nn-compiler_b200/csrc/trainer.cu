@@ -173,6 +173,7 @@ void MoeTrainer::alloc() {
         if (ep) { add(world * E * 4); add(ep_plan_len(E, El) * 4); add(T * K * 4); }
     }
     if (ep) add(T * K * 4);
+    add(Tg * 4); add(64);
     add(T * d * 4); add(T * d * e); add((size_t)T * V * e); add(Tg * 4); add(T * 4); add(64);
     add(T * d * 4); add(T * d * 4); add(T * d * 4); add(T * E * 4); add(T * K * 4);
     add(T * d * e); add(cap * d * e); add(cap * F * e); add(cap * 2 * F * e); add(cap * d * e); add(T * qkvd * e);
@@ -211,6 +212,8 @@ void MoeTrainer::alloc() {
         }
     }
     if (ep) src1 = ac.take<int32_t>(T * K);
+    emb_keys = ac.take<uint32_t>(Tg);
+    emb_m = ac.take<int>(16);
     x_last = ac.take<float>(T * d);
     xf = ac.take<char>(T * d * e);
     lg = ac.take<char>((size_t)T * V * e);
@@ -301,6 +304,11 @@ void MoeTrainer::release() {
     d12 = nullptr;
     if (stamps) cudaFree(stamps);
     stamps = nullptr;
+    if (ev_k) {
+        cudaEventDestroy(ev_k);
+        cudaEventDestroy(ev_kd);
+        ev_k = ev_kd = nullptr;
+    }
     if (us) {
         cudaStreamSynchronize(us);
         cudaEventDestroy(ev_u);
@@ -508,9 +516,10 @@ void MoeTrainer::backward() {
         post_bucket(lb[l], (int)l);
         update_after_main(q.w13, q.w2 + El * F * d - q.w13);
     }
+    CUDA_OK(cudaStreamWaitEvent(c->stream, ev_kd, 0));  // the keys formed during the forward
     if (ep) {
         comm->barrier();  // every rank's token rows of dx are final
-        ep_embedding_bwd(c, tokens, Tg, T, tab(dx), v0, v1, d, G + o_embed);
+        ep_embedding_runs(c, emb_keys, emb_m, Tg, T, tab(dx), v0, v1, d, G + o_embed);
         stamp("bwd embedding");
         update_after_main(o_embed + v0 * d, (v1 - v0) * d);
         // the last all-gather also waits for the embedding update: once it
@@ -519,7 +528,7 @@ void MoeTrainer::backward() {
         if (upd_pending && !pend.empty()) CUDA_OK(cudaEventRecord(ev_g[pend.back()], us));
         flush_gathers();
     } else {
-        embedding_bwd(c, tokens + tok_off, T, dx, G + o_embed, V, d, CATNN_F32);
+        embedding_bwd_runs(c, emb_keys, T, dx, G + o_embed, V, d, CATNN_F32);
         stamp("bwd embedding");
         update_after_main(o_embed, V * d);
     }
@@ -618,6 +627,21 @@ void MoeTrainer::join_updates() {
 void MoeTrainer::run_body() {
     stamp_names.clear();
     stamp("start");
+    // the embedding backward's key sort needs only the token ids: it runs on
+    // the update stream (idle until the first bucket's update) during the forward
+    make_update_stream(&us, &ev_u, &ev_u_done);
+    if (!ev_k) {
+        CUDA_OK(cudaEventCreateWithFlags(&ev_k, cudaEventDisableTiming));
+        CUDA_OK(cudaEventCreateWithFlags(&ev_kd, cudaEventDisableTiming));
+    }
+    CUDA_OK(cudaEventRecord(ev_k, c->stream));
+    CUDA_OK(cudaStreamWaitEvent(us, ev_k, 0));
+    {
+        OnStream on(c, us);
+        if (ep) ep_embedding_keys(c, tokens, Tg, v0, v1, emb_keys, emb_m);
+        else embedding_bwd_keys(c, tokens + tok_off, T, V, emb_keys);
+    }
+    CUDA_OK(cudaEventRecord(ev_kd, us));
     forward();
     backward();  // enqueues the gradient allreduces and the updates bucket by bucket
     if (ep) {

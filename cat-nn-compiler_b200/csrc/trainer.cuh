@@ -85,6 +85,11 @@ struct MoeTrainer {
     void* act_block = nullptr;
     size_t act_bytes = 0;
     int32_t* src1 = nullptr;  // local align-1 map's row sources (expert parallel)
+    // the embedding backward's sorted (id, token) keys: they depend on the
+    // token ids only, so they are formed on the update stream during the forward
+    uint32_t* emb_keys = nullptr;
+    int* emb_m = nullptr;
+    cudaEvent_t ev_k = nullptr, ev_kd = nullptr;
     int map_id = -1;          // act_block's entry in comm->maps
     int map_pid = -1;         // param_block's entry in comm->maps
     std::vector<cudaEvent_t> ev_g;  // per bucket (layers, then the final one): its chunk's update is done
