@@ -159,12 +159,26 @@ __global__ void __launch_bounds__(128) k_ep_unpermute_bwd(const TY* __restrict__
     const i64 i = g - (i64)s * pairs;
     const i64 t = i / k;
     const float wt = ((const float*)w_tab.p[s])[i];
-    const float* dy = (const float*)dy_tab.p[s] + t * hidden;
+    const float* __restrict__ dy = (const float*)dy_tab.p[s] + t * hidden;
     float dot = 0.f;
-    for (i64 c = lane; c < hidden; c += 32) {
-        float gv = dy[c];
-        dot += ld(yp + r * hidden + c) * gv;
-        st(dyp + r * hidden + c, __fmul_rn(gv, wt));
+    // eight of the lane's columns per round: the (remote) loads are all issued
+    // before the stores, and the sum runs over the columns in the same order
+    for (i64 c0 = lane; c0 < hidden; c0 += 32 * 8) {
+        float gv[8], yv[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+            const i64 c = c0 + 32 * u;
+            gv[u] = c < hidden ? dy[c] : 0.f;
+            yv[u] = c < hidden ? ld(yp + r * hidden + c) : 0.f;
+        }
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+            const i64 c = c0 + 32 * u;
+            if (c < hidden) {
+                dot += yv[u] * gv[u];
+                st(dyp + r * hidden + c, __fmul_rn(gv[u], wt));
+            }
+        }
     }
     dot = warp_sum(dot);
     if (lane == 0) ((float*)dw_tab.p[s])[i] = dot;

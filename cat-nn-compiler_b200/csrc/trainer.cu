@@ -422,10 +422,12 @@ void MoeTrainer::forward() {
             ep_publish_counts(c, a.counts, tab(a.cnt_all), rank, world, (int)E);
             comm->barrier();
             ep_plan(c, a.cnt_all, rank, world, (int)E, (int)El, align, a.plan, cap);
+            stamp("moe route + counts");
             // rows straight into the owners' receive buffers
             ep_dispatch(c, a.xm, a.idx, a.row_of, a.off, a.plan, tab(a.xp), tab(a.src_of), a.dest, T, (int)K, d,
                         (int)El, align, rank, world, cap, dt);
             comm->barrier();
+            stamp("moe dispatch");
             if (ilv) {
                 gemm_grouped_swiglu_fwd_tc(c, cap, F, d, (int)El, a.plan, (const bf16*)a.xp, d, (const bf16*)W(q.w13),
                                            (bf16*)a.ac, (bf16*)a.h);
@@ -434,6 +436,7 @@ void MoeTrainer::forward() {
                 swiglu_act(c, a.ac, (char*)a.ac + F * e, a.h, cap, F, 2 * F, F, dt, -1, a.plan + El);
             }
             expert_gemm(c, dt, false, cap, d, F, (int)El, a.plan, a.h, F, W(q.w2), a.yp, d, dt);
+            stamp("moe experts");
             comm->barrier();
             // weighted sum read from the owners' expert outputs
             ep_combine(c, tab(a.yp), a.idx, a.dest, a.w, T, (int)K, d, (int)El, world, cap, x_out, a.x_mid, dt);
@@ -474,6 +477,7 @@ void MoeTrainer::backward() {
             comm->barrier();  // every rank's dx for this layer is final
             ep_unpermute_bwd(c, a.yp, a.src_of, a.plan, tab(a.w), tab(dx), tab(dwts), cap, T * K, (int)K, d, (int)El,
                              world, dyp, dt);
+            stamp("moe bwd unpermute");
         }
         if (ilv) {
             gemm_grouped_swiglu_bwd_tc(c, cap, F, d, ng, goff, (const bf16*)dyp, d, (const bf16*)W(q.w2),
@@ -487,11 +491,13 @@ void MoeTrainer::backward() {
         }
         expert_gemm(c, dt, true, cap, d, 2 * F, ng, goff, dac, 2 * F, W(q.w13), dxp, d, dt);
         expert_wgrad(c, dt, cap, 2 * F, d, ng, goff, a.xp, d, dac, 2 * F, G + q.w13);
+        if (ep) stamp("moe bwd experts");
         if (!ep) {
             permute_bwd(c, dxp, a.row_of, T, K, d, dxm, dt, false, CATNN_F32);
         } else {
             comm->barrier();  // owners' dxp rows and the dwts they wrote are final
             ep_permute_bwd(c, tab(dxp), a.idx, a.dest, T, (int)K, d, (int)El, world, cap, dxm, dt);
+            stamp("moe bwd permute");
         }
         // router straight-through adjoint (adjoint.rs:255-284)
         router_ste(c, a.idx, a.w, dwts, T, E, K, dlog);
