@@ -863,10 +863,24 @@ static int pick_ksplit(Context* c, i64 tiles, i64 klen, i64 part_elems, int BN, 
 
 // Builds both maps for op(A) [M(or rows), K] and op(B) [K, N] and launches.
 // part_rows: rows of one split-K partial slice (0: no split-K).
+// Output tile width of a plain GEMM: 256 columns unless the last wave of
+// 128 x 256 tiles leaves enough SMs idle that 128-column tiles finish
+// sooner. A 128 x 128 tile does half the work in a little over half the
+// time (its MMAs read B at twice the bytes per FLOP); 0.55 of a 256-column
+// tile is taken as its cost. With fewer tiles than SMs the split-K choice
+// (pick_ksplit) applies to whichever width this returns.
+static int pick_bn(Context* c, i64 M, i64 N) {
+    if (N <= 128) return 128;
+    const i64 sms = c->sm_count;
+    const i64 t256 = cdiv(M, BM) * cdiv(N, 256), t128 = cdiv(M, BM) * cdiv(N, 128);
+    const double w256 = (double)cdiv(t256, sms), w128 = 0.55 * (double)cdiv(t128, sms);
+    return w128 < 0.95 * w256 ? 128 : 256;
+}
+
 static void run_tc(Context* c, TcArgs a, bool a_mn, bool b_mn, const void* A, i64 a_rows, i64 a_cols, i64 lda,
                    const void* B, i64 b_rows, i64 b_cols, i64 ldb, int grid_bound, i64 base_tiles = 0,
-                   i64 klen = 0, i64 part_rows = 0, bool tf32 = false) {
-    const int BN = a.N <= 128 ? 128 : 256;
+                   i64 klen = 0, i64 part_rows = 0, bool tf32 = false, int bn = 0) {
+    const int BN = bn ? bn : (a.N <= 128 ? 128 : 256);
     // a box row is one 128-byte swizzle row: 64 bf16 or 32 fp32 elements of K
     const int kbox = tf32 ? 32 : 64;
     CUtensorMap ma = make_map(A, a_rows, a_cols, lda, kbox, a_mn ? 64 : BM, tf32);
@@ -1007,9 +1021,9 @@ void gemm_tf32_tc(Context* c, bool ta, bool tb, i64 M, i64 N, i64 K, const float
     a.bias = bias;
     a.act = act;
     a.accumulate = accumulate ? 1 : 0;
-    const int BN = N <= 128 ? 128 : 256;
+    const int BN = pick_bn(c, M, N);
     int tiles = cdiv(M, BM) * cdiv(N, BN);
-    run_tc(c, a, false, false, Ak, M, K, lak, Bk, N, K, lbk, tiles, tiles, K, M, true);
+    run_tc(c, a, false, false, Ak, M, K, lak, Bk, N, K, lbk, tiles, tiles, K, M, true, BN);
 }
 
 void gemm_bf16_tc(Context* c, bool ta, bool tb, i64 M, i64 N, i64 K, const bf16* A, i64 lda, const bf16* B, i64 ldb,
@@ -1035,11 +1049,12 @@ void gemm_bf16_tc(Context* c, bool ta, bool tb, i64 M, i64 N, i64 K, const bf16*
     a.resid = resid;
     a.act = act;
     a.accumulate = accumulate ? 1 : 0;
-    const int BN = N <= 128 ? 128 : 256;
+    const int BN = pick_bn(c, M, N);
     int tiles = cdiv(M, BM) * cdiv(N, BN);
     // op(A): ta=0 -> A [M,K] K-major; ta=1 -> A [K,M] MN-major.
     // op(B): tb=1 -> B [N,K] K-major; tb=0 -> B [K,N] MN-major.
-    run_tc(c, a, ta, !tb, A, ta ? K : M, ta ? M : K, lda, B, tb ? N : K, tb ? K : N, ldb, tiles, tiles, K, M);
+    run_tc(c, a, ta, !tb, A, ta ? K : M, ta ? M : K, lda, B, tb ? N : K, tb ? K : N, ldb, tiles, tiles, K, M, false,
+           BN);
 }
 
 void gemm_grouped_bf16_tc(Context* c, bool tb, i64 total_rows, i64 N, i64 K, int groups, const int32_t* offsets,
