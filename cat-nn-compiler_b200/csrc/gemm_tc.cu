@@ -863,18 +863,18 @@ static int pick_ksplit(Context* c, i64 tiles, i64 klen, i64 part_elems, int BN, 
 
 // Builds both maps for op(A) [M(or rows), K] and op(B) [K, N] and launches.
 // part_rows: rows of one split-K partial slice (0: no split-K).
-// Output tile width of a plain GEMM: 256 columns unless the last wave of
-// 128 x 256 tiles leaves enough SMs idle that 128-column tiles finish
-// sooner. A 128 x 128 tile does half the work in a little over half the
-// time (its MMAs read B at twice the bytes per FLOP); 0.55 of a 256-column
-// tile is taken as its cost. With fewer tiles than SMs the split-K choice
-// (pick_ksplit) applies to whichever width this returns.
+// Output tile width of a plain GEMM: 256 columns, unless even one wave of
+// 128 x 256 tiles leaves SMs idle and the 128 x 128 tiles still fit in one
+// wave (then twice as many SMs work; split-K, pick_ksplit, is chosen on top
+// for that width). Measured at 2048 rows on B200: x·W_o (2048 x 1024 x 1024)
+// 10.8 -> 9.8 us, the QKV dgrad (2048 x 1024 x 3072) 22.9 -> 19.4 us; with
+// more tiles than SMs the 128-column tiles lost (QKV forward, 192 tiles:
+// 16.5 -> 19.7 us), so the rule stops there.
 static int pick_bn(Context* c, i64 M, i64 N) {
     if (N <= 128) return 128;
     const i64 sms = c->sm_count;
     const i64 t256 = cdiv(M, BM) * cdiv(N, 256), t128 = cdiv(M, BM) * cdiv(N, 128);
-    const double w256 = (double)cdiv(t256, sms), w128 = 0.55 * (double)cdiv(t128, sms);
-    return w128 < 0.95 * w256 ? 128 : 256;
+    return t256 < sms && t128 <= sms ? 128 : 256;
 }
 
 static void run_tc(Context* c, TcArgs a, bool a_mn, bool b_mn, const void* A, i64 a_rows, i64 a_cols, i64 lda,
