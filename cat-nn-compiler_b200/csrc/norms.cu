@@ -497,51 +497,96 @@ __global__ void __launch_bounds__(256) k_rms_router(const float* __restrict__ x,
 #pragma unroll
             for (int e = 0; e < EB; ++e) gv[g][u][e] = e < E ? gate[(i64)(c + u) * E + e] : 0.f;
     }
-    for (i64 r = blockIdx.x; r < rows; r += gridDim.x) {
-        float xv[NC][4];
-        float ss = 0.f;
+    // two rows per pass (r and r + gridDim.x): their loads are in flight
+    // together and they share the block's barriers; each row's arithmetic
+    // (and reduction order) is the one-row computation's
+    __shared__ float red2[8];
+    __shared__ float lred2[8][EB];
+    for (i64 r = blockIdx.x; r < rows; r += 2 * (i64)gridDim.x) {
+        const i64 r2 = r + gridDim.x;
+        const bool two = r2 < rows;
+        float xv[NC][4], xw[NC][4];
+        float ss = 0.f, ss2 = 0.f;
 #pragma unroll
         for (int g = 0; g < NC; ++g) {
             ldv<float, 4>(x + r * last + g * 1024 + threadIdx.x * 4, xv[g]);
+            if (two) ldv<float, 4>(x + r2 * last + g * 1024 + threadIdx.x * 4, xw[g]);
+            else
 #pragma unroll
-            for (int u = 0; u < 4; ++u) ss += xv[g][u] * xv[g][u];
+                for (int u = 0; u < 4; ++u) xw[g][u] = 0.f;
         }
+#pragma unroll
+        for (int g = 0; g < NC; ++g)
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                ss += xv[g][u] * xv[g][u];
+                ss2 += xw[g][u] * xw[g][u];
+            }
         ss = warp_sum(ss);
-        if (lane == 0) red[warp] = ss;
+        ss2 = warp_sum(ss2);
+        if (lane == 0) {
+            red[warp] = ss;
+            red2[warp] = ss2;
+        }
         __syncthreads();
-        float tot = 0.f;
+        float tot = 0.f, tot2 = 0.f;
 #pragma unroll
-        for (int k = 0; k < 8; ++k) tot += red[k];
+        for (int k = 0; k < 8; ++k) {
+            tot += red[k];
+            tot2 += red2[k];
+        }
         const float inv = 1.0f / sqrtf(tot / (float)last + eps);
-        float lg[EB];
+        const float inv2 = 1.0f / sqrtf(tot2 / (float)last + eps);
+        float lg[EB], lg2[EB];
 #pragma unroll
-        for (int e = 0; e < EB; ++e) lg[e] = 0.f;
+        for (int e = 0; e < EB; ++e) lg[e] = lg2[e] = 0.f;
 #pragma unroll
         for (int g = 0; g < NC; ++g) {
-            float yv[4];
+            float yv[4], yw[4];
 #pragma unroll
             for (int u = 0; u < 4; ++u) {
                 yv[u] = xv[g][u] * inv * wv[g][u];
+                yw[u] = xw[g][u] * inv2 * wv[g][u];
 #pragma unroll
-                for (int e = 0; e < EB; ++e) lg[e] = fmaf(yv[u], gv[g][u][e], lg[e]);
+                for (int e = 0; e < EB; ++e) {
+                    lg[e] = fmaf(yv[u], gv[g][u][e], lg[e]);
+                    lg2[e] = fmaf(yw[u], gv[g][u][e], lg2[e]);
+                }
             }
             const i64 o = r * last + g * 1024 + threadIdx.x * 4;
             stv<float, 4>(y32 + o, yv);
             stv<bf16, 4>(y16 + o, yv);
+            if (two) {
+                const i64 o2 = r2 * last + g * 1024 + threadIdx.x * 4;
+                stv<float, 4>(y32 + o2, yw);
+                stv<bf16, 4>(y16 + o2, yw);
+            }
         }
 #pragma unroll
-        for (int e = 0; e < EB; ++e) lg[e] = warp_sum(lg[e]);
+        for (int e = 0; e < EB; ++e) {
+            lg[e] = warp_sum(lg[e]);
+            lg2[e] = warp_sum(lg2[e]);
+        }
         if (lane == 0)
 #pragma unroll
-            for (int e = 0; e < EB; ++e) lred[warp][e] = lg[e];
+            for (int e = 0; e < EB; ++e) {
+                lred[warp][e] = lg[e];
+                lred2[warp][e] = lg2[e];
+            }
         __syncthreads();
         if (threadIdx.x < E) {
             float t = 0.f;
 #pragma unroll
             for (int k = 0; k < 8; ++k) t += lred[k][threadIdx.x];
             logits[r * E + threadIdx.x] = t;
+        } else if (two && threadIdx.x >= 32 && threadIdx.x < 32 + E) {
+            const int e = threadIdx.x - 32;
+            float t = 0.f;
+#pragma unroll
+            for (int k = 0; k < 8; ++k) t += lred2[k][e];
+            logits[r2 * E + e] = t;
         }
-        __syncthreads();  // red / lred are rewritten by the next row
+        __syncthreads();  // red / lred are rewritten by the next pass
     }
 }
 
