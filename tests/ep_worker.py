@@ -22,13 +22,40 @@ CONFIGS = {
     # (SGD on the fp32 path: Adam's first step is lr·sign(g), which turns a
     # last-bit difference of a near-zero gradient into a full lr step)
     "f32": dict(args=(512, 64, 96, 2, 4, 2, 8, 2, 4, 32), dtype=torch.float32, opt="sgd", lr=5e-2),
-    "bf16": dict(args=(2048, 256, 512, 2, 4, 4, 8, 2, 4, 128), dtype=torch.bfloat16, opt="adam", lr=1e-3),
+    # (Adam with eps 1e-3 for the comparison: a gradient far below eps moves its
+    # parameter in proportion to it, not by ±lr as with eps 1e-8, so rounding
+    # noise in near-zero gradients does not become full-size steps)
+    "bf16": dict(args=(2048, 256, 512, 2, 4, 4, 8, 2, 4, 128), dtype=torch.bfloat16, opt="adam", lr=1e-3,
+                 adam_eps=1e-3),
+    # config 5 at its full widths (the benchmark's model): only the losses are
+    # saved (the packed vectors would be 1.7 GB each)
+    "config5": dict(args=(32000, 1024, 3584, 4, 16, 16, 8, 2, 8, 2048), dtype=torch.bfloat16, opt="adam", lr=1e-4,
+                    light=True),
 }
+
+
+def params(cfg, name, device):
+    """init_params for the small configs; for config 5 the same draw on the
+    device (torch's generator, seed 3) on every rank and in the reference."""
+    if not CONFIGS[name].get("light"):
+        return init_params(cfg, seed=3)
+    from catnn_b200.train import packed_layout
+    L = packed_layout(cfg)
+    g = torch.Generator(device=device).manual_seed(3)
+    P = torch.randn(L["total"], generator=g, device=device) * 0.02
+    h = cfg.hidden
+    for l in range(cfg.layers):
+        base = L["layer0"] + l * L["layer_stride"]
+        P[base + L["rms_attn"]:base + L["rms_attn"] + h] = 1.0
+        P[base + L["rms_moe"]:base + L["rms_moe"] + h] = 1.0
+    P[L["final_norm"]:L["final_norm"] + h] = 1.0
+    return P
 
 
 def config(name):
     c = CONFIGS[name]
-    return MoeConfig.make(*c["args"], rope_theta=1e4, dtype=c["dtype"], optimizer=c["opt"], lr=c["lr"])
+    return MoeConfig.make(*c["args"], rope_theta=1e4, dtype=c["dtype"], optimizer=c["opt"], lr=c["lr"],
+                          adam_eps=c.get("adam_eps", 1e-8))
 
 
 def tokens(cfg, seed=9):
@@ -49,7 +76,8 @@ def main():
         comm = D.Comm.from_process_group(local)
         cfg = config(a.config)
         tr = MoeTrainer(cfg, local, comm=comm)
-        tr.set_params(init_params(cfg, seed=3))
+        tr.set_params(params(cfg, a.config, f"cuda:{local}"))
+        light = CONFIGS[a.config].get("light", False)
         if a.graphs:
             # the first update step runs eagerly, the second is captured, later ones replay
             tr.set_graphs(True)
@@ -57,15 +85,18 @@ def main():
         loss = torch.zeros(1, device=f"cuda:{local}")
         tr.step(tok, update=False, loss_out=loss)
         tr.check()
-        out = {"loss0": loss.cpu().numpy(), "grads0": tr.grads().cpu().numpy()}
+        out = {"loss0": loss.cpu().numpy()}
+        if not light:
+            out["grads0"] = tr.grads().cpu().numpy()
         losses = []
         for _ in range(a.steps):
             tr.step(tok, update=True, loss_out=loss)
             losses.append(float(loss.item()))
         tr.check()
         out["losses"] = np.array(losses, np.float32)
-        out["params"] = tr.params().cpu().numpy()
-        out["x_last"] = tr.activation("x_last").cpu().numpy()
+        if not light:
+            out["params"] = tr.params().cpu().numpy()
+            out["x_last"] = tr.activation("x_last").cpu().numpy()
         np.savez(os.path.join(a.out, f"rank{rank}.npz"), **out)
         if a.graphs:
             # replays of the captured steps: every device wait must still hold

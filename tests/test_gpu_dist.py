@@ -161,3 +161,34 @@ def test_ep_two_ranks_match_single_gpu(name, graphs, tmp_path):
         assert rel_l2(g, ref["grads0"]) <= 2e-2
         assert rel_l2(p, ref["params"]) <= 2e-2
         assert rel_l2(x_last, ref["x_last"]) <= 2e-2
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_ep_two_ranks_config5_first_loss(tmp_path):
+    """Config 5 at its full widths (the benchmark's model, 16384 tokens, 8
+    experts over 2 ranks): the loss of the first step, before any update,
+    equals the one-GPU trainer's to 1e-6 relative (the sharded forward is the
+    one-GPU forward; only the two ranks' loss halves are added in another
+    order), and the loss after one Adam step to 1e-3."""
+    world = 2
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", f"--nproc-per-node={world}",
+           "--master-addr=127.0.0.1", "--master-port=29543", os.path.join(HERE, "ep_worker.py"), "--config",
+           "config5", "--out", str(tmp_path), "--steps", "1"]
+    r = subprocess.run(cmd, env=env, capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
+    cfg = W.config("config5")
+    tr = MoeTrainer(cfg, 0)
+    tr.set_params(W.params(cfg, "config5", "cuda:0"))
+    tok = torch.as_tensor(W.tokens(cfg).astype(np.int32)).cuda()
+    loss = torch.zeros(1, device="cuda")
+    tr.step(tok, update=False, loss_out=loss)
+    ref0 = float(loss.item())
+    tr.step(tok, update=True, loss_out=loss)
+    ref1 = float(loss.item())
+    tr.close()
+    for q in range(world):
+        got = np.load(tmp_path / f"rank{q}.npz")
+        l0, l1 = float(got["loss0"][0]), float(got["losses"][0])
+        assert abs(l0 - ref0) <= 1e-6 * abs(ref0), (q, l0, ref0)
+        assert abs(l1 - ref1) <= 1e-3 * abs(ref1), (q, l1, ref1)
