@@ -53,6 +53,7 @@ def parse():
                    help="distinct resident token batches the steps cycle through (1: every step trains the same batch)")
     p.add_argument("--reps", type=int, default=20)
     p.add_argument("--batch", type=int, default=2, help="--kernel step_small: sequences per step (1 layer)")
+    p.add_argument("--attn-batch", type=int, default=8, help="--kernel attn: sequences (8: config 5 on one GPU)")
     return p.parse_args()
 
 
@@ -522,13 +523,13 @@ def run_kernel_only(args):
             timed(lambda: ops.moe_expert_swiglu_backward(DY, W2, ac, off), 2.0 * int(counts.sum()) * F * d,
                   "k_gemm_tc grouped W2 dgrad + SwiGLU adjoint epilogue", rows=rows)
     elif args.kernel == "attn":
-        B, S, H, hd = CFG["global_batch"], CFG["seq"], CFG["heads"], CFG["hidden"] // CFG["heads"]
+        B, S, H, hd = args.attn_batch, CFG["seq"], CFG["heads"], CFG["hidden"] // CFG["heads"]
         q, k, v, do = (torch.randn(B, S, H, hd, device=dev).to(torch.bfloat16) for _ in range(4))
         do = do.reshape(B, S, H * hd)
         o, lse = ops.attention_core(q, k, v, True)
         fwd = 2.0 * B * H * S * S * hd  # causal half of 4·B·H·S²·hd
-        timed(lambda: ops.attention_core(q, k, v, True), fwd, "fa5 forward (causal)")
-        timed(lambda: ops.attention_core_backward(q, k, v, o, lse, do, True), 2.5 * fwd, "fa5 backward (causal)")
+        timed(lambda: ops.attention_core(q, k, v, True), fwd, "fa5 forward (causal)", batch=B)
+        timed(lambda: ops.attention_core_backward(q, k, v, o, lse, do, True), 2.5 * fwd, "fa5 backward (causal)", batch=B)
     elif args.kernel == "gemm_tf32":
         K = 4096
         A = torch.randn(K, K, device=dev) / K ** 0.5
