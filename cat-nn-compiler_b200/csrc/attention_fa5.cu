@@ -123,8 +123,11 @@ __global__ void __launch_bounds__(NT, 2)
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     // heaviest (latest) query tiles first
-    const int qt = gridDim.x - 1 - blockIdx.x;
-    const int q0 = qt * BQ, h = blockIdx.y, bi = blockIdx.z;
+    // the block's weight is the slowest grid index, heaviest (latest) query
+    // tiles first over every head and sequence: the longest CTAs start in
+    // the first wave
+    const int qt = gridDim.z - 1 - blockIdx.z;
+    const int q0 = qt * BQ, h = blockIdx.x, bi = blockIdx.y;
     const int kvh = h / (a.h / a.hkv);
     const int qlast = min(q0 + BQ - 1, a.s - 1);
     const int j0 = klo(a, q0) / BKV, j1 = min(khi(a, qlast), a.s - 1) / BKV;
@@ -479,8 +482,10 @@ __global__ void __launch_bounds__(NTB, 1)
     constexpr uint32_t C_S = 0, C_DP = 128, C_DV = 256, C_DK = 320;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int kb = gridDim.x - 1 - blockIdx.x;  // early keys see the most queries: first
-    const int k0 = kb * 128, kvh = blockIdx.y, bi = blockIdx.z;
+    // early keys see the most queries: the key block is the slowest grid
+    // index, first key blocks first over every head and sequence
+    const int kb = blockIdx.z;
+    const int k0 = kb * 128, kvh = blockIdx.x, bi = blockIdx.y;
     const int grp = a.h / a.hkv;
     const int klast = min(k0 + 127, a.s - 1);
     const int qb0 = bqlo(a, k0) / BB, qb1 = bqhi(a, klast) / BB;
@@ -730,8 +735,9 @@ __global__ void __launch_bounds__(NTB, 1)
     constexpr uint32_t C_S = 0, C_DP = 128, C_DQ = 256;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int qt = gridDim.x - 1 - blockIdx.x;
-    const int q0 = qt * 128, h = blockIdx.y, bi = blockIdx.z;
+    // late queries see the most keys: heaviest query blocks first (slowest grid index)
+    const int qt = gridDim.z - 1 - blockIdx.z;
+    const int q0 = qt * 128, h = blockIdx.x, bi = blockIdx.y;
     const int kvh = h / (a.h / a.hkv);
     const int qlast = min(q0 + 127, a.s - 1);
     const int j0 = bklo(a, q0) / BB, j1 = min(bkhi(a, qlast), a.s - 1) / BB;
@@ -937,6 +943,7 @@ void attention_fwd_tc5(Context* c, const void* q, const void* k, const void* v, 
     using namespace fa5;
     if (b <= 0 || s <= 0 || h <= 0) return;
     CATNN_CHECK(b * s < (1ll << 31) && h % hkv == 0, CATNN_ERR_SHAPE, "attention: sizes");
+    CATNN_CHECK(b <= 65535 && cdiv(s, 128) <= 65535, CATNN_ERR_SHAPE, "attention: grid limits (batch, seq / 128)");
     // maps over all B*S rows; a box that runs past the last row reads zeros,
     // rows of the next sequence inside a box are masked (key >= S) or not stored
     CUtensorMap mq = tma_map_bf16(q, b * s, h * HD, q_stride, HD, BQ);
@@ -958,7 +965,7 @@ void attention_fwd_tc5(Context* c, const void* q, const void* k, const void* v, 
         CUDA_OK(cudaFuncSetAttribute(k_fwd, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM));
         attr[c->device] = true;
     }
-    dim3 grid((unsigned)cdiv(s, BQ), (unsigned)h, (unsigned)b);
+    dim3 grid((unsigned)h, (unsigned)b, (unsigned)cdiv(s, BQ));
     k_fwd<<<grid, NT, SMEM, c->stream>>>(mq, mk, mv, a);
     launched(c);
 }
@@ -973,6 +980,7 @@ void attention_bwd_tc5(Context* c, const void* q, const void* k, const void* v, 
     using namespace fa5;
     if (b <= 0 || s <= 0 || h <= 0) return;
     CATNN_CHECK(b * s < (1ll << 31) && h % hkv == 0, CATNN_ERR_SHAPE, "attention: sizes");
+    CATNN_CHECK(b <= 65535 && cdiv(s, 128) <= 65535, CATNN_ERR_SHAPE, "attention: grid limits (batch, seq / 128)");
     CUtensorMap mq128 = tma_map_bf16(q, b * s, h * HD, q_stride, HD, 128);
     CUtensorMap mdo128 = tma_map_bf16(dout, b * s, h * HD, h * HD, HD, 128);
     CUtensorMap mk128 = tma_map_bf16(k, b * s, hkv * HD, kv_stride, HD, 128);
@@ -999,9 +1007,9 @@ void attention_bwd_tc5(Context* c, const void* q, const void* k, const void* v, 
         CUDA_OK(cudaFuncSetAttribute(k_dq, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_DQ));
         attr[c->device] = true;
     }
-    k_dkdv<<<dim3((unsigned)cdiv(s, 128), (unsigned)hkv, (unsigned)b), NTB, SMEM_DKDV, c->stream>>>(mk128, mv128, mq128,
+    k_dkdv<<<dim3((unsigned)hkv, (unsigned)b, (unsigned)cdiv(s, 128)), NTB, SMEM_DKDV, c->stream>>>(mk128, mv128, mq128,
                                                                                                     mdo128, a);
-    k_dq<<<dim3((unsigned)cdiv(s, 128), (unsigned)h, (unsigned)b), NTB, SMEM_DQ, c->stream>>>(mq128, mdo128, mk128,
+    k_dq<<<dim3((unsigned)h, (unsigned)b, (unsigned)cdiv(s, 128)), NTB, SMEM_DQ, c->stream>>>(mq128, mdo128, mk128,
                                                                                               mv128, a);
     launched(c, 2);
 }
@@ -1013,9 +1021,9 @@ KernelInfo fa5_info(Context* c, const std::string& op, const KShape& s) {
     if (!(op == "attention" || op == "gqa_attention") || s.head_dim != fa5::HD) return k;
     k.fn = (const void*)fa5::k_fwd;
     k.file = "attention_fa5.cu";
-    k.grid[0] = (unsigned)cdiv(s.seq, fa5::BQ);
-    k.grid[1] = (unsigned)s.heads;
-    k.grid[2] = (unsigned)s.batch;
+    k.grid[0] = (unsigned)s.heads;
+    k.grid[1] = (unsigned)s.batch;
+    k.grid[2] = (unsigned)cdiv(s.seq, fa5::BQ);
     k.block[0] = fa5::NT;
     k.dyn_smem = fa5::SMEM;
     return k;

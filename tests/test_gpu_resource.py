@@ -69,7 +69,7 @@ def test_describe_launch_geometry_follows_the_shape():
     small = ops.kernel_describe("linear", torch.bfloat16, rows=128, width=128, inner=64)
     assert small["grid"][0] == 1 and small["block"][0] == 320  # TMA, MMA and 8 epilogue warps
     fa = ops.kernel_describe("gqa_attention", torch.bfloat16, batch=8, seq=2048, heads=16, head_dim=64)
-    assert fa["grid"] == [16, 16, 8] and "fa5" in fa["kernel"]
+    assert fa["grid"] == [16, 8, 16] and "fa5" in fa["kernel"]  # heads, sequences, query tiles (slowest)
     rows = ops.kernel_describe("rms_norm", torch.float32, rows=300, width=256)
     assert rows["grid"][0] == 300
 
