@@ -9,12 +9,23 @@
 //  - expert rows padded to 128 so every expert GEMM tile is single-expert;
 //  - weight gradients land in fp32 directly from the GEMM epilogue.
 #include <cstring>
+#include <utility>
 #include <string>
 
 #include "moe_ep.cuh"
 #include "trainer.cuh"
 
 namespace catnn {
+
+namespace {
+// Enqueue the launchers' work on another stream for the scope's lifetime.
+struct OnStream {
+    Context* c;
+    cudaStream_t saved;
+    OnStream(Context* ctx, cudaStream_t s) : c(ctx), saved(ctx->stream) { c->stream = s; }
+    ~OnStream() { c->stream = saved; }
+};
+}  // namespace
 
 static i64 al128(i64 n) { return (n + 127) / 128 * 128; }
 
@@ -304,6 +315,16 @@ void MoeTrainer::release() {
     d12 = nullptr;
     if (stamps) cudaFree(stamps);
     stamps = nullptr;
+    if (ws) {
+        cudaStreamSynchronize(ws);
+        cudaEventDestroy(ev_w);
+        cudaEventDestroy(ev_wd);
+        cudaStreamDestroy(ws);
+        ws = nullptr;
+    }
+    if (wscratch) cudaFree(wscratch);
+    wscratch = nullptr;
+    wscratch_bytes = 0;
     if (ev_k) {
         cudaEventDestroy(ev_k);
         cudaEventDestroy(ev_kd);
@@ -471,9 +492,11 @@ void MoeTrainer::backward() {
         // MoE adjoint (adjoint.rs:471-526), batched by expert
         const int ng = ep ? (int)El : (int)E;
         const int32_t* goff = ep ? a.plan : a.off;
+        const bool defer = ep && ilv;  // weight gradients on ws (see MoeTrainer::ws)
         if (!ep) {
             unpermute_bwd(c, a.yp, a.src_of, cap, a.w, dx, K, d, dwts, dyp, dt, dt, CATNN_F32);
         } else {
+            join_wgrads();    // the previous layer's weight gradients have read dyp / dac
             comm->barrier();  // every rank's dx for this layer is final
             ep_unpermute_bwd(c, a.yp, a.src_of, a.plan, tab(a.w), tab(dx), tab(dwts), cap, T * K, (int)K, d, (int)El,
                              world, dyp, dt);
@@ -482,7 +505,7 @@ void MoeTrainer::backward() {
         if (ilv) {
             gemm_grouped_swiglu_bwd_tc(c, cap, F, d, ng, goff, (const bf16*)dyp, d, (const bf16*)W(q.w2),
                                        (const bf16*)a.ac, (bf16*)dac);
-            expert_wgrad(c, dt, cap, d, F, ng, goff, a.h, F, dyp, d, G + q.w2);
+            if (!defer) expert_wgrad(c, dt, cap, d, F, ng, goff, a.h, F, dyp, d, G + q.w2);
         } else {
             expert_gemm(c, dt, true, cap, F, d, ng, goff, dyp, d, W(q.w2), dh, F, dt);
             expert_wgrad(c, dt, cap, d, F, ng, goff, a.h, F, dyp, d, G + q.w2);
@@ -490,7 +513,36 @@ void MoeTrainer::backward() {
                            ep ? a.plan + El : nullptr);
         }
         expert_gemm(c, dt, true, cap, d, 2 * F, ng, goff, dac, 2 * F, W(q.w13), dxp, d, dt);
-        expert_wgrad(c, dt, cap, 2 * F, d, ng, goff, a.xp, d, dac, 2 * F, G + q.w13);
+        if (defer) {
+            if (!ws) {
+                CUDA_OK(cudaStreamCreateWithFlags(&ws, cudaStreamNonBlocking));
+                CUDA_OK(cudaEventCreateWithFlags(&ev_w, cudaEventDisableTiming));
+                CUDA_OK(cudaEventCreateWithFlags(&ev_wd, cudaEventDisableTiming));
+            }
+            CUDA_OK(cudaEventRecord(ev_w, c->stream));
+            CUDA_OK(cudaStreamWaitEvent(ws, ev_w, 0));
+            {
+                // the split-K partials of these GEMMs must not share the
+                // context's scratch with the GEMMs running on the step's stream
+                std::swap(c->scratch, wscratch);
+                std::swap(c->scratch_bytes, wscratch_bytes);
+                OnStream on(c, ws);
+                try {
+                    expert_wgrad(c, dt, cap, d, F, ng, goff, a.h, F, dyp, d, G + q.w2);
+                    expert_wgrad(c, dt, cap, 2 * F, d, ng, goff, a.xp, d, dac, 2 * F, G + q.w13);
+                } catch (...) {
+                    std::swap(c->scratch, wscratch);
+                    std::swap(c->scratch_bytes, wscratch_bytes);
+                    throw;
+                }
+                std::swap(c->scratch, wscratch);
+                std::swap(c->scratch_bytes, wscratch_bytes);
+            }
+            CUDA_OK(cudaEventRecord(ev_wd, ws));
+            w_forked = true;
+        } else {
+            expert_wgrad(c, dt, cap, 2 * F, d, ng, goff, a.xp, d, dac, 2 * F, G + q.w13);
+        }
         if (ep) stamp("moe bwd experts");
         if (!ep) {
             permute_bwd(c, dxp, a.row_of, T, K, d, dxm, dt, false, CATNN_F32);
@@ -520,8 +572,10 @@ void MoeTrainer::backward() {
         stamp("bwd attention");
         // this layer's replicated gradients and its experts are final
         post_bucket(lb[l], (int)l);
-        update_after_main(q.w13, q.w2 + El * F * d - q.w13);
+        if (defer) update_after_event(ev_wd, q.w13, q.w2 + El * F * d - q.w13);
+        else update_after_main(q.w13, q.w2 + El * F * d - q.w13);
     }
+    join_wgrads();
     CUDA_OK(cudaStreamWaitEvent(c->stream, ev_kd, 0));  // the keys formed during the forward
     if (ep) {
         comm->barrier();  // every rank's token rows of dx are final
@@ -582,15 +636,6 @@ void MoeTrainer::update_range(i64 off, i64 n) {
     else adam(c, P + off, G + off, Mo + off, Vo + off, n, t_step, lr, b1, b2, aeps, CATNN_F32, sh, d12);
 }
 
-namespace {
-// Enqueue the launchers' work on another stream for the scope's lifetime.
-struct OnStream {
-    Context* c;
-    cudaStream_t saved;
-    OnStream(Context* ctx, cudaStream_t s) : c(ctx), saved(ctx->stream) { c->stream = s; }
-    ~OnStream() { c->stream = saved; }
-};
-}  // namespace
 
 static void make_update_stream(cudaStream_t* us, cudaEvent_t* a, cudaEvent_t* b) {
     if (*us) return;
@@ -619,6 +664,21 @@ void MoeTrainer::update_after_comm(i64 off, i64 n) {
     upd_forked = true;
     OnStream on(c, us);
     update_range(off, n);
+}
+
+void MoeTrainer::update_after_event(cudaEvent_t ev, i64 off, i64 n) {
+    if (!upd_pending || n <= 0) return;
+    make_update_stream(&us, &ev_u, &ev_u_done);
+    CUDA_OK(cudaStreamWaitEvent(us, ev, 0));
+    upd_forked = true;
+    OnStream on(c, us);
+    update_range(off, n);
+}
+
+void MoeTrainer::join_wgrads() {
+    if (!w_forked) return;
+    w_forked = false;
+    CUDA_OK(cudaStreamWaitEvent(c->stream, ev_wd, 0));
 }
 
 void MoeTrainer::join_updates() {

@@ -139,6 +139,19 @@ struct MoeTrainer {
     void update_after_main(i64 off, i64 n);     // on us, after the work enqueued so far
     void update_after_comm(i64 off, i64 n);     // on us, after the last allreduce enqueued
     void join_updates();
+    // Expert parallel: the expert weight-gradient GEMMs run on their own
+    // stream (ws) with their own split-K scratch, beside the barrier, the
+    // permute adjoint and the attention adjoint that follow. No other rank
+    // waits for them, so the barrier after the expert GEMMs waits only for
+    // the slowest rank's data-gradient GEMMs. The next layer's adjoint (which
+    // rewrites dyp / dac) and the experts' update wait for ev_wd.
+    cudaStream_t ws = nullptr;
+    cudaEvent_t ev_w = nullptr, ev_wd = nullptr;
+    bool w_forked = false;
+    void* wscratch = nullptr;
+    size_t wscratch_bytes = 0;
+    void join_wgrads();
+    void update_after_event(cudaEvent_t ev, i64 off, i64 n);  // on us, after ev
     // a bucket's gradients are final: sum and update them (see Bucket)
     void post_bucket(const Bucket& b, int id);
     void flush_gathers();
