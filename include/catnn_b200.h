@@ -89,7 +89,8 @@ int catnn_checksum_f32(catnn_ctx* ctx, const float* x, int64_t n, uint64_t* out)
 /* C[M,N] = act(op(A)·op(B) + bias) (+ C if accumulate).
  * op(A) is [M,K]: trans_a=0 reads A as [M,K] (lda >= K), trans_a=1 as [K,M].
  * op(B) is [K,N]: trans_b=0 reads B as [K,N] (ldb >= N), trans_b=1 as [N,K].
- * A/B in `dtype`; C in c_dtype; bias fp32 [N] or NULL.
+ * A/B in `dtype` (CATNN_TF32: fp32 A/B multiplied as TF32 on the tensor
+ * cores); C in c_dtype; bias fp32 [N] or NULL.
  * The contraction behind cpu::matmul_mk_kn (crates/catnn-compile/src/kernel/cpu.rs:186). */
 int catnn_gemm(catnn_ctx* ctx, int trans_a, int trans_b, int64_t M, int64_t N, int64_t K,
                const void* A, int64_t lda, const void* B, int64_t ldb, void* C, int64_t ldc,
