@@ -154,12 +154,20 @@ __device__ __forceinline__ TileInfo tile_at_base(const TcArgs& a, int t) {
 // results are rounded to bf16, whose unit is 2^-8). One epilogue warp per
 // sub-partition runs these serially, so short dependency chains matter more
 // than the last fp32 bit: the IEEE exp and division cost ~35 instructions
-// with branches, these ~6.
-__device__ __forceinline__ float tc_sigmoid(float x) { return __frcp_rn(1.0f + __expf(-x)); }
+// with branches, these ~4. The reciprocal is the single MUFU instruction
+// (rcp.approx.ftz: relative error under 2^-22); for x below about -88 the
+// exponential overflows to +inf and its reciprocal is 0, so σ = 0.
+__device__ __forceinline__ float tc_rcp(float x) {
+    float y;
+    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+__device__ __forceinline__ float tc_sigmoid(float x) { return tc_rcp(1.0f + __expf(-x)); }
 __device__ __forceinline__ float tc_silu(float x) { return x * tc_sigmoid(x); }
-__device__ __forceinline__ float tc_silu_grad(float x) {
+// silu(x) and silu'(x) = σ + x·σ·(1-σ) from one σ
+__device__ __forceinline__ float2 tc_silu_and_grad(float x) {
     const float s = tc_sigmoid(x);
-    return s + x * s * (1.0f - s);
+    return make_float2(x * s, s + x * s * (1.0f - s));
 }
 
 // 32 bf16 values (packed in pairs) of one row of a warp's 32-row block:
@@ -440,8 +448,9 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
                         for (int j = 0; j < 16; ++j) {
                             const float2 av = unpack_bf16x2(ua[j]), cv = unpack_bf16x2(uc[j]);
                             const float2 g = unpack_bf16x2(pack_bf16x2(__uint_as_float(r[2 * j]), __uint_as_float(r[2 * j + 1])));
-                            pda[j] = pack_bf16x2(g.x * cv.x * tc_silu_grad(av.x), g.y * cv.y * tc_silu_grad(av.y));
-                            pdc[j] = pack_bf16x2(g.x * tc_silu(av.x), g.y * tc_silu(av.y));
+                            const float2 sx = tc_silu_and_grad(av.x), sy = tc_silu_and_grad(av.y);
+                            pda[j] = pack_bf16x2(g.x * cv.x * sx.y, g.y * cv.y * sy.y);
+                            pdc[j] = pack_bf16x2(g.x * sx.x, g.y * sy.x);
                         }
                         st.put(pda, &mapC, tma, col, (int)ybase, dacp + col, rv);
                         st.put(pdc, &mapC, tma, col + 128, (int)ybase, dacp + col + 128, rv);

@@ -604,11 +604,47 @@ bool rms_router_fused(Context* c, const float* x, const float* w, const float* g
     return true;
 }
 
+// fp32 x -> bf16 y at widths NV·128 (k_rms_fwd_mx's expression): one warp
+// per row, each lane holding NV float4 chunks 128 columns apart, so x is read
+// once and the row sum needs only warp shuffles; 8 rows per CTA.
+template <int NV>
+__global__ void __launch_bounds__(256) k_rms_fwd_warp(const float* __restrict__ x, const float* __restrict__ w,
+                                                      bf16* __restrict__ y, i64 rows, float eps) {
+    constexpr int last = NV * 128;
+    const int lane = threadIdx.x & 31;
+    const i64 r = (i64)blockIdx.x * 8 + (threadIdx.x >> 5);
+    if (r >= rows) return;  // warp-uniform; no block barrier below
+    const float* in = x + r * last;
+    float v[NV][4];
+#pragma unroll
+    for (int k = 0; k < NV; ++k) ldv<float, 4>(in + k * 128 + lane * 4, v[k]);
+    float s = 0.f;
+#pragma unroll
+    for (int k = 0; k < NV; ++k)
+#pragma unroll
+        for (int u = 0; u < 4; ++u) s += v[k][u] * v[k][u];
+    const float inv = 1.0f / sqrtf(warp_sum(s) / (float)last + eps);
+#pragma unroll
+    for (int k = 0; k < NV; ++k) {
+        float wv[4], o[4];
+        ldv<float, 4>(w + k * 128 + lane * 4, wv);
+#pragma unroll
+        for (int u = 0; u < 4; ++u) o[u] = v[k][u] * inv * wv[u];
+        stv<bf16, 4>(y + r * last + k * 128 + lane * 4, o);
+    }
+}
+
 void rmsnorm_fwd_mixed(Context* c, const void* x, int x_dtype, const float* w, void* y, int y_dtype, i64 rows, i64 last,
                        float eps) {
     if (rows <= 0 || last <= 0) return;
     int t = row_threads(last);
-    if (x_dtype == CATNN_F32 && y_dtype == CATNN_BF16)
+    if (x_dtype == CATNN_F32 && y_dtype == CATNN_BF16 && (last == 512 || last == 1024 || last == 2048) &&
+        aligned_to(x, 16) && aligned_to(w, 16) && aligned_to(y, 8)) {
+        const int grid = (int)cdiv(rows, 8);
+        if (last == 512) k_rms_fwd_warp<4><<<grid, 256, 0, c->stream>>>((const float*)x, w, (bf16*)y, rows, eps);
+        else if (last == 1024) k_rms_fwd_warp<8><<<grid, 256, 0, c->stream>>>((const float*)x, w, (bf16*)y, rows, eps);
+        else k_rms_fwd_warp<16><<<grid, 256, 0, c->stream>>>((const float*)x, w, (bf16*)y, rows, eps);
+    } else if (x_dtype == CATNN_F32 && y_dtype == CATNN_BF16)
         k_rms_fwd_mx<<<rows, t, 0, c->stream>>>((const float*)x, w, (bf16*)y, last, eps);
     else if (x_dtype == CATNN_F32 && y_dtype == CATNN_F32)
         k_rms_fwd_mx<<<rows, t, 0, c->stream>>>((const float*)x, w, (float*)y, last, eps);
