@@ -590,11 +590,91 @@ __global__ void __launch_bounds__(256) k_rms_router(const float* __restrict__ x,
     }
 }
 
+// Warp-level halving exchange: lanes whose bit `off` is set keep the upper N
+// of their 2N partial sums and send the lower N (the others the reverse), so
+// each step halves the values a lane holds with N shuffles.
+template <int N>
+__device__ __forceinline__ void xchg_half(float* v, int lane, int off) {
+    const bool up = (lane & off) != 0;
+#pragma unroll
+    for (int i = 0; i < N; ++i) {
+        const float send = up ? v[i] : v[i + N];
+        const float keep = up ? v[i + N] : v[i];
+        v[i] = keep + __shfl_xor_sync(0xffffffffu, send, off);
+    }
+}
+
+// The same outputs as k_rms_router<1, 8> (width 1024, E <= 8) with one warp
+// per row: each lane holds 32 values of the row (8 float4 chunks 128 columns
+// apart), the row sum is a warp reduction, and the gate sits expert-major in
+// shared memory (a warp's float4 reads of one expert's row are consecutive).
+// The 8 logit partials are summed over the warp by three halving exchanges
+// and two shuffles (9 shuffles instead of 8 x 5). Persistent CTAs of 8 warps.
+__global__ void __launch_bounds__(256) k_rms_router_warp(const float* __restrict__ x, const float* __restrict__ w,
+                                                         const float* __restrict__ gate, int E, i64 rows, float eps,
+                                                         bf16* __restrict__ y16, float* __restrict__ y32,
+                                                         float* __restrict__ logits) {
+    __shared__ __align__(16) float gs[8][1024];
+    __shared__ __align__(16) float ws[1024];
+    for (int i = threadIdx.x; i < 8 * 1024; i += 256) {
+        const int e = i >> 10, c = i & 1023;
+        gs[e][c] = e < E ? gate[(i64)c * E + e] : 0.f;
+    }
+    for (int i = threadIdx.x; i < 1024; i += 256) ws[i] = w[i];
+    __syncthreads();
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int my_e = ((lane >> 4) & 1) * 4 + ((lane >> 3) & 1) * 2 + ((lane >> 2) & 1);
+    for (i64 r = (i64)blockIdx.x * 8 + warp; r < rows; r += (i64)gridDim.x * 8) {
+        const float* xr = x + r * 1024;
+        float v[8][4];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) ldv<float, 4>(xr + k * 128 + lane * 4, v[k]);
+        float ss = 0.f;
+#pragma unroll
+        for (int k = 0; k < 8; ++k)
+#pragma unroll
+            for (int u = 0; u < 4; ++u) ss += v[k][u] * v[k][u];
+        const float inv = 1.0f / sqrtf(warp_sum(ss) / 1024.f + eps);
+        float lg[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) lg[e] = 0.f;
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+            const int c = k * 128 + lane * 4;
+            const float4 wq = *(const float4*)&ws[c];
+            float yv[4] = {v[k][0] * inv * wq.x, v[k][1] * inv * wq.y, v[k][2] * inv * wq.z, v[k][3] * inv * wq.w};
+            stv<float, 4>(y32 + r * 1024 + c, yv);
+            stv<bf16, 4>(y16 + r * 1024 + c, yv);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+                const float4 g = *(const float4*)&gs[e][c];
+                lg[e] = fmaf(yv[0], g.x, lg[e]);
+                lg[e] = fmaf(yv[1], g.y, lg[e]);
+                lg[e] = fmaf(yv[2], g.z, lg[e]);
+                lg[e] = fmaf(yv[3], g.w, lg[e]);
+            }
+        }
+        xchg_half<4>(lg, lane, 16);
+        xchg_half<2>(lg, lane, 8);
+        xchg_half<1>(lg, lane, 4);
+        float t = lg[0];
+        t += __shfl_xor_sync(0xffffffffu, t, 2);
+        t += __shfl_xor_sync(0xffffffffu, t, 1);
+        if ((lane & 3) == 0 && my_e < E) logits[r * E + my_e] = t;
+    }
+}
+
 bool rms_router_fused(Context* c, const float* x, const float* w, const float* gate, i64 E, i64 rows, i64 last,
                       float eps, bf16* y16, float* y32, float* logits) {
     const int nc = (int)(last / 1024);
     if (rows <= 0 || last % 1024 != 0 || nc < 1 || nc > 2 || E < 1 || E > 16) return false;
     if (!aligned_to(x, 16) || !aligned_to(w, 16) || !aligned_to(y16, 8) || !aligned_to(y32, 16)) return false;
+    if (nc == 1 && E <= 8) {
+        const int g8 = (int)std::min<i64>(cdiv(rows, 8), (i64)c->sm_count * 3);  // 3 CTAs fit an SM (80 registers)
+        k_rms_router_warp<<<g8, 256, 0, c->stream>>>(x, w, gate, (int)E, rows, eps, y16, y32, logits);
+        launched(c);
+        return true;
+    }
     const int grid = (int)std::min<i64>(rows, (i64)c->sm_count * 8);
     if (nc == 1 && E <= 8) k_rms_router<1, 8><<<grid, 256, 0, c->stream>>>(x, w, gate, (int)E, rows, eps, y16, y32, logits);
     else if (nc == 1) k_rms_router<1, 16><<<grid, 256, 0, c->stream>>>(x, w, gate, (int)E, rows, eps, y16, y32, logits);
