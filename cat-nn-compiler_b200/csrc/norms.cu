@@ -5,6 +5,7 @@
 // dbeta, dw) are column reductions done in row chunks, then chunk order:
 // no atomics, so every run gives the same bits.
 #include <mutex>
+#include <type_traits>
 
 #include "ops.cuh"
 
@@ -851,6 +852,83 @@ __global__ void __launch_bounds__(256) k_cols_final8(const float* __restrict__ p
     }
 }
 
+// k_rms_bwd_fused's arithmetic at width 1024 with one warp per row: each
+// lane holds 32 values of x and dy (8 float4 chunks 128 columns apart) and
+// the two row sums are warp reductions (no block barrier per row). Each warp
+// accumulates the weight-gradient partial Σ dy·x·inv of its rows in its own
+// shared-memory row (a lane owns its 32 columns there, which keeps the
+// registers at two CTAs per SM); at the end the CTA's 8 warps are added in
+// warp order into the CTA's partial row pw[blockIdx.x]. Used on the bf16
+// trainer's calls (bf16 dy or a bf16 copy of dx).
+template <typename TG, typename TC>
+__global__ void __launch_bounds__(256, 2) k_rms_bwd_warp(const float* __restrict__ x, const float* __restrict__ w,
+                                                         const TG* __restrict__ dy, const float* __restrict__ dres,
+                                                         float* __restrict__ dx, TC* __restrict__ copy, i64 rows,
+                                                         float* __restrict__ pw, float eps) {
+    __shared__ __align__(16) float ws[1024];
+    __shared__ __align__(16) float red[8][1024];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    for (int i = threadIdx.x; i < 1024; i += 256) ws[i] = w[i];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) *(float4*)&red[warp][k * 128 + lane * 4] = make_float4(0.f, 0.f, 0.f, 0.f);
+    __syncthreads();
+    const float n = 1024.f;
+    for (i64 r = (i64)blockIdx.x * 8 + warp; r < rows; r += (i64)gridDim.x * 8) {
+        const i64 o = r * 1024 + lane * 4;
+        float xv[8][4], gv[8][4];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+            ldv<float, 4>(x + o + k * 128, xv[k]);
+            ldv<TG, 4>(dy + o + k * 128, gv[k]);
+        }
+        float ss = 0.f, di = 0.f;
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+            const float4 wq = *(const float4*)&ws[k * 128 + lane * 4];
+            const float wv[4] = {wq.x, wq.y, wq.z, wq.w};
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                ss += xv[k][u] * xv[k][u];
+                di += gv[k][u] * xv[k][u] * wv[u];
+            }
+        }
+        const float ms = warp_sum(ss) / n;
+        di = warp_sum(di);
+        const float inv = 1.0f / sqrtf(ms + eps);
+        const float dms = di * -0.5f * powf(ms + eps, -1.5f);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+            const int c = k * 128 + lane * 4;
+            const float4 wq = *(const float4*)&ws[c];
+            const float wv[4] = {wq.x, wq.y, wq.z, wq.w};
+            float out[4], dr[4];
+            if (dres) ldv<float, 4>(dres + o + k * 128, dr);
+            float4 a = *(float4*)&red[warp][c];
+            float acc[4] = {a.x, a.y, a.z, a.w};
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const float v = xv[k][u];
+                float rr = gv[k][u] * inv * wv[u] + dms * (2.0f * v / n);
+                if (dres) rr += dr[u];
+                out[u] = rr;
+                acc[u] += gv[k][u] * v * inv;
+            }
+            *(float4*)&red[warp][c] = make_float4(acc[0], acc[1], acc[2], acc[3]);
+            stv<float, 4>(dx + o + k * 128, out);
+            if (copy) stv<TC, 4>(copy + o + k * 128, out);
+        }
+    }
+    if (pw) {
+        __syncthreads();
+        for (int col = threadIdx.x; col < 1024; col += 256) {
+            float t = red[0][col];
+#pragma unroll
+            for (int k = 1; k < 8; ++k) t += red[k][col];
+            pw[(i64)blockIdx.x * 1024 + col] = t;
+        }
+    }
+}
+
 template <typename TG, typename TC>
 static bool rms_bwd_fused(Context* c, const float* x, const float* w, const TG* dy, const float* dres, float* dx, TC* copy,
                           float* dw, bool dw_acc, i64 rows, i64 last, float eps) {
@@ -859,6 +937,16 @@ static bool rms_bwd_fused(Context* c, const float* x, const float* w, const TG* 
     if (!aligned_to(x, 16) || !aligned_to(w, 16) || !aligned_to(dy, 16) || !aligned_to(dres, 16) ||
         !aligned_to(dx, 16) || !aligned_to(copy, 16))
         return false;
+    constexpr bool bf16_step = std::is_same<TG, bf16>::value || std::is_same<TC, bf16>::value;
+    if (bf16_step && last == 1024 && (std::is_same<TG, bf16>::value || copy)) {
+        // persistent CTAs, 2 per SM (registers); one partial row of dw each
+        const int chunks = (int)std::min<i64>(cdiv(rows, 8), (i64)c->sm_count * 2);
+        float* pw = dw ? (float*)c->scratch_for((size_t)chunks * last * 4) : nullptr;
+        k_rms_bwd_warp<TG, TC><<<chunks, 256, 0, c->stream>>>(x, w, dy, dres, dx, copy, rows, pw, eps);
+        if (dw) k_cols_final8<<<(unsigned)cdiv(last, 32), 256, 0, c->stream>>>(pw, chunks, last, dw, dw_acc ? 1 : 0);
+        launched(c, dw ? 2 : 1);
+        return true;
+    }
     // chunks: enough CTAs to fill the GPU, a multiple of RB_ROWS rows each
     i64 crows = cdiv(rows, (i64)c->sm_count * 4);
     crows = std::max<i64>(RB_ROWS, cdiv(crows, RB_ROWS) * RB_ROWS);
