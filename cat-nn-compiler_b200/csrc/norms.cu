@@ -929,6 +929,29 @@ __global__ void __launch_bounds__(256, 2) k_rms_bwd_warp(const float* __restrict
     }
 }
 
+// Sums the partial rows of k_rms_bwd_warp: 8 columns x 32 slices per CTA
+// (four times the CTAs of k_cols_final8, a quarter of the dependent loads per
+// thread); slice j adds chunks j, j+32, ... in order, slices are added 0..31.
+__global__ void __launch_bounds__(256) k_cols_final32(const float* __restrict__ p, int chunks, i64 last,
+                                                      float* __restrict__ out, int acc) {
+    __shared__ float red[32][9];
+    const int col = threadIdx.x & 7, slice = threadIdx.x >> 3;
+    const i64 j = (i64)blockIdx.x * 8 + col;
+    float s = 0.f;
+    if (j < last) {
+#pragma unroll 4
+        for (int ch = slice; ch < chunks; ch += 32) s += p[(i64)ch * last + j];
+    }
+    red[slice][col] = s;
+    __syncthreads();
+    if (slice == 0 && j < last) {
+        float t = red[0][col];
+#pragma unroll
+        for (int k = 1; k < 32; ++k) t += red[k][col];
+        out[j] = acc ? out[j] + t : t;
+    }
+}
+
 template <typename TG, typename TC>
 static bool rms_bwd_fused(Context* c, const float* x, const float* w, const TG* dy, const float* dres, float* dx, TC* copy,
                           float* dw, bool dw_acc, i64 rows, i64 last, float eps) {
@@ -943,7 +966,7 @@ static bool rms_bwd_fused(Context* c, const float* x, const float* w, const TG* 
         const int chunks = (int)std::min<i64>(cdiv(rows, 8), (i64)c->sm_count * 2);
         float* pw = dw ? (float*)c->scratch_for((size_t)chunks * last * 4) : nullptr;
         k_rms_bwd_warp<TG, TC><<<chunks, 256, 0, c->stream>>>(x, w, dy, dres, dx, copy, rows, pw, eps);
-        if (dw) k_cols_final8<<<(unsigned)cdiv(last, 32), 256, 0, c->stream>>>(pw, chunks, last, dw, dw_acc ? 1 : 0);
+        if (dw) k_cols_final32<<<(unsigned)cdiv(last, 8), 256, 0, c->stream>>>(pw, chunks, last, dw, dw_acc ? 1 : 0);
         launched(c, dw ? 2 : 1);
         return true;
     }
