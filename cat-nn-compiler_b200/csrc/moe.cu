@@ -438,6 +438,46 @@ __global__ void k_unpermute_bwd(const TY* __restrict__ yp, const int32_t* __rest
     if (lane == 0) dw[p] = dot;
 }
 
+// k_unpermute_bwd for a bf16 dyp at hidden % 256 == 0: a lane takes 8
+// consecutive columns per step (16-byte loads of yp and stores of dyp, 8-wide
+// loads of dy), hidden/256 steps per row with their loads in flight
+// together. The lane's part of the dot product adds its 8 products per step
+// in column order, then the warp sums the lanes.
+template <typename TY, typename TG>
+__global__ void __launch_bounds__(128) k_unpermute_bwd_v(const TY* __restrict__ yp, const int32_t* __restrict__ src_of,
+                                                         const float* __restrict__ w, const TG* __restrict__ dy,
+                                                         i64 rows, int k, i64 hidden, float* __restrict__ dw,
+                                                         bf16* __restrict__ dyp) {
+    const i64 r = blockIdx.x * 4 + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    if (r >= rows) return;
+    const int p = src_of[r];
+    bf16* out = dyp + r * hidden;
+    if (p < 0) {
+        for (i64 i = lane * 8; i < hidden; i += 256) *(uint4*)(out + i) = make_uint4(0, 0, 0, 0);
+        return;
+    }
+    const i64 t = p / k;
+    const float wt = w[p];
+    const TY* yr = yp + r * hidden;
+    const TG* gr = dy + t * hidden;
+    float dot = 0.f;
+#pragma unroll 4
+    for (i64 i = lane * 8; i < hidden; i += 256) {
+        float g[8], yv[8], o[8];
+        ldv<TG, 8>(gr + i, g);
+        ldv<TY, 8>(yr + i, yv);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            dot += yv[j] * g[j];
+            o[j] = __fmul_rn(g[j], wt);
+        }
+        stv<bf16, 8>(out + i, o);
+    }
+    dot = warp_sum(dot);
+    if (lane == 0) dw[p] = dot;
+}
+
 // dx[t] (+)= Σ_j dxp[row_of[t,j]] in slot order.
 template <typename TI, typename T>
 __global__ void k_permute_bwd(const TI* __restrict__ dxp, const int32_t* __restrict__ row_of, i64 Tn, int k, i64 hidden,
@@ -459,7 +499,14 @@ void unpermute_bwd(Context* c, const void* yp, const int32_t* src_of, i64 rows, 
     dim3 g(cdiv(rows, 4));
 #define UPB(TY, TG, T) \
     k_unpermute_bwd<<<g, 128, 0, c->stream>>>((const TY*)yp, src_of, w, (const TG*)dy, rows, (int)k, hidden, dw, (T*)dyp)
-    if (dtype == CATNN_BF16) {
+#define UPBV(TY, TG) \
+    k_unpermute_bwd_v<<<g, 128, 0, c->stream>>>((const TY*)yp, src_of, w, (const TG*)dy, rows, (int)k, hidden, dw, (bf16*)dyp)
+    if (dtype == CATNN_BF16 && hidden % 256 == 0 && aligned_to(yp, 16) && aligned_to(dy, 16) && aligned_to(dyp, 16)) {
+        if (yp_dtype == CATNN_F32 && dy_dtype == CATNN_F32) UPBV(float, float);
+        else if (yp_dtype == CATNN_F32) UPBV(float, bf16);
+        else if (dy_dtype == CATNN_F32) UPBV(bf16, float);
+        else UPBV(bf16, bf16);
+    } else if (dtype == CATNN_BF16) {
         if (yp_dtype == CATNN_F32 && dy_dtype == CATNN_F32) UPB(float, float, bf16);
         else if (yp_dtype == CATNN_F32) UPB(float, bf16, bf16);
         else if (dy_dtype == CATNN_F32) UPB(bf16, float, bf16);
@@ -469,6 +516,7 @@ void unpermute_bwd(Context* c, const void* yp, const int32_t* src_of, i64 rows, 
         UPB(float, float, float);
     }
 #undef UPB
+#undef UPBV
     launched(c);
 }
 
