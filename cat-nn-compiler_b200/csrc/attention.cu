@@ -75,6 +75,30 @@ __global__ void k_embed_bwd_runs(const uint32_t* __restrict__ keys, i64 n, const
     }
 }
 
+// k_embed_bwd_runs with 4 consecutive columns per thread (16-byte loads of
+// fp32 dy rows and stores of dw, 8-byte loads of bf16 rows); each column is
+// still summed in token order onto zero, so the result is the same bits.
+template <typename T>
+__global__ void __launch_bounds__(256) k_embed_bwd_runs4(const uint32_t* __restrict__ keys, i64 n,
+                                                         const T* __restrict__ dy, float* __restrict__ dw, i64 hidden) {
+    const i64 i = blockIdx.x;
+    const uint32_t id = keys[i] / (uint32_t)n;
+    if (i > 0 && keys[i - 1] / (uint32_t)n == id) return;
+    i64 end = i + 1;
+    while (end < n && keys[end] / (uint32_t)n == id) ++end;
+    for (i64 col = (i64)threadIdx.x * 4; col < hidden; col += (i64)blockDim.x * 4) {
+        float s[4] = {0.f, 0.f, 0.f, 0.f};
+        for (i64 r = i; r < end; ++r) {
+            const i64 t = keys[r] % (uint32_t)n;
+            float v[4];
+            ldv<T, 4>(dy + t * hidden + col, v);
+#pragma unroll
+            for (int u = 0; u < 4; ++u) s[u] = __fadd_rn(s[u], v[u]);
+        }
+        stv<float, 4>(dw + (i64)id * hidden + col, s);
+    }
+}
+
 static void embed_bwd_check(i64 n, i64 vocab) {
     CATNN_CHECK(n <= 32768, CATNN_ERR_UNSUPPORTED, "embedding_bwd: at most 32768 tokens per call");
     CATNN_CHECK((unsigned long long)vocab * (unsigned long long)n < 0xFFFFFFFFull, CATNN_ERR_UNSUPPORTED,
@@ -101,7 +125,11 @@ void embedding_bwd_runs(Context* c, const uint32_t* keys, i64 n, const void* dy,
     CUDA_OK(cudaMemsetAsync(dw, 0, (size_t)vocab * hidden * 4, c->stream));
     if (n <= 0) return;
     int th = hidden >= 256 ? 256 : 64;
-    if (dtype == CATNN_BF16) k_embed_bwd_runs<<<n, th, 0, c->stream>>>(keys, n, (const bf16*)dy, dw, hidden);
+    if (hidden % 4 == 0 && aligned_to(dw, 16) && aligned_to(dy, dtype == CATNN_BF16 ? 8 : 16)) {
+        const int t4 = (int)std::min<i64>(256, std::max<i64>(32, cdiv(hidden / 4, 32) * 32));
+        if (dtype == CATNN_BF16) k_embed_bwd_runs4<<<n, t4, 0, c->stream>>>(keys, n, (const bf16*)dy, dw, hidden);
+        else k_embed_bwd_runs4<<<n, t4, 0, c->stream>>>(keys, n, (const float*)dy, dw, hidden);
+    } else if (dtype == CATNN_BF16) k_embed_bwd_runs<<<n, th, 0, c->stream>>>(keys, n, (const bf16*)dy, dw, hidden);
     else k_embed_bwd_runs<<<n, th, 0, c->stream>>>(keys, n, (const float*)dy, dw, hidden);
     launched(c);
 }
